@@ -1,0 +1,385 @@
+"""Benchmark: julia-cuda's headline metric on B200.
+
+Workload: one request of 293 tokens, 4 markers, question type 0, through the
+hidden-768 / 12-head / 22-layer encoder, the 2-layer head and the 768 -> 384 -> 1 scorer, batch 1
+per engine; synthetic token ids (uniform over the 50368-token vocabulary, seeded) and seeded
+random-init weights (N(0, 0.02), LayerNorm gamma 1 + N(0, 0.05)). A step is one request
+embed -> logits. With --gpus N (torchrun), every rank runs its own engine on its own requests
+(replicas: a request does not shard), no collective on the data path.
+
+  value      requests/s over all ranks, inputs resident in HBM, device time (CUDA events) of the
+             K timed steps, max over ranks; L2 flushed (a 256 MiB write) before every step, outside
+             the timed events.
+  e2e        the same metric through julia_cuda_run (the reference's C ABI) from host arrays:
+             host -> pinned -> device copies of the ids and markers and the device -> host copy of
+             the logits are inside the timed region (host wall clock).
+  roofline   the kernel with the largest share of a forward pass, timed alone with CUDA events.
+  cpu_baseline  the oracle's f32 forward (C, OpenMP over the host's cores) on a bounded sample.
+
+--impl reference: the reference's own CPU path cannot be built here (Rust / julia-rs absent), so
+the reference arm times the oracle's f32 restatement of it on all host cores.
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQ = 293
+MARKERS = 4
+SEED = 1234
+MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC = os.path.join(ROOT, "profiles", "traffic.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    try:
+        with open(MEASURED) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def request(rank, vocab):
+    rng = np.random.default_rng(1000 + rank)
+    ids = rng.integers(0, vocab, SEQ).astype(np.uint32)
+    markers = np.sort(rng.choice(SEQ, MARKERS, replace=False)).astype(np.uint32)
+    return ids, markers
+
+
+def cpu_forward_sample(budget_s=20.0, max_runs=5):
+    """The oracle's f32 forward at config 0 on all host threads; returns (s/request, runs, cores)."""
+    from oracle import oracle as O
+    c = O.config(max_positions=1024)
+    raw = O.init_random(c, SEED)
+    ids, markers = request(0, c.vocab)
+    O.forward_f32(c, raw, ids[:32], markers[:1] % 32, 0)  # warm the thread pool
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < max_runs and (time.perf_counter() - t_all) < budget_s:
+        t0 = time.perf_counter()
+        O.forward_f32(c, raw, ids, markers, 0)
+        times.append(time.perf_counter() - t0)
+    return statistics.mean(times), len(times), O.num_threads()
+
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU while the timed region runs."""
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([s.strip() for s in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return None
+        sm = [float(r[0]) for r in self.rows if r and r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for i, nm in enumerate(names):
+                if len(r) > 4 + i and r[4 + i].lower() == "active":
+                    reasons.add(nm)
+        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.rows)}
+
+
+def gemm_shapes(cfg, n):
+    """The forward pass's GEMMs: name, epilogue, n_out-cols, k, launches per forward."""
+    D, I, F, S, L, HL = (cfg.d_model, cfg.inter, cfg.head_ff, cfg.scorer_hidden, cfg.n_layers,
+                         cfg.n_head_layers)
+    return [("qkv", "lnrope", 3 * D, D, L), ("wo", "resstats", D, D, L),
+            ("wi", "lngeglu", 2 * I, D, L), ("wo_mlp", "resstats", D, I, L),
+            ("head_in", "lnbias", 3 * D, D, HL), ("head_l1", "lnbiasrelu", F, D, HL),
+            ("head_l2", "biasresstats", D, F, HL)]
+
+
+def time_kernels(jc, torch, cfg, flush, reps=30):
+    """Each GEMM shape and attention of the forward pass alone, CUDA events on the launching
+    stream, L2 flushed before every launch. Returns {name: (avg ms, launches per forward,
+    algorithmic bytes, flops)}."""
+    from oracle import oracle as O
+    n = SEQ
+    out = {}
+    stream = torch.cuda.current_stream()
+    for name, epi_name, N, K, count in gemm_shapes(cfg, n):
+        epi = jc.EPILOGUES[epi_name]
+        a = torch.randn(n, K, device="cuda").half()
+        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        n_out = N // 2 if epi & jc.EPI_GEGLU else N
+        c = torch.randn(n, n_out, device="cuda").half()
+        st = torch.rand(2 * n, device="cuda") + 1.0
+        st[1::2] += 800.0
+        cs = torch.randn(N, device="cuda")
+        rope = torch.from_numpy(O.rope_table(160000.0, n)).cuda()
+        bias = torch.randn(N, device="cuda")
+        so = torch.zeros(2 * n, device="cuda")
+        ws, cnt = jc.gemm_scratch(n, N, K)
+
+        def launch():
+            jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st, colsum=cs,
+                    stats_out=so, rope=rope, bias=bias, ws=ws, counters=cnt, stream=stream)
+        for _ in range(3):
+            launch()
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.mean(times)
+        bytes_ = 2 * (n * K + N * K + n * n_out) + (2 * n * N if epi & jc.EPI_RES else 0) + \
+            (8 * n + 4 * N if epi & jc.EPI_LN else 0) + (4 * N if epi & jc.EPI_BIAS else 0) + \
+            (256 * n if epi & jc.EPI_ROPE else 0) + (8 * n if epi & jc.EPI_STATS else 0)
+        out[name] = (ms, count, bytes_, 2.0 * n * N * K)
+    heads = cfg.n_heads
+    qkv = torch.randn(n, 3 * heads * 64, device="cuda").half()
+    o = torch.zeros(n, heads * 64, device="cuda").half()
+    n_global = len([l for l in range(cfg.n_layers) if l % cfg.global_every == 0])
+    for name, window, count in [("attn_global", 0, n_global + cfg.n_head_layers),
+                                ("attn_window", cfg.window, cfg.n_layers - n_global)]:
+        for _ in range(3):
+            jc.attention(qkv, o, heads, window, stream=stream)
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            jc.attention(qkv, o, heads, window, stream=stream)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        keys = n if window == 0 else sum(min(i + window, n - 1) - max(i - window, 0) + 1
+                                         for i in range(n)) / n
+        out[name] = (statistics.mean(times), count, 2 * (n * 3 * heads * 64 + n * heads * 64),
+                     4.0 * n * keys * heads * 64)
+    return out
+
+
+def reference_arm(args, rank, world):
+    """The reference's CPU path (restated: the oracle's f32 forward) on all host cores."""
+    if rank != 0:
+        return
+    per, runs, cores = None, 0, None
+    from oracle import oracle as O
+    c = O.config(max_positions=1024)
+    raw = O.init_random(c, SEED)
+    ids, markers = request(0, c.vocab)
+    for _ in range(min(args.warmup, 1)):
+        O.forward_f32(c, raw, ids, markers, 0)
+    steps = max(1, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.forward_f32(c, raw, ids, markers, 0)
+    el = time.perf_counter() - t0
+    per = el / steps
+    cores = O.num_threads()
+    v = 1.0 / per
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "requests/s",
+        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
+        "ms_per_step": per * 1e3, "us_per_request": per * 1e6, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config0: 293-token request, batch 1, hidden 768, 22 layers + head",
+                   "global_batch": 1, "seq_len": SEQ, "parallelism": "host threads"},
+        "cpu_baseline": {"value": v, "unit": "requests/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} full requests (f32 restatement of julia-rs; the Rust "
+                                   f"reference and julia-rs cannot be built here)"},
+        "e2e": {"value": v, "unit": "requests/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layer-fused", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if args.warmup < 3:
+        args.warmup = 3
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
+    ids, markers = request(rank, cfg.vocab)
+    ids_d = torch.from_numpy(ids.view(np.int32)).cuda()
+    mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
+    logits = torch.zeros(MARKERS, dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    fused = args.layer_fused
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=fused, stream=stream)
+    torch.cuda.synchronize()
+    assert jc.device_error() == 0
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=fused, stream=stream)
+            ev[i][1].record(stream)
+        barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_s = sum(step_ms) / 1e3
+    assert jc.device_error() == 0
+    if world > 1:
+        t = torch.tensor([total_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_s = float(t.item())
+    value = world * args.steps / total_s
+    ms_per_step = total_s * 1e3 / args.steps
+
+    # e2e through julia_cuda_run: host arrays in, logits out, copies inside the timed region.
+    seqs = [(ids, markers, 0)]
+    for _ in range(3):
+        eng.run(seqs, layer_fused=fused)
+    e2e_times, gpu_ms = [], []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _, ms = eng.run(seqs, layer_fused=fused)
+        e2e_times.append(time.perf_counter() - t0)
+        gpu_ms.append(float(ms[0]))
+    barrier()
+    e2e_total = sum(e2e_times)
+    if world > 1:
+        t = torch.tensor([e2e_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = world * args.steps / e2e_total
+
+    roofline = kernels = None
+    cpu = None
+    if rank == 0:
+        pk, src = peaks()
+        kt = time_kernels(jc, torch, cfg, flush)
+        dom = max(kt, key=lambda k: kt[k][0] * kt[k][1])
+        ms, count, bytes_, flops = kt[dom]
+        achieved = bytes_ / (ms * 1e-3) / 1e9
+        traffic = None
+        try:
+            with open(TRAFFIC) as f:
+                traffic = json.load(f).get(dom)
+        except Exception:
+            pass
+        roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved,
+                    "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                    "traffic": traffic, "peak_source": src,
+                    "tflops": flops / (ms * 1e-3) / 1e12, "us_per_launch": ms * 1e3,
+                    "launches_per_forward": count, "algorithmic_bytes": bytes_}
+        kernels = {k: {"us": v[0] * 1e3, "per_forward": v[1],
+                       "gbs": v[2] / (v[0] * 1e-3) / 1e9, "tflops": v[3] / (v[0] * 1e-3) / 1e12}
+                   for k, v in kt.items()}
+        if world == 1 and not args.no_cpu_baseline:
+            per, runs, cores = cpu_forward_sample()
+            cpu = {"value": 1.0 / per, "unit": "requests/s", "cores": cores, "kind": "port",
+                   "sample": f"{runs} full 293-token requests, f32 restatement of the reference's "
+                             f"CPU path (julia-rs), OpenMP"}
+    launches = eng.launches_per_forward(SEQ, MARKERS, fused) * args.steps
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "us_per_request": ms_per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
+            "config": {"workload": "config0: 293-token request, 4 markers, batch 1 per engine; "
+                                   "hidden 768, 12 heads, 22 layers, 2 head layers, scorer 384",
+                       "global_batch": world, "seq_len": SEQ, "parallelism": f"replicas x{world}",
+                       "l2": "flushed (256 MiB write) before every timed step",
+                       "path": "persistent layer kernel" if fused else "per-step kernels, CUDA graph + PDL"},
+            "e2e": {"value": e2e_value, "unit": "requests/s",
+                    "us_per_request": e2e_total / args.steps * 1e6,
+                    "gpu_ms_per_request": statistics.mean(gpu_ms),
+                    "h2d_bytes_per_step": SEQ * 4 + MARKERS * 4,
+                    "d2h_bytes_per_step": MARKERS * 4},
+            "gpu_launches": launches,
+            "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

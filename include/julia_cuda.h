@@ -1,0 +1,193 @@
+/*
+ * julia-cuda-b200: the julia-cuda encoder hot path (ModernBERT-style encoder, 2-layer head and
+ * scorer of Julia-1) on NVIDIA B200 (sm_100a). C ABI of libjulia_cuda.so.
+ *
+ * Conventions (as the reference's src/capi.rs:4-6, 23-54): functions returning a pointer give NULL
+ * on failure and those returning an int give -1; the message goes to `err` (err_len bytes,
+ * NUL-terminated, truncated) when the function takes one, else to jc_last_error(). Nothing throws
+ * across the boundary. The caller owns every array. An engine must not be used by two threads at
+ * once (src/capi.rs:116); use one engine per GPU for several GPUs.
+ *
+ * f16 values are passed as uint16_t bit patterns. "Device" pointers are CUDA device memory of the
+ * current device; `stream` is a cudaStream_t (NULL: the legacy default stream).
+ */
+#ifndef JULIA_CUDA_H
+#define JULIA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct JcEngine JcEngine;
+
+/* The model's shape: the fields of julia-rs's ModelConfig the reference reads
+ * (src/checkpoint.rs:29; hidden, intermediate, n_layers, norm_eps, local_window/2, max_positions,
+ * rope_theta_global/local, vocab, head_ff) plus the head/scorer widths. */
+typedef struct jc_model_config {
+    int32_t d_model;       /* hidden width, a multiple of 128 up to 1024 */
+    int32_t n_heads;       /* d_model / 64 */
+    int32_t inter;         /* GeGLU intermediate width, a multiple of 64 */
+    int32_t n_layers;      /* encoder layers */
+    int32_t vocab;
+    int32_t head_ff;       /* head linear1 width, a multiple of 64 */
+    int32_t scorer_hidden; /* scorer lin1 width, a multiple of 64 */
+    int32_t n_head_layers;
+    int32_t global_every;  /* layer l uses global attention when l % global_every == 0 */
+    int32_t window;        /* sliding-window reach: keys with |q - k| <= window */
+    int32_t max_positions; /* RoPE table length (longest sequence) */
+    int32_t n_qtypes;      /* type embeddings: 0 choice, 1 score, 2 noul */
+    float norm_eps;        /* encoder LayerNorm eps */
+    float head_eps;        /* head and scorer LayerNorm eps */
+    float theta_global;    /* RoPE base of the global layers */
+    float theta_local;     /* RoPE base of the sliding-window layers */
+} jc_model_config;
+
+/* ============================ the reference's C ABI (src/capi.rs) ============================ */
+
+/* The kernel tier this library was built for ("sm_100a"), static. Replaces src/capi.rs:56-62. */
+const char *julia_cuda_tier(void);
+
+/* Opens a checkpoint directory and uploads it to GPU 0 (src/capi.rs:64-85). Reads the raw model
+ * format below from `dir/jc_config.bin` + `dir/jc_weights.f32` (written by
+ * julia_cuda_save_raw); `max_length` 0 means the model's max_positions. */
+JcEngine *julia_cuda_load(const char *dir, size_t max_length, char *err, size_t err_len);
+
+/* Frees an engine (NULL is fine). Replaces src/capi.rs:87-96. */
+void julia_cuda_free(JcEngine *engine);
+
+/* The GPU's name into buf (len bytes, NUL-terminated). Replaces src/capi.rs:98-106. */
+void julia_cuda_device(const JcEngine *engine, char *buf, size_t len);
+
+/* Runs b sequences back to back: sequence i is lens[i] token ids (concatenated in ids) with
+ * n_markers[i] marker positions (concatenated in markers) and question type qtypes[i]. Writes each
+ * sequence's logits (one per marker, concatenated) and its GPU time in ms (embed to logits) into
+ * gpu_ms[i]. layer_fused: the persistent per-layer kernel instead of the per-step kernels.
+ * Returns 0, or -1 with the error in err (also for non-finite logits and device-side timeouts).
+ * Replaces src/capi.rs:108-190. */
+int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const size_t *lens,
+                   const uint32_t *markers, const size_t *n_markers, const uint32_t *qtypes,
+                   int layer_fused, float *logits, float *gpu_ms, char *err, size_t err_len);
+
+/* ================================ additions to the reference ================================ */
+
+/* The benchmark model: hidden 768, 12 heads, GeGLU 1152, 22 layers, vocab 50368, head_ff 2048,
+ * scorer 768 -> 384 -> 1, global every 3rd layer, window 64, theta 160000 / 10000. */
+void julia_cuda_default_config(jc_model_config *cfg);
+
+/* The raw model format: every tensor f32, [out, in] matrices, packed in this order:
+ * tok_embeddings [vocab, D], emb_norm [D]; per layer: attn_norm [D] (absent in layer 0),
+ * Wqkv [3D, D], Wo [D, D], mlp_norm [D], Wi [2I, D] (GELU inputs, then gates), Wo_mlp [D, I];
+ * final_norm [D], type_emb [n_qtypes, D]; per head layer: norm1 w, b [D], in_proj w [3D, D], b [3D],
+ * out_proj w [D, D], b [D], norm2 w, b [D], linear1 w [F, D], b [F], linear2 w [D, F], b [D];
+ * scorer norm w, b [D], lin1 w [S, D], b [S], lin2 w [1, S], b [1]. */
+size_t julia_cuda_raw_size(const jc_model_config *cfg);
+/* The offset of every tensor above, in order (cap entries at most); returns the count or -1. */
+int julia_cuda_raw_offsets(const jc_model_config *cfg, size_t *offsets, size_t cap);
+/* Seeded synthetic weights in the raw format: matrices, embeddings, biases, betas and type
+ * embeddings N(0, 0.02); LayerNorm gammas 1 + N(0, 0.05). */
+void julia_cuda_init_random(const jc_model_config *cfg, uint64_t seed, float *raw);
+/* Writes cfg + raw to dir (jc_config.bin, jc_weights.f32) for julia_cuda_load. */
+int julia_cuda_save_raw(const char *dir, const jc_model_config *cfg, const float *raw,
+                        char *err, size_t err_len);
+
+/* Builds an engine on GPU `device` from raw weights (prepared on the host: LayerNorm folds,
+ * GeGLU interleave, f16 conversion, RoPE tables), buffers for sequences up to max_length. */
+JcEngine *julia_cuda_load_raw(const jc_model_config *cfg, const float *raw, size_t raw_len,
+                              size_t max_length, int device, char *err, size_t err_len);
+JcEngine *julia_cuda_load_random(const jc_model_config *cfg, uint64_t seed, size_t max_length,
+                                 int device, char *err, size_t err_len);
+
+/* One sequence with inputs already on the engine's device: d_ids [n], d_markers [n_markers];
+ * writes d_logits [n_markers]. Queued on `stream` (NULL: the engine's stream), not waited for.
+ * d_trace, if not NULL, receives the residual stream (f16) after every encoder layer,
+ * [n_layers][n][D] (slower: no CUDA graph). Returns 0 or -1. */
+int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                              const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                              int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
+                              char *err, size_t err_len);
+
+/* How many kernels one forward pass launches (for launch accounting). */
+int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,
+                                    int layer_fused);
+/* Model config and limits of an engine. */
+int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_t *max_length,
+                             int *device, int *sms);
+
+/* ============================ per-kernel entry points (device) ============================ */
+/* Kernel-level boundary of the reference (src/gemm.rs:254 gemm::launch, kernels/src/main.rs:
+ * 1043-1066 gemm_*(a, w, c, res, ws, counters, stats_in, colsum, stats_out, zero, zero_len, m, n,
+ * k, eps, rope, bias)). Return 0, or -1 with jc_last_error(). */
+
+/* Epilogue flags (kernels/src/main.rs:870-877). */
+#define JC_EPI_RES 1u    /* c += a.w^T (res may alias c) */
+#define JC_EPI_GEGLU 2u  /* c[:, j] = GELU(u_j) * g_j over interleaved Wi rows; c is [m, n/2] */
+#define JC_EPI_LN 4u     /* LayerNorm folded: rstd * (acc - mean * colsum), stats from stats_in */
+#define JC_EPI_STATS 8u  /* row sum / sum of squares of the stored f16 outputs added to stats_out */
+#define JC_EPI_ROPE 16u  /* rotate-half RoPE on dims (i, i+32) of q and k heads (natural order) */
+#define JC_EPI_BIAS 32u
+#define JC_EPI_RELU 64u
+#define JC_EPI_GELU 128u
+
+/* c = epilogue(a . w^T): a [m, k] f16, w [n, k] f16, c [m, n] f16 ([m, n/2] for GEGLU), k a
+ * multiple of 64. bn (32/64/128) and splits (1..8) of 0 choose automatically. ws / counters: the
+ * split-K workspace (jc_gemm_ws_floats floats, jc_gemm_counters zeroed u32, kept zero between
+ * calls). stats_in / stats_out: [m][2] f32 (sum, sum of squares). rope: [>= m][32][2] (cos, sin).
+ * zero / zero_len: a float buffer to clear on the way. Replaces src/gemm.rs:254-392. */
+int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t *w, uint16_t *c,
+            const uint16_t *res, float *ws, uint32_t *counters, const float *stats_in,
+            const float *colsum, float *stats_out, float *zero, uint32_t zero_len, uint32_t m,
+            uint32_t n, uint32_t k, float eps, const float *rope, const float *bias, void *stream);
+size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
+size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
+/* The automatic choice (gemm::choose, src/gemm.rs:153-172, refit for the B200's SMs). */
+int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *splits);
+
+/* o = softmax(q k^T / 8) v per 64-wide head, qkv [n, 3*heads*64] (q | k | v, natural order),
+ * o [n, heads*64]; window 0 = global, else keys with |q - k| <= window. kv_chunks > 1 splits the
+ * keys into ranges (needs ws / counters, jc_attention_ws_floats / jc_attention_counters; counters
+ * zero, kept zero); 0 chooses. Replaces kernels/src/main.rs:303-542 and src/attn.rs:20-56. */
+int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, uint32_t window,
+                 uint32_t kv_chunks, float *ws, uint32_t *counters, void *stream);
+size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
+size_t jc_attention_counters(uint32_t n, uint32_t heads);
+
+/* x[i] = LayerNorm(table[ids[i]]) * gamma, f16; stats (optional) [n][2]. Replaces
+ * kernels/src/main.rs:47-103 + src/lib.rs:164-219. */
+int jc_embed(const uint32_t *ids, uint32_t n, const uint16_t *table, const float *gamma,
+             uint32_t d, float eps, uint16_t *x, float *stats, void *stream);
+/* out = LayerNorm(x) * gamma + add, stats [n][2] of out. Replaces kernels/src/main.rs:108-176. */
+int jc_norm_add(const uint16_t *x, uint32_t n, uint32_t d, const float *gamma, const float *add,
+                float eps, uint16_t *out, float *stats, void *stream);
+/* logits[i] = y[markers[i]] . w + b. Replaces kernels/src/main.rs:180-200. */
+int jc_score(const uint16_t *y, uint32_t d, const uint16_t *w, float b, const uint32_t *markers,
+             uint32_t k, float *logits, void *stream);
+
+/* The last error message of this thread. */
+const char *jc_last_error(void);
+/* Reads and clears the device error word of the current device (0: none). */
+int jc_device_error(uint32_t *code);
+
+/* ============================== host weight preparation ============================== */
+/* src/prep.rs. f16 outputs are bit patterns. */
+
+/* W' = f16(w * gamma) ([out, k]), colsum[j] = sum_k W'[j, k] (f64 of the rounded values). */
+void jc_prep_fold_layernorm(const float *w, const float *gamma, uint32_t out, uint32_t k,
+                            uint16_t *w16, float *colsum);
+/* Also bias' = b + W . beta (f64, from the f32 w). */
+void jc_prep_fold_layernorm_bias(const float *w, const float *gamma, const float *beta,
+                                 const float *b, uint32_t out, uint32_t k, uint16_t *w16,
+                                 float *colsum, float *bias);
+/* Wi rows [2I, k] (GELU inputs, then gates) in the GeGLU epilogue's order: packed row
+ * 64t + 32s + e is source row 32t + e (+ I when s = 1). k = 1 reorders a vector. */
+void jc_prep_interleave_geglu_f16(const uint16_t *w, uint32_t n, uint32_t k, uint16_t *out);
+void jc_prep_interleave_geglu_f32(const float *w, uint32_t n, uint32_t k, float *out);
+/* RoPE (cos, sin) table [n][32][2] in f32. */
+void jc_prep_rope_table(float theta, uint32_t n, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JULIA_CUDA_H */

@@ -1,0 +1,384 @@
+"""julia-cuda-b200: the julia-cuda encoder hot path on B200, from Python.
+
+A thin ctypes layer over libjulia_cuda.so (include/julia_cuda.h), mirroring the reference's own
+FFI surface: the engine calls of src/capi.rs (julia_cuda_load / run / free / device / tier) and the
+kernel-level launches of src/gemm.rs, src/attn.rs and src/lib.rs. torch tensors are used only for
+device memory and streams. There is no CPU fallback: importing this package on a machine without
+the built library raises, and every kernel call fails loudly if its launch fails.
+
+The directory name is not an identifier; import it with importlib.import_module("julia-cuda_b200").
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libjulia_cuda.so")
+
+EPI_RES, EPI_GEGLU, EPI_LN, EPI_STATS = 1, 2, 4, 8
+EPI_ROPE, EPI_BIAS, EPI_RELU, EPI_GELU = 16, 32, 64, 128
+
+# The reference's eight GEMM variants (src/gemm.rs:57-87) as epilogue flags.
+EPILOGUES = {
+    "rope": EPI_ROPE,
+    "lnrope": EPI_LN | EPI_ROPE,
+    "lngeglu": EPI_LN | EPI_GEGLU,
+    "resstats": EPI_RES | EPI_STATS,
+    "lnbias": EPI_LN | EPI_BIAS,
+    "lnbiasrelu": EPI_LN | EPI_BIAS | EPI_RELU,
+    "lnbiasgelu": EPI_LN | EPI_BIAS | EPI_GELU,
+    "biasresstats": EPI_BIAS | EPI_RES | EPI_STATS,
+}
+
+
+class JuliaCudaError(RuntimeError):
+    pass
+
+
+class Config(ctypes.Structure):
+    """jc_model_config."""
+
+    _fields_ = [
+        ("d_model", ctypes.c_int32), ("n_heads", ctypes.c_int32), ("inter", ctypes.c_int32),
+        ("n_layers", ctypes.c_int32), ("vocab", ctypes.c_int32), ("head_ff", ctypes.c_int32),
+        ("scorer_hidden", ctypes.c_int32), ("n_head_layers", ctypes.c_int32),
+        ("global_every", ctypes.c_int32), ("window", ctypes.c_int32),
+        ("max_positions", ctypes.c_int32), ("n_qtypes", ctypes.c_int32),
+        ("norm_eps", ctypes.c_float), ("head_eps", ctypes.c_float),
+        ("theta_global", ctypes.c_float), ("theta_local", ctypes.c_float),
+    ]
+
+    def replace(self, **kw) -> "Config":
+        c = Config()
+        ctypes.memmove(ctypes.byref(c), ctypes.byref(self), ctypes.sizeof(Config))
+        for k, v in kw.items():
+            setattr(c, k, v)
+        if "d_model" in kw and "n_heads" not in kw:
+            c.n_heads = c.d_model // 64
+        return c
+
+
+def build() -> None:
+    """Compiles libjulia_cuda.so in place (nvcc -gencode arch=compute_100a,code=sm_100a)."""
+    subprocess.run(["make", "-s", "-j8", "-C", HERE], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise JuliaCudaError(f"{LIB_PATH} is not built (run build() / make -C julia-cuda_b200)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, u32, i32, f32, sz, u64 = (ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_float,
+                                 ctypes.c_size_t, ctypes.c_uint64)
+    cfgp = ctypes.POINTER(Config)
+    ch = ctypes.c_char_p
+    sig = {
+        "julia_cuda_tier": ([], ch),
+        "julia_cuda_load": ([ch, sz, P, sz], P),
+        "julia_cuda_free": ([P], None),
+        "julia_cuda_device": ([P, P, sz], None),
+        "julia_cuda_run": ([P, sz, P, P, P, P, P, i32, P, P, P, sz], i32),
+        "julia_cuda_default_config": ([cfgp], None),
+        "julia_cuda_raw_size": ([cfgp], sz),
+        "julia_cuda_raw_offsets": ([cfgp, P, sz], i32),
+        "julia_cuda_init_random": ([cfgp, u64, P], None),
+        "julia_cuda_save_raw": ([ch, cfgp, P, P, sz], i32),
+        "julia_cuda_load_raw": ([cfgp, P, sz, sz, i32, P, sz], P),
+        "julia_cuda_load_random": ([cfgp, u64, sz, i32, P, sz], P),
+        "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
+        "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
+        "julia_cuda_engine_config": ([P, cfgp, P, P, P], i32),
+        "jc_gemm": ([u32, i32, i32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32, f32, P, P, P],
+                    i32),
+        "jc_gemm_ws_floats": ([u32, u32, u32, i32, i32], sz),
+        "jc_gemm_counters": ([u32, u32, u32, i32, i32], sz),
+        "jc_choose_gemm": ([u32, u32, u32, i32, P, P], i32),
+        "jc_attention": ([P, P, u32, u32, u32, u32, P, P, P], i32),
+        "jc_attention_ws_floats": ([u32, u32, u32], sz),
+        "jc_attention_counters": ([u32, u32], sz),
+        "jc_embed": ([P, u32, P, P, u32, f32, P, P, P], i32),
+        "jc_norm_add": ([P, u32, u32, P, P, f32, P, P, P], i32),
+        "jc_score": ([P, u32, P, f32, P, u32, P, P], i32),
+        "jc_last_error": ([], ch),
+        "jc_device_error": ([P], i32),
+        "jc_prep_fold_layernorm": ([P, P, u32, u32, P, P], None),
+        "jc_prep_fold_layernorm_bias": ([P, P, P, P, u32, u32, P, P, P], None),
+        "jc_prep_interleave_geglu_f16": ([P, u32, u32, P], None),
+        "jc_prep_interleave_geglu_f32": ([P, u32, u32, P], None),
+        "jc_prep_rope_table": ([f32, u32, P], None),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return lib().jc_last_error().decode(errors="replace")
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise JuliaCudaError(f"{what}: {last_error()}")
+
+
+def default_config(**kw) -> Config:
+    c = Config()
+    lib().julia_cuda_default_config(ctypes.byref(c))
+    return c.replace(**kw) if kw else c
+
+
+def _np_ptr(a):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def _t_ptr(t):
+    """Device pointer of a contiguous torch tensor (or None)."""
+    if t is None:
+        return None
+    if not t.is_contiguous():
+        raise JuliaCudaError("tensors passed to the kernels must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+# ------------------------------------------------------------------------------------------------
+# raw model format and host preparation
+
+def raw_size(cfg: Config) -> int:
+    return lib().julia_cuda_raw_size(ctypes.byref(cfg))
+
+
+def raw_offsets(cfg: Config) -> np.ndarray:
+    cap = 16 * (cfg.n_layers + cfg.n_head_layers) + 64
+    out = np.zeros(cap, np.uint64)
+    n = lib().julia_cuda_raw_offsets(ctypes.byref(cfg), _np_ptr(out), cap)
+    if n < 0:
+        raise JuliaCudaError(last_error())
+    return out[:n]
+
+
+def init_random(cfg: Config, seed: int) -> np.ndarray:
+    raw = np.empty(raw_size(cfg), np.float32)
+    lib().julia_cuda_init_random(ctypes.byref(cfg), seed, _np_ptr(raw))
+    return raw
+
+
+def prep_fold_layernorm(w: np.ndarray, gamma: np.ndarray):
+    out, k = w.shape
+    w16 = np.zeros((out, k), np.uint16)
+    cs = np.zeros(out, np.float32)
+    lib().jc_prep_fold_layernorm(_np_ptr(np.ascontiguousarray(w, np.float32)),
+                                 _np_ptr(np.ascontiguousarray(gamma, np.float32)), out, k,
+                                 _np_ptr(w16), _np_ptr(cs))
+    return w16, cs
+
+
+def prep_fold_layernorm_bias(w, gamma, beta, b):
+    out, k = w.shape
+    w16 = np.zeros((out, k), np.uint16)
+    cs = np.zeros(out, np.float32)
+    bias = np.zeros(out, np.float32)
+    f = lambda a: _np_ptr(np.ascontiguousarray(a, np.float32))
+    lib().jc_prep_fold_layernorm_bias(f(w), f(gamma), f(beta), f(b), out, k, _np_ptr(w16),
+                                      _np_ptr(cs), _np_ptr(bias))
+    return w16, cs, bias
+
+
+def prep_interleave_geglu(w: np.ndarray) -> np.ndarray:
+    """Wi rows (GELU inputs, then gates) in the GeGLU epilogue's order; 1-D: a vector."""
+    a = np.ascontiguousarray(w)
+    n = a.shape[0]
+    k = a.shape[1] if a.ndim == 2 else 1
+    out = np.empty_like(a)
+    if a.dtype == np.uint16:
+        lib().jc_prep_interleave_geglu_f16(_np_ptr(a), n, k, _np_ptr(out))
+    elif a.dtype == np.float32:
+        lib().jc_prep_interleave_geglu_f32(_np_ptr(a), n, k, _np_ptr(out))
+    else:
+        raise JuliaCudaError("interleave: uint16 (f16 bits) or float32 only")
+    return out
+
+
+def prep_rope_table(theta: float, n: int) -> np.ndarray:
+    t = np.zeros((n, 32, 2), np.float32)
+    lib().jc_prep_rope_table(theta, n, _np_ptr(t))
+    return t
+
+
+# ------------------------------------------------------------------------------------------------
+# kernels on torch device tensors (f16 tensors are torch.float16)
+
+def gemm_scratch(m: int, n: int, k: int, bn: int = 0, splits: int = 0, device="cuda"):
+    """Split-K workspace and zeroed counters for jc_gemm with this shape / configuration."""
+    import torch
+    ws = lib().jc_gemm_ws_floats(m, n, k, bn, splits)
+    cnt = lib().jc_gemm_counters(m, n, k, bn, splits)
+    return (torch.empty(max(ws, 1), dtype=torch.float32, device=device),
+            torch.zeros(max(cnt, 1), dtype=torch.int32, device=device))
+
+
+def gemm(epi: int, a, w, c, *, res=None, stats_in=None, colsum=None, stats_out=None, zero=None,
+         eps: float = 1e-5, rope=None, bias=None, bn: int = 0, splits: int = 0, ws=None,
+         counters=None, stream=None) -> None:
+    """c = epilogue(a . w^T) (jc_gemm); a [m, k], w [n, k] f16."""
+    m, k = a.shape
+    n = w.shape[0]
+    if ws is None or counters is None:
+        ws, counters = gemm_scratch(m, n, k, bn, splits, a.device)
+    rc = lib().jc_gemm(epi, bn, splits, _t_ptr(a), _t_ptr(w), _t_ptr(c), _t_ptr(res), _t_ptr(ws),
+                       _t_ptr(counters), _t_ptr(stats_in), _t_ptr(colsum), _t_ptr(stats_out),
+                       _t_ptr(zero), 0 if zero is None else zero.numel(), m, n, k, eps,
+                       _t_ptr(rope), _t_ptr(bias), _stream(stream))
+    _check(rc, "jc_gemm")
+
+
+def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=None) -> None:
+    import torch
+    n = qkv.shape[0]
+    chunks = kv_chunks
+    ws = cnt = None
+    if kv_chunks != 1:
+        probe = 16 if kv_chunks == 0 else kv_chunks
+        ws = torch.empty(max(lib().jc_attention_ws_floats(n, heads, probe), 1), dtype=torch.float32,
+                         device=qkv.device)
+        cnt = torch.zeros(max(lib().jc_attention_counters(n, heads), 1), dtype=torch.int32,
+                          device=qkv.device)
+    rc = lib().jc_attention(_t_ptr(qkv), _t_ptr(o), n, heads, window, chunks, _t_ptr(ws),
+                            _t_ptr(cnt), _stream(stream))
+    _check(rc, "jc_attention")
+
+
+def embed(ids, table, gamma, x, eps=1e-5, stats=None, stream=None) -> None:
+    rc = lib().jc_embed(_t_ptr(ids), ids.numel(), _t_ptr(table), _t_ptr(gamma), table.shape[1],
+                        eps, _t_ptr(x), _t_ptr(stats), _stream(stream))
+    _check(rc, "jc_embed")
+
+
+def norm_add(x, gamma, add, out, stats, eps=1e-5, stream=None) -> None:
+    n, d = x.shape
+    rc = lib().jc_norm_add(_t_ptr(x), n, d, _t_ptr(gamma), _t_ptr(add), eps, _t_ptr(out),
+                           _t_ptr(stats), _stream(stream))
+    _check(rc, "jc_norm_add")
+
+
+def score(y, w, b: float, markers, logits, stream=None) -> None:
+    rc = lib().jc_score(_t_ptr(y), y.shape[1], _t_ptr(w), b, _t_ptr(markers), markers.numel(),
+                        _t_ptr(logits), _stream(stream))
+    _check(rc, "jc_score")
+
+
+def device_error() -> int:
+    code = ctypes.c_uint32(0)
+    _check(lib().jc_device_error(ctypes.byref(code)), "jc_device_error")
+    return code.value
+
+
+# ------------------------------------------------------------------------------------------------
+# engine (the reference's Engine / C ABI)
+
+class Engine:
+    """One model on one GPU: julia_cuda_load_raw / julia_cuda_load_random + julia_cuda_run."""
+
+    def __init__(self, handle, cfg: Config):
+        self._h = handle
+        self.cfg = cfg
+
+    @classmethod
+    def load_raw(cls, cfg: Config, raw: np.ndarray, max_length: int = 1024, device: int = 0):
+        raw = np.ascontiguousarray(raw, np.float32)
+        err = ctypes.create_string_buffer(1024)
+        h = lib().julia_cuda_load_raw(ctypes.byref(cfg), _np_ptr(raw), raw.size, max_length,
+                                      device, err, 1024)
+        if not h:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        return cls(h, cfg)
+
+    @classmethod
+    def load_random(cls, cfg: Config, seed: int, max_length: int = 1024, device: int = 0):
+        err = ctypes.create_string_buffer(1024)
+        h = lib().julia_cuda_load_random(ctypes.byref(cfg), seed, max_length, device, err, 1024)
+        if not h:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        return cls(h, cfg)
+
+    @classmethod
+    def load(cls, directory: str, max_length: int = 0):
+        err = ctypes.create_string_buffer(1024)
+        h = lib().julia_cuda_load(directory.encode(), max_length, err, 1024)
+        if not h:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        cfg = Config()
+        lib().julia_cuda_engine_config(h, ctypes.byref(cfg), None, None, None)
+        return cls(h, cfg)
+
+    def close(self) -> None:
+        if self._h:
+            lib().julia_cuda_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def device_name(self) -> str:
+        buf = ctypes.create_string_buffer(256)
+        lib().julia_cuda_device(self._h, buf, 256)
+        return buf.value.decode()
+
+    def run(self, seqs, layer_fused: bool = False):
+        """seqs: list of (ids, markers, qtype). Returns (list of logits arrays, gpu_ms array)."""
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(s[0], np.uint32) for s in seqs]))
+        lens = np.array([len(s[0]) for s in seqs], np.uint64)
+        mk = [np.asarray(s[1], np.uint32) for s in seqs]
+        markers = np.ascontiguousarray(np.concatenate(mk) if mk else np.zeros(0, np.uint32))
+        nmk = np.array([len(m) for m in mk], np.uint64)
+        qt = np.array([s[2] for s in seqs], np.uint32)
+        logits = np.zeros(max(int(nmk.sum()), 1), np.float32)
+        gpu_ms = np.zeros(len(seqs), np.float32)
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_run(self._h, len(seqs), _np_ptr(ids), _np_ptr(lens),
+                                  _np_ptr(markers), _np_ptr(nmk), _np_ptr(qt), int(layer_fused),
+                                  _np_ptr(logits), _np_ptr(gpu_ms), err, 1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        out, at = [], 0
+        for k in nmk:
+            out.append(logits[at:at + int(k)].copy())
+            at += int(k)
+        return out, gpu_ms
+
+    def forward_device(self, ids, markers, qtype: int, logits, trace=None, layer_fused=False,
+                       stream=None) -> None:
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_forward_device(self._h, _t_ptr(ids), ids.numel(), _t_ptr(markers),
+                                             markers.numel(), qtype, int(layer_fused),
+                                             _t_ptr(logits), _t_ptr(trace), _stream(stream), err,
+                                             1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+
+    def launches_per_forward(self, n: int, n_markers: int, layer_fused=False) -> int:
+        return lib().julia_cuda_launches_per_forward(self._h, n, n_markers, int(layer_fused))

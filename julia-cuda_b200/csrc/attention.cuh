@@ -1,0 +1,294 @@
+// Attention for the encoder and the head: o = softmax(q k^T / 8) v per 64-wide head, over all keys
+// (global layers, the head) or keys with |q - k| <= window (sliding-window layers).
+//
+// Replaces the reference's `attention` / `attention_task` (kernels/src/main.rs:303-542) and its
+// key-range merge (kernels/src/attn.rs:104-204). FlashAttention-2 structure: a CTA takes
+// 16 * WARPS queries of one head (16 per warp), streams 64-key tiles of K and V through
+// double-buffered, XOR-swizzled shared memory with cp.async, keeps S and the running
+// max / sum in registers (online softmax in exp2), rounds P to f16 for the P.V product and keeps
+// O in f32 registers. d = 64 tiles are too small for 128-row tcgen05 tiles at these sequence
+// lengths, so the products use the 16x8x16 tensor-core MMA.
+//
+// Sliding-window CTAs only visit the key tiles some query of theirs can reach. Global layers can
+// split each (query tile, head)'s key tiles into `chunks` contiguous ranges (gridDim.z): each
+// range stores its unnormalised partial; the last range of the tile to finish (atomic counter,
+// reset by it) merges all of them in range order, so the result does not depend on timing.
+//
+// qkv rows are [q | k | v], each `heads` heads of 64, in natural (checkpoint) order.
+#pragma once
+#include "common.cuh"
+
+namespace jc {
+
+struct AttnParams {
+    const __half *qkv;
+    __half *o;
+    float *ws;
+    uint32_t *counters;
+    uint32_t n, heads, window;
+};
+
+// Swizzled [rows][64] f16 tile: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
+__device__ __forceinline__ uint32_t swz64_off(uint32_t row, uint32_t chunk) {
+    return row * 64 + ((chunk ^ (row & 7)) << 3);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                 "r"(pred ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                          uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// c += a (16x16, row) * b (16x8, col), f16 inputs, f32 accumulators.
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Loads rows [row0, row0 + ROWS) of one head of one third (0 q, 1 k, 2 v) into a swizzled tile;
+// rows past n are zero-filled.
+template <int ROWS, int THREADS>
+__device__ __forceinline__ void load_head_tile(uint32_t tile, const AttnParams &p, uint32_t row0,
+                                               uint32_t head, uint32_t third) {
+    const uint32_t D = p.heads * 64;
+#pragma unroll
+    for (int i = 0; i < ROWS * 8 / THREADS; i++) {
+        const uint32_t c = threadIdx.x + i * THREADS;
+        const uint32_t row = c >> 3, ch = c & 7;
+        const uint32_t r = row0 + row;
+        const bool ok = r < p.n;
+        const __half *src = p.qkv + (size_t)(ok ? r : 0) * 3 * D + third * D + head * 64 + ch * 8;
+        cp_async16(tile + swz64_off(row, ch) * 2, src, ok);
+    }
+}
+
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnParams p) {
+    constexpr int QT = 16 * WARPS;  // queries per CTA
+    constexpr int THREADS = WARPS * 32;
+    __shared__ __align__(128) __half qs[QT * 64];
+    __shared__ __align__(128) __half ks[2][64 * 64];
+    __shared__ __align__(128) __half vs[2][64 * 64];
+    __shared__ uint32_t last_flag;
+
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, t = lane & 3;
+    const uint32_t q0 = blockIdx.x * QT, head = blockIdx.y;
+    const uint32_t chunk = blockIdx.z, chunks = gridDim.z;
+    const uint32_t n = p.n, window = p.window;
+
+    // Key tiles some query of this CTA can reach, then this chunk's share of them.
+    const uint32_t nb = (n + 63) / 64;
+    uint32_t kb_lo = 0, kb_hi = nb;
+    if (window > 0) {
+        kb_lo = (q0 > window ? q0 - window : 0) / 64;
+        uint32_t last_q = min(q0 + QT - 1, n - 1);
+        kb_hi = min(last_q + window, n - 1) / 64 + 1;
+    }
+    const uint32_t span = kb_hi - kb_lo;
+    const uint32_t kb0 = kb_lo + chunk * span / chunks, kb1 = kb_lo + (chunk + 1) * span / chunks;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const uint32_t qs_a = smem_u32(qs);
+    const uint32_t ks_a[2] = {smem_u32(ks[0]), smem_u32(ks[1])};
+    const uint32_t vs_a[2] = {smem_u32(vs[0]), smem_u32(vs[1])};
+
+    load_head_tile<QT, THREADS>(qs_a, p, q0, head, 0);
+    if (kb0 < kb1) {
+        load_head_tile<64, THREADS>(ks_a[0], p, kb0 * 64, head, 1);
+        load_head_tile<64, THREADS>(vs_a[0], p, kb0 * 64, head, 2);
+    }
+    cp_async_commit();
+
+    const float scale = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
+    const uint32_t qrow[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
+    float mx[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    uint32_t qf[4][4];
+
+    for (uint32_t kb = kb0; kb < kb1; kb++) {
+        const uint32_t buf = (kb - kb0) & 1;
+        if (kb + 1 < kb1) {
+            load_head_tile<64, THREADS>(ks_a[buf ^ 1], p, (kb + 1) * 64, head, 1);
+            load_head_tile<64, THREADS>(vs_a[buf ^ 1], p, (kb + 1) * 64, head, 2);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (kb == kb0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+                ldsm_x4(qs_a + swz64_off(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)) * 2,
+                        qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        }
+
+        // S = Q K^T: 16 queries x 64 keys per warp (8 n-tiles of 8 keys).
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+#pragma unroll
+            for (int jp = 0; jp < 4; jp++) {
+                const uint32_t mi = lane >> 3;
+                const uint32_t key = jp * 16 + (mi >> 1) * 8 + (lane & 7);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(ks_a[buf] + swz64_off(key, kk * 2 + (mi & 1)) * 2, b0, b1, b2, b3);
+                mma16816(s[2 * jp], qf[kk], b0, b1);
+                mma16816(s[2 * jp + 1], qf[kk], b2, b3);
+            }
+        }
+
+        // Mask, scale and the online softmax. Row h of this lane: elements 2h, 2h+1 of each tile.
+        const uint32_t k0 = kb * 64;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int jt = 0; jt < 8; jt++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const uint32_t key = k0 + 8 * jt + 2 * t + e;
+                    const uint32_t qq = qrow[h];
+                    const uint32_t dist = qq > key ? qq - key : key - qq;
+                    const bool ok = key < n && (window == 0 || dist <= window);
+                    float v = ok ? s[jt][2 * h + e] * scale : -INFINITY;
+                    s[jt][2 * h + e] = v;
+                    m = fmaxf(m, v);
+                }
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            const float m_new = fmaxf(mx[h], m);
+            const float base = m_new == -INFINITY ? 0.f : m_new;
+            const float alpha = exp2f(mx[h] - base);
+            mx[h] = m_new;
+            float rs = 0.f;
+#pragma unroll
+            for (int jt = 0; jt < 8; jt++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const float pv = exp2f(s[jt][2 * h + e] - base);
+                    s[jt][2 * h + e] = pv;
+                    rs += pv;
+                }
+                acc[jt][2 * h] *= alpha;
+                acc[jt][2 * h + 1] *= alpha;
+            }
+            lsum[h] = lsum[h] * alpha + rs;
+        }
+
+        // O += P V: P (rounded to f16) as the A operand, V through ldmatrix.trans.
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t a[4];
+            a[0] = pack_half2(s[2 * kk][0], s[2 * kk][1]);
+            a[1] = pack_half2(s[2 * kk][2], s[2 * kk][3]);
+            a[2] = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            a[3] = pack_half2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {
+                const uint32_t mi = lane >> 3;
+                const uint32_t key = kk * 16 + (mi & 1) * 8 + (lane & 7);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vs_a[buf] + swz64_off(key, dp * 2 + (mi >> 1)) * 2, b0, b1, b2, b3);
+                mma16816(acc[2 * dp], a, b0, b1);
+                mma16816(acc[2 * dp + 1], a, b2, b3);
+            }
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+
+    if (chunks > 1) {
+        // Partial of this key range: 32 accumulators, then max and lane sum of both rows, stored
+        // [value][thread] so the stores coalesce.
+        const uint32_t tile = blockIdx.x * p.heads + head;
+        float *slot = p.ws + ((size_t)tile * chunks + chunk) * 36 * THREADS + threadIdx.x;
+#pragma unroll
+        for (int jt = 0; jt < 8; jt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) slot[(jt * 4 + e) * THREADS] = acc[jt][e];
+        slot[32 * THREADS] = mx[0];
+        slot[33 * THREADS] = mx[1];
+        slot[34 * THREADS] = lsum[0];
+        slot[35 * THREADS] = lsum[1];
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t old = atomicAdd(&p.counters[tile], 1u);
+            const bool last = old == chunks - 1;
+            if (last) p.counters[tile] = 0;
+            last_flag = last ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!last_flag) return;
+        __threadfence();
+        const float *base_slot = p.ws + (size_t)tile * chunks * 36 * THREADS + threadIdx.x;
+        float m2[2] = {-INFINITY, -INFINITY};
+        for (uint32_t zz = 0; zz < chunks; zz++) {
+            const float *sl = base_slot + (size_t)zz * 36 * THREADS;
+            m2[0] = fmaxf(m2[0], __ldcg(sl + 32 * THREADS));
+            m2[1] = fmaxf(m2[1], __ldcg(sl + 33 * THREADS));
+        }
+#pragma unroll
+        for (int jt = 0; jt < 8; jt++) acc[jt][0] = acc[jt][1] = acc[jt][2] = acc[jt][3] = 0.f;
+        lsum[0] = lsum[1] = 0.f;
+        for (uint32_t zz = 0; zz < chunks; zz++) {
+            const float *sl = base_slot + (size_t)zz * 36 * THREADS;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float b = m2[h] == -INFINITY ? 0.f : m2[h];
+                const float f = exp2f(__ldcg(sl + (32 + h) * THREADS) - b);
+                lsum[h] += __ldcg(sl + (34 + h) * THREADS) * f;
+#pragma unroll
+                for (int jt = 0; jt < 8; jt++) {
+                    acc[jt][2 * h] += __ldcg(sl + (jt * 4 + 2 * h) * THREADS) * f;
+                    acc[jt][2 * h + 1] += __ldcg(sl + (jt * 4 + 2 * h + 1) * THREADS) * f;
+                }
+            }
+        }
+    }
+
+    const uint32_t D = p.heads * 64;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        float l = lsum[h];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        if (qrow[h] < n) {
+            uint32_t *dst = reinterpret_cast<uint32_t *>(p.o + (size_t)qrow[h] * D + head * 64);
+#pragma unroll
+            for (int jt = 0; jt < 8; jt++)
+                dst[(8 * jt + 2 * t) / 2] = pack_half2(acc[jt][2 * h] * inv, acc[jt][2 * h + 1] * inv);
+        }
+    }
+}
+
+}  // namespace jc

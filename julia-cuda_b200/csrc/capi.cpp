@@ -1,0 +1,522 @@
+// The C ABI (include/julia_cuda.h): the reference's julia_cuda_* entry points (src/capi.rs), the
+// added raw-model / device-pointer entry points, the per-kernel entry points and host prep.
+// Every entry point catches C++ exceptions and reports them as errors.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <fstream>
+#include <string>
+#include <vector>
+
+#include "../../include/julia_cuda.h"
+#include "engine.h"
+#include "jc_internal.h"
+#include "model.h"
+
+struct JcEngine {
+    jc::Engine *e;
+};
+
+namespace {
+
+void report(char *err, size_t len, const std::string &msg) {
+    jc::set_error(msg);
+    if (!err || len == 0) return;
+    const size_t n = std::min(msg.size(), len - 1);
+    std::memcpy(err, msg.data(), n);
+    err[n] = 0;
+}
+
+template <typename F>
+auto guarded(char *err, size_t len, F &&f) -> decltype(f()) {
+    try {
+        return f();
+    } catch (const std::exception &ex) {
+        report(err, len, std::string("julia-cuda: exception: ") + ex.what());
+    } catch (...) {
+        report(err, len, "julia-cuda: unknown exception");
+    }
+    return decltype(f())();
+}
+
+bool set_device(int dev, char *err, size_t len) {
+    cudaError_t e = cudaSetDevice(dev);
+    if (e != cudaSuccess) {
+        report(err, len, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *julia_cuda_tier(void) { return "sm_100a"; }
+
+void julia_cuda_default_config(jc_model_config *c) {
+    c->d_model = 768;
+    c->n_heads = 12;
+    c->inter = 1152;
+    c->n_layers = 22;
+    c->vocab = 50368;
+    c->head_ff = 2048;
+    c->scorer_hidden = 384;
+    c->n_head_layers = 2;
+    c->global_every = 3;
+    c->window = 64;
+    c->max_positions = 8192;
+    c->n_qtypes = 3;
+    c->norm_eps = 1e-5f;
+    c->head_eps = 1e-5f;
+    c->theta_global = 160000.0f;
+    c->theta_local = 10000.0f;
+}
+
+size_t julia_cuda_raw_size(const jc_model_config *cfg) {
+    std::string why;
+    if (!cfg || !jc::check_config(*cfg, &why)) return 0;
+    return jc::raw_layout(*cfg).total;
+}
+
+int julia_cuda_raw_offsets(const jc_model_config *cfg, size_t *offsets, size_t cap) {
+    std::string why;
+    if (!cfg || !jc::check_config(*cfg, &why)) {
+        jc::set_error(why);
+        return -1;
+    }
+    const jc::RawLayout L = jc::raw_layout(*cfg);
+    for (size_t i = 0; i < L.order.size() && i < cap; i++) offsets[i] = L.order[i].off;
+    return (int)L.order.size();
+}
+
+void julia_cuda_init_random(const jc_model_config *cfg, uint64_t seed, float *raw) {
+    std::string why;
+    if (!cfg || !raw || !jc::check_config(*cfg, &why)) return;
+    jc::init_random(*cfg, seed, raw);
+}
+
+int julia_cuda_save_raw(const char *dir, const jc_model_config *cfg, const float *raw, char *err,
+                        size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        std::string why;
+        if (!dir || !cfg || !raw || !jc::check_config(*cfg, &why)) {
+            report(err, err_len, "save: " + (why.empty() ? std::string("null argument") : why));
+            return -1;
+        }
+        const size_t n = jc::raw_layout(*cfg).total;
+        std::ofstream c(std::string(dir) + "/jc_config.bin", std::ios::binary);
+        c.write(reinterpret_cast<const char *>(cfg), sizeof(*cfg));
+        std::ofstream w(std::string(dir) + "/jc_weights.f32", std::ios::binary);
+        w.write(reinterpret_cast<const char *>(raw), (std::streamsize)(n * 4));
+        if (!c || !w) {
+            report(err, err_len, std::string("save: cannot write to ") + dir);
+            return -1;
+        }
+        return 0;
+    });
+}
+
+JcEngine *julia_cuda_load_raw(const jc_model_config *cfg, const float *raw, size_t raw_len,
+                              size_t max_length, int device, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> JcEngine * {
+        std::string why;
+        if (!cfg || !raw) {
+            report(err, err_len, "load: null config or weights");
+            return nullptr;
+        }
+        if (!jc::check_config(*cfg, &why)) {
+            report(err, err_len, "load: " + why);
+            return nullptr;
+        }
+        if (raw_len != jc::raw_layout(*cfg).total) {
+            report(err, err_len, "load: the weights are not the size the config describes");
+            return nullptr;
+        }
+        jc::Engine *e = jc::Engine::create(*cfg, raw, max_length, device, &why);
+        if (!e) {
+            report(err, err_len, "load: " + why);
+            return nullptr;
+        }
+        return new JcEngine{e};
+    });
+}
+
+JcEngine *julia_cuda_load_random(const jc_model_config *cfg, uint64_t seed, size_t max_length,
+                                 int device, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> JcEngine * {
+        std::string why;
+        if (!cfg || !jc::check_config(*cfg, &why)) {
+            report(err, err_len, "load: " + (why.empty() ? std::string("null config") : why));
+            return nullptr;
+        }
+        std::vector<float> raw(jc::raw_layout(*cfg).total);
+        jc::init_random(*cfg, seed, raw.data());
+        return julia_cuda_load_raw(cfg, raw.data(), raw.size(), max_length, device, err, err_len);
+    });
+}
+
+JcEngine *julia_cuda_load(const char *dir, size_t max_length, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> JcEngine * {
+        if (!dir) {
+            report(err, err_len, "load: null directory");
+            return nullptr;
+        }
+        jc_model_config cfg;
+        std::ifstream c(std::string(dir) + "/jc_config.bin", std::ios::binary);
+        if (!c.read(reinterpret_cast<char *>(&cfg), sizeof(cfg))) {
+            report(err, err_len, std::string("load: no model at ") + dir +
+                                     " (jc_config.bin + jc_weights.f32, see julia_cuda_save_raw)");
+            return nullptr;
+        }
+        std::string why;
+        if (!jc::check_config(cfg, &why)) {
+            report(err, err_len, "load: " + why);
+            return nullptr;
+        }
+        const size_t n = jc::raw_layout(cfg).total;
+        std::vector<float> raw(n);
+        std::ifstream w(std::string(dir) + "/jc_weights.f32", std::ios::binary);
+        if (!w.read(reinterpret_cast<char *>(raw.data()), (std::streamsize)(n * 4))) {
+            report(err, err_len, std::string("load: jc_weights.f32 in ") + dir + " is short");
+            return nullptr;
+        }
+        return julia_cuda_load_raw(&cfg, raw.data(), n, max_length, 0, err, err_len);
+    });
+}
+
+void julia_cuda_free(JcEngine *engine) {
+    if (!engine) return;
+    try {
+        delete engine->e;
+    } catch (...) {
+    }
+    delete engine;
+}
+
+void julia_cuda_device(const JcEngine *engine, char *buf, size_t len) {
+    if (!engine) return;
+    report(buf, len, engine->e->name);
+}
+
+int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_t *max_length,
+                             int *device, int *sms) {
+    if (!engine) return -1;
+    if (cfg) *cfg = engine->e->cfg;
+    if (max_length) *max_length = engine->e->max_length;
+    if (device) *device = engine->e->device;
+    if (sms) *sms = engine->e->sms;
+    return 0;
+}
+
+int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,
+                                    int layer_fused) {
+    if (!engine) return -1;
+    return engine->e->launches_per_forward(n, n_markers, layer_fused);
+}
+
+int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                              const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                              int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
+                              char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!engine) {
+            report(err, err_len, "forward: null engine");
+            return -1;
+        }
+        jc::Engine *e = engine->e;
+        if (!set_device(e->device, err, err_len)) return -1;
+        if (n == 0 || n > e->max_length || n_markers > e->max_length) {
+            report(err, err_len, "forward: " + std::to_string(n) + " tokens / " +
+                                     std::to_string(n_markers) + " markers, limit " +
+                                     std::to_string(e->max_length));
+            return -1;
+        }
+        cudaStream_t s = stream ? (cudaStream_t)stream : e->stream;
+        if (!jc::cuda_ok(cudaMemcpyAsync(e->ids, d_ids, n * 4, cudaMemcpyDeviceToDevice, s), "ids") ||
+            (n_markers && !jc::cuda_ok(cudaMemcpyAsync(e->markers, d_markers, n_markers * 4,
+                                                       cudaMemcpyDeviceToDevice, s),
+                                       "markers"))) {
+            report(err, err_len, jc::last_error());
+            return -1;
+        }
+        const bool ok = d_trace ? e->enqueue_forward(n, n_markers, qtype, layer_fused, d_trace, s)
+                                : e->launch_forward(n, n_markers, qtype, layer_fused, s);
+        if (!ok) {
+            report(err, err_len, std::string("forward: ") + jc::last_error());
+            return -1;
+        }
+        if (n_markers && !jc::cuda_ok(cudaMemcpyAsync(d_logits, e->logits, n_markers * 4,
+                                                      cudaMemcpyDeviceToDevice, s),
+                                      "logits")) {
+            report(err, err_len, jc::last_error());
+            return -1;
+        }
+        return 0;
+    });
+}
+
+int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const size_t *lens,
+                   const uint32_t *markers, const size_t *n_markers, const uint32_t *qtypes,
+                   int layer_fused, float *logits, float *gpu_ms, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!engine) {
+            report(err, err_len, "run: null engine");
+            return -1;
+        }
+        jc::Engine *e = engine->e;
+        if (!set_device(e->device, err, err_len)) return -1;
+        // Validate every sequence before queueing any (src/capi.rs:154-179).
+        size_t at_id = 0, at_mk = 0;
+        for (size_t i = 0; i < b; i++) {
+            if (qtypes[i] >= (uint32_t)e->cfg.n_qtypes) {
+                report(err, err_len, "sequence " + std::to_string(i) + ": no question type " +
+                                         std::to_string(qtypes[i]));
+                return -1;
+            }
+            if (lens[i] == 0 || lens[i] > e->max_length) {
+                report(err, err_len, "sequence " + std::to_string(i) + ": " + std::to_string(lens[i]) +
+                                         " tokens, not 1 to " + std::to_string(e->max_length));
+                return -1;
+            }
+            if (n_markers[i] > e->max_length) {
+                report(err, err_len, "sequence " + std::to_string(i) + ": too many markers");
+                return -1;
+            }
+            for (size_t j = 0; j < lens[i]; j++)
+                if (ids[at_id + j] >= (uint32_t)e->cfg.vocab) {
+                    report(err, err_len, "sequence " + std::to_string(i) + ": token id " +
+                                             std::to_string(ids[at_id + j]) + " is past the vocabulary");
+                    return -1;
+                }
+            for (size_t j = 0; j < n_markers[i]; j++)
+                if (markers[at_mk + j] >= lens[i]) {
+                    report(err, err_len, "sequence " + std::to_string(i) + ": a marker is past the sequence");
+                    return -1;
+                }
+            at_id += lens[i];
+            at_mk += n_markers[i];
+        }
+        const size_t L = e->max_length;
+        cudaStream_t s = e->stream;
+        at_id = at_mk = 0;
+        size_t out_at = 0;
+        for (size_t c0 = 0; c0 < b; c0 += jc::Engine::QUEUE) {
+            const size_t c1 = std::min(b, c0 + (size_t)jc::Engine::QUEUE);
+            size_t mk_at[jc::Engine::QUEUE];
+            for (size_t i = c0; i < c1; i++) {
+                const int slot = (int)(i - c0);
+                const size_t n = lens[i], k = n_markers[i];
+                std::memcpy(e->h_ids + slot * L, ids + at_id, n * 4);
+                std::memcpy(e->h_markers + slot * L, markers + at_mk, k * 4);
+                mk_at[slot] = at_mk;
+                bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, e->h_ids + slot * L, n * 4,
+                                                      cudaMemcpyHostToDevice, s), "ids") &&
+                          (k == 0 || jc::cuda_ok(cudaMemcpyAsync(e->markers, e->h_markers + slot * L,
+                                                                 k * 4, cudaMemcpyHostToDevice, s),
+                                                 "markers")) &&
+                          jc::cuda_ok(cudaEventRecord(e->ev_start[slot], s), "event") &&
+                          e->launch_forward((uint32_t)n, (uint32_t)k, qtypes[i], layer_fused, s) &&
+                          jc::cuda_ok(cudaEventRecord(e->ev_end[slot], s), "event") &&
+                          (k == 0 || jc::cuda_ok(cudaMemcpyAsync(e->h_logits + slot * L, e->logits,
+                                                                 k * 4, cudaMemcpyDeviceToHost, s),
+                                                 "logits"));
+                if (!ok) {
+                    cudaStreamSynchronize(s);
+                    report(err, err_len, std::string("run: ") + jc::last_error());
+                    return -1;
+                }
+                at_id += n;
+                at_mk += k;
+            }
+            if (!jc::cuda_ok(cudaStreamSynchronize(s), "run")) {
+                report(err, err_len, std::string("run: ") + jc::last_error());
+                return -1;
+            }
+            std::string why;
+            if (!e->check_device_error(&why)) {
+                report(err, err_len, "run: " + why);
+                return -1;
+            }
+            for (size_t i = c0; i < c1; i++) {
+                const int slot = (int)(i - c0);
+                const size_t k = n_markers[i];
+                for (size_t j = 0; j < k; j++) {
+                    const float v = e->h_logits[slot * L + j];
+                    if (!std::isfinite(v)) {
+                        report(err, err_len, "run: inference returned nonfinite logits");
+                        return -1;
+                    }
+                    logits[out_at + j] = v;
+                }
+                (void)mk_at;
+                out_at += k;
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, e->ev_start[slot], e->ev_end[slot]);
+                gpu_ms[i] = ms;
+            }
+        }
+        return 0;
+    });
+}
+
+// ------------------------------------------------------------------------------------------
+// per-kernel entry points
+
+const char *jc_last_error(void) { return jc::last_error(); }
+
+int jc_device_error(uint32_t *code) {
+    unsigned int c = 0;
+    if (!jc::read_device_error(&c)) return -1;
+    if (code) *code = c;
+    return 0;
+}
+
+static jc::GemmConfig pick(uint32_t m, uint32_t n, uint32_t k, int bn, int splits, uint32_t epi) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    jc::GemmConfig c = jc::choose_gemm(m, n, k, sms);
+    if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && c.bn < 64) c.bn = 64;
+    if (bn) c.bn = bn;
+    if (splits) c.splits = splits;
+    return c;
+}
+
+size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits) {
+    return jc::gemm_ws_floats(m, n, pick(m, n, k, bn, splits, 0));
+}
+
+size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits) {
+    return jc::gemm_counters(m, n, pick(m, n, k, bn, splits, 0));
+}
+
+int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *splits) {
+    jc::GemmConfig c = jc::choose_gemm(m, n, k, sms);
+    if (bn) *bn = c.bn;
+    if (splits) *splits = c.splits;
+    return 0;
+}
+
+int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t *w, uint16_t *c,
+            const uint16_t *res, float *ws, uint32_t *counters, const float *stats_in,
+            const float *colsum, float *stats_out, float *zero, uint32_t zero_len, uint32_t m,
+            uint32_t n, uint32_t k, float eps, const float *rope, const float *bias, void *stream) {
+    return guarded(nullptr, 0, [&]() -> int {
+        if (!a || !w) {
+            jc::set_error("gemm: null a or w");
+            return -1;
+        }
+        jc::GemmConfig cfg = pick(m, n, k, bn, splits, epi);
+        jc::GemmArgs g;
+        g.epi = epi;
+        if (!jc::make_tmap_f16(&g.map_a, a, m, k, 128) ||
+            !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
+            return -1;
+        g.c = reinterpret_cast<__half *>(c);
+        g.res = reinterpret_cast<const __half *>(res);
+        g.ws = ws;
+        g.counters = counters;
+        g.stats_in = stats_in;
+        g.colsum = colsum;
+        g.stats_out = stats_out;
+        g.zero = zero;
+        g.zero_len = zero_len;
+        g.m = m;
+        g.n = n;
+        g.k = k;
+        g.eps = eps;
+        g.rope = rope;
+        g.bias = bias;
+        return jc::launch_gemm(g, cfg, (cudaStream_t)stream, false) ? 0 : -1;
+    });
+}
+
+size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
+    return jc::attn_ws_floats(n, heads, kv_chunks);
+}
+
+size_t jc_attention_counters(uint32_t n, uint32_t heads) { return jc::attn_counters(n, heads); }
+
+int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, uint32_t window,
+                 uint32_t kv_chunks, float *ws, uint32_t *counters, void *stream) {
+    return guarded(nullptr, 0, [&]() -> int {
+        jc::AttnArgs a;
+        a.qkv = reinterpret_cast<const __half *>(qkv);
+        a.o = reinterpret_cast<__half *>(o);
+        a.n = n;
+        a.heads = heads;
+        a.window = window;
+        if (kv_chunks == 0) {
+            int dev = 0, sms = 148;
+            if (cudaGetDevice(&dev) == cudaSuccess)
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            kv_chunks = jc::choose_kv_chunks(n, heads, window, sms);
+            if (!ws || !counters) kv_chunks = 1;
+        }
+        a.kv_chunks = kv_chunks;
+        a.ws = ws;
+        a.counters = counters;
+        return jc::launch_attention(a, (cudaStream_t)stream, false) ? 0 : -1;
+    });
+}
+
+int jc_embed(const uint32_t *ids, uint32_t n, const uint16_t *table, const float *gamma,
+             uint32_t d, float eps, uint16_t *x, float *stats, void *stream) {
+    return guarded(nullptr, 0, [&]() -> int {
+        return jc::launch_embed(ids, n, reinterpret_cast<const __half *>(table), gamma, d, eps,
+                                reinterpret_cast<__half *>(x), stats, (cudaStream_t)stream, false)
+                   ? 0
+                   : -1;
+    });
+}
+
+int jc_norm_add(const uint16_t *x, uint32_t n, uint32_t d, const float *gamma, const float *add,
+                float eps, uint16_t *out, float *stats, void *stream) {
+    return guarded(nullptr, 0, [&]() -> int {
+        return jc::launch_norm_add(reinterpret_cast<const __half *>(x), n, d, gamma, add, eps,
+                                   reinterpret_cast<__half *>(out), stats, (cudaStream_t)stream,
+                                   false)
+                   ? 0
+                   : -1;
+    });
+}
+
+int jc_score(const uint16_t *y, uint32_t d, const uint16_t *w, float b, const uint32_t *markers,
+             uint32_t k, float *logits, void *stream) {
+    return guarded(nullptr, 0, [&]() -> int {
+        return jc::launch_score(reinterpret_cast<const __half *>(y), d,
+                                reinterpret_cast<const __half *>(w), b, markers, k, logits,
+                                (cudaStream_t)stream, false)
+                   ? 0
+                   : -1;
+    });
+}
+
+// ------------------------------------------------------------------------------------------
+// host prep
+
+void jc_prep_fold_layernorm(const float *w, const float *gamma, uint32_t out, uint32_t k,
+                            uint16_t *w16, float *colsum) {
+    jc::fold_layernorm(w, gamma, out, k, w16, colsum);
+}
+
+void jc_prep_fold_layernorm_bias(const float *w, const float *gamma, const float *beta,
+                                 const float *b, uint32_t out, uint32_t k, uint16_t *w16,
+                                 float *colsum, float *bias) {
+    jc::fold_layernorm_bias(w, gamma, beta, b, out, k, w16, colsum, bias);
+}
+
+void jc_prep_interleave_geglu_f16(const uint16_t *w, uint32_t n, uint32_t k, uint16_t *out) {
+    jc::interleave_geglu(w, n, k, out);
+}
+
+void jc_prep_interleave_geglu_f32(const float *w, uint32_t n, uint32_t k, float *out) {
+    jc::interleave_geglu(w, n, k, out);
+}
+
+void jc_prep_rope_table(float theta, uint32_t n, float *out) { jc::rope_table(theta, n, out); }
+
+}  // extern "C"

@@ -1,0 +1,114 @@
+// Internal declarations shared by the kernels (.cu) and the host runtime (.cpp).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/julia_cuda.h"
+
+// Longest a device-side wait may spin before it records an error and gives up (ns).
+#define JC_WAIT_NS 2000000000ull
+
+// Device error codes (the module error word holds the first one recorded).
+#define JC_DEV_TIMEOUT_FULL 1u     // MMA issuer: a TMA stage never arrived
+#define JC_DEV_TIMEOUT_EMPTY 2u    // TMA producer: a stage was never released by the MMAs
+#define JC_DEV_TIMEOUT_MMA 3u      // epilogue: the accumulator was never committed
+#define JC_DEV_TIMEOUT_GRID 4u     // persistent kernel: a grid barrier timed out
+#define JC_DEV_TIMEOUT_SPLIT 5u    // split-K / split-KV: partials never became complete
+#define JC_DEV_BAD_INDEX 6u        // an index a kernel checks was out of range
+
+// GEMM epilogue flags: JC_EPI_* from the public header (the reference's bit values,
+// kernels/src/main.rs:870-877).
+
+namespace jc {
+
+// Thread-local last error message of the C ABI.
+void set_error(const std::string &msg);
+const char *last_error();
+
+// Records a CUDA error; returns false if `e` is an error.
+bool cuda_ok(cudaError_t e, const char *what);
+
+// ---------------------------------------------------------------------------------------------
+// TMA descriptors
+
+// A row-major [rows, cols] f16 matrix, loaded in boxes of box_rows x 64 columns with the 128-byte
+// swizzle. Returns false (and sets the error) on failure.
+bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                   uint32_t box_rows);
+
+// ---------------------------------------------------------------------------------------------
+// GEMM: c = epilogue(a . w^T), a [m,k] f16, w [n,k] f16, tcgen05 with TMEM accumulators.
+
+struct GemmArgs {
+    uint32_t epi = 0;
+    CUtensorMap map_a{}, map_w{};
+    __half *c = nullptr;
+    const __half *res = nullptr;
+    float *ws = nullptr;
+    uint32_t *counters = nullptr;
+    const float *stats_in = nullptr;
+    const float *colsum = nullptr;
+    float *stats_out = nullptr;
+    float *zero = nullptr;
+    uint32_t zero_len = 0;
+    uint32_t m = 0, n = 0, k = 0;
+    float eps = 0.f;
+    const float *rope = nullptr;
+    const float *bias = nullptr;
+};
+
+struct GemmConfig {
+    int bn = 64;      // output columns per CTA: 32, 64 or 128
+    int splits = 1;   // split-K factor, 1..8
+};
+
+// Floats of split-K workspace and counters a launch of this shape needs.
+size_t gemm_ws_floats(uint32_t m, uint32_t n, GemmConfig cfg);
+size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg);
+
+// Validates and launches; false (with the error set) if the arguments are inconsistent.
+bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl);
+
+// The configuration for an m x n x k GEMM on `sms` SMs (the B200 refit of gemm::choose).
+GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms);
+
+// ---------------------------------------------------------------------------------------------
+// attention: o = softmax(q k^T / 8) v per head, global or |q - k| <= window
+
+struct AttnArgs {
+    const __half *qkv = nullptr;  // [n, 3 * heads * 64]
+    __half *o = nullptr;          // [n, heads * 64]
+    uint32_t n = 0, heads = 0, window = 0;
+    uint32_t kv_chunks = 1;       // split-KV: key ranges per (query tile, head)
+    float *ws = nullptr;          // kv_chunks > 1: partials
+    uint32_t *counters = nullptr; // kv_chunks > 1: one zeroed counter per (query tile, head)
+};
+size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
+size_t attn_counters(uint32_t n, uint32_t heads);
+bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
+uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms);
+
+// ---------------------------------------------------------------------------------------------
+// memory-bound edges
+
+bool launch_embed(const uint32_t *ids, uint32_t n, const __half *table, const float *gamma,
+                  uint32_t d, float eps, __half *x, float *stats, cudaStream_t s, bool pdl);
+bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma,
+                     const float *add, float eps, __half *out, float *stats, cudaStream_t s,
+                     bool pdl);
+bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,
+                  uint32_t k, float *logits, cudaStream_t s, bool pdl);
+// Gathers the marker rows of x and their statistics (for the scorer, which only needs those).
+bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
+                        uint32_t k, __half *out, float *out_stats, cudaStream_t s, bool pdl);
+
+// The device error word: read (and clear) it.
+bool read_device_error(unsigned int *code);
+const char *device_error_name(unsigned int code);
+
+}  // namespace jc

@@ -1,0 +1,338 @@
+// The library's only CUDA translation unit: every kernel template is instantiated here, next to
+// its host launcher (argument checks, launch shape, PDL attribute). Keeping one unit lets all
+// kernels share the device error word without relocatable device code.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "attention.cuh"
+#include "edges.cuh"
+#include "gemm.cuh"
+#include "jc_internal.h"
+
+namespace jc {
+
+static thread_local std::string t_error;
+void set_error(const std::string &msg) { t_error = msg; }
+const char *last_error() { return t_error.c_str(); }
+
+bool cuda_ok(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return false;
+}
+
+bool read_device_error(unsigned int *code) {
+    unsigned int zero = 0;
+    if (!cuda_ok(cudaMemcpyFromSymbol(code, g_dev_error, sizeof(unsigned int)), "read error word"))
+        return false;
+    if (*code) return cuda_ok(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(zero)), "clear error word");
+    return true;
+}
+
+const char *device_error_name(unsigned int code) {
+    switch (code) {
+        case 0: return "none";
+        case JC_DEV_TIMEOUT_FULL: return "a GEMM operand stage never arrived (TMA wait timed out)";
+        case JC_DEV_TIMEOUT_EMPTY: return "a GEMM stage was never released (MMA wait timed out)";
+        case JC_DEV_TIMEOUT_MMA: return "a GEMM accumulator was never committed (wait timed out)";
+        case JC_DEV_TIMEOUT_GRID: return "a grid barrier timed out";
+        case JC_DEV_TIMEOUT_SPLIT: return "split partials never completed (wait timed out)";
+        case JC_DEV_BAD_INDEX: return "an index checked on the device was out of range";
+        default: return "unknown device error";
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// launch helper: cudaLaunchKernelEx with programmatic stream serialization when `pdl`
+
+template <typename... KArgs, typename... Args>
+static bool launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      bool pdl, const char *what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? attr : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_ok(cudaLaunchKernelEx(&cfg, kern, args...), what);
+}
+
+// Sets a kernel's dynamic shared-memory limit once per device.
+template <typename K>
+static bool ensure_smem(K kern, int bytes, std::atomic<uint64_t> &done_mask) {
+    int dev = 0;
+    if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return false;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done_mask.load() & bit) return true;
+    if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                 "cudaFuncSetAttribute"))
+        return false;
+    done_mask.fetch_or(bit);
+    return true;
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMA descriptors
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                   uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+        return false;
+    }
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || cols < 64 || rows == 0) {
+        set_error("tensor map: base must be 16-byte aligned and rows whole 16-byte multiples of >= 64 columns");
+        return false;
+    }
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides,
+                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+        return false;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------------------------
+// GEMM
+
+size_t gemm_ws_floats(uint32_t m, uint32_t n, GemmConfig cfg) {
+    if (cfg.splits <= 1) return 0;
+    const size_t tiles = (size_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / cfg.bn);
+    return tiles * cfg.splits * cfg.bn * GEMM_BM;
+}
+
+size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg) {
+    if (cfg.splits <= 1) return 0;
+    return (size_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / cfg.bn);
+}
+
+template <int BN, uint32_t EPI>
+static bool launch_gemm_inst(const GemmParams &p, dim3 grid, cudaStream_t s, bool pdl) {
+    static std::atomic<uint64_t> smem_set{0};
+    auto kern = gemm_tc_kernel<BN, EPI>;
+    constexpr int smem = GemmShape<BN>::SMEM_BYTES;
+    if (!ensure_smem(kern, smem, smem_set)) return false;
+    return launch_ex(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, "gemm launch", p);
+}
+
+template <int BN>
+static bool launch_gemm_bn(uint32_t epi, const GemmParams &p, dim3 grid, cudaStream_t s, bool pdl) {
+    switch (epi) {
+        case 0: return launch_gemm_inst<BN, 0>(p, grid, s, pdl);
+        case JC_EPI_RES | JC_EPI_STATS: return launch_gemm_inst<BN, JC_EPI_RES | JC_EPI_STATS>(p, grid, s, pdl);
+        case JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS:
+            return launch_gemm_inst<BN, JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS>(p, grid, s, pdl);
+        case JC_EPI_LN | JC_EPI_BIAS: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS>(p, grid, s, pdl);
+        case JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU:
+            return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU>(p, grid, s, pdl);
+        case JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU:
+            return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU>(p, grid, s, pdl);
+        default: break;
+    }
+    if constexpr (BN >= 64) {
+        switch (epi) {
+            case JC_EPI_ROPE: return launch_gemm_inst<BN, JC_EPI_ROPE>(p, grid, s, pdl);
+            case JC_EPI_LN | JC_EPI_ROPE: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_ROPE>(p, grid, s, pdl);
+            case JC_EPI_LN | JC_EPI_GEGLU: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_GEGLU>(p, grid, s, pdl);
+            default: break;
+        }
+    }
+    set_error("gemm: no kernel for epilogue " + std::to_string(epi) + " with " +
+              std::to_string(BN) + "-column tiles");
+    return false;
+}
+
+bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
+    const uint32_t e = g.epi;
+    const bool ln = e & JC_EPI_LN, res = e & JC_EPI_RES, stats = e & JC_EPI_STATS,
+               rope = e & JC_EPI_ROPE, geglu = e & JC_EPI_GEGLU, bias = e & JC_EPI_BIAS;
+    auto fail = [](const char *m) { set_error(std::string("gemm: ") + m); return false; };
+    if (cfg.bn != 32 && cfg.bn != 64 && cfg.bn != 128) return fail("tile width must be 32, 64 or 128");
+    if (g.m == 0) return fail("no rows");
+    if (g.k == 0 || g.k % GEMM_BK) return fail("k must be a positive multiple of 64");
+    if (g.n == 0 || g.n % cfg.bn) return fail("n must be a multiple of the tile width");
+    if (cfg.splits < 1 || cfg.splits > 8 || (uint32_t)cfg.splits > g.k / GEMM_BK)
+        return fail("split-K must be 1..8 and at most k/64");
+    if ((rope || geglu) && cfg.bn < 64) return fail("RoPE and GeGLU need 64- or 128-column tiles");
+    if (rope && g.n % 192) return fail("RoPE needs a qkv output (n a multiple of 3 x 64)");
+    if (rope && geglu) return fail("RoPE and GeGLU do not combine");
+    if ((res || stats) && geglu) return fail("residual / statistics do not combine with GeGLU");
+    if (!g.c) return fail("no output");
+    if (ln && (!g.stats_in || !g.colsum)) return fail("the LayerNorm epilogue needs stats_in and colsum");
+    if (rope && !g.rope) return fail("the RoPE epilogue needs the (cos, sin) table");
+    if (bias && !g.bias) return fail("the bias epilogues need a bias");
+    if (res && !g.res) return fail("the residual epilogue needs res");
+    if (stats && !g.stats_out) return fail("the statistics epilogue needs stats_out");
+    if (g.zero_len && (!g.zero || g.zero == g.stats_in || g.zero == g.stats_out))
+        return fail("the buffer to clear must exist and not be one this GEMM reads or adds to");
+    if ((reinterpret_cast<uintptr_t>(g.c) | reinterpret_cast<uintptr_t>(g.res) |
+         reinterpret_cast<uintptr_t>(g.colsum) | reinterpret_cast<uintptr_t>(g.bias) |
+         reinterpret_cast<uintptr_t>(g.rope)) & 15)
+        return fail("c, res, colsum, bias and the RoPE table must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(g.stats_in) & 7) return fail("stats_in must be 8-byte aligned");
+    if (cfg.splits > 1 && (!g.ws || !g.counters)) return fail("split-K needs a workspace and counters");
+    GemmParams p;
+    p.map_a = g.map_a;
+    p.map_w = g.map_w;
+    p.c = g.c;
+    p.res = g.res;
+    p.ws = g.ws;
+    p.counters = g.counters;
+    p.stats_in = g.stats_in;
+    p.colsum = g.colsum;
+    p.stats_out = g.stats_out;
+    p.zero = g.zero;
+    p.rope = g.rope;
+    p.bias = g.bias;
+    p.zero_len = g.zero_len;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.eps = g.eps;
+    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.splits);
+    switch (cfg.bn) {
+        case 32: return launch_gemm_bn<32>(e, p, grid, s, pdl);
+        case 64: return launch_gemm_bn<64>(e, p, grid, s, pdl);
+        default: return launch_gemm_bn<128>(e, p, grid, s, pdl);
+    }
+}
+
+GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
+    GemmConfig c;
+    const uint32_t tiles_m = (m + GEMM_BM - 1) / GEMM_BM;
+    c.bn = (n % 128 == 0 && tiles_m * (n / 128) >= (uint32_t)sms) ? 128 : 64;
+    if (n % c.bn) c.bn = 32;
+    const uint32_t ctas = tiles_m * (n / c.bn);
+    c.splits = 1;
+    while (c.splits < 4 && ctas * c.splits * 2 <= (uint32_t)sms && k / GEMM_BK / (c.splits * 2) >= 3)
+        c.splits *= 2;
+    return c;
+}
+
+// ---------------------------------------------------------------------------------------------
+// attention
+
+constexpr int ATTN_WARPS = 4;
+constexpr int ATTN_QT = 16 * ATTN_WARPS;
+
+size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
+    if (kv_chunks <= 1) return 0;
+    return (size_t)((n + ATTN_QT - 1) / ATTN_QT) * heads * kv_chunks * 36 * ATTN_WARPS * 32;
+}
+
+size_t attn_counters(uint32_t n, uint32_t heads) {
+    return (size_t)((n + ATTN_QT - 1) / ATTN_QT) * heads;
+}
+
+bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
+    if (!a.qkv || !a.o || a.n == 0 || a.heads == 0) {
+        set_error("attention: no input, output, rows or heads");
+        return false;
+    }
+    if (a.kv_chunks < 1 || a.kv_chunks > 16 || (a.kv_chunks > 1 && (!a.ws || !a.counters))) {
+        set_error("attention: key ranges must be 1..16, and need a workspace and counters when > 1");
+        return false;
+    }
+    if ((reinterpret_cast<uintptr_t>(a.qkv) | reinterpret_cast<uintptr_t>(a.o)) & 15) {
+        set_error("attention: qkv and o must be 16-byte aligned");
+        return false;
+    }
+    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window};
+    dim3 grid((a.n + ATTN_QT - 1) / ATTN_QT, a.heads, a.kv_chunks);
+    return launch_ex(attention_kernel<ATTN_WARPS>, grid, dim3(ATTN_WARPS * 32), 0, s, pdl,
+                     "attention launch", p);
+}
+
+uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) {
+    if (window > 0) return 1;
+    const uint32_t tiles = ((n + ATTN_QT - 1) / ATTN_QT) * heads;
+    const uint32_t key_tiles = (n + 63) / 64;
+    uint32_t c = (uint32_t)(2 * sms) / (tiles ? tiles : 1);
+    if (c > key_tiles) c = key_tiles;
+    if (c > 8) c = 8;
+    return c < 1 ? 1 : c;
+}
+
+// ---------------------------------------------------------------------------------------------
+// edges
+
+
+bool launch_embed(const uint32_t *ids, uint32_t n, const __half *table, const float *gamma,
+                  uint32_t d, float eps, __half *x, float *stats, cudaStream_t s, bool pdl) {
+    if (n == 0) return true;
+    dim3 grid((n + 3) / 4), block(128);
+#define JC_EMBED(DD) \
+    case DD: return launch_ex(embed_kernel<DD>, grid, block, 0, s, pdl, "embed launch", ids, n, table, gamma, eps, x, stats);
+    switch (d) {
+        JC_EMBED(128) JC_EMBED(256) JC_EMBED(384) JC_EMBED(512) JC_EMBED(640) JC_EMBED(768)
+        JC_EMBED(896) JC_EMBED(1024)
+        default: set_error("embed: width must be a multiple of 128 up to 1024"); return false;
+    }
+#undef JC_EMBED
+}
+
+bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma,
+                     const float *add, float eps, __half *out, float *stats, cudaStream_t s,
+                     bool pdl) {
+    if (n == 0) return true;
+    dim3 grid((n + 3) / 4), block(128);
+#define JC_NA(DD) \
+    case DD: return launch_ex(norm_add_kernel<DD>, grid, block, 0, s, pdl, "norm_add launch", x, n, gamma, add, eps, out, stats);
+    switch (d) {
+        JC_NA(128) JC_NA(256) JC_NA(384) JC_NA(512) JC_NA(640) JC_NA(768) JC_NA(896) JC_NA(1024)
+        default: set_error("norm_add: width must be a multiple of 128 up to 1024"); return false;
+    }
+#undef JC_NA
+}
+
+bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
+                        uint32_t k, __half *out, float *out_stats, cudaStream_t s, bool pdl) {
+    if (k == 0) return true;
+    if (d % 8) {
+        set_error("gather: width must be a multiple of 8");
+        return false;
+    }
+    return launch_ex(gather_rows_kernel, dim3((k + 3) / 4), dim3(128), 0, s, pdl, "gather launch",
+                     x, stats, d, rows, k, out, out_stats);
+}
+
+bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,
+                  uint32_t k, float *logits, cudaStream_t s, bool pdl) {
+    if (k == 0) return true;
+    if (d % 2) {
+        set_error("score: width must be even");
+        return false;
+    }
+    return launch_ex(score_kernel, dim3((k + 3) / 4), dim3(128), 0, s, pdl, "score launch", y, d,
+                     w, b, markers, k, logits);
+}
+
+}  // namespace jc

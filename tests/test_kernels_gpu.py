@@ -1,0 +1,216 @@
+"""Each sm_100a kernel, called through the C ABI (jc_*), against the oracle's emulation of the
+same f16/f32 arithmetic. Tolerances are the reference's (src/check.rs:107, :154, :382-389):
+GEMM outputs within 1e-3 relative of the emulation, row statistics 1e-4, attention 2e-3 of the
+emulation and 4e-3 of f32, embed within 1 f16 ulp."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def stats_err(x16, stats):
+    """src/check.rs:286-298: max over rows of |dS| / sqrt(S2) and |dS2| / S2."""
+    x = x16.view(np.float16).astype(np.float64)
+    s_ref = x.sum(1)
+    q_ref = np.maximum((x * x).sum(1), 1e-30)
+    st = stats.reshape(-1, 2).astype(np.float64)
+    return float(np.max(np.maximum(np.abs(st[:, 0] - s_ref) / np.sqrt(q_ref),
+                                   np.abs(st[:, 1] - q_ref) / q_ref)))
+
+
+def ulps(a16, b16):
+    def ordered(h):
+        h = h.astype(np.int32)
+        return np.where(h & 0x8000, -(h & 0x7FFF), h)
+    return np.abs(ordered(a16) - ordered(b16))
+
+
+def cuda_u16(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda().view(torch.float16)
+
+
+def cuda_f32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host_u16(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+GEMM_CASES = [
+    # name, n, k: BASELINE config 1's encoder GEMMs and the head's variants (hidden 768)
+    ("lnrope", 2304, 768),
+    ("rope", 2304, 768),
+    ("resstats", 768, 768),
+    ("lngeglu", 2304, 768),
+    ("resstats", 768, 1152),
+    ("lnbias", 2304, 768),
+    ("lnbiasrelu", 2048, 768),
+    ("biasresstats", 768, 2048),
+    ("lnbiasgelu", 384, 768),
+]
+
+
+def run_gemm_case(jc, O, name, m, n, k, bn=0, splits=0, seed=0):
+    epi = jc.EPILOGUES[name]
+    a = O.f16(O.normal((m, k), seed + 1))
+    w = O.f16(O.normal((n, k), seed + 2, std=0.05))
+    stats_in = O.row_stats(a)
+    colsum = O.f32(w).astype(np.float64).sum(1).astype(np.float32)
+    rope = O.rope_table(160000.0, max(m, 1))
+    bias = O.normal(n, seed + 3, std=0.1)
+    res = O.f16(O.normal((m, n), seed + 4))
+    want, want_stats = O.emu_gemm(epi, a, w, m, n, k, c16=res if epi & jc.EPI_RES else None,
+                                  stats_in=stats_in, colsum=colsum, eps=1e-5, rope=rope,
+                                  bias=bias)
+    w_dev, cs_dev = w, colsum
+    if epi & jc.EPI_GEGLU:
+        w_dev = jc.prep_interleave_geglu(w)
+        cs_dev = jc.prep_interleave_geglu(colsum)
+    n_out = n // 2 if epi & jc.EPI_GEGLU else n
+    c = cuda_u16(res) if epi & jc.EPI_RES else torch.zeros(m, n_out, dtype=torch.float16,
+                                                         device="cuda")
+    stats_out = torch.zeros(2 * m, dtype=torch.float32, device="cuda")
+    zero = torch.ones(2 * m + 5, dtype=torch.float32, device="cuda")
+    jc.gemm(epi, cuda_u16(a), cuda_u16(w_dev), c, res=c if epi & jc.EPI_RES else None,
+            stats_in=cuda_f32(stats_in), colsum=cuda_f32(cs_dev), stats_out=stats_out, zero=zero,
+            eps=1e-5, rope=cuda_f32(rope), bias=cuda_f32(bias), bn=bn, splits=splits)
+    torch.cuda.synchronize()
+    assert jc.device_error() == 0
+    got = host_u16(c)
+    assert float(zero.abs().max()) == 0.0, "the zero buffer was not cleared"
+    e = rel_err(O.f32(got), O.f32(want))
+    assert e < 1e-3, f"{name} m={m} n={n} k={k} bn={bn} splits={splits}: rel err {e:.2e}"
+    if epi & jc.EPI_STATS:
+        se = stats_err(got, stats_out.cpu().numpy())
+        assert se < 1e-4, f"{name}: stats err {se:.2e}"
+    return e
+
+
+@pytest.mark.parametrize("name,n,k", GEMM_CASES)
+@pytest.mark.parametrize("m", [72, 293, 1024])
+def test_gemm_epilogues(jc, O, name, n, k, m):
+    run_gemm_case(jc, O, name, m, n, k)
+
+
+@pytest.mark.parametrize("m", [1, 2, 63, 127, 128, 129, 255, 448])
+def test_gemm_ragged_rows(jc, O, m):
+    run_gemm_case(jc, O, "lnrope", m, 2304, 768)
+    run_gemm_case(jc, O, "resstats", m, 768, 1152)
+
+
+@pytest.mark.parametrize("bn", [32, 64, 128])
+@pytest.mark.parametrize("splits", [1, 2, 3, 4, 8])
+def test_gemm_tile_and_split_sweep(jc, O, bn, splits):
+    """Every tile width x split-K on the resstats and lnbias shapes (the reference's
+    configuration sweep, src/check.rs:765-796)."""
+    run_gemm_case(jc, O, "resstats", 293, 768, 768, bn=bn, splits=splits)
+    run_gemm_case(jc, O, "lnbias", 200, 768, 768, bn=bn, splits=splits)
+    if bn >= 64:
+        run_gemm_case(jc, O, "lngeglu", 293, 2304, 768, bn=bn, splits=splits)
+        run_gemm_case(jc, O, "lnrope", 100, 2304, 768, bn=bn, splits=splits)
+
+
+def test_gemm_split_k_deterministic(jc, O):
+    """Split partials are summed in split order: repeated runs are bit-identical."""
+    m, n, k = 293, 768, 1152
+    a = cuda_u16(O.f16(O.normal((m, k), 1)))
+    w = cuda_u16(O.f16(O.normal((n, k), 2, std=0.05)))
+    outs = []
+    for _ in range(3):
+        c = torch.zeros(m, n, dtype=torch.float16, device="cuda")
+        jc.gemm(0, a, w, c, bn=64, splits=4)
+        outs.append(host_u16(c))
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+def test_gemm_rejects_bad_shapes(jc):
+    a = torch.zeros(10, 100, dtype=torch.float16, device="cuda")
+    w = torch.zeros(64, 100, dtype=torch.float16, device="cuda")
+    c = torch.zeros(10, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(jc.JuliaCudaError, match="multiple of 64"):
+        jc.gemm(0, a, w, c)
+    a = torch.zeros(10, 128, dtype=torch.float16, device="cuda")
+    w = torch.zeros(64, 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(jc.JuliaCudaError, match="LayerNorm"):
+        jc.gemm(jc.EPI_LN, a, w, c)
+
+
+@pytest.mark.parametrize("n", [1, 2, 63, 64, 65, 127, 129, 293, 512, 1024])
+@pytest.mark.parametrize("window", [0, 64])
+def test_attention(jc, O, n, window):
+    heads = 12
+    qkv = O.f16(O.normal((n, 3 * heads * 64), n + window))
+    want = O.emu_attention(qkv, n, heads, window)
+    f32 = O.attention_f32(O.f32(qkv), n, heads, window)
+    for chunks in ([1, 0, 3] if window == 0 else [1]):
+        o = torch.zeros(n, heads * 64, dtype=torch.float16, device="cuda")
+        jc.attention(cuda_u16(qkv), o, heads, window, kv_chunks=chunks)
+        torch.cuda.synchronize()
+        got = O.f32(host_u16(o))
+        e1, e2 = rel_err(got, O.f32(want)), rel_err(got, f32)
+        assert e1 < 2e-3 and e2 < 4e-3, f"n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
+
+
+def test_attention_reference_width(jc, O):
+    """Six heads (the reference's 384-wide model)."""
+    n, heads = 363, 6
+    qkv = O.f16(O.normal((n, 3 * heads * 64), 99))
+    for window in (0, 64):
+        o = torch.zeros(n, heads * 64, dtype=torch.float16, device="cuda")
+        jc.attention(cuda_u16(qkv), o, heads, window)
+        torch.cuda.synchronize()
+        assert rel_err(O.f32(host_u16(o)), O.f32(O.emu_attention(qkv, n, heads, window))) < 2e-3
+
+
+@pytest.mark.parametrize("d", [384, 768])
+def test_embed(jc, O, d):
+    vocab, n = 1000, 293
+    table = O.f16(O.normal((vocab, d), 5, std=0.02))
+    gamma = O.normal(d, 6, mean=1.0, std=0.05)
+    ids = np.random.default_rng(0).integers(0, vocab, n).astype(np.uint32)
+    want = O.emu_embed(table, gamma, ids, d, 1e-5)
+    x = torch.zeros(n, d, dtype=torch.float16, device="cuda")
+    stats = torch.zeros(2 * n, dtype=torch.float32, device="cuda")
+    jc.embed(torch.from_numpy(ids.view(np.int32)).cuda(), cuda_u16(table), cuda_f32(gamma), x,
+             stats=stats)
+    torch.cuda.synchronize()
+    got = host_u16(x)
+    assert ulps(got, want).max() <= 1
+    assert stats_err(got, stats.cpu().numpy()) < 1e-4
+
+
+@pytest.mark.parametrize("d", [384, 768])
+def test_norm_add(jc, O, d):
+    n = 293
+    x = O.f16(O.normal((n, d), 7))
+    gamma = O.normal(d, 8, mean=1.0, std=0.05)
+    add = O.normal(d, 9, std=0.02)
+    want, want_st = O.emu_norm_add(x, gamma, add, 1e-5)
+    out = torch.zeros(n, d, dtype=torch.float16, device="cuda")
+    st = torch.zeros(2 * n, dtype=torch.float32, device="cuda")
+    jc.norm_add(cuda_u16(x), cuda_f32(gamma), cuda_f32(add), out, st)
+    torch.cuda.synchronize()
+    got = host_u16(out)
+    assert ulps(got, want).max() <= 1
+    assert stats_err(got, st.cpu().numpy()) < 1e-4
+
+
+def test_score(jc, O):
+    n, d = 293, 384
+    y = O.f16(O.normal((n, d), 10))
+    w = O.f16(O.normal(d, 11, std=0.05))
+    markers = np.array([0, 17, 200, 292, 17], np.uint32)
+    want = O.emu_score(y, w, 0.25, markers)
+    logits = torch.zeros(len(markers), dtype=torch.float32, device="cuda")
+    jc.score(cuda_u16(y), cuda_u16(w), 0.25, torch.from_numpy(markers.view(np.int32)).cuda(),
+             logits)
+    torch.cuda.synchronize()
+    assert np.max(np.abs(logits.cpu().numpy() - want)) < 1e-4
