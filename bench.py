@@ -161,18 +161,7 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
         def launch():
             jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st, colsum=cs,
                     stats_out=so, rope=rope, bias=bias, ws=ws, counters=cnt, stream=stream)
-        for _ in range(3):
-            launch()
-        times = []
-        for _ in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            launch()
-            e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        ms = statistics.mean(times)
+        ms = timed(torch, stream, flush, launch, reps)
         bytes_ = 2 * (n * K + N * K + n * n_out) + (2 * n * N if epi & jc.EPI_RES else 0) + \
             (8 * n + 4 * N if epi & jc.EPI_LN else 0) + (4 * N if epi & jc.EPI_BIAS else 0) + \
             (256 * n if epi & jc.EPI_ROPE else 0) + (8 * n if epi & jc.EPI_STATS else 0)
@@ -183,22 +172,31 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
     n_global = len([l for l in range(cfg.n_layers) if l % cfg.global_every == 0])
     for name, window, count in [("attn_global", 0, n_global + cfg.n_head_layers),
                                 ("attn_window", cfg.window, cfg.n_layers - n_global)]:
-        for _ in range(3):
-            jc.attention(qkv, o, heads, window, stream=stream)
-        times = []
-        for _ in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            jc.attention(qkv, o, heads, window, stream=stream)
-            e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
+        ms = timed(torch, stream, flush,
+                   lambda: jc.attention(qkv, o, heads, window, stream=stream), reps)
         keys = n if window == 0 else sum(min(i + window, n - 1) - max(i - window, 0) + 1
                                          for i in range(n)) / n
-        out[name] = (statistics.mean(times), count, 2 * (n * 3 * heads * 64 + n * heads * 64),
+        out[name] = (ms, count, 2 * (n * 3 * heads * 64 + n * heads * 64),
                      4.0 * n * keys * heads * 64)
     return out
+
+
+def timed(torch, stream, flush, launch, reps):
+    """Average device time of `launch` (ms): CUDA events on the launching stream around each
+    launch, L2 flushed before each, every launch queued before the host waits (so host-side
+    launch latency never shows up as device time)."""
+    for _ in range(3):
+        launch()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(reps)]
+    torch.cuda.synchronize()
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record(stream)
+        launch()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
 
 
 def reference_arm(args, rank, world):

@@ -101,7 +101,8 @@ JcEngine *julia_cuda_load_random(const jc_model_config *cfg, uint64_t seed, size
                                  int device, char *err, size_t err_len);
 
 /* One sequence with inputs already on the engine's device: d_ids [n], d_markers [n_markers];
- * writes d_logits [n_markers]. Queued on `stream` (NULL: the engine's stream), not waited for.
+ * writes d_logits [n_markers]. Queued on `stream` (NULL: the legacy default stream), not waited
+ * for.
  * d_trace, if not NULL, receives the residual stream (f16) after every encoder layer,
  * [n_layers][n][D] (slower: no CUDA graph). Returns 0 or -1. */
 int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,

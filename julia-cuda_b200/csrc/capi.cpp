@@ -235,7 +235,7 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
                                      std::to_string(e->max_length));
             return -1;
         }
-        cudaStream_t s = stream ? (cudaStream_t)stream : e->stream;
+        cudaStream_t s = (cudaStream_t)stream;
         if (!jc::cuda_ok(cudaMemcpyAsync(e->ids, d_ids, n * 4, cudaMemcpyDeviceToDevice, s), "ids") ||
             (n_markers && !jc::cuda_ok(cudaMemcpyAsync(e->markers, d_markers, n_markers * 4,
                                                        cudaMemcpyDeviceToDevice, s),
@@ -382,6 +382,7 @@ static jc::GemmConfig pick(uint32_t m, uint32_t n, uint32_t k, int bn, int split
     if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && c.bn < 64) c.bn = 64;
     if (bn) c.bn = bn;
     if (splits) c.splits = splits;
+    jc::set_gemm_depth(c, m, n, sms);
     return c;
 }
 
@@ -412,9 +413,6 @@ int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t 
         jc::GemmConfig cfg = pick(m, n, k, bn, splits, epi);
         jc::GemmArgs g;
         g.epi = epi;
-        if (!jc::make_tmap_f16(&g.map_a, a, m, k, 128) ||
-            !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
-            return -1;
         g.c = reinterpret_cast<__half *>(c);
         g.res = reinterpret_cast<const __half *>(res);
         g.ws = ws;
@@ -430,7 +428,10 @@ int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t 
         g.eps = eps;
         g.rope = rope;
         g.bias = bias;
-        return jc::launch_gemm(g, cfg, (cudaStream_t)stream, false) ? 0 : -1;
+        if (!jc::check_gemm(g, cfg) || !jc::make_tmap_f16(&g.map_a, a, m, k, 128) ||
+            !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
+            return -1;
+        return jc::launch_gemm(g, cfg, (cudaStream_t)stream, true) ? 0 : -1;
     });
 }
 
@@ -459,7 +460,7 @@ int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, u
         a.kv_chunks = kv_chunks;
         a.ws = ws;
         a.counters = counters;
-        return jc::launch_attention(a, (cudaStream_t)stream, false) ? 0 : -1;
+        return jc::launch_attention(a, (cudaStream_t)stream, true) ? 0 : -1;
     });
 }
 
@@ -467,7 +468,7 @@ int jc_embed(const uint32_t *ids, uint32_t n, const uint16_t *table, const float
              uint32_t d, float eps, uint16_t *x, float *stats, void *stream) {
     return guarded(nullptr, 0, [&]() -> int {
         return jc::launch_embed(ids, n, reinterpret_cast<const __half *>(table), gamma, d, eps,
-                                reinterpret_cast<__half *>(x), stats, (cudaStream_t)stream, false)
+                                reinterpret_cast<__half *>(x), stats, (cudaStream_t)stream, true)
                    ? 0
                    : -1;
     });
@@ -478,7 +479,7 @@ int jc_norm_add(const uint16_t *x, uint32_t n, uint32_t d, const float *gamma, c
     return guarded(nullptr, 0, [&]() -> int {
         return jc::launch_norm_add(reinterpret_cast<const __half *>(x), n, d, gamma, add, eps,
                                    reinterpret_cast<__half *>(out), stats, (cudaStream_t)stream,
-                                   false)
+                                   true)
                    ? 0
                    : -1;
     });
@@ -489,7 +490,7 @@ int jc_score(const uint16_t *y, uint32_t d, const uint16_t *w, float b, const ui
     return guarded(nullptr, 0, [&]() -> int {
         return jc::launch_score(reinterpret_cast<const __half *>(y), d,
                                 reinterpret_cast<const __half *>(w), b, markers, k, logits,
-                                (cudaStream_t)stream, false)
+                                (cudaStream_t)stream, true)
                    ? 0
                    : -1;
     });

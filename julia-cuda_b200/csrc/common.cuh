@@ -63,19 +63,47 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread (up to `hint_ns`) until the phase completes,
+// instead of spinning on the issue slots the working warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `bar` with this parity to complete; gives up after ~JC_WAIT_NS and
 // records `code`. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-        for (int i = 0; i < 64; i++)
+        for (int i = 0; i < 16; i++)
             if (mbar_try_wait(bar, parity)) return true;
         if (globaltimer() - t0 > JC_WAIT_NS) {
             dev_fail(code);
             return false;
         }
     }
+}
+
+// The same for threads with nothing else to do meanwhile: suspended between polls.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                unsigned int code) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait_sleep(bar, parity, 200000u)) {
+        if (globaltimer() - t0 > JC_WAIT_NS) {
+            dev_fail(code);
+            return false;
+        }
+    }
+    return true;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -152,7 +180,37 @@ __device__ __forceinline__ void tc_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes 32w..32w+31).
+// 16 / 8 consecutive f32 columns of this thread's TMEM lane into v[off..].
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float *v);
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes 32(w%4)..+31).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile(

@@ -147,7 +147,10 @@ bool Engine::gemm(uint32_t epi, const CUtensorMap &amap, const void *w, uint32_t
                   const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
                   const float *rope, const float *bias, float eps, cudaStream_t s) {
     GemmConfig cfgg = choose_gemm(m, n, k, sms);
-    if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && cfgg.bn < 64) cfgg.bn = 64;
+    if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && cfgg.bn < 64) {
+        cfgg.bn = 64;
+        set_gemm_depth(cfgg, m, n, sms);
+    }
     GemmArgs g;
     g.epi = epi;
     g.map_a = amap;

@@ -65,6 +65,7 @@ struct GemmArgs {
 struct GemmConfig {
     int bn = 64;      // output columns per CTA: 32, 64 or 128
     int splits = 1;   // split-K factor, 1..8
+    bool deep = false;  // twice the pipeline stages (one CTA per SM)
 };
 
 // Floats of split-K workspace and counters a launch of this shape needs.
@@ -73,9 +74,13 @@ size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg);
 
 // Validates and launches; false (with the error set) if the arguments are inconsistent.
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl);
+// The argument checks alone (the tensor maps are not looked at).
+bool check_gemm(const GemmArgs &g, GemmConfig cfg);
 
 // The configuration for an m x n x k GEMM on `sms` SMs (the B200 refit of gemm::choose).
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms);
+// Picks the pipeline depth for a configuration whose tile width / splits are already set.
+void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms);
 
 // ---------------------------------------------------------------------------------------------
 // attention: o = softmax(q k^T / 8) v per head, global or |q - k| <= window

@@ -49,9 +49,19 @@ const char *device_error_name(unsigned int code) {
 // ---------------------------------------------------------------------------------------------
 // launch helper: cudaLaunchKernelEx with programmatic stream serialization when `pdl`
 
+// Programmatic dependent launch is on unless the environment sets JC_PDL=0 (for A/B timing).
+static bool pdl_allowed() {
+    static const bool on = [] {
+        const char *v = getenv("JC_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 template <typename... KArgs, typename... Args>
 static bool launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                       bool pdl, const char *what, Args... args) {
+    pdl = pdl && pdl_allowed();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -134,34 +144,43 @@ size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg) {
     return (size_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / cfg.bn);
 }
 
-template <int BN, uint32_t EPI>
+// Stage depths: "shallow" keeps a CTA near 100 KB of shared memory so two fit on an SM (a GEMM
+// and the next kernel's early CTAs under PDL); "deep" doubles the bytes in flight per CTA for
+// grids of at most one CTA per SM, where one CTA's pipeline latency bounds the kernel.
+template <int BN> struct Depth;
+template <> struct Depth<32> { static constexpr int shallow = 5, deep = 10; };
+template <> struct Depth<64> { static constexpr int shallow = 4, deep = 8; };
+template <> struct Depth<128> { static constexpr int shallow = 3, deep = 6; };
+
+template <int BN, int STAGES, uint32_t EPI>
 static bool launch_gemm_inst(const GemmParams &p, dim3 grid, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
-    auto kern = gemm_tc_kernel<BN, EPI>;
-    constexpr int smem = GemmShape<BN>::SMEM_BYTES;
+    auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
+    constexpr int smem = GemmShape<BN, STAGES>::SMEM_BYTES;
     if (!ensure_smem(kern, smem, smem_set)) return false;
     return launch_ex(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, "gemm launch", p);
 }
 
-template <int BN>
-static bool launch_gemm_bn(uint32_t epi, const GemmParams &p, dim3 grid, cudaStream_t s, bool pdl) {
+template <int BN, int STAGES>
+static bool launch_gemm_depth(uint32_t epi, const GemmParams &p, dim3 grid, cudaStream_t s,
+                              bool pdl) {
+    constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
     switch (epi) {
-        case 0: return launch_gemm_inst<BN, 0>(p, grid, s, pdl);
-        case JC_EPI_RES | JC_EPI_STATS: return launch_gemm_inst<BN, JC_EPI_RES | JC_EPI_STATS>(p, grid, s, pdl);
-        case JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS:
-            return launch_gemm_inst<BN, JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS>(p, grid, s, pdl);
-        case JC_EPI_LN | JC_EPI_BIAS: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS>(p, grid, s, pdl);
-        case JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU:
-            return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU>(p, grid, s, pdl);
-        case JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU:
-            return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU>(p, grid, s, pdl);
+        case 0: return launch_gemm_inst<BN, STAGES, 0>(p, grid, s, pdl);
+        case RS: return launch_gemm_inst<BN, STAGES, RS>(p, grid, s, pdl);
+        case JC_EPI_BIAS | RS: return launch_gemm_inst<BN, STAGES, JC_EPI_BIAS | RS>(p, grid, s, pdl);
+        case LB: return launch_gemm_inst<BN, STAGES, LB>(p, grid, s, pdl);
+        case LB | JC_EPI_RELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_RELU>(p, grid, s, pdl);
+        case LB | JC_EPI_GELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_GELU>(p, grid, s, pdl);
         default: break;
     }
     if constexpr (BN >= 64) {
         switch (epi) {
-            case JC_EPI_ROPE: return launch_gemm_inst<BN, JC_EPI_ROPE>(p, grid, s, pdl);
-            case JC_EPI_LN | JC_EPI_ROPE: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_ROPE>(p, grid, s, pdl);
-            case JC_EPI_LN | JC_EPI_GEGLU: return launch_gemm_inst<BN, JC_EPI_LN | JC_EPI_GEGLU>(p, grid, s, pdl);
+            case JC_EPI_ROPE: return launch_gemm_inst<BN, STAGES, JC_EPI_ROPE>(p, grid, s, pdl);
+            case JC_EPI_LN | JC_EPI_ROPE:
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_ROPE>(p, grid, s, pdl);
+            case JC_EPI_LN | JC_EPI_GEGLU:
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_GEGLU>(p, grid, s, pdl);
             default: break;
         }
     }
@@ -170,7 +189,42 @@ static bool launch_gemm_bn(uint32_t epi, const GemmParams &p, dim3 grid, cudaStr
     return false;
 }
 
+template <int BN>
+static bool launch_gemm_bn(uint32_t epi, bool deep, const GemmParams &p, dim3 grid,
+                           cudaStream_t s, bool pdl) {
+    return deep ? launch_gemm_depth<BN, Depth<BN>::deep>(epi, p, grid, s, pdl)
+                : launch_gemm_depth<BN, Depth<BN>::shallow>(epi, p, grid, s, pdl);
+}
+
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
+    if (!check_gemm(g, cfg)) return false;
+    GemmParams p;
+    p.map_a = g.map_a;
+    p.map_w = g.map_w;
+    p.c = g.c;
+    p.res = g.res;
+    p.ws = g.ws;
+    p.counters = g.counters;
+    p.stats_in = g.stats_in;
+    p.colsum = g.colsum;
+    p.stats_out = g.stats_out;
+    p.zero = g.zero;
+    p.rope = g.rope;
+    p.bias = g.bias;
+    p.zero_len = g.zero_len;
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.eps = g.eps;
+    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.splits);
+    switch (cfg.bn) {
+        case 32: return launch_gemm_bn<32>(g.epi, cfg.deep, p, grid, s, pdl);
+        case 64: return launch_gemm_bn<64>(g.epi, cfg.deep, p, grid, s, pdl);
+        default: return launch_gemm_bn<128>(g.epi, cfg.deep, p, grid, s, pdl);
+    }
+}
+
+bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     const uint32_t e = g.epi;
     const bool ln = e & JC_EPI_LN, res = e & JC_EPI_RES, stats = e & JC_EPI_STATS,
                rope = e & JC_EPI_ROPE, geglu = e & JC_EPI_GEGLU, bias = e & JC_EPI_BIAS;
@@ -199,30 +253,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
         return fail("c, res, colsum, bias and the RoPE table must be 16-byte aligned");
     if (reinterpret_cast<uintptr_t>(g.stats_in) & 7) return fail("stats_in must be 8-byte aligned");
     if (cfg.splits > 1 && (!g.ws || !g.counters)) return fail("split-K needs a workspace and counters");
-    GemmParams p;
-    p.map_a = g.map_a;
-    p.map_w = g.map_w;
-    p.c = g.c;
-    p.res = g.res;
-    p.ws = g.ws;
-    p.counters = g.counters;
-    p.stats_in = g.stats_in;
-    p.colsum = g.colsum;
-    p.stats_out = g.stats_out;
-    p.zero = g.zero;
-    p.rope = g.rope;
-    p.bias = g.bias;
-    p.zero_len = g.zero_len;
-    p.m = g.m;
-    p.n = g.n;
-    p.k = g.k;
-    p.eps = g.eps;
-    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.splits);
-    switch (cfg.bn) {
-        case 32: return launch_gemm_bn<32>(e, p, grid, s, pdl);
-        case 64: return launch_gemm_bn<64>(e, p, grid, s, pdl);
-        default: return launch_gemm_bn<128>(e, p, grid, s, pdl);
-    }
+    return true;
 }
 
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
@@ -231,10 +262,22 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     c.bn = (n % 128 == 0 && tiles_m * (n / 128) >= (uint32_t)sms) ? 128 : 64;
     if (n % c.bn) c.bn = 32;
     const uint32_t ctas = tiles_m * (n / c.bn);
+    // Split-K measured slower than one CTA per tile for every encoder shape at 72-1024 tokens
+    // (the partial round trip costs more than the shorter K loop saves), so it stays at 1.
     c.splits = 1;
-    while (c.splits < 4 && ctas * c.splits * 2 <= (uint32_t)sms && k / GEMM_BK / (c.splits * 2) >= 3)
-        c.splits *= 2;
+    (void)k;
+    (void)ctas;
+    set_gemm_depth(c, m, n, sms);
     return c;
+}
+
+void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
+    // At most one CTA per SM: the pipeline depth of one CTA bounds the kernel, so go deep.
+    const uint32_t ctas = (m + GEMM_BM - 1) / GEMM_BM * (n / c.bn) * c.splits;
+    c.deep = ctas <= (uint32_t)sms;
+    static const char *force = getenv("JC_GEMM_DEPTH");  // A/B knob: "deep" / "shallow"
+    if (force && force[0] == 'd') c.deep = true;
+    if (force && force[0] == 's') c.deep = false;
 }
 
 // ---------------------------------------------------------------------------------------------
