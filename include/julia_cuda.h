@@ -64,7 +64,9 @@ void julia_cuda_device(const JcEngine *engine, char *buf, size_t len);
 /* Runs b sequences back to back: sequence i is lens[i] token ids (concatenated in ids) with
  * n_markers[i] marker positions (concatenated in markers) and question type qtypes[i]. Writes each
  * sequence's logits (one per marker, concatenated) and its GPU time in ms (embed to logits) into
- * gpu_ms[i]. layer_fused: the persistent per-layer kernel instead of the per-step kernels.
+ * gpu_ms[i]. layer_fused: 0 runs one kernel per step (the reference's per-step kernels), 1 one
+ * persistent launch per encoder layer (the reference's layer kernel), 2 one persistent launch for
+ * the whole model, embed to logits.
  * Returns 0, or -1 with the error in err (also for non-finite logits and device-side timeouts).
  * Replaces src/capi.rs:108-190. */
 int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const size_t *lens,
@@ -109,6 +111,13 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
                               const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
                               int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
                               char *err, size_t err_len);
+
+/* Failure detection: runs the persistent kernel with a grid barrier that waits for one CTA more
+ * than the grid has, so every wait must give up after timeout_ns; writes the device error code it
+ * recorded (JC_DEV_TIMEOUT_GRID = 4) and leaves the engine usable. No counterpart in the
+ * reference (its grid barrier spins forever, kernels/src/gemm.rs:444-463). */
+int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint32_t *code,
+                                     char *err, size_t err_len);
 
 /* How many kernels one forward pass launches (for launch accounting). */
 int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,

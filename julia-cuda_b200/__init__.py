@@ -96,6 +96,7 @@ def lib():
         "julia_cuda_load_random": ([cfgp, u64, sz, i32, P, sz], P),
         "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
         "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
+        "julia_cuda_barrier_timeout_probe": ([P, u64, P, P, sz], i32),
         "julia_cuda_engine_config": ([P, cfgp, P, P, P], i32),
         "jc_gemm": ([u32, i32, i32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32, f32, P, P, P],
                     i32),
@@ -348,8 +349,9 @@ class Engine:
         lib().julia_cuda_device(self._h, buf, 256)
         return buf.value.decode()
 
-    def run(self, seqs, layer_fused: bool = False):
-        """seqs: list of (ids, markers, qtype). Returns (list of logits arrays, gpu_ms array)."""
+    def run(self, seqs, layer_fused: int = 0):
+        """seqs: list of (ids, markers, qtype). Returns (list of logits arrays, gpu_ms array).
+        layer_fused: 0 per-step kernels, 1 one persistent launch per layer, 2 whole model."""
         ids = np.ascontiguousarray(np.concatenate([np.asarray(s[0], np.uint32) for s in seqs]))
         lens = np.array([len(s[0]) for s in seqs], np.uint64)
         mk = [np.asarray(s[1], np.uint32) for s in seqs]
@@ -382,3 +384,14 @@ class Engine:
 
     def launches_per_forward(self, n: int, n_markers: int, layer_fused=False) -> int:
         return lib().julia_cuda_launches_per_forward(self._h, n, n_markers, int(layer_fused))
+
+    def barrier_timeout_probe(self, timeout_ns: int) -> int:
+        """Makes a persistent-kernel grid barrier time out on purpose; returns the device error
+        code the kernel recorded (4: a grid barrier timed out)."""
+        code = ctypes.c_uint32(0)
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_barrier_timeout_probe(self._h, timeout_ns, ctypes.byref(code), err,
+                                                   1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        return code.value

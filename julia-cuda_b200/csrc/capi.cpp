@@ -218,6 +218,22 @@ int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t
     return engine->e->launches_per_forward(n, n_markers, layer_fused);
 }
 
+int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint32_t *code,
+                                     char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!engine || !code) {
+            report(err, err_len, "probe: null engine or code");
+            return -1;
+        }
+        if (!set_device(engine->e->device, err, err_len)) return -1;
+        if (!engine->e->barrier_timeout_probe(timeout_ns, code)) {
+            report(err, err_len, std::string("probe: ") + jc::last_error());
+            return -1;
+        }
+        return 0;
+    });
+}
+
 int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
                               const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
                               int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,

@@ -1,4 +1,4 @@
-// The engine: weights on the device, preallocated buffers, and the forward pass.
+// The engine: weights on the device, preallocated buffers, and the forward pass as steps.
 #include "engine.h"
 
 #include <algorithm>
@@ -30,7 +30,10 @@ Engine *Engine::create(const jc_model_config &cfg, const float *raw, size_t max_
 Engine::~Engine() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
-    for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
+    for (auto &kv : graphs) {
+        cudaGraphExecDestroy(kv.second.exec);
+        if (kv.second.descs) cudaFree(kv.second.descs);
+    }
     for (int i = 0; i < QUEUE; i++) {
         if (ev_start[i]) cudaEventDestroy(ev_start[i]);
         if (ev_end[i]) cudaEventDestroy(ev_end[i]);
@@ -40,6 +43,17 @@ Engine::~Engine() {
     if (h_markers) cudaFreeHost(h_markers);
     if (h_logits) cudaFreeHost(h_logits);
     if (stream) cudaStreamDestroy(stream);
+}
+
+int Engine::add_map(const void *p, uint32_t rows, uint32_t cols, uint32_t box) {
+    auto key = std::make_tuple(p, rows, cols, box);
+    auto it = map_index.find(key);
+    if (it != map_index.end()) return it->second;
+    CUtensorMap m;
+    if (!make_tmap_f16(&m, p, rows, cols, box)) return -1;
+    hmaps.push_back(m);
+    map_index.emplace(key, (int)hmaps.size() - 1);
+    return (int)hmaps.size() - 1;
 }
 
 bool Engine::init(const float *raw, std::string *why) {
@@ -93,7 +107,8 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
               dalloc((void **)&ids, L * 4) && dalloc((void **)&markers, L * 4) &&
-              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4);
+              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4) &&
+              dalloc((void **)&bar, 64);
     if (!ok) return false;
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
     const size_t widest = std::max({3 * D, 2 * I, F, S});
@@ -106,7 +121,8 @@ bool Engine::init(const float *raw, std::string *why) {
     if (!ok) return false;
     if (!cu(cudaMemset(gemm_cnt, 0, gemm_cnt_cap * 4), "memset") ||
         !cu(cudaMemset(attn_cnt, 0, attn_cnt_cap * 4), "memset") ||
-        !cu(cudaMemset(x, 0, rows * D * 2), "memset") || !cu(cudaMemset(o, 0, rows * D * 2), "memset") ||
+        !cu(cudaMemset(bar, 0, 64), "memset") || !cu(cudaMemset(x, 0, rows * D * 2), "memset") ||
+        !cu(cudaMemset(o, 0, rows * D * 2), "memset") ||
         !cu(cudaMemset(mb, 0, rows * wide * 2), "memset") ||
         !cu(cudaMemset(hx, 0, rows * D * 2), "memset") || !cu(cudaMemset(xs, 0, rows * D * 2), "memset"))
         return false;
@@ -114,13 +130,41 @@ bool Engine::init(const float *raw, std::string *why) {
     for (size_t i = 0; i < L; i++) io[i] = (uint32_t)i;
     if (!cu(cudaMemcpy(iota, io.data(), L * 4, cudaMemcpyHostToDevice), "upload")) return false;
 
-    // A-operand tensor maps over the whole (row-padded) activation buffers.
-    if (!make_tmap_f16(&tm_x, x, rows, D, 128) || !make_tmap_f16(&tm_o, o, rows, D, 128) ||
-        !make_tmap_f16(&tm_m, mb, rows, I, 128) || !make_tmap_f16(&tm_f, mb, rows, F, 128) ||
-        !make_tmap_f16(&tm_hx, hx, rows, D, 128) || !make_tmap_f16(&tm_xs, xs, rows, D, 128)) {
+    // Tensor maps: A operands over the whole (row-padded) activation buffers (128-row boxes),
+    // weights in 64-row boxes (the persistent kernel's tile width).
+    const PreparedLayout &P = hw.layout;
+    m_x = add_map(x, rows, D, 128);
+    m_o = add_map(o, rows, D, 128);
+    m_m = add_map(mb, rows, I, 128);
+    m_f = add_map(mb, rows, F, 128);
+    m_hx = add_map(hx, rows, D, 128);
+    m_xs = add_map(xs, rows, D, 128);
+    for (const LayerSpans &ls : P.layers)
+        lmaps.push_back({add_map(w16 + ls.wqkv.off, 3 * D, D, 64), add_map(w16 + ls.wo.off, D, D, 64),
+                         add_map(w16 + ls.wi.off, 2 * I, D, 64),
+                         add_map(w16 + ls.wo_mlp.off, D, I, 64)});
+    for (const HeadSpans &h : P.head)
+        hmaps_head.push_back({add_map(w16 + h.in_w.off, 3 * D, D, 64),
+                              add_map(w16 + h.out_w.off, D, D, 64), add_map(w16 + h.l1_w.off, F, D, 64),
+                              add_map(w16 + h.l2_w.off, D, F, 64)});
+    m_s1 = add_map(w16 + P.s_lin1_w.off, S, D, 64);
+    if (m_x < 0 || m_o < 0 || m_m < 0 || m_f < 0 || m_hx < 0 || m_xs < 0 || m_s1 < 0) {
         *why = last_error();
         return false;
     }
+    for (auto &lm : lmaps)
+        if (lm.wqkv < 0 || lm.wo < 0 || lm.wi < 0 || lm.wo_mlp < 0) {
+            *why = last_error();
+            return false;
+        }
+    if (!dalloc((void **)&dmaps, hmaps.size() * sizeof(CUtensorMap)) ||
+        !cu(cudaMemcpy(dmaps, hmaps.data(), hmaps.size() * sizeof(CUtensorMap),
+                       cudaMemcpyHostToDevice),
+            "upload tensor maps"))
+        return false;
+    scratch_cap = 16 + 6 * (size_t)cfg.n_layers + 6 * (size_t)cfg.n_head_layers + 8;
+    if (!dalloc((void **)&scratch_descs, scratch_cap * sizeof(PhaseDesc))) return false;
+    persist_grid = (uint32_t)(sms * std::max(0, persist_blocks_per_sm()));
 
     if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * L * 4), "cudaMallocHost") ||
         !cu(cudaMallocHost((void **)&h_markers, QUEUE * L * 4), "cudaMallocHost") ||
@@ -142,21 +186,19 @@ const CUtensorMap *Engine::wmap(const void *p, uint32_t rows, uint32_t cols, int
     return &wmaps.emplace(key, m).first->second;
 }
 
-bool Engine::gemm(uint32_t epi, const CUtensorMap &amap, const void *w, uint32_t m, uint32_t n,
-                  uint32_t k, __half *c, const __half *res, const float *stats_in,
-                  const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
-                  const float *rope, const float *bias, float eps, cudaStream_t s) {
-    GemmConfig cfgg = choose_gemm(m, n, k, sms);
-    if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && cfgg.bn < 64) {
-        cfgg.bn = 64;
-        set_gemm_depth(cfgg, m, n, sms);
-    }
-    GemmArgs g;
-    g.epi = epi;
-    g.map_a = amap;
-    const CUtensorMap *wm = wmap(w, n, k, cfgg.bn);
-    if (!wm) return false;
-    g.map_w = *wm;
+// ---------------------------------------------------------------------------------------------
+// the forward pass as steps
+
+Step Engine::gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32_t m, uint32_t n,
+                       uint32_t k, __half *c, const __half *res, const float *stats_in,
+                       const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
+                       const float *rope, const float *bias, float eps, int layer) const {
+    Step st;
+    st.d.kind = PH_GEMM;
+    st.d.epi = epi;
+    GemmParams &g = st.d.g;
+    g.map_a = dmaps + map_a;
+    g.map_w = dmaps + map_w;
     g.c = c;
     g.res = res;
     g.ws = gemm_ws;
@@ -165,157 +207,343 @@ bool Engine::gemm(uint32_t epi, const CUtensorMap &amap, const void *w, uint32_t
     g.colsum = colsum;
     g.stats_out = stats_out;
     g.zero = zero;
+    g.rope = rope;
+    g.bias = bias;
     g.zero_len = zero_len;
     g.m = m;
     g.n = n;
     g.k = k;
     g.eps = eps;
-    g.rope = rope;
-    g.bias = bias;
-    if (gemm_ws_floats(m, n, cfgg) > gemm_ws_cap || gemm_counters(m, n, cfgg) > gemm_cnt_cap) {
-        set_error("engine: split-K scratch too small");
-        return false;
-    }
-    return launch_gemm(g, cfgg, s, true);
+    st.map_a = map_a;
+    st.w = w;
+    st.layer = layer;
+    return st;
 }
 
-bool Engine::attention(const __half *q, __half *out, uint32_t n, uint32_t window, cudaStream_t s) {
-    AttnArgs a;
-    a.qkv = q;
-    a.o = out;
-    a.n = n;
-    a.heads = cfg.n_heads;
-    a.window = window;
-    a.kv_chunks = choose_kv_chunks(n, cfg.n_heads, window, sms);
-    a.ws = attn_ws;
-    a.counters = attn_cnt;
-    if (attn_ws_floats(n, cfg.n_heads, a.kv_chunks) > attn_ws_cap) a.kv_chunks = 1;
-    return launch_attention(a, s, true);
-}
-
-bool Engine::encoder_layer(int l, uint32_t n, cudaStream_t s) {
-    const LayerSpans &ls = hw.layout.layers[l];
-    const uint32_t D = cfg.d_model, I = cfg.inter;
-    const float *rope = w32 + (ls.global ? hw.layout.rope_global.off : hw.layout.rope_local.off);
-    // qkv: LayerNorm folded (from layer 1) + RoPE; clears stats_a for wo.
-    if (!gemm(ls.has_ln ? (JC_EPI_LN | JC_EPI_ROPE) : JC_EPI_ROPE, tm_x, w16 + ls.wqkv.off, n,
-              3 * D, D, qkv, nullptr, stats_b, ls.has_ln ? w32 + ls.qkv_colsum.off : nullptr,
-              nullptr, stats_a, 2 * n, rope, nullptr, cfg.norm_eps, s))
-        return false;
-    if (!attention(qkv, o, n, ls.global ? 0 : (uint32_t)cfg.window, s)) return false;
-    // wo: x += o . Wo^T, row statistics into stats_a.
-    if (!gemm(JC_EPI_RES | JC_EPI_STATS, tm_o, w16 + ls.wo.off, n, D, D, x, x, nullptr, nullptr,
-              stats_a, nullptr, 0, nullptr, nullptr, 0.f, s))
-        return false;
-    // wi: m = GeGLU(LN(x) . Wi^T); clears stats_b for wo_mlp.
-    if (!gemm(JC_EPI_LN | JC_EPI_GEGLU, tm_x, w16 + ls.wi.off, n, 2 * I, D, mb, nullptr, stats_a,
-              w32 + ls.wi_colsum.off, nullptr, stats_b, 2 * n, nullptr, nullptr, cfg.norm_eps, s))
-        return false;
-    // wo_mlp: x += m . Wo_mlp^T, row statistics into stats_b.
-    return gemm(JC_EPI_RES | JC_EPI_STATS, tm_m, w16 + ls.wo_mlp.off, n, D, I, x, x, nullptr,
-                nullptr, stats_b, nullptr, 0, nullptr, nullptr, 0.f, s);
-}
-
-bool Engine::head_and_scorer(uint32_t n, uint32_t k, uint32_t qtype, cudaStream_t s) {
+std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+                                      int mode) const {
     const PreparedLayout &P = hw.layout;
-    const uint32_t D = cfg.d_model, F = cfg.head_ff, S = cfg.scorer_hidden;
-    const float eps = cfg.head_eps;
+    const uint32_t D = cfg.d_model, I = cfg.inter, F = cfg.head_ff, S = cfg.scorer_hidden;
+    std::vector<Step> steps;
+    auto row_step = [&](uint32_t kind, int layer) {
+        Step st;
+        st.d.kind = kind;
+        st.layer = layer;
+        return st;
+    };
+    auto attn_step = [&](uint32_t window, int layer) {
+        Step st;
+        st.d.kind = PH_ATTN;
+        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, n, (uint32_t)cfg.n_heads, window};
+        st.layer = layer;
+        return st;
+    };
+    {
+        Step st = row_step(PH_EMBED, -1);
+        RowParams &r = st.d.r;
+        r.x = reinterpret_cast<const __half *>(w16 + P.tok_emb.off);
+        r.rows = ids;
+        r.gamma = w32 + P.emb_norm.off;
+        r.out = x;
+        r.n = n;
+        r.d = D;
+        r.eps = cfg.norm_eps;
+        steps.push_back(st);
+    }
+    for (int l = 0; l < cfg.n_layers; l++) {
+        const LayerSpans &ls = P.layers[l];
+        const LayerMaps &lm = lmaps[l];
+        const float *rope = w32 + (ls.global ? P.rope_global.off : P.rope_local.off);
+        // qkv: LayerNorm folded (from layer 1) + RoPE; clears stats_a for wo.
+        steps.push_back(gemm_step(ls.has_ln ? (JC_EPI_LN | JC_EPI_ROPE) : JC_EPI_ROPE, m_x, lm.wqkv,
+                                  w16 + ls.wqkv.off, n, 3 * D, D, qkv, nullptr, stats_b,
+                                  ls.has_ln ? w32 + ls.qkv_colsum.off : nullptr, nullptr, stats_a,
+                                  2 * n, rope, nullptr, cfg.norm_eps, l));
+        steps.push_back(attn_step(ls.global ? 0 : (uint32_t)cfg.window, l));
+        // wo: x += o . Wo^T, row statistics into stats_a.
+        steps.push_back(gemm_step(JC_EPI_RES | JC_EPI_STATS, m_o, lm.wo, w16 + ls.wo.off, n, D, D,
+                                  x, x, nullptr, nullptr, stats_a, nullptr, 0, nullptr, nullptr,
+                                  0.f, l));
+        // wi: m = GeGLU(LN(x) . Wi^T); clears stats_b for wo_mlp.
+        steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_GEGLU, m_x, lm.wi, w16 + ls.wi.off, n, 2 * I, D,
+                                  mb, nullptr, stats_a, w32 + ls.wi_colsum.off, nullptr, stats_b,
+                                  2 * n, nullptr, nullptr, cfg.norm_eps, l));
+        // wo_mlp: x += m . Wo_mlp^T, row statistics into stats_b.
+        steps.push_back(gemm_step(JC_EPI_RES | JC_EPI_STATS, m_m, lm.wo_mlp, w16 + ls.wo_mlp.off, n,
+                                  D, I, x, x, nullptr, nullptr, stats_b, nullptr, 0, nullptr,
+                                  nullptr, 0.f, l));
+        if (d_trace && mode == MODE_MODEL) {
+            Step st = row_step(PH_COPY, l);
+            st.d.r.x = x;
+            st.d.r.out = reinterpret_cast<__half *>(d_trace) + (size_t)l * n * D;
+            st.d.r.n = n;
+            st.d.r.d = D;
+            steps.push_back(st);
+        }
+    }
     // Head input: final LayerNorm + type embedding, statistics into stats_a.
-    if (!launch_norm_add(x, n, D, w32 + P.final_norm.off, w32 + P.type_emb.off + (size_t)qtype * D,
-                         cfg.norm_eps, hx, stats_a, s, true))
-        return false;
+    {
+        Step st = row_step(PH_NORM_ADD, -2);
+        RowParams &r = st.d.r;
+        r.x = x;
+        r.gamma = w32 + P.final_norm.off;
+        r.add = w32 + P.type_emb.off + (size_t)qtype * D;
+        r.out = hx;
+        r.stats = stats_a;
+        r.n = n;
+        r.d = D;
+        r.eps = cfg.norm_eps;
+        steps.push_back(st);
+    }
+    const float heps = cfg.head_eps;
     for (size_t l = 0; l < P.head.size(); l++) {
         const HeadSpans &h = P.head[l];
-        if (!gemm(JC_EPI_LN | JC_EPI_BIAS, tm_hx, w16 + h.in_w.off, n, 3 * D, D, qkv, nullptr,
-                  stats_a, w32 + h.in_colsum.off, nullptr, stats_b, 2 * n, nullptr,
-                  w32 + h.in_b.off, eps, s))
-            return false;
-        if (!attention(qkv, o, n, 0, s)) return false;
-        if (!gemm(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, tm_o, w16 + h.out_w.off, n, D, D, hx, hx,
-                  nullptr, nullptr, stats_b, nullptr, 0, nullptr, w32 + h.out_b.off, 0.f, s))
-            return false;
-        if (!gemm(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU, tm_hx, w16 + h.l1_w.off, n, F, D, mb,
-                  nullptr, stats_b, w32 + h.l1_colsum.off, nullptr, stats_a, 2 * n, nullptr,
-                  w32 + h.l1_b.off, eps, s))
-            return false;
-        if (!gemm(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, tm_f, w16 + h.l2_w.off, n, D, F, hx, hx,
-                  nullptr, nullptr, stats_a, nullptr, 0, nullptr, w32 + h.l2_b.off, 0.f, s))
-            return false;
+        const HeadMaps &hm = hmaps_head[l];
+        steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS, m_hx, hm.in, w16 + h.in_w.off, n, 3 * D, D,
+                                  qkv, nullptr, stats_a, w32 + h.in_colsum.off, nullptr, stats_b,
+                                  2 * n, nullptr, w32 + h.in_b.off, heps, -2));
+        steps.push_back(attn_step(0, -2));
+        steps.push_back(gemm_step(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, m_o, hm.out,
+                                  w16 + h.out_w.off, n, D, D, hx, hx, nullptr, nullptr, stats_b,
+                                  nullptr, 0, nullptr, w32 + h.out_b.off, 0.f, -2));
+        steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU, m_hx, hm.l1, w16 + h.l1_w.off,
+                                  n, F, D, mb, nullptr, stats_b, w32 + h.l1_colsum.off, nullptr,
+                                  stats_a, 2 * n, nullptr, w32 + h.l1_b.off, heps, -2));
+        steps.push_back(gemm_step(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, m_f, hm.l2,
+                                  w16 + h.l2_w.off, n, D, F, hx, hx, nullptr, nullptr, stats_a,
+                                  nullptr, 0, nullptr, w32 + h.l2_b.off, 0.f, -2));
     }
-    if (k == 0) return true;
+    if (k == 0) return steps;
     // Scorer on the marker rows only (rows do not interact after the head's last attention).
-    if (!launch_gather_rows(hx, stats_a, D, markers, k, xs, stats_s, s, true)) return false;
-    if (!gemm(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU, tm_xs, w16 + P.s_lin1_w.off, k, S, D, ys,
-              nullptr, stats_s, w32 + P.s_lin1_colsum.off, nullptr, nullptr, 0, nullptr,
-              w32 + P.s_lin1_b.off, eps, s))
-        return false;
-    return launch_score(ys, S, reinterpret_cast<const __half *>(w16 + P.s_lin2_w.off), P.s_lin2_b, iota, k, logits, s, true);
+    {
+        Step st = row_step(PH_GATHER, -2);
+        RowParams &r = st.d.r;
+        r.x = hx;
+        r.rows = markers;
+        r.stats_in = stats_a;
+        r.out = xs;
+        r.stats = stats_s;
+        r.n = k;
+        r.d = D;
+        steps.push_back(st);
+    }
+    steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU, m_xs, m_s1,
+                              w16 + P.s_lin1_w.off, k, S, D, ys, nullptr, stats_s,
+                              w32 + P.s_lin1_colsum.off, nullptr, nullptr, 0, nullptr,
+                              w32 + P.s_lin1_b.off, heps, -2));
+    {
+        Step st = row_step(PH_SCORE, -2);
+        RowParams &r = st.d.r;
+        r.x = ys;
+        r.rows = iota;
+        r.w = reinterpret_cast<const __half *>(w16 + P.s_lin2_w.off);
+        r.b = P.s_lin2_b;
+        r.logits = logits;
+        r.n = k;
+        r.d = S;
+        steps.push_back(st);
+    }
+    return steps;
 }
 
-bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int fused,
+bool Engine::run_step(const Step &st, cudaStream_t s) {
+    const PhaseDesc &d = st.d;
+    switch (d.kind) {
+        case PH_GEMM: {
+            const GemmParams &p = d.g;
+            GemmConfig c = choose_gemm(p.m, p.n, p.k, sms);
+            if ((d.epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && c.bn < 64) {
+                c.bn = 64;
+                set_gemm_depth(c, p.m, p.n, sms);
+            }
+            if (gemm_ws_floats(p.m, p.n, c) > gemm_ws_cap || gemm_counters(p.m, p.n, c) > gemm_cnt_cap) {
+                set_error("engine: split-K scratch too small");
+                return false;
+            }
+            const CUtensorMap *wm = wmap(st.w, p.n, p.k, c.bn);
+            if (!wm) return false;
+            GemmArgs g;
+            g.epi = d.epi;
+            g.map_a = hmaps[st.map_a];
+            g.map_w = *wm;
+            g.c = p.c;
+            g.res = p.res;
+            g.ws = p.ws;
+            g.counters = p.counters;
+            g.stats_in = p.stats_in;
+            g.colsum = p.colsum;
+            g.stats_out = p.stats_out;
+            g.zero = p.zero;
+            g.zero_len = p.zero_len;
+            g.m = p.m;
+            g.n = p.n;
+            g.k = p.k;
+            g.eps = p.eps;
+            g.rope = p.rope;
+            g.bias = p.bias;
+            return launch_gemm(g, c, s, true);
+        }
+        case PH_ATTN: {
+            AttnArgs a;
+            a.qkv = d.a.qkv;
+            a.o = d.a.o;
+            a.n = d.a.n;
+            a.heads = d.a.heads;
+            a.window = d.a.window;
+            a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms);
+            a.ws = attn_ws;
+            a.counters = attn_cnt;
+            if (attn_ws_floats(a.n, a.heads, a.kv_chunks) > attn_ws_cap) a.kv_chunks = 1;
+            return launch_attention(a, s, true);
+        }
+        case PH_EMBED:
+            return launch_embed(d.r.rows, d.r.n, d.r.x, d.r.gamma, d.r.d, d.r.eps, d.r.out,
+                                d.r.stats, s, true);
+        case PH_NORM_ADD:
+            return launch_norm_add(d.r.x, d.r.n, d.r.d, d.r.gamma, d.r.add, d.r.eps, d.r.out,
+                                   d.r.stats, s, true);
+        case PH_GATHER:
+            return launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n, d.r.out,
+                                      d.r.stats, s, true);
+        case PH_SCORE:
+            return launch_score(d.r.x, d.r.d, d.r.w, d.r.b, d.r.rows, d.r.n, d.r.logits, s, true);
+        case PH_COPY:
+            return cuda_ok(cudaMemcpyAsync(d.r.out, d.r.x, (size_t)d.r.n * d.r.d * 2,
+                                           cudaMemcpyDeviceToDevice, s),
+                           "copy");
+        default:
+            set_error("engine: unknown step");
+            return false;
+    }
+}
+
+bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const PhaseDesc *descs,
+                           uint16_t *d_trace, uint32_t n, cudaStream_t s) {
+    const uint32_t D = cfg.d_model;
+    auto trace_copy = [&](int l) {
+        return cuda_ok(cudaMemcpyAsync(d_trace + (size_t)l * n * D, x, (size_t)n * D * 2,
+                                       cudaMemcpyDeviceToDevice, s),
+                       "trace copy");
+    };
+    if (mode == MODE_MODEL)
+        return launch_persist(descs, (uint32_t)steps.size(), bar, persist_grid, persist_grid,
+                              barrier_timeout_ns, s);
+    size_t i = 0;
+    while (i < steps.size()) {
+        const int layer = steps[i].layer;
+        if (mode == MODE_LAYER && layer >= 0) {
+            size_t j = i;
+            while (j < steps.size() && steps[j].layer == layer) j++;
+            if (!launch_persist(descs + i, (uint32_t)(j - i), bar, persist_grid, persist_grid,
+                                barrier_timeout_ns, s))
+                return false;
+            i = j;
+        } else {
+            if (!run_step(steps[i], s)) return false;
+            i++;
+        }
+        if (d_trace && layer >= 0 && (i == steps.size() || steps[i].layer != layer) &&
+            !trace_copy(layer))
+            return false;
+    }
+    return true;
+}
+
+bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
                              uint16_t *d_trace, cudaStream_t s) {
     if (n == 0 || n > max_length || k > max_length || qtype >= (uint32_t)cfg.n_qtypes) {
         set_error("engine: sequence length, marker count or question type out of range");
         return false;
     }
-    if (fused) {
-        set_error("engine: the persistent layer kernel is not available in this build");
+    if (mode < MODE_STEPS || mode > MODE_MODEL) {
+        set_error("engine: no such execution mode");
         return false;
     }
-    const uint32_t D = cfg.d_model;
-    if (!launch_embed(ids, n, reinterpret_cast<const __half *>(w16 + hw.layout.tok_emb.off), w32 + hw.layout.emb_norm.off, D,
-                      cfg.norm_eps, x, nullptr, s, true))
+    if (mode != MODE_STEPS && persist_grid == 0) {
+        set_error("engine: the persistent kernel cannot be resident on this GPU");
         return false;
-    for (int l = 0; l < cfg.n_layers; l++) {
-        if (!encoder_layer(l, n, s)) return false;
-        if (d_trace && !cuda_ok(cudaMemcpyAsync(d_trace + (size_t)l * n * D, x, (size_t)n * D * 2,
-                                                cudaMemcpyDeviceToDevice, s),
-                                "trace copy"))
-            return false;
     }
-    return head_and_scorer(n, k, qtype, s);
-}
-
-int Engine::launches_per_forward(uint32_t n, uint32_t k, int fused) const {
-    (void)n;
-    (void)fused;
-    int c = 1 + 5 * cfg.n_layers + 1 + 5 * cfg.n_head_layers;
-    if (k) c += 3;
-    return c;
-}
-
-bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int fused, cudaStream_t s) {
-    GraphKey key{n, k, qtype, fused};
-    auto it = graphs.find(key);
-    if (it == graphs.end()) {
-        cudaStream_t cap = stream;
-        if (!cuda_ok(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "begin capture"))
-            return false;
-        const bool ok = enqueue_forward(n, k, qtype, fused, nullptr, cap);
-        cudaGraph_t graph = nullptr;
-        cudaError_t e = cudaStreamEndCapture(cap, &graph);
-        if (!ok) {
-            if (graph) cudaGraphDestroy(graph);
+    const std::vector<Step> steps = build_steps(n, k, qtype, d_trace, mode);
+    if (mode != MODE_STEPS) {
+        if (steps.size() > scratch_cap) {
+            set_error("engine: too many phases");
             return false;
         }
-        if (!cuda_ok(e, "end capture")) return false;
-        cudaGraphExec_t exec = nullptr;
-        e = cudaGraphInstantiate(&exec, graph, 0);
+        std::vector<PhaseDesc> descs(steps.size());
+        for (size_t i = 0; i < steps.size(); i++) descs[i] = steps[i].d;
+        if (!cuda_ok(cudaMemcpyAsync(scratch_descs, descs.data(), descs.size() * sizeof(PhaseDesc),
+                                     cudaMemcpyHostToDevice, s),
+                     "phase upload"))
+            return false;
+        // The copy above is from pageable memory, so it is staged before this call returns.
+    }
+    return enqueue_steps(steps, mode, scratch_descs, d_trace, n, s);
+}
+
+int Engine::launches_per_forward(uint32_t n, uint32_t k, int mode) const {
+    (void)n;
+    const int head = 1 + 5 * cfg.n_head_layers + (k ? 3 : 0);
+    if (mode == MODE_MODEL) return 1;
+    if (mode == MODE_LAYER) return 1 + cfg.n_layers + head;
+    return 1 + 5 * cfg.n_layers + head;
+}
+
+bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s) {
+    GraphKey key{n, k, qtype, mode};
+    auto it = graphs.find(key);
+    if (it == graphs.end()) {
+        if (n == 0 || n > max_length || k > max_length || qtype >= (uint32_t)cfg.n_qtypes ||
+            mode < MODE_STEPS || mode > MODE_MODEL || (mode != MODE_STEPS && persist_grid == 0)) {
+            set_error("engine: sequence length, marker count, question type or mode out of range");
+            return false;
+        }
+        GraphEntry entry;
+        const std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode);
+        if (mode != MODE_STEPS) {
+            std::vector<PhaseDesc> descs(steps.size());
+            for (size_t i = 0; i < steps.size(); i++) descs[i] = steps[i].d;
+            if (!cuda_ok(cudaMalloc(&entry.descs, descs.size() * sizeof(PhaseDesc)), "cudaMalloc") ||
+                !cuda_ok(cudaMemcpy(entry.descs, descs.data(), descs.size() * sizeof(PhaseDesc),
+                                    cudaMemcpyHostToDevice),
+                         "phase upload")) {
+                if (entry.descs) cudaFree(entry.descs);
+                return false;
+            }
+        }
+        cudaStream_t cap = stream;
+        if (!cuda_ok(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "begin capture")) {
+            if (entry.descs) cudaFree(entry.descs);
+            return false;
+        }
+        const bool ok = enqueue_steps(steps, mode, (const PhaseDesc *)entry.descs, nullptr, n, cap);
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(cap, &graph);
+        if (!ok || !cuda_ok(e, "end capture")) {
+            if (graph) cudaGraphDestroy(graph);
+            if (entry.descs) cudaFree(entry.descs);
+            return false;
+        }
+        e = cudaGraphInstantiate(&entry.exec, graph, 0);
         cudaGraphDestroy(graph);
-        if (!cuda_ok(e, "graph instantiate")) return false;
+        if (!cuda_ok(e, "graph instantiate")) {
+            if (entry.descs) cudaFree(entry.descs);
+            return false;
+        }
         if ((int)graphs.size() >= GRAPH_CACHE) {
             GraphKey old = graph_lru.back();
             graph_lru.pop_back();
-            cudaGraphExecDestroy(graphs[old]);
+            cudaStreamSynchronize(stream);
+            cudaGraphExecDestroy(graphs[old].exec);
+            if (graphs[old].descs) cudaFree(graphs[old].descs);
             graphs.erase(old);
         }
-        it = graphs.emplace(key, exec).first;
+        it = graphs.emplace(key, entry).first;
         graph_lru.push_front(key);
     } else {
         graph_lru.remove(key);
         graph_lru.push_front(key);
     }
-    return cuda_ok(cudaGraphLaunch(it->second, s), "graph launch");
+    return cuda_ok(cudaGraphLaunch(it->second.exec, s), "graph launch");
 }
 
 bool Engine::check_device_error(std::string *why) {
@@ -325,10 +553,42 @@ bool Engine::check_device_error(std::string *why) {
         return false;
     }
     if (code) {
+        // A timed-out grid barrier leaves its counters mid-way: start them afresh.
+        cudaMemset(bar, 0, 64);
+        cudaDeviceSynchronize();
         *why = std::string("device error: ") + device_error_name(code);
         return false;
     }
     return true;
+}
+
+bool Engine::barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code) {
+    if (persist_grid == 0) {
+        set_error("engine: the persistent kernel cannot be resident on this GPU");
+        return false;
+    }
+    // Two row phases (a copy each) with a barrier between them that waits for one CTA more than
+    // the grid has: it cannot complete, so every CTA must give up after timeout_ns.
+    std::vector<PhaseDesc> descs(2);
+    for (auto &d : descs) {
+        d.kind = PH_COPY;
+        d.r.x = x;
+        d.r.out = o;
+        d.r.n = 1;
+        d.r.d = (uint32_t)cfg.d_model;
+    }
+    unsigned int before = 0;
+    if (!read_device_error(&before)) return false;
+    if (!cuda_ok(cudaMemcpy(scratch_descs, descs.data(), 2 * sizeof(PhaseDesc), cudaMemcpyHostToDevice),
+                 "phase upload") ||
+        !launch_persist(scratch_descs, 2, bar, persist_grid, persist_grid + 1, timeout_ns, stream) ||
+        !cuda_ok(cudaStreamSynchronize(stream), "probe"))
+        return false;
+    unsigned int c = 0;
+    if (!read_device_error(&c)) return false;
+    *code = c;
+    return cuda_ok(cudaMemset(bar, 0, 64), "reset barrier") &&
+           cuda_ok(cudaDeviceSynchronize(), "reset barrier");
 }
 
 }  // namespace jc

@@ -1,7 +1,9 @@
 // Engine: one model on one GPU with every buffer a request needs preallocated for max_length
-// tokens, the forward pass as a chain of launches (or one persistent launch per layer), captured
-// into CUDA graphs per request shape. The reference's Engine / GpuEncoder / GpuHead
-// (src/engine.rs, src/forward.rs), re-planned for the B200.
+// tokens. The forward pass is a list of steps (GEMMs with fused epilogues, attention, row-wise
+// edges) that runs either as one kernel per step, as one persistent launch per encoder layer, or
+// as a single persistent launch for the whole model; each request shape is captured once into a
+// CUDA graph. The reference's Engine / GpuEncoder / GpuHead (src/engine.rs, src/forward.rs),
+// re-planned for the B200.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -14,18 +16,29 @@
 
 #include "jc_internal.h"
 #include "model.h"
+#include "params.h"
 
 namespace jc {
 
+// Execution modes (the C ABI's layer_fused argument).
+enum : int { MODE_STEPS = 0, MODE_LAYER = 1, MODE_MODEL = 2 };
+
 struct GraphKey {
     uint32_t n, k, qtype;
-    int fused;
+    int mode;
     bool operator==(const GraphKey &o) const {
-        return n == o.n && k == o.k && qtype == o.qtype && fused == o.fused;
+        return n == o.n && k == o.k && qtype == o.qtype && mode == o.mode;
     }
     bool operator<(const GraphKey &o) const {
-        return std::tie(n, k, qtype, fused) < std::tie(o.n, o.k, o.qtype, o.fused);
+        return std::tie(n, k, qtype, mode) < std::tie(o.n, o.k, o.qtype, o.mode);
     }
+};
+
+struct Step {
+    PhaseDesc d{};      // device-ready descriptor (tensor-map pointers into the device map array)
+    int map_a = -1;     // host copy of the A operand's tensor map (index)
+    const void *w = nullptr;  // GEMM weights, for the single-GEMM kernels' own maps
+    int layer = -1;     // encoder layer, or -1 before the encoder, -2 after it
 };
 
 class Engine {
@@ -35,18 +48,24 @@ class Engine {
     ~Engine();
 
     // Queues one sequence whose ids / markers are already in the engine's buffers.
-    bool enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int fused, uint16_t *d_trace,
+    bool enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, uint16_t *d_trace,
                          cudaStream_t s);
     // Same, through a cached CUDA graph of that shape.
-    bool launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int fused, cudaStream_t s);
-    int launches_per_forward(uint32_t n, uint32_t k, int fused) const;
+    bool launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s);
+    int launches_per_forward(uint32_t n, uint32_t k, int mode) const;
+    // Reads (and clears) the device error word; on an error also resets the grid barrier.
     bool check_device_error(std::string *why);
+    // Runs the persistent kernel with a grid barrier that waits for one CTA too many, so it must
+    // time out after timeout_ns; returns the device error code it recorded.
+    bool barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code);
 
     jc_model_config cfg{};
     int device = 0, sms = 0;
+    uint32_t persist_grid = 0;
     size_t max_length = 0;
     std::string name;
     cudaStream_t stream = nullptr;
+    uint64_t barrier_timeout_ns = 2000000000ull;
 
     // inputs / outputs of one request (device)
     uint32_t *ids = nullptr, *markers = nullptr, *iota = nullptr;
@@ -58,16 +77,23 @@ class Engine {
     cudaEvent_t ev_start[QUEUE] = {}, ev_end[QUEUE] = {};
 
    private:
+    struct GraphEntry {
+        cudaGraphExec_t exec = nullptr;
+        void *descs = nullptr;
+    };
     Engine() = default;
     bool init(const float *raw, std::string *why);
+    int add_map(const void *p, uint32_t rows, uint32_t cols, uint32_t box);
     const CUtensorMap *wmap(const void *p, uint32_t rows, uint32_t cols, int bn);
-    bool gemm(uint32_t epi, const CUtensorMap &amap, const void *w, uint32_t m, uint32_t n,
-              uint32_t k, __half *c, const __half *res, const float *stats_in,
-              const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
-              const float *rope, const float *bias, float eps, cudaStream_t s);
-    bool attention(const __half *qkv, __half *o, uint32_t n, uint32_t window, cudaStream_t s);
-    bool encoder_layer(int l, uint32_t n, cudaStream_t s);
-    bool head_and_scorer(uint32_t n, uint32_t k, uint32_t qtype, cudaStream_t s);
+    std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+                                  int mode) const;
+    Step gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32_t m, uint32_t n,
+                   uint32_t k, __half *c, const __half *res, const float *stats_in,
+                   const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
+                   const float *rope, const float *bias, float eps, int layer) const;
+    bool run_step(const Step &st, cudaStream_t s);
+    bool enqueue_steps(const std::vector<Step> &steps, int mode, const PhaseDesc *descs,
+                       uint16_t *d_trace, uint32_t n, cudaStream_t s);
 
     HostWeights hw;  // layout only after upload (arenas freed)
     uint16_t *w16 = nullptr;
@@ -76,11 +102,27 @@ class Engine {
            *xs = nullptr, *ys = nullptr;
     float *stats_a = nullptr, *stats_b = nullptr, *stats_s = nullptr;
     float *gemm_ws = nullptr, *attn_ws = nullptr;
-    uint32_t *gemm_cnt = nullptr, *attn_cnt = nullptr;
+    uint32_t *gemm_cnt = nullptr, *attn_cnt = nullptr, *bar = nullptr;
     size_t gemm_ws_cap = 0, gemm_cnt_cap = 0, attn_ws_cap = 0, attn_cnt_cap = 0;
-    CUtensorMap tm_x{}, tm_o{}, tm_m{}, tm_f{}, tm_hx{}, tm_xs{};
+    // tensor maps: host copies and the device array the persistent kernel reads
+    std::vector<CUtensorMap> hmaps;
+    std::map<std::tuple<const void *, uint32_t, uint32_t, uint32_t>, int> map_index;
+    CUtensorMap *dmaps = nullptr;
+    int m_x = -1, m_o = -1, m_m = -1, m_f = -1, m_hx = -1, m_xs = -1;
+    struct LayerMaps {
+        int wqkv, wo, wi, wo_mlp;
+    };
+    std::vector<LayerMaps> lmaps;
+    struct HeadMaps {
+        int in, out, l1, l2;
+    };
+    std::vector<HeadMaps> hmaps_head;
+    int m_s1 = -1;
+    // descriptors for launches outside a graph (one forward's worth)
+    PhaseDesc *scratch_descs = nullptr;
+    size_t scratch_cap = 0;
     std::map<std::tuple<const void *, uint32_t, uint32_t, int>, CUtensorMap> wmaps;
-    std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::map<GraphKey, GraphEntry> graphs;
     std::list<GraphKey> graph_lru;
     std::vector<void *> allocations;
 };

@@ -116,4 +116,15 @@ bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const u
 bool read_device_error(unsigned int *code);
 const char *device_error_name(unsigned int code);
 
+// ---------------------------------------------------------------------------------------------
+// persistent kernel (persist.cuh): a phase list run by one cooperative launch
+
+struct PhaseDesc;
+// Resident CTAs of the persistent kernel per SM (0 on error).
+int persist_blocks_per_sm();
+// bar: 3 zeroed u32 (arrivals, generation, abort flag) kept across launches; expected: the CTAs
+// each grid barrier waits for (normally grid); timeout_ns: how long a barrier may wait.
+bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t *bar, uint32_t grid,
+                    uint32_t expected, uint64_t timeout_ns, cudaStream_t s);
+
 }  // namespace jc

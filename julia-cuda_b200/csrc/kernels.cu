@@ -12,6 +12,7 @@
 #include "edges.cuh"
 #include "gemm.cuh"
 #include "jc_internal.h"
+#include "persist.cuh"
 
 namespace jc {
 
@@ -153,7 +154,7 @@ template <> struct Depth<64> { static constexpr int shallow = 4, deep = 8; };
 template <> struct Depth<128> { static constexpr int shallow = 3, deep = 6; };
 
 template <int BN, int STAGES, uint32_t EPI>
-static bool launch_gemm_inst(const GemmParams &p, dim3 grid, cudaStream_t s, bool pdl) {
+static bool launch_gemm_inst(const GemmKernelParams &p, dim3 grid, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
     auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
     constexpr int smem = GemmShape<BN, STAGES>::SMEM_BYTES;
@@ -162,7 +163,7 @@ static bool launch_gemm_inst(const GemmParams &p, dim3 grid, cudaStream_t s, boo
 }
 
 template <int BN, int STAGES>
-static bool launch_gemm_depth(uint32_t epi, const GemmParams &p, dim3 grid, cudaStream_t s,
+static bool launch_gemm_depth(uint32_t epi, const GemmKernelParams &p, dim3 grid, cudaStream_t s,
                               bool pdl) {
     constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
     switch (epi) {
@@ -190,7 +191,7 @@ static bool launch_gemm_depth(uint32_t epi, const GemmParams &p, dim3 grid, cuda
 }
 
 template <int BN>
-static bool launch_gemm_bn(uint32_t epi, bool deep, const GemmParams &p, dim3 grid,
+static bool launch_gemm_bn(uint32_t epi, bool deep, const GemmKernelParams &p, dim3 grid,
                            cudaStream_t s, bool pdl) {
     return deep ? launch_gemm_depth<BN, Depth<BN>::deep>(epi, p, grid, s, pdl)
                 : launch_gemm_depth<BN, Depth<BN>::shallow>(epi, p, grid, s, pdl);
@@ -198,9 +199,12 @@ static bool launch_gemm_bn(uint32_t epi, bool deep, const GemmParams &p, dim3 gr
 
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     if (!check_gemm(g, cfg)) return false;
-    GemmParams p;
-    p.map_a = g.map_a;
-    p.map_w = g.map_w;
+    GemmKernelParams kp;
+    kp.map_a = g.map_a;
+    kp.map_w = g.map_w;
+    GemmParams &p = kp.p;
+    p.map_a = nullptr;  // the kernel points these at its own copies
+    p.map_w = nullptr;
     p.c = g.c;
     p.res = g.res;
     p.ws = g.ws;
@@ -218,9 +222,9 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.eps = g.eps;
     dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.splits);
     switch (cfg.bn) {
-        case 32: return launch_gemm_bn<32>(g.epi, cfg.deep, p, grid, s, pdl);
-        case 64: return launch_gemm_bn<64>(g.epi, cfg.deep, p, grid, s, pdl);
-        default: return launch_gemm_bn<128>(g.epi, cfg.deep, p, grid, s, pdl);
+        case 32: return launch_gemm_bn<32>(g.epi, cfg.deep, kp, grid, s, pdl);
+        case 64: return launch_gemm_bn<64>(g.epi, cfg.deep, kp, grid, s, pdl);
+        default: return launch_gemm_bn<128>(g.epi, cfg.deep, kp, grid, s, pdl);
     }
 }
 
@@ -283,16 +287,30 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // ---------------------------------------------------------------------------------------------
 // attention
 
-constexpr int ATTN_WARPS = 4;
-constexpr int ATTN_QT = 16 * ATTN_WARPS;
+// Two shapes: up to 512 tokens, 32-query CTAs whose 4 key groups each take every 4th key tile
+// (the most CTAs and the shortest per-warp key loop); longer, 64-query CTAs with 2 key groups.
+struct AttnVariant {
+    int qw, ks;
+};
+static AttnVariant attn_variant(uint32_t n) { return n <= 512 ? AttnVariant{2, 4} : AttnVariant{4, 2}; }
 
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
     if (kv_chunks <= 1) return 0;
-    return (size_t)((n + ATTN_QT - 1) / ATTN_QT) * heads * kv_chunks * 36 * ATTN_WARPS * 32;
+    const AttnVariant v = attn_variant(n);
+    const uint32_t qt = 16 * v.qw;
+    return (size_t)((n + qt - 1) / qt) * heads * kv_chunks * ATTN_PART * 32 * v.qw;
 }
 
-size_t attn_counters(uint32_t n, uint32_t heads) {
-    return (size_t)((n + ATTN_QT - 1) / ATTN_QT) * heads;
+size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32) * heads; }
+
+template <int QW, int KS>
+static bool launch_attn_inst(const AttnParams &p, uint32_t chunks, cudaStream_t s, bool pdl) {
+    static std::atomic<uint64_t> smem_set{0};
+    using S = AttnShape<QW, KS>;
+    auto kern = attention_kernel<QW, KS>;
+    if (!ensure_smem(kern, S::SMEM, smem_set)) return false;
+    dim3 grid((p.n + S::QT - 1) / S::QT, p.heads, chunks);
+    return launch_ex(kern, grid, dim3(S::THREADS), S::SMEM, s, pdl, "attention launch", p);
 }
 
 bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
@@ -309,17 +327,22 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         return false;
     }
     AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window};
-    dim3 grid((a.n + ATTN_QT - 1) / ATTN_QT, a.heads, a.kv_chunks);
-    return launch_ex(attention_kernel<ATTN_WARPS>, grid, dim3(ATTN_WARPS * 32), 0, s, pdl,
-                     "attention launch", p);
+    const AttnVariant v = attn_variant(a.n);
+    if (v.qw == 2) return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);
+    return launch_attn_inst<4, 2>(p, a.kv_chunks, s, pdl);
 }
 
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) {
+    // Split the keys across CTAs only when a (query tile, head) grid leaves most SMs idle and each
+    // key group would still walk several key tiles.
     if (window > 0) return 1;
-    const uint32_t tiles = ((n + ATTN_QT - 1) / ATTN_QT) * heads;
+    const AttnVariant v = attn_variant(n);
+    const uint32_t qt = 16 * v.qw;
+    const uint32_t tiles = ((n + qt - 1) / qt) * heads;
     const uint32_t key_tiles = (n + 63) / 64;
-    uint32_t c = (uint32_t)(2 * sms) / (tiles ? tiles : 1);
-    if (c > key_tiles) c = key_tiles;
+    if (2 * tiles >= (uint32_t)sms || key_tiles <= (uint32_t)(2 * v.ks)) return 1;
+    uint32_t c = (uint32_t)sms / (tiles ? tiles : 1);
+    if (c > key_tiles / v.ks) c = key_tiles / v.ks;
     if (c > 8) c = 8;
     return c < 1 ? 1 : c;
 }
@@ -376,6 +399,38 @@ bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const u
     }
     return launch_ex(score_kernel, dim3((k + 3) / 4), dim3(128), 0, s, pdl, "score launch", y, d,
                      w, b, markers, k, logits);
+}
+
+// ---------------------------------------------------------------------------------------------
+// persistent kernel
+
+int persist_blocks_per_sm() {
+    static std::atomic<uint64_t> smem_set{0};
+    if (!ensure_smem(persist_kernel, PERSIST_SMEM, smem_set)) return 0;
+    int per_sm = 0;
+    if (!cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, persist_kernel,
+                                                               PERSIST_THREADS, PERSIST_SMEM),
+                 "occupancy"))
+        return 0;
+    return per_sm;
+}
+
+bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t *bar, uint32_t grid,
+                    uint32_t expected, uint64_t timeout_ns, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_set{0};
+    if (!ensure_smem(persist_kernel, PERSIST_SMEM, smem_set)) return false;
+    PersistParams P{phases, n_phases, bar, expected, timeout_ns};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(PERSIST_THREADS);
+    cfg.dynamicSmemBytes = PERSIST_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_ok(cudaLaunchKernelEx(&cfg, persist_kernel, P), "persistent kernel launch");
 }
 
 }  // namespace jc

@@ -24,12 +24,12 @@ def small_cfg(jc):
                              scorer_hidden=128, max_positions=2048)
 
 
-def device_forward(jc, eng, ids, markers, qtype, n_layers, d, trace=True):
+def device_forward(jc, eng, ids, markers, qtype, n_layers, d, trace=True, mode=0):
     ids_t = torch.from_numpy(np.asarray(ids, np.uint32).view(np.int32)).cuda()
     mk_t = torch.from_numpy(np.asarray(markers, np.uint32).view(np.int32)).cuda()
     logits = torch.zeros(len(markers), dtype=torch.float32, device="cuda")
     tr = torch.zeros(n_layers, len(ids), d, dtype=torch.float16, device="cuda") if trace else None
-    eng.forward_device(ids_t, mk_t, qtype, logits, trace=tr)
+    eng.forward_device(ids_t, mk_t, qtype, logits, trace=tr, layer_fused=mode)
     torch.cuda.synchronize()
     assert jc.device_error() == 0
     out = logits.cpu().numpy()
@@ -179,3 +179,55 @@ def test_load_from_directory(jc, O, tmp_path):
     want = O.forward_f32(oracle_cfg(O, c), raw, np.arange(50), [0, 49], 0)
     assert np.max(np.abs(outs[0] - want)) < 0.15
     eng.close()
+
+
+# ---- the persistent kernel: one launch per encoder layer (mode 1), one for the model (mode 2) ----
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("n,qtype", [(1, 0), (65, 1), (293, 2), (600, 0)])
+def test_persistent_modes(jc, O, small_engine, mode, n, qtype):
+    """The persistent layer kernel (the reference's layer-fused mode, src/forward.rs:226-359) and
+    the whole-model kernel against the emulation and the f32 model, and against the per-step
+    kernels (same tiles; only the order of the row statistics' atomic additions differs)."""
+    c, raw, eng = small_engine
+    rng = np.random.default_rng(n + 7)
+    ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+    markers = np.unique(rng.integers(0, n, 4)).astype(np.uint32)
+    got, tr = device_forward(jc, eng, ids, markers, qtype, c.n_layers, c.d_model, mode=mode)
+    oc = oracle_cfg(O, c)
+    emu, tr_emu = O.forward_emu(oc, raw, ids, markers, qtype, trace=True)
+    f32 = O.forward_f32(oc, raw, ids, markers, qtype)
+    for l in range(c.n_layers):
+        assert rel_err(tr[l], tr_emu[l]) < 5e-3, f"layer {l} vs emulation"
+    assert np.max(np.abs(got - emu)) < 2e-3
+    assert np.max(np.abs(got - f32)) < 0.15
+    steps = device_forward(jc, eng, ids, markers, qtype, c.n_layers, c.d_model, trace=False)
+    graphed = device_forward(jc, eng, ids, markers, qtype, c.n_layers, c.d_model, trace=False,
+                             mode=mode)
+    assert np.max(np.abs(graphed - steps)) < 1e-3
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_persistent_benchmark_config(jc, O, full_engine, mode):
+    c, raw, eng = full_engine
+    rng = np.random.default_rng(293)
+    ids = rng.integers(0, c.vocab, 293).astype(np.uint32)
+    markers = np.sort(rng.choice(293, 4, replace=False)).astype(np.uint32)
+    outs, ms = eng.run([(ids, markers, 0)], layer_fused=mode)
+    f32 = O.forward_f32(oracle_cfg(O, c), raw, ids, markers, 0)
+    assert np.max(np.abs(outs[0] - f32)) < 0.15 and np.argmax(outs[0]) == np.argmax(f32)
+    steps, _ = eng.run([(ids, markers, 0)], layer_fused=0)
+    assert np.max(np.abs(outs[0] - steps[0])) < 1e-3
+
+
+def test_grid_barrier_timeout_is_reported(jc, small_engine):
+    """Failure detection without a GPU fault: a grid barrier that waits for one CTA more than the
+    grid has must give up after its limit (0.2 s here), record JC_DEV_TIMEOUT_GRID (4) and leave
+    the engine usable."""
+    c, raw, eng = small_engine
+    assert eng.barrier_timeout_probe(200_000_000) == 4
+    assert jc.device_error() == 0
+    ids = np.arange(40, dtype=np.uint32)
+    for mode in (0, 1, 2):
+        outs, _ = eng.run([(ids, np.array([0, 39], np.uint32), 0)], layer_fused=mode)
+        assert np.isfinite(outs[0]).all()
