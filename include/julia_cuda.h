@@ -150,6 +150,17 @@ int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t 
             const uint16_t *res, float *ws, uint32_t *counters, const float *stats_in,
             const float *colsum, float *stats_out, float *zero, uint32_t zero_len, uint32_t m,
             uint32_t n, uint32_t k, float eps, const float *rope, const float *bias, void *stream);
+/* jc_gemm for callers that cannot allocate device memory (a serving loop whose memory is planned
+ * up front, or code where a cudaMalloc would synchronise or fail): the same arguments without
+ * ws / counters. The split-K scratch is a fixed array in the library's own device memory (4 Mi
+ * floats of partials + 4096 counters, 16 MiB per GPU, held until the process exits); a shape whose
+ * split-K needs more is rejected with an error. Allocates nothing. The first call on a device
+ * looks the array's address up (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. No counterpart in the reference. */
+int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t *w,
+                    uint16_t *c, const uint16_t *res, const float *stats_in, const float *colsum,
+                    float *stats_out, float *zero, uint32_t zero_len, uint32_t m, uint32_t n,
+                    uint32_t k, float eps, const float *rope, const float *bias, void *stream);
 size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 /* The automatic choice (gemm::choose, src/gemm.rs:153-172, refit for the B200's SMs). */
