@@ -144,7 +144,10 @@ int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_
 /* c = epilogue(a . w^T): a [m, k] f16, w [n, k] f16, c [m, n] f16 ([m, n/2] for GEGLU), k a
  * multiple of 64. bn (32/64/128) and splits (1..8) of 0 choose automatically. ws / counters: the
  * split-K workspace (jc_gemm_ws_floats floats, jc_gemm_counters zeroed u32, kept zero between
- * calls). stats_in / stats_out: [m][2] f32 (sum, sum of squares). rope: [>= m][32][2] (cos, sin).
+ * calls). splits = -2 or -4 splits K across a thread-block cluster of that many CTAs instead, which
+ * reduce their partials through distributed shared memory (64- or 128-column tiles; no workspace,
+ * ws / counters unused; same result bits as that many workspace splits). stats_in / stats_out:
+ * [m][2] f32 (sum, sum of squares). rope: [>= m][32][2] (cos, sin).
  * zero / zero_len: a float buffer to clear on the way. Replaces src/gemm.rs:254-392. */
 int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t *w, uint16_t *c,
             const uint16_t *res, float *ws, uint32_t *counters, const float *stats_in,

@@ -397,7 +397,7 @@ static jc::GemmConfig pick(uint32_t m, uint32_t n, uint32_t k, int bn, int split
     jc::GemmConfig c = jc::choose_gemm(m, n, k, sms);
     if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && c.bn < 64) c.bn = 64;
     if (bn) c.bn = bn;
-    if (splits) c.splits = splits;
+    jc::request_splits(c, splits);
     jc::set_gemm_depth(c, m, n, sms);
     return c;
 }
@@ -413,7 +413,7 @@ size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits) 
 int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *splits) {
     jc::GemmConfig c = jc::choose_gemm(m, n, k, sms);
     if (bn) *bn = c.bn;
-    if (splits) *splits = c.splits;
+    if (splits) *splits = c.cluster > 1 ? -c.cluster : c.splits;
     return 0;
 }
 

@@ -124,6 +124,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 3-D tiled load at (x, y, z) (GEMM operands: x the column inside a 64-wide k-block, always 0;
+// y the row; z the k-block), completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // programmatic dependent launch (no-ops when the launch has no PDL attribute)
 
@@ -180,7 +191,7 @@ __device__ __forceinline__ void tc_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 16 / 8 consecutive f32 columns of this thread's TMEM lane into v[off..].
+// 16 / 8 / 4 consecutive f32 columns of this thread's TMEM lane into v.
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float *v);
 
@@ -208,6 +219,16 @@ __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float *v) {
         : "r"(taddr));
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, float *v) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes 32(w%4)..+31).
@@ -267,7 +288,7 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
 // GELU(x) = x * Phi(x) with Phi from the Abramowitz & Stegun 7.1.26 erf approximation (the
 // formula julia-rs and the reference kernels use; kernels/src/gemm.rs:139-150).
 __device__ __forceinline__ float gelu_as(float x) {
-    float t = 1.0f / (1.0f + 0.2316419f * fabsf(x));
+    float t = __frcp_rn(1.0f + 0.2316419f * fabsf(x));
     float p = 0.5f * 1.061405429f;
     p = p * t + 0.5f * -1.453152027f;
     p = p * t + 0.5f * 1.421413741f;
@@ -275,6 +296,12 @@ __device__ __forceinline__ float gelu_as(float x) {
     p = p * t + 0.5f * 0.254829592f;
     float q = p * t * __expf(-0.5f * x * x);
     return x * (x >= 0.0f ? 1.0f - q : q);
+}
+
+// p[0] += a, p[1] += b as one vector reduction (p 8-byte aligned), no return value.
+__device__ __forceinline__ void red_add_f32x2(float *p, float a, float b) {
+    asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b)
+                 : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -8,8 +8,15 @@
 //   - a CTA computes a 128 x BN tile (BN = 32, 64 or 128) with 256 threads;
 //   - warp 0 lane 0 streams 64-deep K blocks of A and W into a ring of STAGES 128B-swizzled
 //     shared-memory stages with TMA (no multicast), each stage completing on an mbarrier;
-//   - warp 1 lane 0 issues tcgen05.mma (M=128, N=BN, K=16, kind::f16) into a TMEM accumulator and
-//     releases each stage with tcgen05.commit;
+//   - lane 0 of warps 1..NI issue tcgen05.mma (M=128, N=BN, K=16, kind::f16), each into its own
+//     TMEM accumulator: one thread's MMAs complete in order at about 130 cycles each whatever N
+//     is, so narrow tiles need independent issuers to keep up with the operand stream;
+//     every issuer takes its share of each stage's MMAs and releases the stage with
+//     tcgen05.commit (the stage's empty barrier counts NI arrivals); the epilogue sums the
+//     accumulators in issuer order;
+//   - a stage holds GEMM_KPS 64-deep k-blocks of A and W, each operand brought by ONE 3-D TMA
+//     box (column-in-block, row, k-block): a TMA request costs ~300 cycles whatever its size, so
+//     fewer, larger requests raise a CTA's ingest rate;
 //   - meanwhile the other warps fetch everything the epilogue reads (column sums and biases into
 //     shared memory, each row's LayerNorm statistics, residuals and RoPE angles into registers),
 //     so no global round trip is left after the accumulator is ready;
@@ -39,13 +46,25 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 256;
 
 
+// 64-deep k-blocks per pipeline stage: one 3-D TMA box per operand brings all of them.
+constexpr int GEMM_KPS = 2;
+
 template <int BN, int STAGES_>
 struct GemmShape {
     static constexpr int STAGES = STAGES_;
-    static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-    static constexpr int B_BYTES = BN * GEMM_BK * 2;
+    static constexpr int KPS = GEMM_KPS;
+    static constexpr int A_KB = GEMM_BM * GEMM_BK * 2;  // one k-block of A: 128 rows x 128 B
+    static constexpr int W_KB = BN * GEMM_BK * 2;       // one k-block of W
+    static constexpr int A_BYTES = KPS * A_KB;
+    static constexpr int B_BYTES = KPS * W_KB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+    // MMA issuer warps, each with its own accumulator (tcgen05.mma from one thread completes in
+    // order at about one 128-row instruction per 130 cycles whatever N is, so narrow tiles need
+    // several independent issuers; four measured faster than two for 32- and 64-column tiles).
+    static constexpr int NI = BN <= 64 ? 4 : 2;
+    static constexpr int ACC_COLS = NI * BN;
+    static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
+                                     : ACC_COLS <= 256 ? 256 : 512;
     static constexpr int CH = BN < 64 ? BN : 64;  // epilogue chunk
     static constexpr int G = CH / 4;              // columns per thread per half-chunk group
     static constexpr int NCH = BN / CH;           // chunks per tile
@@ -55,54 +74,77 @@ struct GemmShape {
     static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 
-// Stores G values (plus the residual, already in registers, and their statistics) at dst.
-template <int G, uint32_t EPI>
-__device__ __forceinline__ void store_group(const float *v, __half *dst, const uint4 *resv,
-                                            float &s, float &q) {
+// G f16 values as G/2 packed half2 words, moved with 16-byte accesses (G % 8 == 0) or 8-byte ones.
+template <int G>
+__device__ __forceinline__ void load_halves(const __half *src, uint32_t *out) {
+    if constexpr (G % 8 == 0) {
 #pragma unroll
-    for (int j = 0; j < G / 8; j++) {
-        float w[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) w[e] = v[8 * j + e];
-        if constexpr ((EPI & JC_EPI_RES) != 0) {
-            const uint4 rr = resv[j];
-            const float2 a = unpack_half2(rr.x), b = unpack_half2(rr.y);
-            const float2 cc = unpack_half2(rr.z), d = unpack_half2(rr.w);
-            w[0] += a.x; w[1] += a.y; w[2] += b.x; w[3] += b.y;
-            w[4] += cc.x; w[5] += cc.y; w[6] += d.x; w[7] += d.y;
+        for (int j = 0; j < G / 8; j++) {
+            const uint4 t = reinterpret_cast<const uint4 *>(src)[j];
+            out[4 * j] = t.x; out[4 * j + 1] = t.y; out[4 * j + 2] = t.z; out[4 * j + 3] = t.w;
         }
-        uint4 o;
-        o.x = pack_half2(w[0], w[1]);
-        o.y = pack_half2(w[2], w[3]);
-        o.z = pack_half2(w[4], w[5]);
-        o.w = pack_half2(w[6], w[7]);
-        reinterpret_cast<uint4 *>(dst)[j] = o;
-        if constexpr ((EPI & JC_EPI_STATS) != 0) {
-            // Statistics of the values as stored (f16), as the next LayerNorm sees them.
-            const uint32_t pk[4] = {o.x, o.y, o.z, o.w};
+    } else {
+        static_assert(G % 4 == 0, "groups of 4 columns at least");
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float2 f = unpack_half2(pk[e]);
-                s += f.x + f.y;
-                q = fmaf(f.x, f.x, q);
-                q = fmaf(f.y, f.y, q);
-            }
+        for (int j = 0; j < G / 4; j++) {
+            const uint2 t = reinterpret_cast<const uint2 *>(src)[j];
+            out[2 * j] = t.x; out[2 * j + 1] = t.y;
         }
     }
 }
 
-// The epilogue of one thread's share of chunk `ci`: v[0, G) are tile columns la.., v[G, 2G) tile
-// columns la + CH/2.. (la = ci * CH + G * half). cs / bs: the tile's column sums / biases in
-// shared memory. For RoPE / GeGLU chunks (CH = 64) the pair index of v[j] / v[G + j] is 16h + j.
-template <int CH, uint32_t EPI>
+template <int G>
+__device__ __forceinline__ void store_halves(__half *dst, const uint32_t *in) {
+    if constexpr (G % 8 == 0) {
+#pragma unroll
+        for (int j = 0; j < G / 8; j++)
+            reinterpret_cast<uint4 *>(dst)[j] = make_uint4(in[4 * j], in[4 * j + 1], in[4 * j + 2], in[4 * j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < G / 4; j++)
+            reinterpret_cast<uint2 *>(dst)[j] = make_uint2(in[2 * j], in[2 * j + 1]);
+    }
+}
+
+// Stores G values at dst, after adding the residual (already in registers as G/2 half2 words),
+// and accumulates the statistics of the values as stored (f16), as the next LayerNorm sees them.
+template <int G, uint32_t EPI>
+__device__ __forceinline__ void store_group(const float *v, __half *dst, const uint32_t *resw,
+                                            float &s, float &q) {
+    uint32_t out[G / 2];
+#pragma unroll
+    for (int j = 0; j < G / 2; j++) {
+        float lo = v[2 * j], hi = v[2 * j + 1];
+        if constexpr ((EPI & JC_EPI_RES) != 0) {
+            const float2 r = unpack_half2(resw[j]);
+            lo += r.x;
+            hi += r.y;
+        }
+        out[j] = pack_half2(lo, hi);
+        if constexpr ((EPI & JC_EPI_STATS) != 0) {
+            const float2 f = unpack_half2(out[j]);
+            s += f.x + f.y;
+            q = fmaf(f.x, f.x, q);
+            q = fmaf(f.y, f.y, q);
+        }
+    }
+    store_halves<G>(dst, out);
+}
+
+// The epilogue of one thread's share of a chunk of 2 * HALF columns starting at global column c0:
+// v[0, G) are columns c0 + pair0 + j, v[G, 2G) columns c0 + HALF + pair0 + j (HALF = 32 for the
+// 64-column chunks RoPE and GeGLU need: v[j] and v[G + j] are then a RoPE pair (i, i + 32) of one
+// head, or a GeGLU input and its gate). cs / bs: the tile's column sums / biases in shared memory
+// (tile-local, the tile starting at n0); resw: the residual of those columns (G/2 + G/2 words);
+// ropev: (cos, sin) of pairs pair0 .. pair0 + G, two per float4.
+template <int G, int HALF, uint32_t EPI>
 __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v, uint32_t r,
-                                                   bool valid, uint32_t n0, uint32_t la,
-                                                   uint32_t half, float mean, float rstd,
+                                                   bool valid, uint32_t n0, uint32_t c0,
+                                                   uint32_t pair0, float mean, float rstd,
                                                    const float *cs, const float *bs,
-                                                   const uint4 *resv, const float4 *ropev,
+                                                   const uint32_t *resw, const float4 *ropev,
                                                    float &s, float &q) {
-    constexpr int G = CH / 4;
-    const uint32_t lb = la + CH / 2;
+    const uint32_t la = c0 - n0 + pair0, lb = la + HALF;
     if constexpr ((EPI & JC_EPI_LN) != 0) {
 #pragma unroll
         for (int j = 0; j < G; j++) {
@@ -126,48 +168,39 @@ __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v
         for (int j = 0; j < 2 * G; j++) v[j] = gelu_as(v[j]);
     }
     if constexpr ((EPI & JC_EPI_ROPE) != 0) {
-        static_assert(CH == 64, "RoPE needs whole 64-column heads");
+        static_assert(HALF == 32, "RoPE needs whole 64-column heads");
         // q and k are the first two thirds of a qkv row; the chunk is exactly one head.
-        if (valid && n0 + la < 2 * (p.n / 3)) {
+        if (valid && c0 < 2 * (p.n / 3)) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float4 t = ropev[i];  // (cos, sin) of pairs 16h + 2i and 16h + 2i + 1
-                float x1 = v[2 * i], x2 = v[2 * i + 16];
+            for (int i = 0; i < G / 2; i++) {
+                const float4 t = ropev[i];  // (cos, sin) of pairs pair0 + 2i and pair0 + 2i + 1
+                float x1 = v[2 * i], x2 = v[2 * i + G];
                 v[2 * i] = x1 * t.x - x2 * t.y;
-                v[2 * i + 16] = x2 * t.x + x1 * t.y;
+                v[2 * i + G] = x2 * t.x + x1 * t.y;
                 x1 = v[2 * i + 1];
-                x2 = v[2 * i + 17];
+                x2 = v[2 * i + 1 + G];
                 v[2 * i + 1] = x1 * t.z - x2 * t.w;
-                v[2 * i + 17] = x2 * t.z + x1 * t.w;
+                v[2 * i + 1 + G] = x2 * t.z + x1 * t.w;
             }
         }
     }
     if constexpr ((EPI & JC_EPI_GEGLU) != 0) {
-        static_assert(CH == 64, "GeGLU needs 32 input and 32 gate columns per chunk");
+        static_assert(HALF == 32, "GeGLU needs 32 input and 32 gate columns per chunk");
         if (valid) {
             // Packed columns [c0, c0 + 32) are GELU inputs of output columns [c0/2, c0/2 + 32),
-            // [c0 + 32, c0 + 64) their gates; this thread has inputs / gates 16h .. 16h + 15.
-            const uint32_t c0 = n0 + la - 16 * half;
-            uint4 *dst = reinterpret_cast<uint4 *>(p.c + (size_t)r * (p.n / 2) + c0 / 2 + 16 * half);
+            // [c0 + 32, c0 + 64) their gates.
+            uint32_t out[G / 2];
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                uint4 o;
-                o.x = pack_half2(gelu_as(v[8 * j + 0]) * v[8 * j + 16],
-                                 gelu_as(v[8 * j + 1]) * v[8 * j + 17]);
-                o.y = pack_half2(gelu_as(v[8 * j + 2]) * v[8 * j + 18],
-                                 gelu_as(v[8 * j + 3]) * v[8 * j + 19]);
-                o.z = pack_half2(gelu_as(v[8 * j + 4]) * v[8 * j + 20],
-                                 gelu_as(v[8 * j + 5]) * v[8 * j + 21]);
-                o.w = pack_half2(gelu_as(v[8 * j + 6]) * v[8 * j + 22],
-                                 gelu_as(v[8 * j + 7]) * v[8 * j + 23]);
-                dst[j] = o;
-            }
+            for (int j = 0; j < G / 2; j++)
+                out[j] = pack_half2(gelu_as(v[2 * j]) * v[G + 2 * j],
+                                    gelu_as(v[2 * j + 1]) * v[G + 2 * j + 1]);
+            store_halves<G>(p.c + (size_t)r * (p.n / 2) + c0 / 2 + pair0, out);
         }
     } else {
         if (valid) {
             __half *row = p.c + (size_t)r * p.n + n0;
-            store_group<G, EPI>(v, row + la, resv, s, q);
-            store_group<G, EPI>(v + G, row + lb, resv + G / 8, s, q);
+            store_group<G, EPI>(v, row + la, resw, s, q);
+            store_group<G, EPI>(v + G, row + lb, resw + G / 2, s, q);
         }
     }
 }

@@ -29,9 +29,9 @@ struct GemmSmemView {
     }
 };
 
-// A CTA's pipeline position across tiles (every thread keeps the same copy): k-blocks issued so
-// far (stage = it % STAGES, ring round = it / STAGES) and tiles finished (the accumulator
-// barrier's parity).
+// A CTA's pipeline position across tiles (every thread keeps the same copy): stages filled so far
+// (slot = it % STAGES, ring round = it / STAGES) and tiles finished (the accumulator barrier's
+// parity).
 struct GemmRun {
     uint32_t it = 0;
     uint32_t tiles = 0;
@@ -40,12 +40,13 @@ struct GemmRun {
 // Barrier initialisation and the TMEM accumulator; every thread calls it, returns the TMEM base.
 template <int BN, int STAGES>
 __device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES> &sv) {
+    constexpr uint32_t NI = GemmShape<BN, STAGES>::NI;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&sv.full[s], 1);
-            mbar_init(&sv.empty[s], 1);
+            mbar_init(&sv.empty[s], NI);  // every issuer releases every stage
         }
-        mbar_init(sv.done, 1);
+        mbar_init(sv.done, NI);
         fence_barrier_init();
     }
     if ((threadIdx.x >> 5) == 0) tmem_alloc(sv.tmem_slot, GemmShape<BN, STAGES>::TMEM_COLS);
@@ -65,8 +66,13 @@ __device__ __forceinline__ void gemm_teardown(uint32_t tmem) {
     }
 }
 
-// Producer thread only: the W half of the first `count` stages of a tile whose pipeline starts at
-// run.it (expect_tx covers A and W; the A halves follow once the activations are ready).
+// Stages a range of nkb k-blocks takes.
+__device__ __forceinline__ uint32_t gemm_stages(uint32_t nkb) { return (nkb + GEMM_KPS - 1) / GEMM_KPS; }
+
+// Producer thread only: the W half of stages [first, count) of a tile whose pipeline starts at
+// run.it and whose k range starts at k-block kb0 (expect_tx covers A and W; the A halves follow
+// once the activations are ready). A stage's box may reach past the range (or past k): those
+// k-blocks are loaded (zeros past k) but never multiplied.
 template <int BN, int STAGES>
 __device__ __forceinline__ bool gemm_issue_w(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
                                              uint32_t it, uint32_t n0, uint32_t kb0,
@@ -78,10 +84,42 @@ __device__ __forceinline__ bool gemm_issue_w(const GemmParams &p, const GemmSmem
             return false;
         uint8_t *st = sv.stages + s * S::STAGE_BYTES;
         mbar_arrive_expect_tx(&sv.full[s], S::STAGE_BYTES);
-        tma_load_2d(st + S::A_BYTES, p.map_w, &sv.full[s], (int32_t)((kb0 + i) * GEMM_BK),
-                    (int32_t)n0);
+        tma_load_3d(st + S::A_BYTES, p.map_w, &sv.full[s], 0, (int32_t)n0,
+                    (int32_t)(kb0 + i * GEMM_KPS));
     }
     return true;
+}
+
+// Producer thread only: the A half of stage i (whose W half and expect_tx are already issued).
+template <int BN, int STAGES>
+__device__ __forceinline__ void gemm_issue_a(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
+                                             uint32_t it, uint32_t m0, uint32_t kb0, uint32_t i) {
+    using S = GemmShape<BN, STAGES>;
+    const uint32_t s = (it + i) % STAGES;
+    tma_load_3d(sv.stages + s * S::STAGE_BYTES, p.map_a, &sv.full[s], 0, (int32_t)m0,
+                (int32_t)(kb0 + i * GEMM_KPS));
+}
+
+// v[0, G) = columns [ta, ta + G) and v[G, 2G) = columns [tb, tb + G) of this thread's TMEM lane,
+// each summed over the NI accumulators (BN columns apart) in accumulator order, so the result does
+// not depend on timing. The first two accumulators are read with one wait.
+template <int G, int NI, int BN>
+__device__ __forceinline__ void acc_ld2(uint32_t ta, uint32_t tb, float *v) {
+    tmem_ld<G>(ta, v);
+    tmem_ld<G>(tb, v + G);
+    if constexpr (NI > 1) {
+        float t[2 * G];
+#pragma unroll
+        for (int j = 1; j < NI; j++) {
+            tmem_ld<G>(ta + j * BN, t);
+            tmem_ld<G>(tb + j * BN, t + G);
+            tc_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 2 * G; c++) v[c] += t[c];
+        }
+    } else {
+        tc_wait_ld();
+    }
 }
 
 // Clears p.zero (a statistics buffer a later GEMM accumulates into), striding over nblk CTAs.
@@ -97,19 +135,48 @@ __device__ __forceinline__ void k_range(uint32_t kb_total, uint32_t z, uint32_t 
     nkb = (z + 1) * kb_total / splits - kb0;
 }
 
+// Barrier across the CTAs of a thread-block cluster (every thread of every CTA); release /
+// acquire so shared-memory writes into peers before it are visible after it.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+// The shared::cluster address of local shared address `a` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // One 128 x BN output tile (split z of `splits`; `tile` numbers it for the split counters). Every
 // thread of the CTA calls it. `prefetched`: leading stages whose W half gemm_issue_w already
 // issued. `standalone`: the single-GEMM kernel (programmatic dependent launch waits here); in the
 // persistent kernel a grid barrier has already ordered the inputs.
-template <int BN, int STAGES, uint32_t EPI>
+//
+// CS > 1: the CTA is rank z of a cluster of CS CTAs that split K for the same tile. After their
+// MMAs the CTAs reduce-scatter the f32 partials through distributed shared memory: CTA c owns
+// columns [Go c, Go (c + 1)) of each 32-column half of every 64-column chunk (so RoPE pairs and
+// GeGLU input / gate pairs stay together), receives the other CTAs' partials of them into its own
+// (now idle) stage memory, sums them in rank order (deterministic) and runs the epilogue on them.
+template <int BN, int STAGES, uint32_t EPI, int CS = 1>
 __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
                                           uint32_t tmem, GemmRun &run, uint32_t tile_n,
                                           uint32_t tile_m, uint32_t z, uint32_t splits,
                                           uint32_t tile, uint32_t prefetched, bool standalone) {
     using S = GemmShape<BN, STAGES>;
-    constexpr int CH = S::CH, G = S::G, NCH = S::NCH;
+    constexpr int CH = S::CH, NCH = S::NCH, HALF = CH / 2;
+    constexpr int GT = CH / (4 * CS);  // columns per thread per half-chunk group
+    constexpr int GO = 2 * GT;         // columns a cluster rank owns per half-chunk group
+    static_assert(CS == 1 || CH == 64, "cluster split-K needs 64-column chunks");
+    static_assert(GT >= 4, "at least 4 columns per thread group");
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n0 = tile_n * BN, m0 = tile_m * GEMM_BM;
+    const uint32_t rank = CS > 1 ? z : 0;
     uint32_t kb0, nkb;
     k_range(p.k / GEMM_BK, z, splits, kb0, nkb);
 
@@ -120,110 +187,137 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         if constexpr ((EPI & JC_EPI_BIAS) != 0) sv.bs_s[j] = __ldg(p.bias + n0 + j);
     }
 
+    const uint32_t nst = gemm_stages(nkb);
+    const uint32_t pre = nst < (uint32_t)STAGES ? nst : (uint32_t)STAGES;
+    bool ok = true;
     if (warp == 0 && lane == 0) {
         // TMA producer: weights of the first stages first (they do not depend on the previous
         // kernel), then the activations.
-        const uint32_t pre = nkb < (uint32_t)STAGES ? nkb : (uint32_t)STAGES;
-        bool ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, prefetched < pre ? prefetched : pre, pre);
+        ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, prefetched < pre ? prefetched : pre, pre);
         if (standalone) pdl_wait();
-        for (uint32_t i = 0; ok && i < pre; i++) {
-            const uint32_t s = (run.it + i) % STAGES;
-            tma_load_2d(sv.stages + s * S::STAGE_BYTES, p.map_a, &sv.full[s],
-                        (int32_t)((kb0 + i) * GEMM_BK), (int32_t)m0);
+        for (uint32_t i = 0; ok && i < pre; i++) gemm_issue_a<BN, STAGES>(p, sv, run.it, m0, kb0, i);
+    }
+
+    // Epilogue geometry: warp w owns rows 32(w%4)..+31 and half w/4 of the columns it handles.
+    const uint32_t quarter = warp & 3, half = warp >> 2;
+    const uint32_t row = quarter * 32 + lane;
+    const uint32_t r = m0 + row;
+    const bool valid = r < p.m;
+    const uint32_t pair0 = GO * rank + GT * half;  // first column of this thread's groups
+    if (standalone) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+
+    // Everything the epilogue reads from the previous step, requested by every thread (the MMA
+    // issuers included) before the main loop so its latency hides under the MMAs.
+    float2 st_in = make_float2(0.f, 0.f);
+    if constexpr ((EPI & JC_EPI_LN) != 0) {
+        if (valid) st_in = *reinterpret_cast<const float2 *>(p.stats_in + 2 * (size_t)r);
+    }
+    constexpr int RES_W = (EPI & JC_EPI_RES) ? NCH * GT : 1;
+    uint32_t resw[RES_W];
+    if constexpr ((EPI & JC_EPI_RES) != 0) {
+        if (valid) {
+            const __half *src = p.res + (size_t)r * p.n + n0;
+#pragma unroll
+            for (int ci = 0; ci < NCH; ci++) {
+                load_halves<GT>(src + ci * CH + pair0, resw + ci * GT);
+                load_halves<GT>(src + ci * CH + HALF + pair0, resw + ci * GT + GT / 2);
+            }
         }
-        for (uint32_t i = pre; ok && i < nkb; i++) {
-            const uint32_t g = run.it + i, s = g % STAGES, round = g / STAGES;
-            if (!mbar_wait(&sv.empty[s], (round & 1) ^ 1, JC_DEV_TIMEOUT_EMPTY)) break;
-            uint8_t *st = sv.stages + s * S::STAGE_BYTES;
-            mbar_arrive_expect_tx(&sv.full[s], S::STAGE_BYTES);
-            tma_load_2d(st + S::A_BYTES, p.map_w, &sv.full[s], (int32_t)((kb0 + i) * GEMM_BK),
-                        (int32_t)n0);
-            tma_load_2d(st, p.map_a, &sv.full[s], (int32_t)((kb0 + i) * GEMM_BK), (int32_t)m0);
+    }
+    // RoPE angles depend only on the position inside the head: one set serves every chunk.
+    constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? GT / 2 : 1;
+    float4 ropev[ROPE_V];
+    if constexpr ((EPI & JC_EPI_ROPE) != 0) {
+        if (valid) {
+            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope + (size_t)r * 64 + 2 * pair0);
+#pragma unroll
+            for (int i = 0; i < GT / 2; i++) ropev[i] = __ldg(t4 + i);
         }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer: 4 x (128 x BN x 16) per 64-deep K block.
+    }
+
+    if (warp == 0 && lane == 0) {
+        for (uint32_t i = pre; ok && i < nst; i++) {
+            ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, i, i + 1);
+            if (ok) gemm_issue_a<BN, STAGES>(p, sv, run.it, m0, kb0, i);
+        }
+    } else if (warp >= 1 && warp <= (uint32_t)S::NI && lane == 0) {
+        // MMA issuer j = warp - 1: of each stage's 4 x kbs MMAs (128 x BN x 16 each), those whose
+        // index is j modulo NI, into accumulator j.
         constexpr uint32_t idesc = umma_idesc_f16(GEMM_BM, BN);
-        for (uint32_t i = 0; i < nkb; i++) {
+        const uint32_t j = warp - 1, acc = tmem + j * BN;
+        bool started = false;
+        for (uint32_t i = 0; i < nst; i++) {
             const uint32_t g = run.it + i, s = g % STAGES, round = g / STAGES;
             if (!mbar_wait(&sv.full[s], round & 1, JC_DEV_TIMEOUT_FULL)) break;
             tc_fence_after();
+            const uint32_t kbs = nkb - i * GEMM_KPS < (uint32_t)GEMM_KPS ? nkb - i * GEMM_KPS : GEMM_KPS;
             uint8_t *st = sv.stages + s * S::STAGE_BYTES;
-            const uint64_t ad = umma_desc_sw128(smem_u32(st));
-            const uint64_t bd = umma_desc_sw128(smem_u32(st + S::A_BYTES));
 #pragma unroll
-            for (uint32_t kk = 0; kk < GEMM_BK / 16; kk++)
-                // +32 bytes (2 in descriptor units) per 16-element K step inside the 128B row.
-                tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0);
+            for (uint32_t q = j; q < 4 * GEMM_KPS; q += S::NI) {
+                const uint32_t kb = q / 4, kk = q % 4;
+                if (kb < kbs) {
+                    const uint64_t ad = umma_desc_sw128(smem_u32(st + kb * S::A_KB));
+                    const uint64_t bd = umma_desc_sw128(smem_u32(st + S::A_BYTES + kb * S::W_KB));
+                    // +32 bytes (2 in descriptor units) per 16-element K step inside a 128B row.
+                    tc_mma_f16(acc, ad + 2 * kk, bd + 2 * kk, idesc, started);
+                    started = true;
+                }
+            }
             tc_commit(&sv.empty[s]);
         }
         tc_commit(sv.done);
     }
     __syncwarp();
 
-    // ---- epilogue: warp w owns rows 32(w%4)..+31 and column half w/4 of each chunk ----
-    const uint32_t quarter = warp & 3, half = warp >> 2;
-    const uint32_t row = quarter * 32 + lane;
-    const uint32_t r = m0 + row;
-    const bool valid = r < p.m;
-    if (standalone) {
-        pdl_launch_dependents();
-        pdl_wait();
-    }
-
-    // Everything the epilogue reads from the previous step, fetched while the MMAs run.
-    float mean = 0.f, rstd = 0.f;
-    if constexpr ((EPI & JC_EPI_LN) != 0) {
-        if (valid) {
-            const float2 st = *reinterpret_cast<const float2 *>(p.stats_in + 2 * (size_t)r);
-            mean = st.x / (float)p.k;
-            const float var = st.y / (float)p.k - mean * mean;
-            rstd = rsqrtf(fmaxf(var, 0.0f) + p.eps);
-        }
-    }
-    constexpr int RES_V = (EPI & JC_EPI_RES) ? NCH * 2 * G / 8 : 1;
-    uint4 resv[RES_V];
-    if constexpr ((EPI & JC_EPI_RES) != 0) {
-        if (valid) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.res + (size_t)r * p.n + n0);
-#pragma unroll
-            for (int ci = 0; ci < NCH; ci++)
-#pragma unroll
-                for (int j = 0; j < G / 8; j++) {
-                    resv[ci * 2 * G / 8 + j] = src[(ci * CH + G * half) / 8 + j];
-                    resv[ci * 2 * G / 8 + G / 8 + j] = src[(ci * CH + CH / 2 + G * half) / 8 + j];
-                }
-        }
-    }
-    constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? NCH * 8 : 1;
-    float4 ropev[ROPE_V];
-    if constexpr ((EPI & JC_EPI_ROPE) != 0) {
-        if (valid) {
-            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope + (size_t)r * 64 + 32 * half);
-#pragma unroll
-            for (int ci = 0; ci < NCH; ci++)
-#pragma unroll
-                for (int i = 0; i < 8; i++) ropev[ci * 8 + i] = __ldg(t4 + i);
-        }
-    }
-
     const bool mma_ok =
         __syncthreads_and(mbar_wait_sleep(sv.done, run.tiles & 1, JC_DEV_TIMEOUT_MMA)) != 0;
     tc_fence_after();
+    float mean = 0.f, rstd = 0.f;
+    if constexpr ((EPI & JC_EPI_LN) != 0) {
+        mean = st_in.x / (float)p.k;
+        const float var = st_in.y / (float)p.k - mean * mean;
+        rstd = rsqrtf(fmaxf(var, 0.0f) + p.eps);
+    }
     const uint32_t lane_base = tmem + ((quarter * 32) << 16);
     bool run_epilogue = mma_ok;
+    float *recv = reinterpret_cast<float *>(sv.stages);  // cluster partials: [CS][NCH][2 GO][128]
 
-    if (splits > 1 && mma_ok) {
-        float *mine = p.ws + ((size_t)tile * splits + z) * BN * GEMM_BM;
-#pragma unroll 1
-        for (int cb = 0; cb < BN; cb += CH) {
-            float v[2 * G];
-            tmem_ld<G>(lane_base + cb + G * half, v);
-            tmem_ld<G>(lane_base + cb + CH / 2 + G * half, v + G);
-            tc_wait_ld();
+    if constexpr (CS > 1) {
+        // Every CTA of the cluster is past its MMAs, so every stage memory is free.
+        cluster_sync_all();
+        if (mma_ok) {
+            const uint32_t recv_s = smem_u32(recv);
 #pragma unroll
-            for (int j = 0; j < G; j++) {
-                mine[(size_t)(cb + G * half + j) * GEMM_BM + row] = v[j];
-                mine[(size_t)(cb + CH / 2 + G * half + j) * GEMM_BM + row] = v[G + j];
+            for (int ci = 0; ci < NCH; ci++)
+#pragma unroll
+                for (uint32_t o = 0; o < (uint32_t)CS; o++) {
+                    if (o == rank) continue;
+                    float t[2 * GT];
+                    acc_ld2<GT, S::NI, BN>(lane_base + ci * CH + GO * o + GT * half,
+                                           lane_base + ci * CH + HALF + GO * o + GT * half, t);
+                    const uint32_t base = map_to_rank(recv_s, o) +
+                                          (uint32_t)(((rank * NCH + ci) * 2 * GO) * GEMM_BM) * 4u;
+#pragma unroll
+                    for (int j = 0; j < GT; j++) {
+                        st_cluster_f32(base + ((GT * half + j) * GEMM_BM + row) * 4u, t[j]);
+                        st_cluster_f32(base + ((GO + GT * half + j) * GEMM_BM + row) * 4u, t[GT + j]);
+                    }
+                }
+        }
+        cluster_sync_all();
+    } else if (splits > 1 && mma_ok) {
+        float *mine = p.ws + ((size_t)tile * splits + z) * BN * GEMM_BM;
+#pragma unroll
+        for (int ci = 0; ci < NCH; ci++) {
+            float v[2 * GT];
+            acc_ld2<GT, S::NI, BN>(lane_base + ci * CH + pair0, lane_base + ci * CH + HALF + pair0, v);
+#pragma unroll
+            for (int j = 0; j < GT; j++) {
+                mine[(size_t)(ci * CH + pair0 + j) * GEMM_BM + row] = v[j];
+                mine[(size_t)(ci * CH + HALF + pair0 + j) * GEMM_BM + row] = v[GT + j];
             }
         }
         __threadfence();
@@ -243,52 +337,68 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         float s = 0.f, q = 0.f;
 #pragma unroll
         for (int ci = 0; ci < NCH; ci++) {
-            float v[2 * G];
-            const uint32_t la = ci * CH + G * half, lb = la + CH / 2;
-            if (splits == 1) {
-                tmem_ld<G>(lane_base + la, v);
-                tmem_ld<G>(lane_base + lb, v + G);
-                tc_wait_ld();
+            float v[2 * GT];
+            const uint32_t ca = ci * CH + pair0, cb = ca + HALF;
+            if constexpr (CS > 1) {
+                // Sum the ranks' partials in rank order: this CTA's own from TMEM, the others
+                // from its stage memory.
+#pragma unroll
+                for (int j = 0; j < 2 * GT; j++) v[j] = 0.0f;
+#pragma unroll
+                for (uint32_t zz = 0; zz < (uint32_t)CS; zz++) {
+                    if (zz == rank) {
+                        float t[2 * GT];
+                        acc_ld2<GT, S::NI, BN>(lane_base + ca, lane_base + cb, t);
+#pragma unroll
+                        for (int j = 0; j < 2 * GT; j++) v[j] += t[j];
+                    } else {
+                        const float *src = recv + (size_t)((zz * NCH + ci) * 2 * GO) * GEMM_BM;
+#pragma unroll
+                        for (int j = 0; j < GT; j++) {
+                            v[j] += src[(GT * half + j) * GEMM_BM + row];
+                            v[GT + j] += src[(GO + GT * half + j) * GEMM_BM + row];
+                        }
+                    }
+                }
+            } else if (splits == 1) {
+                acc_ld2<GT, S::NI, BN>(lane_base + ca, lane_base + cb, v);
             } else {
 #pragma unroll
-                for (int j = 0; j < 2 * G; j++) v[j] = 0.0f;
+                for (int j = 0; j < 2 * GT; j++) v[j] = 0.0f;
                 for (uint32_t zz = 0; zz < splits; zz++) {
                     if (zz == z) {
-                        float t[2 * G];
-                        tmem_ld<G>(lane_base + la, t);
-                        tmem_ld<G>(lane_base + lb, t + G);
-                        tc_wait_ld();
+                        float t[2 * GT];
+                        acc_ld2<GT, S::NI, BN>(lane_base + ca, lane_base + cb, t);
 #pragma unroll
-                        for (int j = 0; j < 2 * G; j++) v[j] += t[j];
+                        for (int j = 0; j < 2 * GT; j++) v[j] += t[j];
                     } else {
                         const float *part = p.ws + ((size_t)tile * splits + zz) * BN * GEMM_BM;
 #pragma unroll
-                        for (int j = 0; j < G; j++) {
-                            v[j] += __ldcg(part + (size_t)(la + j) * GEMM_BM + row);
-                            v[G + j] += __ldcg(part + (size_t)(lb + j) * GEMM_BM + row);
+                        for (int j = 0; j < GT; j++) {
+                            v[j] += __ldcg(part + (size_t)(ca + j) * GEMM_BM + row);
+                            v[GT + j] += __ldcg(part + (size_t)(cb + j) * GEMM_BM + row);
                         }
                     }
                 }
             }
-            gemm_epilogue_part<CH, EPI>(p, v, r, valid, n0, la, half, mean, rstd, sv.cs_s, sv.bs_s,
-                                        resv + ((EPI & JC_EPI_RES) ? ci * 2 * G / 8 : 0),
-                                        ropev + ((EPI & JC_EPI_ROPE) ? ci * 8 : 0), s, q);
+            gemm_epilogue_part<GT, HALF, EPI>(p, v, r, valid, n0, n0 + ci * CH, pair0, mean, rstd,
+                                              sv.cs_s, sv.bs_s, resw + ((EPI & JC_EPI_RES) ? ci * GT : 0),
+                                              ropev, s, q);
         }
         if constexpr ((EPI & JC_EPI_STATS) != 0) {
-            // The two halves of a row meet in shared memory; one atomic pair per row per tile.
+            // The two halves of a row meet in shared memory; one atomic pair per row per CTA.
             if (half) sv.row_part[row] = make_float2(s, q);
             __syncthreads();
             if (!half && valid) {
                 const float2 o = sv.row_part[row];
-                atomicAdd(p.stats_out + 2 * (size_t)r, s + o.x);
-                atomicAdd(p.stats_out + 2 * (size_t)r + 1, q + o.y);
+                red_add_f32x2(p.stats_out + 2 * (size_t)r, s + o.x, q + o.y);
             }
         }
     }
     // Every TMEM read and shared-memory use of this tile is done before the next one starts.
     tc_fence_before();
     __syncthreads();
-    run.it += nkb;
+    run.it += nst;
     run.tiles += 1;
 }
 
@@ -299,7 +409,7 @@ struct GemmKernelParams {
     GemmParams p;
 };
 
-template <int BN, int STAGES, uint32_t EPI>
+template <int BN, int STAGES, uint32_t EPI, int CS>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ GemmKernelParams kp) {
     extern __shared__ uint8_t smem_raw[];
@@ -315,8 +425,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     const uint32_t tmem = gemm_setup<BN, STAGES>(sv);
     GemmRun run;
-    gemm_tile<BN, STAGES, EPI>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z,
-                               blockIdx.y * gridDim.x + blockIdx.x, 0, true);
+    gemm_tile<BN, STAGES, EPI, CS>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z,
+                                   blockIdx.y * gridDim.x + blockIdx.x, 0, true);
     gemm_zero(p, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
               gridDim.x * gridDim.y * gridDim.z);
     gemm_teardown<BN, STAGES>(tmem);

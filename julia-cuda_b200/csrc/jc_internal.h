@@ -36,8 +36,10 @@ bool cuda_ok(cudaError_t e, const char *what);
 // ---------------------------------------------------------------------------------------------
 // TMA descriptors
 
-// A row-major [rows, cols] f16 matrix, loaded in boxes of box_rows x 64 columns with the 128-byte
-// swizzle. Returns false (and sets the error) on failure.
+// A row-major [rows, cols] f16 GEMM operand (cols a multiple of 64) seen as 3-D: (column inside a
+// 64-wide k-block, row, k-block), loaded in boxes of 64 x box_rows x GEMM_KPS with the 128-byte
+// swizzle, so one box lands as GEMM_KPS consecutive [box_rows][128 B] k-block tiles. Returns false
+// (and sets the error) on failure.
 bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                    uint32_t box_rows);
 
@@ -64,7 +66,8 @@ struct GemmArgs {
 
 struct GemmConfig {
     int bn = 64;      // output columns per CTA: 32, 64 or 128
-    int splits = 1;   // split-K factor, 1..8
+    int splits = 1;   // split-K factor through a global workspace, 1..8
+    int cluster = 1;  // split-K factor inside a thread-block cluster (1, 2 or 4; DSMEM reduction)
     bool deep = false;  // twice the pipeline stages (one CTA per SM)
 };
 
@@ -79,6 +82,9 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg);
 
 // The configuration for an m x n x k GEMM on `sms` SMs (the B200 refit of gemm::choose).
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms);
+// A caller's split-K request: > 0 that many splits through the workspace, < 0 a cluster of -splits
+// CTAs reducing through distributed shared memory (no workspace), 0 keeps the automatic choice.
+void request_splits(GemmConfig &c, int splits);
 // Picks the pipeline depth for a configuration whose tile width / splits are already set.
 void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms);
 

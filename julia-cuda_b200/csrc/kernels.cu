@@ -76,6 +76,36 @@ static bool launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     return cuda_ok(cudaLaunchKernelEx(&cfg, kern, args...), what);
 }
 
+// launch_ex with the grid grouped into thread-block clusters of `cluster_z` CTAs along z (1: none).
+template <typename... KArgs, typename... Args>
+static bool launch_ex_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, bool pdl, int cluster_z, const char *what,
+                              Args... args) {
+    pdl = pdl && pdl_allowed();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    if (cluster_z > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = 1;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = (unsigned)cluster_z;
+        n++;
+    }
+    cfg.attrs = n ? attr : nullptr;
+    cfg.numAttrs = n;
+    return cuda_ok(cudaLaunchKernelEx(&cfg, kern, args...), what);
+}
+
 // Sets a kernel's dynamic shared-memory limit once per device.
 template <typename K>
 static bool ensure_smem(K kern, int bytes, std::atomic<uint64_t> &done_mask) {
@@ -113,15 +143,16 @@ bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t c
         set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
         return false;
     }
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || cols < 64 || rows == 0) {
-        set_error("tensor map: base must be 16-byte aligned and rows whole 16-byte multiples of >= 64 columns");
+    if (cols % 64) {
+        set_error("a GEMM operand's columns must be a multiple of 64");
         return false;
     }
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides,
+    // dims: 64 columns of a k-block, rows, k-blocks; strides (bytes): a row, a k-block (128 B).
+    cuuint64_t dims[3] = {64, rows, cols / 64};
+    cuuint64_t strides[2] = {cols * 2, 128};
+    cuuint32_t box[3] = {64, box_rows, (cuuint32_t)GEMM_KPS};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides,
                     box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -149,39 +180,39 @@ size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg) {
 // and the next kernel's early CTAs under PDL); "deep" doubles the bytes in flight per CTA for
 // grids of at most one CTA per SM, where one CTA's pipeline latency bounds the kernel.
 template <int BN> struct Depth;
-template <> struct Depth<32> { static constexpr int shallow = 5, deep = 10; };
-template <> struct Depth<64> { static constexpr int shallow = 4, deep = 8; };
-template <> struct Depth<128> { static constexpr int shallow = 3, deep = 6; };
+template <> struct Depth<32> { static constexpr int shallow = 2, deep = 5; };
+template <> struct Depth<64> { static constexpr int shallow = 2, deep = 4; };
+template <> struct Depth<128> { static constexpr int shallow = 2, deep = 3; };
 
-template <int BN, int STAGES, uint32_t EPI>
+template <int BN, int STAGES, uint32_t EPI, int CS>
 static bool launch_gemm_inst(const GemmKernelParams &p, dim3 grid, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
-    auto kern = gemm_tc_kernel<BN, STAGES, EPI>;
+    auto kern = gemm_tc_kernel<BN, STAGES, EPI, CS>;
     constexpr int smem = GemmShape<BN, STAGES>::SMEM_BYTES;
     if (!ensure_smem(kern, smem, smem_set)) return false;
-    return launch_ex(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, "gemm launch", p);
+    return launch_ex_cluster(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, CS, "gemm launch", p);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CS>
 static bool launch_gemm_depth(uint32_t epi, const GemmKernelParams &p, dim3 grid, cudaStream_t s,
                               bool pdl) {
     constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
     switch (epi) {
-        case 0: return launch_gemm_inst<BN, STAGES, 0>(p, grid, s, pdl);
-        case RS: return launch_gemm_inst<BN, STAGES, RS>(p, grid, s, pdl);
-        case JC_EPI_BIAS | RS: return launch_gemm_inst<BN, STAGES, JC_EPI_BIAS | RS>(p, grid, s, pdl);
-        case LB: return launch_gemm_inst<BN, STAGES, LB>(p, grid, s, pdl);
-        case LB | JC_EPI_RELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_RELU>(p, grid, s, pdl);
-        case LB | JC_EPI_GELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_GELU>(p, grid, s, pdl);
+        case 0: return launch_gemm_inst<BN, STAGES, 0, CS>(p, grid, s, pdl);
+        case RS: return launch_gemm_inst<BN, STAGES, RS, CS>(p, grid, s, pdl);
+        case JC_EPI_BIAS | RS: return launch_gemm_inst<BN, STAGES, JC_EPI_BIAS | RS, CS>(p, grid, s, pdl);
+        case LB: return launch_gemm_inst<BN, STAGES, LB, CS>(p, grid, s, pdl);
+        case LB | JC_EPI_RELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_RELU, CS>(p, grid, s, pdl);
+        case LB | JC_EPI_GELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_GELU, CS>(p, grid, s, pdl);
         default: break;
     }
     if constexpr (BN >= 64) {
         switch (epi) {
-            case JC_EPI_ROPE: return launch_gemm_inst<BN, STAGES, JC_EPI_ROPE>(p, grid, s, pdl);
+            case JC_EPI_ROPE: return launch_gemm_inst<BN, STAGES, JC_EPI_ROPE, CS>(p, grid, s, pdl);
             case JC_EPI_LN | JC_EPI_ROPE:
-                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_ROPE>(p, grid, s, pdl);
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_ROPE, CS>(p, grid, s, pdl);
             case JC_EPI_LN | JC_EPI_GEGLU:
-                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_GEGLU>(p, grid, s, pdl);
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_GEGLU, CS>(p, grid, s, pdl);
             default: break;
         }
     }
@@ -191,10 +222,15 @@ static bool launch_gemm_depth(uint32_t epi, const GemmKernelParams &p, dim3 grid
 }
 
 template <int BN>
-static bool launch_gemm_bn(uint32_t epi, bool deep, const GemmKernelParams &p, dim3 grid,
-                           cudaStream_t s, bool pdl) {
-    return deep ? launch_gemm_depth<BN, Depth<BN>::deep>(epi, p, grid, s, pdl)
-                : launch_gemm_depth<BN, Depth<BN>::shallow>(epi, p, grid, s, pdl);
+static bool launch_gemm_bn(uint32_t epi, const GemmConfig &cfg, const GemmKernelParams &p,
+                           dim3 grid, cudaStream_t s, bool pdl) {
+    // Cluster split-K runs with the shallow ring: a cluster's CTAs share the tile's K loop.
+    if constexpr (BN >= 64) {
+        if (cfg.cluster == 2) return launch_gemm_depth<BN, Depth<BN>::shallow, 2>(epi, p, grid, s, pdl);
+        if (cfg.cluster == 4) return launch_gemm_depth<BN, Depth<BN>::shallow, 4>(epi, p, grid, s, pdl);
+    }
+    return cfg.deep ? launch_gemm_depth<BN, Depth<BN>::deep, 1>(epi, p, grid, s, pdl)
+                    : launch_gemm_depth<BN, Depth<BN>::shallow, 1>(epi, p, grid, s, pdl);
 }
 
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
@@ -220,11 +256,11 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.n = g.n;
     p.k = g.k;
     p.eps = g.eps;
-    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.splits);
+    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.cluster > 1 ? cfg.cluster : cfg.splits);
     switch (cfg.bn) {
-        case 32: return launch_gemm_bn<32>(g.epi, cfg.deep, kp, grid, s, pdl);
-        case 64: return launch_gemm_bn<64>(g.epi, cfg.deep, kp, grid, s, pdl);
-        default: return launch_gemm_bn<128>(g.epi, cfg.deep, kp, grid, s, pdl);
+        case 32: return launch_gemm_bn<32>(g.epi, cfg, kp, grid, s, pdl);
+        case 64: return launch_gemm_bn<64>(g.epi, cfg, kp, grid, s, pdl);
+        default: return launch_gemm_bn<128>(g.epi, cfg, kp, grid, s, pdl);
     }
 }
 
@@ -239,6 +275,10 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     if (g.n == 0 || g.n % cfg.bn) return fail("n must be a multiple of the tile width");
     if (cfg.splits < 1 || cfg.splits > 8 || (uint32_t)cfg.splits > g.k / GEMM_BK)
         return fail("split-K must be 1..8 and at most k/64");
+    if (cfg.cluster != 1 && cfg.cluster != 2 && cfg.cluster != 4)
+        return fail("a split-K cluster must be 1, 2 or 4 CTAs");
+    if (cfg.cluster > 1 && (cfg.splits != 1 || cfg.bn < 64 || (uint32_t)cfg.cluster > g.k / GEMM_BK))
+        return fail("cluster split-K needs 64- or 128-column tiles, no workspace split and k/64 >= cluster");
     if ((rope || geglu) && cfg.bn < 64) return fail("RoPE and GeGLU need 64- or 128-column tiles");
     if (rope && g.n % 192) return fail("RoPE needs a qkv output (n a multiple of 3 x 64)");
     if (rope && geglu) return fail("RoPE and GeGLU do not combine");
@@ -255,7 +295,8 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
          reinterpret_cast<uintptr_t>(g.colsum) | reinterpret_cast<uintptr_t>(g.bias) |
          reinterpret_cast<uintptr_t>(g.rope)) & 15)
         return fail("c, res, colsum, bias and the RoPE table must be 16-byte aligned");
-    if (reinterpret_cast<uintptr_t>(g.stats_in) & 7) return fail("stats_in must be 8-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(g.stats_in) | reinterpret_cast<uintptr_t>(g.stats_out)) & 7)
+        return fail("stats_in and stats_out must be 8-byte aligned");
     if (cfg.splits > 1 && (!g.ws || !g.counters)) return fail("split-K needs a workspace and counters");
     return true;
 }
@@ -275,10 +316,20 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     return c;
 }
 
+void request_splits(GemmConfig &c, int splits) {
+    if (splits > 0) {
+        c.splits = splits;
+        c.cluster = 1;
+    } else if (splits < 0) {
+        c.splits = 1;
+        c.cluster = -splits;
+    }
+}
+
 void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
     // At most one CTA per SM: the pipeline depth of one CTA bounds the kernel, so go deep.
-    const uint32_t ctas = (m + GEMM_BM - 1) / GEMM_BM * (n / c.bn) * c.splits;
-    c.deep = ctas <= (uint32_t)sms;
+    const uint32_t ctas = (m + GEMM_BM - 1) / GEMM_BM * (n / c.bn) * c.splits * c.cluster;
+    c.deep = ctas <= (uint32_t)sms && c.cluster == 1;
     static const char *force = getenv("JC_GEMM_DEPTH");  // A/B knob: "deep" / "shallow"
     if (force && force[0] == 'd') c.deep = true;
     if (force && force[0] == 's') c.deep = false;

@@ -73,7 +73,7 @@ extern "C" int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t 
         jc::GemmConfig cfg = jc::choose_gemm(m, n, k, sms);
         if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) && cfg.bn < 64) cfg.bn = 64;
         if (bn) cfg.bn = bn;
-        if (splits) cfg.splits = splits;
+        jc::request_splits(cfg, splits);
         jc::set_gemm_depth(cfg, m, n, sms);
         if (cfg.bn <= 0 || n % cfg.bn) {
             jc::set_error("gemm_noalloc: n must be a multiple of the tile width");

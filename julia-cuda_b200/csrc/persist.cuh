@@ -7,8 +7,8 @@
 // per-step kernels. Here the phase list is data (a device array of descriptors), so the same
 // kernel runs one encoder layer per launch (the reference's layer-fused mode) or the whole model,
 // embed to logits, in a single launch. B200 specifics:
-//   - one CTA of 256 threads per SM holding a 64-column TMEM accumulator and an 8-stage TMA ring
-//     for the whole launch (barriers initialised and TMEM allocated once);
+//   - one CTA of 256 threads per SM holding the GEMM's TMEM accumulators and a 4-stage TMA ring
+//     (8 k-blocks deep) for the whole launch (barriers initialised and TMEM allocated once);
 //   - before each grid barrier the producer thread already requests the weight half of its first
 //     stages of the next GEMM phase (weights never depend on the barrier), so the phase starts
 //     with its weights on chip and only the activations left to fetch;
@@ -24,7 +24,7 @@
 namespace jc {
 
 constexpr int PERSIST_BN = 64;
-constexpr int PERSIST_STAGES = 8;
+constexpr int PERSIST_STAGES = 4;
 using PersistGemm = GemmShape<PERSIST_BN, PERSIST_STAGES>;
 using PersistAttn = AttnShape<2, 4>;
 constexpr int PERSIST_THREADS = 256;
@@ -231,8 +231,8 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const Persi
         __syncthreads();
         const PhaseDesc &nx = P.phases[ph + 1];
         if (nx.kind == PH_GEMM && blockIdx.x < gemm_tiles(nx.g)) {
-            const uint32_t nkb = nx.g.k / GEMM_BK;
-            prefetched = nkb < (uint32_t)PERSIST_STAGES ? nkb : (uint32_t)PERSIST_STAGES;
+            const uint32_t nst = gemm_stages(nx.g.k / GEMM_BK);
+            prefetched = nst < (uint32_t)PERSIST_STAGES ? nst : (uint32_t)PERSIST_STAGES;
             if (threadIdx.x == 0) {
                 tma_prefetch_desc(nx.g.map_a);
                 tma_prefetch_desc(nx.g.map_w);
@@ -247,12 +247,9 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const Persi
             // halves too, so the stage barriers can finish) and wait for them, within limits.
             if (threadIdx.x == 0 && prefetched) {
                 const uint32_t tiles_n = nx.g.n / PERSIST_BN;
-                const int32_t m0 = (int32_t)((blockIdx.x / tiles_n) * GEMM_BM);
-                for (uint32_t i = 0; i < prefetched; i++) {
-                    const uint32_t s = (run.it + i) % PERSIST_STAGES;
-                    tma_load_2d(sv.stages + s * PersistGemm::STAGE_BYTES, nx.g.map_a, &sv.full[s],
-                                (int32_t)(i * GEMM_BK), m0);
-                }
+                const uint32_t m0 = (blockIdx.x / tiles_n) * GEMM_BM;
+                for (uint32_t i = 0; i < prefetched; i++)
+                    gemm_issue_a<PERSIST_BN, PERSIST_STAGES>(nx.g, sv, run.it, m0, 0, i);
                 for (uint32_t i = 0; i < prefetched; i++) {
                     const uint32_t g = run.it + i;
                     mbar_wait(&sv.full[g % PERSIST_STAGES], (g / PERSIST_STAGES) & 1,

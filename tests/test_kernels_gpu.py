@@ -131,6 +131,46 @@ def test_gemm_split_k_deterministic(jc, O):
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
 
 
+@pytest.mark.parametrize("bn", [64, 128])
+@pytest.mark.parametrize("cluster", [2, 4])
+@pytest.mark.parametrize("m", [1, 129, 293])
+def test_gemm_cluster_split(jc, O, bn, cluster, m):
+    """Split-K inside a thread-block cluster (splits = -cluster: partials reduced through
+    distributed shared memory, no workspace), every epilogue."""
+    for name, n, k in GEMM_CASES:
+        run_gemm_case(jc, O, name, m, n, k, bn=bn, splits=-cluster)
+
+
+@pytest.mark.parametrize("bn", [64, 128])
+@pytest.mark.parametrize("cluster", [2, 4])
+def test_gemm_cluster_split_matches_workspace_split(jc, O, bn, cluster):
+    """Both split-K forms sum the same partials in split order from zero, so their outputs are
+    bit-identical, and repeated cluster runs are too."""
+    m, n, k = 293, 768, 1152
+    a = cuda_u16(O.f16(O.normal((m, k), 1)))
+    w = cuda_u16(O.f16(O.normal((n, k), 2, std=0.05)))
+    res = cuda_u16(O.f16(O.normal((m, n), 3)))
+    outs = []
+    for splits in (cluster, -cluster, -cluster):
+        c = res.clone()
+        st = torch.zeros(2 * m, dtype=torch.float32, device="cuda")
+        jc.gemm(jc.EPILOGUES["resstats"], a, w, c, res=c, stats_out=st, bn=bn, splits=splits)
+        outs.append(host_u16(c))
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+def test_gemm_rejects_bad_cluster(jc):
+    a = torch.zeros(10, 128, dtype=torch.float16, device="cuda")
+    w = torch.zeros(64, 128, dtype=torch.float16, device="cuda")
+    c = torch.zeros(10, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(jc.JuliaCudaError, match="cluster must be 1, 2 or 4"):
+        jc.gemm(0, a, w, c, bn=64, splits=-3)
+    with pytest.raises(jc.JuliaCudaError, match="cluster split-K needs"):
+        jc.gemm(0, a, w, c, bn=32, splits=-2)
+    with pytest.raises(jc.JuliaCudaError, match="cluster split-K needs"):
+        jc.gemm(0, a, w, c, bn=64, splits=-4)  # k/64 = 2 < 4
+
+
 def test_gemm_rejects_bad_shapes(jc):
     a = torch.zeros(10, 100, dtype=torch.float16, device="cuda")
     w = torch.zeros(64, 100, dtype=torch.float16, device="cuda")
