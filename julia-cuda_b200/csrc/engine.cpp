@@ -107,8 +107,7 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
               dalloc((void **)&ids, L * 4) && dalloc((void **)&markers, L * 4) &&
-              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4) &&
-              dalloc((void **)&bar, 64);
+              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4);
     if (!ok) return false;
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
     const size_t widest = std::max({3 * D, 2 * I, F, S});
@@ -121,7 +120,7 @@ bool Engine::init(const float *raw, std::string *why) {
     if (!ok) return false;
     if (!cu(cudaMemset(gemm_cnt, 0, gemm_cnt_cap * 4), "memset") ||
         !cu(cudaMemset(attn_cnt, 0, attn_cnt_cap * 4), "memset") ||
-        !cu(cudaMemset(bar, 0, 64), "memset") || !cu(cudaMemset(x, 0, rows * D * 2), "memset") ||
+        !cu(cudaMemset(x, 0, rows * D * 2), "memset") ||
         !cu(cudaMemset(o, 0, rows * D * 2), "memset") ||
         !cu(cudaMemset(mb, 0, rows * wide * 2), "memset") ||
         !cu(cudaMemset(hx, 0, rows * D * 2), "memset") || !cu(cudaMemset(xs, 0, rows * D * 2), "memset"))
@@ -164,6 +163,10 @@ bool Engine::init(const float *raw, std::string *why) {
         return false;
     scratch_cap = 16 + 6 * (size_t)cfg.n_layers + 6 * (size_t)cfg.n_head_layers + 8;
     if (!dalloc((void **)&scratch_descs, scratch_cap * sizeof(PhaseDesc))) return false;
+    flow_blocks = (uint32_t)(rows / FLOW_BLOCK);
+    const size_t words = flow_counter_words((uint32_t)scratch_cap, flow_blocks);
+    if (!dalloc((void **)&flow_ctr, words * 4) || !cu(cudaMemset(flow_ctr, 0, words * 4), "memset"))
+        return false;
     persist_grid = (uint32_t)(sms * std::max(0, persist_blocks_per_sm()));
 
     if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * L * 4), "cudaMallocHost") ||
@@ -426,16 +429,16 @@ bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const Phase
                        "trace copy");
     };
     if (mode == MODE_MODEL)
-        return launch_persist(descs, (uint32_t)steps.size(), bar, persist_grid, persist_grid,
-                              barrier_timeout_ns, s);
+        return launch_persist(descs, (uint32_t)steps.size(), steps[0].flow_total, flow_ctr,
+                              flow_blocks, persist_grid, barrier_timeout_ns, s);
     size_t i = 0;
     while (i < steps.size()) {
         const int layer = steps[i].layer;
         if (mode == MODE_LAYER && layer >= 0) {
             size_t j = i;
             while (j < steps.size() && steps[j].layer == layer) j++;
-            if (!launch_persist(descs + i, (uint32_t)(j - i), bar, persist_grid, persist_grid,
-                                barrier_timeout_ns, s))
+            if (!launch_persist(descs + i, (uint32_t)(j - i), steps[i].flow_total, flow_ctr,
+                                flow_blocks, persist_grid, barrier_timeout_ns, s))
                 return false;
             i = j;
         } else {
@@ -463,8 +466,9 @@ bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
         set_error("engine: the persistent kernel cannot be resident on this GPU");
         return false;
     }
-    const std::vector<Step> steps = build_steps(n, k, qtype, d_trace, mode);
+    std::vector<Step> steps = build_steps(n, k, qtype, d_trace, mode);
     if (mode != MODE_STEPS) {
+        plan_steps(steps, mode);
         if (steps.size() > scratch_cap) {
             set_error("engine: too many phases");
             return false;
@@ -498,8 +502,9 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
             return false;
         }
         GraphEntry entry;
-        const std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode);
+        std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode);
         if (mode != MODE_STEPS) {
+            plan_steps(steps, mode);
             std::vector<PhaseDesc> descs(steps.size());
             for (size_t i = 0; i < steps.size(); i++) descs[i] = steps[i].d;
             if (!cuda_ok(cudaMalloc(&entry.descs, descs.size() * sizeof(PhaseDesc)), "cudaMalloc") ||
@@ -553,8 +558,9 @@ bool Engine::check_device_error(std::string *why) {
         return false;
     }
     if (code) {
-        // A timed-out grid barrier leaves its counters mid-way: start them afresh.
-        cudaMemset(bar, 0, 64);
+        // A timed-out dependency wait can leave the persistent kernel's counters mid-way: start
+        // them afresh.
+        cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4);
         cudaDeviceSynchronize();
         *why = std::string("device error: ") + device_error_name(code);
         return false;
@@ -567,28 +573,52 @@ bool Engine::barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code) {
         set_error("engine: the persistent kernel cannot be resident on this GPU");
         return false;
     }
-    // Two row phases (a copy each) with a barrier between them that waits for one CTA more than
-    // the grid has: it cannot complete, so every CTA must give up after timeout_ns.
+    // Two row phases (a copy each); the second waits for one item more than the first has, so
+    // the wait cannot end and every CTA must give up after timeout_ns.
     std::vector<PhaseDesc> descs(2);
     for (auto &d : descs) {
+        d = PhaseDesc{};
         d.kind = PH_COPY;
         d.r.x = x;
         d.r.out = o;
         d.r.n = 1;
         d.r.d = (uint32_t)cfg.d_model;
     }
+    const uint32_t total = plan_flow(descs.data(), 2);
+    descs[0].extra = 1;
     unsigned int before = 0;
     if (!read_device_error(&before)) return false;
     if (!cuda_ok(cudaMemcpy(scratch_descs, descs.data(), 2 * sizeof(PhaseDesc), cudaMemcpyHostToDevice),
                  "phase upload") ||
-        !launch_persist(scratch_descs, 2, bar, persist_grid, persist_grid + 1, timeout_ns, stream) ||
+        !launch_persist(scratch_descs, 2, total, flow_ctr, flow_blocks, persist_grid, timeout_ns, stream) ||
         !cuda_ok(cudaStreamSynchronize(stream), "probe"))
         return false;
     unsigned int c = 0;
     if (!read_device_error(&c)) return false;
     *code = c;
-    return cuda_ok(cudaMemset(bar, 0, 64), "reset barrier") &&
-           cuda_ok(cudaDeviceSynchronize(), "reset barrier");
+    return cuda_ok(cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4),
+                   "reset counters") &&
+           cuda_ok(cudaDeviceSynchronize(), "reset counters");
+}
+
+void Engine::plan_steps(std::vector<Step> &steps, int mode) const {
+    size_t i = 0;
+    while (i < steps.size()) {
+        size_t j = steps.size();
+        if (mode == MODE_LAYER) {
+            j = i + 1;
+            if (steps[i].layer >= 0)
+                while (j < steps.size() && steps[j].layer == steps[i].layer) j++;
+        }
+        std::vector<PhaseDesc> d(j - i);
+        for (size_t t = i; t < j; t++) d[t - i] = steps[t].d;
+        const uint32_t total = plan_flow(d.data(), (uint32_t)(j - i));
+        for (size_t t = i; t < j; t++) {
+            steps[t].d = d[t - i];
+            steps[t].flow_total = t == i ? total : 0;
+        }
+        i = j;
+    }
 }
 
 }  // namespace jc

@@ -39,6 +39,7 @@ struct Step {
     int map_a = -1;     // host copy of the A operand's tensor map (index)
     const void *w = nullptr;  // GEMM weights, for the single-GEMM kernels' own maps
     int layer = -1;     // encoder layer, or -1 before the encoder, -2 after it
+    uint32_t flow_total = 0;  // first step of a persistent launch: the launch's work items
 };
 
 class Engine {
@@ -85,6 +86,9 @@ class Engine {
     bool init(const float *raw, std::string *why);
     int add_map(const void *p, uint32_t rows, uint32_t cols, uint32_t box);
     const CUtensorMap *wmap(const void *p, uint32_t rows, uint32_t cols, int bn);
+    // Fills the persistent kernel's schedule of each launch the mode makes (the whole list, or
+    // each encoder layer's steps) and the launches' item counts.
+    void plan_steps(std::vector<Step> &steps, int mode) const;
     std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
                                   int mode) const;
     Step gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32_t m, uint32_t n,
@@ -102,7 +106,10 @@ class Engine {
            *xs = nullptr, *ys = nullptr;
     float *stats_a = nullptr, *stats_b = nullptr, *stats_s = nullptr;
     float *gemm_ws = nullptr, *attn_ws = nullptr;
-    uint32_t *gemm_cnt = nullptr, *attn_cnt = nullptr, *bar = nullptr;
+    uint32_t *gemm_cnt = nullptr, *attn_cnt = nullptr;
+    // the persistent kernel's completion / work counters (scratch_cap phases x flow_blocks + 3)
+    uint32_t *flow_ctr = nullptr;
+    uint32_t flow_blocks = 0;
     size_t gemm_ws_cap = 0, gemm_cnt_cap = 0, attn_ws_cap = 0, attn_cnt_cap = 0;
     // tensor maps: host copies and the device array the persistent kernel reads
     std::vector<CUtensorMap> hmaps;

@@ -153,21 +153,33 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
+// How a tile waits for its inputs (the activations, statistics and residuals a previous step
+// writes): gate.producer() is called by the TMA thread after it has requested the first stages'
+// weights and before it requests activations; gate.all() by every thread before the epilogue's
+// loads. The single-GEMM kernel waits on programmatic dependent launch.
+struct PdlGate {
+    __device__ void producer() const { pdl_wait(); }
+    __device__ void all() const {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+};
+
 // One 128 x BN output tile (split z of `splits`; `tile` numbers it for the split counters). Every
 // thread of the CTA calls it. `prefetched`: leading stages whose W half gemm_issue_w already
-// issued. `standalone`: the single-GEMM kernel (programmatic dependent launch waits here); in the
-// persistent kernel a grid barrier has already ordered the inputs.
+// issued. `gate`: how the tile waits for its inputs (PdlGate, or the persistent kernel's
+// dependency counters).
 //
 // CS > 1: the CTA is rank z of a cluster of CS CTAs that split K for the same tile. After their
 // MMAs the CTAs reduce-scatter the f32 partials through distributed shared memory: CTA c owns
 // columns [Go c, Go (c + 1)) of each 32-column half of every 64-column chunk (so RoPE pairs and
 // GeGLU input / gate pairs stay together), receives the other CTAs' partials of them into its own
 // (now idle) stage memory, sums them in rank order (deterministic) and runs the epilogue on them.
-template <int BN, int STAGES, uint32_t EPI, int CS = 1>
+template <int BN, int STAGES, uint32_t EPI, int CS = 1, class Gate = PdlGate>
 __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
                                           uint32_t tmem, GemmRun &run, uint32_t tile_n,
                                           uint32_t tile_m, uint32_t z, uint32_t splits,
-                                          uint32_t tile, uint32_t prefetched, bool standalone) {
+                                          uint32_t tile, uint32_t prefetched, const Gate &gate) {
     using S = GemmShape<BN, STAGES>;
     constexpr int CH = S::CH, NCH = S::NCH, HALF = CH / 2;
     constexpr int GT = CH / (4 * CS);  // columns per thread per half-chunk group
@@ -194,7 +206,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         // TMA producer: weights of the first stages first (they do not depend on the previous
         // kernel), then the activations.
         ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, prefetched < pre ? prefetched : pre, pre);
-        if (standalone) pdl_wait();
+        gate.producer();
         for (uint32_t i = 0; ok && i < pre; i++) gemm_issue_a<BN, STAGES>(p, sv, run.it, m0, kb0, i);
     }
 
@@ -204,10 +216,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
     const uint32_t r = m0 + row;
     const bool valid = r < p.m;
     const uint32_t pair0 = GO * rank + GT * half;  // first column of this thread's groups
-    if (standalone) {
-        pdl_launch_dependents();
-        pdl_wait();
-    }
+    gate.all();
 
     // Everything the epilogue reads from the previous step, requested by every thread (the MMA
     // issuers included) before the main loop so its latency hides under the MMAs.
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t tmem = gemm_setup<BN, STAGES>(sv);
     GemmRun run;
     gemm_tile<BN, STAGES, EPI, CS>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z,
-                                   blockIdx.y * gridDim.x + blockIdx.x, 0, true);
+                                   blockIdx.y * gridDim.x + blockIdx.x, 0, PdlGate{});
     gemm_zero(p, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
               gridDim.x * gridDim.y * gridDim.z);
     gemm_teardown<BN, STAGES>(tmem);

@@ -128,9 +128,17 @@ const char *device_error_name(unsigned int code);
 struct PhaseDesc;
 // Resident CTAs of the persistent kernel per SM (0 on error).
 int persist_blocks_per_sm();
-// bar: 3 zeroed u32 (arrivals, generation, abort flag) kept across launches; expected: the CTAs
-// each grid barrier waits for (normally grid); timeout_ns: how long a barrier may wait.
-bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t *bar, uint32_t grid,
-                    uint32_t expected, uint64_t timeout_ns, cudaStream_t s);
+// Fills the dataflow schedule of a launch's phases d[0, n) (rows, items, first item, dependencies
+// on the phases before it in the same launch; PhaseDesc::extra set to 0) and returns the launch's
+// item count. Its GEMM phases run 64-column tiles, so their n is a multiple of 64.
+uint32_t plan_flow(PhaseDesc *d, uint32_t n);
+// Counter words a launch of n_phases phases over `blocks` 128-row blocks needs (zeroed once; the
+// kernel leaves them zero).
+inline size_t flow_counter_words(uint32_t n_phases, uint32_t blocks) {
+    return (size_t)n_phases * blocks + 3;
+}
+// phases: device copies of plan_flow's output; timeout_ns: how long a dependency wait may last.
+bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
+                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s);
 
 }  // namespace jc

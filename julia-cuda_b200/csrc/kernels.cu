@@ -466,11 +466,50 @@ int persist_blocks_per_sm() {
     return per_sm;
 }
 
-bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t *bar, uint32_t grid,
-                    uint32_t expected, uint64_t timeout_ns, cudaStream_t s) {
+uint32_t plan_flow(PhaseDesc *d, uint32_t n) {
+    uint32_t first = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        PhaseDesc &p = d[i];
+        if (p.kind == PH_GEMM) {
+            p.rows = p.g.m;
+            p.items = (p.g.m + GEMM_BM - 1) / GEMM_BM * (p.g.n / PERSIST_BN);
+        } else if (p.kind == PH_ATTN) {
+            p.rows = p.a.n;
+            p.items = (p.a.n + FLOW_CHUNK - 1) / FLOW_CHUNK * p.a.heads;
+        } else {
+            p.rows = p.r.n;
+            p.items = (p.r.n + FLOW_ROWS - 1) / FLOW_ROWS;
+        }
+        p.first_item = first;
+        first += p.items;
+        p.extra = 0;
+        p.dep[0] = PhaseDep{DEP_NONE, 0, 0};
+        p.dep[1] = PhaseDep{DEP_NONE, 0, 0};
+        if (i > 0) {
+            // The previous phase's output is this phase's input: the same rows, except attention
+            // (keys within the window, or every key) and the marker gather (any row).
+            if (p.kind == PH_ATTN)
+                p.dep[0] = p.a.window ? PhaseDep{DEP_WINDOW, i - 1, p.a.window} : PhaseDep{DEP_ALL, i - 1, 0};
+            else
+                p.dep[0] = PhaseDep{p.kind == PH_GATHER ? DEP_ALL : DEP_ROWS, i - 1, 0};
+        }
+        // A GEMM that overwrites an attention phase's qkv input also waits for every task that
+        // may still read the rows it writes (write after read).
+        if (p.kind == PH_GEMM)
+            for (uint32_t j = i; j-- > 0;)
+                if (d[j].kind == PH_ATTN && d[j].a.qkv == p.g.c) {
+                    p.dep[1] = d[j].a.window ? PhaseDep{DEP_WINDOW, j, d[j].a.window} : PhaseDep{DEP_ALL, j, 0};
+                    break;
+                }
+    }
+    return first;
+}
+
+bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
+                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s) {
     static std::atomic<uint64_t> smem_set{0};
     if (!ensure_smem(persist_kernel, PERSIST_SMEM, smem_set)) return false;
-    PersistParams P{phases, n_phases, bar, expected, timeout_ns};
+    FlowParams P{phases, n_phases, total_items, blocks, ctr, timeout_ns};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(PERSIST_THREADS);

@@ -57,18 +57,46 @@ struct RowParams {
     float eps, b;
 };
 
+// How a phase's items wait for an earlier phase: DEP_ROWS, the earlier phase's row block(s) that
+// hold the item's own rows; DEP_WINDOW, those within `window` rows of them; DEP_ALL, every row
+// block of the earlier phase.
+enum : uint32_t { DEP_NONE = 0, DEP_ROWS = 1, DEP_WINDOW = 2, DEP_ALL = 3 };
+
+struct PhaseDep {
+    uint32_t kind;    // DEP_*
+    uint32_t phase;   // index (within the launch) of the phase waited for
+    uint32_t window;  // DEP_WINDOW: rows either side
+};
+
+// Rows are grouped in blocks of FLOW_BLOCK (the GEMM tile height): every finished item adds one to
+// its block's completion counter, and a waiting item compares that counter with the number of
+// items the block holds.
+constexpr uint32_t FLOW_BLOCK = 128;
+constexpr uint32_t FLOW_CHUNK = 32;  // query rows per attention item
+constexpr uint32_t FLOW_ROWS = 8;    // rows per item of the row-wise phases (one per warp)
+
 struct PhaseDesc {
     uint32_t kind, epi;
     GemmParams g;
     AttnParams a;
     RowParams r;
+    // dataflow schedule (filled by the host)
+    uint32_t rows;        // rows of this phase's output (the row space its counters cover)
+    uint32_t items;       // work items: GEMM tiles (row-block major), attention (query chunk,
+                          // head) pairs, or FLOW_ROWS-row chunks
+    uint32_t first_item;  // global index of its first item within the launch
+    uint32_t extra;       // added to every expected count of this phase (0; the timeout probe
+                          // uses it to make a wait that cannot end)
+    PhaseDep dep[2];
 };
 
-struct PersistParams {
+// The persistent kernel's launch: `ctr` holds n_phases x blocks completion counters followed by
+// the work counter, the exit counter and the abort flag; all are zero between launches (the last
+// CTA to leave clears them).
+struct FlowParams {
     const PhaseDesc *phases;
-    uint32_t n_phases;
-    uint32_t *bar;        // [0] arrivals, [1] generation, [2] abort flag
-    uint32_t expected;    // CTAs each grid barrier waits for (gridDim.x)
+    uint32_t n_phases, total_items, blocks;
+    uint32_t *ctr;
     uint64_t timeout_ns;
 };
 

@@ -1,20 +1,26 @@
 // The persistent kernel: one cooperative launch runs a list of phases (fused-epilogue GEMMs,
-// attention, and the row-wise edges: embedding, head input, marker gather, score), every CTA
-// striding over each phase's tasks, with a grid barrier between consecutive phases.
+// attention, and the row-wise edges: embedding, head input, marker gather, score) as a dataflow
+// graph of work items, with no grid-wide barrier.
 //
 // It replaces the reference's persistent `layer` kernel (kernels/src/main.rs:579-826, host
-// src/forward.rs:226-359): there, five phases of one encoder layer with the same tile code as the
-// per-step kernels. Here the phase list is data (a device array of descriptors), so the same
-// kernel runs one encoder layer per launch (the reference's layer-fused mode) or the whole model,
-// embed to logits, in a single launch. B200 specifics:
-//   - one CTA of 256 threads per SM holding the GEMM's TMEM accumulators and a 4-stage TMA ring
-//     (8 k-blocks deep) for the whole launch (barriers initialised and TMEM allocated once);
-//   - before each grid barrier the producer thread already requests the weight half of its first
-//     stages of the next GEMM phase (weights never depend on the barrier), so the phase starts
-//     with its weights on chip and only the activations left to fetch;
-//   - the grid barrier is a counter plus a generation word (no reset between launches, so a CUDA
-//     graph can replay it); every wait gives up after `timeout_ns`, records JC_DEV_TIMEOUT_GRID and
-//     raises an abort flag that makes every other CTA leave at its next barrier.
+// src/forward.rs:226-359), which runs five phases of one encoder layer separated by grid barriers.
+// Here the phase list is data (a device array of descriptors), so the same kernel runs one encoder
+// layer per launch (the reference's layer-fused mode) or the whole model, embed to logits, in a
+// single launch. B200 specifics:
+//   - one CTA of 256 threads per SM holds the GEMM's TMEM accumulators and a 4-stage TMA ring for
+//     the whole launch (barriers initialised and TMEM allocated once);
+//   - items (GEMM tiles, row-block major; (32-query chunk, head) attention tasks; 8-row chunks of
+//     the row-wise phases, one row per warp) are handed out in phase order by one atomic counter,
+//     a CTA taking its next item when it has finished the current one;
+//   - an item waits only for the rows it reads: each finished item adds one to its 128-row block's
+//     completion counter (a release reduction), and an item's TMA thread polls the counters of the
+//     blocks it depends on (acquire loads; same block, a window of blocks for sliding-window
+//     attention, every block for global attention and the marker gather). A GEMM tile requests its
+//     weights before it waits, so they stream in while the producing phase finishes;
+//   - items are taken in order and every CTA is resident, so the lowest unfinished item always has
+//     its inputs: no deadlock. Every wait gives up after `timeout_ns`, records JC_DEV_TIMEOUT_GRID
+//     and raises an abort flag that makes every other CTA leave;
+//   - the last CTA to leave clears every counter, so a CUDA graph can replay the launch.
 #pragma once
 #include "attention.cuh"
 #include "edges.cuh"
@@ -33,77 +39,130 @@ static_assert(PersistAttn::SMEM <= PersistGemm::STAGES * PersistGemm::STAGE_BYTE
               "attention tasks reuse the GEMM stages' shared memory");
 static_assert(PersistAttn::THREADS == PERSIST_THREADS && GEMM_THREADS == PERSIST_THREADS,
               "one CTA shape for every phase");
+static_assert(PersistAttn::QT == FLOW_CHUNK && FLOW_BLOCK == GEMM_BM && FLOW_BLOCK % FLOW_CHUNK == 0 &&
+                  FLOW_ROWS == PERSIST_THREADS / 32 && FLOW_BLOCK % FLOW_ROWS == 0,
+              "attention chunks, row chunks and GEMM row blocks tile the flow blocks");
+static_assert(sizeof(PhaseDesc) % 4 == 0, "descriptors are copied to shared memory as words");
 
-// Grid-wide barrier. Returns false if it (or another CTA's) timed out: the caller leaves.
-__device__ __forceinline__ bool grid_barrier(uint32_t *bar, uint32_t expected, uint64_t timeout_ns) {
-    __shared__ uint32_t ok_s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        volatile uint32_t *abort_flag = bar + 2;
-        uint32_t gen;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
-        __threadfence();
-        const uint32_t old = atomicAdd(bar, 1u);
-        bool ok = true;
-        if (old == expected - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar + 1) : "memory");
-        } else {
-            const uint64_t t0 = globaltimer();
-            while (true) {
-                uint32_t now;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(now) : "l"(bar + 1) : "memory");
-                if (now != gen) break;
-                if (*abort_flag) {
-                    ok = false;
-                    break;
-                }
-                if (globaltimer() - t0 > timeout_ns) {
-                    dev_fail(JC_DEV_TIMEOUT_GRID);
-                    *abort_flag = 1u;
-                    __threadfence();
-                    ok = false;
-                    break;
-                }
-                __nanosleep(64);
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Items of phase d that report to row block b (what a waiting item compares the counter with).
+__device__ __forceinline__ uint32_t block_items(const PhaseDesc &d, uint32_t b) {
+    const uint32_t r0 = b * FLOW_BLOCK;
+    if (r0 >= d.rows) return d.extra;
+    const uint32_t r1 = min(r0 + FLOW_BLOCK, d.rows);
+    uint32_t c;
+    if (d.kind == PH_GEMM)
+        c = d.g.n / PERSIST_BN;
+    else if (d.kind == PH_ATTN)
+        c = (r1 - r0 + FLOW_CHUNK - 1) / FLOW_CHUNK * d.a.heads;
+    else
+        c = (r1 - r0 + FLOW_ROWS - 1) / FLOW_ROWS;
+    return c + d.extra;
+}
+
+// TMA thread of an item covering rows [r0, r1): waits until the phase `dep` names has finished
+// every item those rows read. false if the wait timed out (or another CTA's did).
+__device__ __noinline__ bool wait_dep(const FlowParams &F, const PhaseDep &dep, uint32_t r0, uint32_t r1) {
+    if (dep.kind == DEP_NONE) return true;
+    const PhaseDesc &src = F.phases[dep.phase];
+    const uint32_t nb = (src.rows + FLOW_BLOCK - 1) / FLOW_BLOCK;
+    uint32_t b0 = 0, b1 = nb;
+    if (dep.kind != DEP_ALL) {
+        const uint32_t w = dep.kind == DEP_WINDOW ? dep.window : 0;
+        b0 = (r0 > w ? r0 - w : 0) / FLOW_BLOCK;
+        b1 = min((r1 + w + FLOW_BLOCK - 1) / FLOW_BLOCK, nb);
+    }
+    const uint32_t *ctr = F.ctr + dep.phase * F.blocks;
+    volatile uint32_t *abort_flag = F.ctr + F.n_phases * F.blocks + 2;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t b = b0; b < b1; b++) {
+        const uint32_t want = block_items(src, b);
+        while (ld_acquire_u32(ctr + b) < want) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > F.timeout_ns) {
+                dev_fail(JC_DEV_TIMEOUT_GRID);
+                *abort_flag = 1u;
+                __threadfence();
+                return false;
             }
         }
-        __threadfence();
-        ok_s = ok ? 1u : 0u;
     }
-    __syncthreads();
-    return ok_s != 0;
+    return true;
 }
 
-__device__ __forceinline__ uint32_t gemm_tiles(const GemmParams &g) {
-    return (g.m + GEMM_BM - 1) / GEMM_BM * (g.n / PERSIST_BN);
+// The TMA thread waits for both dependencies of an item; generic-proxy writes of other CTAs are
+// then ordered before this CTA's TMA reads.
+__device__ __forceinline__ bool wait_item(const FlowParams &F, const PhaseDesc &d, uint32_t r0, uint32_t r1) {
+    const bool ok = wait_dep(F, d.dep[0], r0, r1) && wait_dep(F, d.dep[1], r0, r1);
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return ok;
 }
 
+// gemm_tile's gate in the persistent kernel: the TMA thread waits for the tile's row block; the
+// other threads wait for it at a CTA barrier.
+struct FlowGate {
+    const FlowParams *F;
+    const PhaseDesc *d;
+    uint32_t r0, r1;
+    uint32_t *ok_s;
+    __device__ void producer() const { *ok_s = wait_item(*F, *d, r0, r1) ? 1u : 0u; }
+    __device__ void all() const { __syncthreads(); }
+};
+
+// One GEMM tile of the current phase. Everything the tile code reads repeatedly is a local value
+// here (parameters copied out of shared memory, the shared-memory view rebuilt from its base, the
+// pipeline position passed in and returned), so it stays in registers across the tile's fences.
 template <uint32_t EPI>
-__device__ __forceinline__ void persist_gemm(const GemmParams &g, const GemmSmemView<PERSIST_BN, PERSIST_STAGES> &sv,
-                                             uint32_t tmem, GemmRun &run, uint32_t prefetched) {
-    const uint32_t tiles_n = g.n / PERSIST_BN, tiles = gemm_tiles(g);
-    for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x)
-        gemm_tile<PERSIST_BN, PERSIST_STAGES, EPI>(g, sv, tmem, run, t % tiles_n, t / tiles_n, 0, 1,
-                                                   t, t == blockIdx.x ? prefetched : 0, false);
+__device__ __noinline__ uint2 flow_gemm_tile(const FlowParams *F, const PhaseDesc *d, uint8_t *base,
+                                             uint32_t tmem, uint2 pos, uint32_t tm, uint32_t tn,
+                                             uint32_t *ok_s) {
+    const GemmParams g = d->g;
+    const GemmSmemView<PERSIST_BN, PERSIST_STAGES> sv(base);
+    GemmRun run;
+    run.it = pos.x;
+    run.tiles = pos.y;
+    const FlowGate gate{F, d, tm * GEMM_BM, min((tm + 1) * GEMM_BM, d->rows), ok_s};
+    gemm_tile<PERSIST_BN, PERSIST_STAGES, EPI>(g, sv, tmem, run, tn, tm, 0, 1, 0, 0, gate);
+    return make_uint2(run.it, run.tiles);
 }
 
-__device__ __forceinline__ void persist_gemm_dispatch(uint32_t epi, const GemmParams &g,
-                                                      const GemmSmemView<PERSIST_BN, PERSIST_STAGES> &sv,
-                                                      uint32_t tmem, GemmRun &run, uint32_t pf) {
+__device__ __forceinline__ uint2 flow_gemm(const FlowParams *F, const PhaseDesc *d, uint8_t *base,
+                                           uint32_t tmem, uint2 pos, uint32_t tm, uint32_t tn,
+                                           uint32_t *ok_s) {
     constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
-    switch (epi) {
-        case JC_EPI_ROPE: persist_gemm<JC_EPI_ROPE>(g, sv, tmem, run, pf); break;
-        case JC_EPI_LN | JC_EPI_ROPE: persist_gemm<JC_EPI_LN | JC_EPI_ROPE>(g, sv, tmem, run, pf); break;
-        case JC_EPI_LN | JC_EPI_GEGLU: persist_gemm<JC_EPI_LN | JC_EPI_GEGLU>(g, sv, tmem, run, pf); break;
-        case RS: persist_gemm<RS>(g, sv, tmem, run, pf); break;
-        case JC_EPI_BIAS | RS: persist_gemm<JC_EPI_BIAS | RS>(g, sv, tmem, run, pf); break;
-        case LB: persist_gemm<LB>(g, sv, tmem, run, pf); break;
-        case LB | JC_EPI_RELU: persist_gemm<LB | JC_EPI_RELU>(g, sv, tmem, run, pf); break;
-        case LB | JC_EPI_GELU: persist_gemm<LB | JC_EPI_GELU>(g, sv, tmem, run, pf); break;
-        default: dev_fail(JC_DEV_BAD_INDEX); break;
+    switch (d->epi) {
+        case JC_EPI_ROPE: return flow_gemm_tile<JC_EPI_ROPE>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case JC_EPI_LN | JC_EPI_ROPE: return flow_gemm_tile<JC_EPI_LN | JC_EPI_ROPE>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case JC_EPI_LN | JC_EPI_GEGLU: return flow_gemm_tile<JC_EPI_LN | JC_EPI_GEGLU>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case RS: return flow_gemm_tile<RS>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case JC_EPI_BIAS | RS: return flow_gemm_tile<JC_EPI_BIAS | RS>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB: return flow_gemm_tile<LB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB | JC_EPI_RELU: return flow_gemm_tile<LB | JC_EPI_RELU>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB | JC_EPI_GELU: return flow_gemm_tile<LB | JC_EPI_GELU>(F, d, base, tmem, pos, tm, tn, ok_s);
+        default:
+            // Unknown epilogue (the host never builds one): record it and leave the tile undone.
+            if (threadIdx.x == 0) {
+                dev_fail(JC_DEV_BAD_INDEX);
+                *ok_s = 0u;
+            }
+            __syncthreads();
+            return pos;
     }
+}
+
+// One attention task of the current phase, its parameters as local values.
+__device__ __noinline__ void flow_attention(const PhaseDesc *d, uint8_t *base, uint32_t chunk, uint32_t head) {
+    const AttnParams a = d->a;
+    attention_task<2, 4>(a, base, chunk, head, 0, 1, false);
 }
 
 // ---- row-wise phases: one warp per row, striding over every warp of the grid ----
@@ -162,106 +221,128 @@ __device__ __forceinline__ void ln_row(const __half *src, uint32_t d, const floa
     }
 }
 
-__device__ __forceinline__ void persist_rows(uint32_t kind, const RowParams &r) {
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
-    for (uint32_t i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < r.n; i += warps) {
-        if (kind == PH_EMBED) {
-            ln_row(r.x + (size_t)r.rows[i] * r.d, r.d, r.gamma, nullptr, r.eps,
-                   r.out + (size_t)i * r.d, r.stats ? r.stats + 2 * i : nullptr, lane);
-        } else if (kind == PH_NORM_ADD) {
-            ln_row(r.x + (size_t)i * r.d, r.d, r.gamma, r.add, r.eps, r.out + (size_t)i * r.d,
-                   r.stats + 2 * i, lane);
-        } else if (kind == PH_GATHER) {
-            const uint32_t src = r.rows[i];
-            const uint4 *s4 = reinterpret_cast<const uint4 *>(r.x + (size_t)src * r.d);
-            uint4 *d4 = reinterpret_cast<uint4 *>(r.out + (size_t)i * r.d);
-            for (uint32_t j = lane; j < r.d / 8; j += 32) d4[j] = s4[j];
-            if (lane == 0) {
-                r.stats[2 * i] = r.stats_in[2 * src];
-                r.stats[2 * i + 1] = r.stats_in[2 * src + 1];
-            }
-        } else if (kind == PH_COPY) {
-            const uint4 *s4 = reinterpret_cast<const uint4 *>(r.x + (size_t)i * r.d);
-            uint4 *d4 = reinterpret_cast<uint4 *>(r.out + (size_t)i * r.d);
-            for (uint32_t j = lane; j < r.d / 8; j += 32) d4[j] = s4[j];
-        } else {  // PH_SCORE
-            const uint32_t *row = reinterpret_cast<const uint32_t *>(r.x + (size_t)r.rows[i] * r.d);
-            const uint32_t *wr = reinterpret_cast<const uint32_t *>(r.w);
-            float acc = 0.f;
-            for (uint32_t j = lane; j < r.d / 2; j += 32) {
-                const float2 a = unpack_half2(row[j]), c = unpack_half2(__ldg(wr + j));
-                acc = fmaf(a.x, c.x, acc);
-                acc = fmaf(a.y, c.y, acc);
-            }
-            acc = warp_sum(acc);
-            if (lane == 0) r.logits[i] = acc + r.b;
+// Row i of a row-wise phase, by one warp.
+__device__ __noinline__ void row_op(uint32_t kind, const RowParams &r, uint32_t i, uint32_t lane) {
+    if (kind == PH_EMBED) {
+        ln_row(r.x + (size_t)r.rows[i] * r.d, r.d, r.gamma, nullptr, r.eps,
+               r.out + (size_t)i * r.d, r.stats ? r.stats + 2 * i : nullptr, lane);
+    } else if (kind == PH_NORM_ADD) {
+        ln_row(r.x + (size_t)i * r.d, r.d, r.gamma, r.add, r.eps, r.out + (size_t)i * r.d,
+               r.stats + 2 * i, lane);
+    } else if (kind == PH_GATHER) {
+        const uint32_t src = r.rows[i];
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(r.x + (size_t)src * r.d);
+        uint4 *d4 = reinterpret_cast<uint4 *>(r.out + (size_t)i * r.d);
+        for (uint32_t j = lane; j < r.d / 8; j += 32) d4[j] = s4[j];
+        if (lane == 0) {
+            r.stats[2 * i] = r.stats_in[2 * src];
+            r.stats[2 * i + 1] = r.stats_in[2 * src + 1];
         }
+    } else if (kind == PH_COPY) {
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(r.x + (size_t)i * r.d);
+        uint4 *d4 = reinterpret_cast<uint4 *>(r.out + (size_t)i * r.d);
+        for (uint32_t j = lane; j < r.d / 8; j += 32) d4[j] = s4[j];
+    } else {  // PH_SCORE
+        const uint32_t *row = reinterpret_cast<const uint32_t *>(r.x + (size_t)r.rows[i] * r.d);
+        const uint32_t *wr = reinterpret_cast<const uint32_t *>(r.w);
+        float acc = 0.f;
+        for (uint32_t j = lane; j < r.d / 2; j += 32) {
+            const float2 a = unpack_half2(row[j]), c = unpack_half2(__ldg(wr + j));
+            acc = fmaf(a.x, c.x, acc);
+            acc = fmaf(a.y, c.y, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) r.logits[i] = acc + r.b;
     }
 }
 
-__global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const PersistParams P) {
+__global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __grid_constant__ FlowParams F) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
-    const GemmSmemView<PERSIST_BN, PERSIST_STAGES> sv(base);
-    const uint32_t tmem = gemm_setup<PERSIST_BN, PERSIST_STAGES>(sv);
-    GemmRun run;
+    __shared__ uint32_t item_s[2], ok_s;
+    // The current item's descriptor: read from shared memory, not global memory (the item's code
+    // reads its parameters many times, across fences that would force global reloads).
+    __shared__ __align__(16) PhaseDesc desc_s;
+    const uint32_t tmem = gemm_setup<PERSIST_BN, PERSIST_STAGES>(GemmSmemView<PERSIST_BN, PERSIST_STAGES>(base));
+    uint2 pos = make_uint2(0, 0);  // the GEMM pipeline's position (GemmRun) across tiles
     pdl_wait();
     pdl_launch_dependents();
-    uint32_t prefetched = 0;
-    for (uint32_t ph = 0; ph < P.n_phases; ph++) {
-        const PhaseDesc &d = P.phases[ph];
-        const uint32_t kind = d.kind;
-        if (kind == PH_GEMM) {
-            persist_gemm_dispatch(d.epi, d.g, sv, tmem, run, prefetched);
-            gemm_zero(d.g, blockIdx.x, gridDim.x);
-        } else if (kind == PH_ATTN) {
-            const uint32_t qtiles = (d.a.n + PersistAttn::QT - 1) / PersistAttn::QT;
-            const uint32_t tasks = qtiles * d.a.heads;
-            for (uint32_t t = blockIdx.x; t < tasks; t += gridDim.x)
-                attention_task<2, 4>(d.a, base, t / d.a.heads, t % d.a.heads, 0, 1, false);
-        } else {
-            persist_rows(kind, d.r);
-        }
-        prefetched = 0;
-        if (ph + 1 == P.n_phases) break;
-        // Hand the shared memory from the generic proxy (attention, row phases) to TMA.
-        fence_proxy_async();
+    uint32_t *work = F.ctr + F.n_phases * F.blocks;  // then the exit counter, the abort flag
+    uint32_t next = 0;
+    if (threadIdx.x == 0) next = atomicAdd(work, 1u);
+    uint32_t ph = 0, desc_ph = 0;
+    for (uint32_t iter = 0;; iter++) {
+        if (threadIdx.x == 0) item_s[iter & 1] = next;
         __syncthreads();
-        const PhaseDesc &nx = P.phases[ph + 1];
-        if (nx.kind == PH_GEMM && blockIdx.x < gemm_tiles(nx.g)) {
-            const uint32_t nst = gemm_stages(nx.g.k / GEMM_BK);
-            prefetched = nst < (uint32_t)PERSIST_STAGES ? nst : (uint32_t)PERSIST_STAGES;
-            if (threadIdx.x == 0) {
-                tma_prefetch_desc(nx.g.map_a);
-                tma_prefetch_desc(nx.g.map_w);
-                const uint32_t tiles_n = nx.g.n / PERSIST_BN;
-                gemm_issue_w<PERSIST_BN, PERSIST_STAGES>(nx.g, sv, run.it,
-                                                         (blockIdx.x % tiles_n) * PERSIST_BN, 0, 0,
-                                                         prefetched);
+        const uint32_t item = item_s[iter & 1];
+        if (item >= F.total_items) break;
+        while (item >= F.phases[ph].first_item + F.phases[ph].items) ph++;
+        if (iter == 0 || ph != desc_ph) {
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(F.phases + ph);
+            uint32_t *dst = reinterpret_cast<uint32_t *>(&desc_s);
+            for (uint32_t i = threadIdx.x; i < sizeof(PhaseDesc) / 4; i += PERSIST_THREADS) dst[i] = src[i];
+            desc_ph = ph;
+            if (threadIdx.x == 0 && F.phases[ph].kind == PH_GEMM) {
+                tma_prefetch_desc(F.phases[ph].g.map_a);
+                tma_prefetch_desc(F.phases[ph].g.map_w);
             }
+            __syncthreads();
         }
-        if (!grid_barrier(P.bar, P.expected, P.timeout_ns)) {
-            // Leaving early: complete the stages whose weights are already in flight (their A
-            // halves too, so the stage barriers can finish) and wait for them, within limits.
-            if (threadIdx.x == 0 && prefetched) {
-                const uint32_t tiles_n = nx.g.n / PERSIST_BN;
-                const uint32_t m0 = (blockIdx.x / tiles_n) * GEMM_BM;
-                for (uint32_t i = 0; i < prefetched; i++)
-                    gemm_issue_a<PERSIST_BN, PERSIST_STAGES>(nx.g, sv, run.it, m0, 0, i);
-                for (uint32_t i = 0; i < prefetched; i++) {
-                    const uint32_t g = run.it + i;
-                    mbar_wait(&sv.full[g % PERSIST_STAGES], (g / PERSIST_STAGES) & 1,
-                              JC_DEV_TIMEOUT_FULL);
+        const PhaseDesc &d = desc_s;
+        const uint32_t local = item - d.first_item;
+        uint32_t block;
+        if (d.kind == PH_GEMM) {
+            const uint32_t tiles_n = d.g.n / PERSIST_BN;
+            const uint32_t tm = local / tiles_n, tn = local % tiles_n;
+            block = tm;
+            pos = flow_gemm(&F, &desc_s, base, tmem, pos, tm, tn, &ok_s);
+            // The first tile of a row block clears that block's rows of the statistics buffer a
+            // later GEMM adds into (its readers are done: they precede this tile's inputs).
+            if (tn == 0 && d.g.zero)
+                for (uint32_t i = tm * 2 * GEMM_BM + threadIdx.x; i < min((tm + 1) * 2 * GEMM_BM, d.g.zero_len);
+                     i += PERSIST_THREADS)
+                    d.g.zero[i] = 0.0f;
+        } else {
+            const uint32_t rows = d.kind == PH_ATTN ? FLOW_CHUNK : FLOW_ROWS;
+            const uint32_t chunk = d.kind == PH_ATTN ? local / d.a.heads : local;
+            block = chunk * rows / FLOW_BLOCK;
+            const uint32_t r0 = chunk * rows, r1 = min(r0 + rows, d.rows);
+            if (threadIdx.x == 0) ok_s = wait_item(F, d, r0, r1) ? 1u : 0u;
+            __syncthreads();
+            if (ok_s) {
+                if (d.kind == PH_ATTN) {
+                    flow_attention(&desc_s, base, chunk, local % d.a.heads);
+                } else {
+                    const uint32_t lane = threadIdx.x & 31;
+                    for (uint32_t i = r0 + (threadIdx.x >> 5); i < r1; i += PERSIST_THREADS / 32)
+                        row_op(d.kind, d.r, i, lane);
                 }
+                // Hand the shared memory from the generic proxy back to TMA.
+                fence_proxy_async();
             }
-            break;
         }
-        // Activations written by other CTAs before the barrier are read by TMA after it.
-        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncthreads();
+        if (!ok_s) break;
+        // Report the item, then take the next one (taken only now: an item held by a busy CTA
+        // could not start on an idle one).
+        if (threadIdx.x == 0) {
+            red_release_add(F.ctr + ph * F.blocks + block, 1u);
+            next = atomicAdd(work, 1u);
+        }
     }
     gemm_teardown<PERSIST_BN, PERSIST_STAGES>(tmem);
+    // The last CTA to leave clears every counter for the next launch.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t old = atomicAdd(work + 1, 1u);
+        ok_s = old == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (ok_s) {
+        __threadfence();
+        for (uint32_t i = threadIdx.x; i < F.n_phases * F.blocks + 3; i += PERSIST_THREADS) F.ctr[i] = 0u;
+    }
 }
 
 }  // namespace jc
