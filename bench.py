@@ -13,7 +13,8 @@ embed -> logits. With --gpus N (torchrun), every rank runs its own engine on its
   e2e        the same metric through julia_cuda_run (the reference's C ABI) from host arrays:
              host -> pinned -> device copies of the ids and markers and the device -> host copy of
              the logits are inside the timed region (host wall clock).
-  roofline   the kernel with the largest share of a forward pass, timed alone with CUDA events.
+  roofline   the kernel with the largest share of a forward pass, timed alone (its launches in a CUDA
+             graph, each after an L2 flush, less the flushes' own time) with CUDA events.
   cpu_baseline  the oracle's f32 forward (C, OpenMP over the host's cores) on a bounded sample.
 
 --impl reference: the reference's own CPU path cannot be built here (Rust / julia-rs absent), so
@@ -89,7 +90,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -126,6 +127,13 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
+# The compiled kernel (epilogue instantiation) each timed shape runs.
+KERNEL_OF = {"qkv": "gemm LN+RoPE", "wo": "gemm residual+stats", "wo_mlp": "gemm residual+stats",
+             "wi": "gemm LN+GeGLU", "head_in": "gemm LN+bias", "head_l1": "gemm LN+bias+ReLU",
+             "head_l2": "gemm bias+residual+stats", "attn_global": "attention",
+             "attn_window": "attention"}
+
+
 def gemm_shapes(cfg, n):
     """The forward pass's GEMMs: name, epilogue, n_out-cols, k, launches per forward."""
     D, I, F, S, L, HL = (cfg.d_model, cfg.inter, cfg.head_ff, cfg.scorer_hidden, cfg.n_layers,
@@ -137,9 +145,9 @@ def gemm_shapes(cfg, n):
 
 
 def time_kernels(jc, torch, cfg, flush, reps=30):
-    """Each GEMM shape and attention of the forward pass alone, CUDA events on the launching
-    stream, L2 flushed before every launch. Returns {name: (avg ms, launches per forward,
-    algorithmic bytes, flops)}."""
+    """Each GEMM shape and attention of the forward pass alone (timed(): its launches in a CUDA
+    graph on the launching stream, L2 flushed before every launch). Returns {name: (avg ms,
+    launches per forward, algorithmic bytes, flops)}."""
     from oracle import oracle as O
     n = SEQ
     out = {}
@@ -160,7 +168,7 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
 
         def launch():
             jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st, colsum=cs,
-                    stats_out=so, rope=rope, bias=bias, ws=ws, counters=cnt, stream=stream)
+                    stats_out=so, rope=rope, bias=bias, ws=ws, counters=cnt)
         ms = timed(torch, stream, flush, launch, reps)
         bytes_ = 2 * (n * K + N * K + n * n_out) + (2 * n * N if epi & jc.EPI_RES else 0) + \
             (8 * n + 4 * N if epi & jc.EPI_LN else 0) + (4 * N if epi & jc.EPI_BIAS else 0) + \
@@ -170,10 +178,13 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
     qkv = torch.randn(n, 3 * heads * 64, device="cuda").half()
     o = torch.zeros(n, heads * 64, device="cuda").half()
     n_global = len([l for l in range(cfg.n_layers) if l % cfg.global_every == 0])
+    aws = torch.empty(max(jc.lib().jc_attention_ws_floats(n, heads, 16), 1), device="cuda")
+    acnt = torch.zeros(max(jc.lib().jc_attention_counters(n, heads), 1), dtype=torch.int32,
+                       device="cuda")
     for name, window, count in [("attn_global", 0, n_global + cfg.n_head_layers),
                                 ("attn_window", cfg.window, cfg.n_layers - n_global)]:
         ms = timed(torch, stream, flush,
-                   lambda: jc.attention(qkv, o, heads, window, stream=stream), reps)
+                   lambda: jc.attention(qkv, o, heads, window, ws=aws, counters=acnt), reps)
         keys = n if window == 0 else sum(min(i + window, n - 1) - max(i - window, 0) + 1
                                          for i in range(n)) / n
         out[name] = (ms, count, 2 * (n * 3 * heads * 64 + n * heads * 64),
@@ -182,21 +193,41 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
 
 
 def timed(torch, stream, flush, launch, reps):
-    """Average device time of `launch` (ms): CUDA events on the launching stream around each
-    launch, L2 flushed before each, every launch queued before the host waits (so host-side
-    launch latency never shows up as device time)."""
-    for _ in range(3):
-        launch()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(reps)]
+    """Device time (ms) one launch adds to a stream with a cold L2, as inside the forward pass's
+    CUDA graph: a graph of `reps` (L2 flush, launch) pairs and a graph of `reps` flushes alone are
+    each replayed between CUDA events on their stream, and the difference is divided by reps (so
+    host launch latency, which a graph does not have, never shows up as device time)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(stream)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        with_k, flush_only = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(with_k, stream=s):
+            for _ in range(reps):
+                flush.zero_()
+                launch()
+        with torch.cuda.graph(flush_only, stream=s):
+            for _ in range(reps):
+                flush.zero_()
+
+        def run(g):
+            g.replay()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                g.replay()
+                e1.record(s)
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            return statistics.median(ts)
+        ms = (run(with_k) - run(flush_only)) / reps
+        del with_k, flush_only
     torch.cuda.synchronize()
-    for e0, e1 in ev:
-        flush.zero_()
-        e0.record(stream)
-        launch()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    return ms
 
 
 def reference_arm(args, rank, world):
@@ -240,7 +271,7 @@ METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -330,16 +361,29 @@ def main():
     if rank == 0:
         pk, src = peaks()
         kt = time_kernels(jc, torch, cfg, flush)
-        dom = max(kt, key=lambda k: kt[k][0] * kt[k][1])
-        ms, count, bytes_, flops = kt[dom]
+        # The dominant kernel is a compiled kernel (one epilogue instantiation), whose launches in
+        # a forward pass may have several shapes: per-launch averages over them.
+        groups = {}
+        for k, (ms_k, count_k, bytes_k, flops_k) in kt.items():
+            g = groups.setdefault(KERNEL_OF.get(k, k), [[], 0, 0.0, 0.0, 0.0])
+            g[0].append(k)
+            g[1] += count_k
+            g[2] += ms_k * count_k
+            g[3] += bytes_k * count_k
+            g[4] += flops_k * count_k
+        dom = max(groups, key=lambda g: groups[g][2])
+        names, count, tot_ms, tot_bytes, tot_flops = groups[dom]
+        ms, bytes_, flops = tot_ms / count, tot_bytes / count, tot_flops / count
         achieved = bytes_ / (ms * 1e-3) / 1e9
         traffic = None
         try:
             with open(TRAFFIC) as f:
-                traffic = json.load(f).get(dom)
+                tr = json.load(f)
+            if all(n in tr for n in names):
+                traffic = sum(tr[n] * kt[n][1] for n in names) / count
         except Exception:
             pass
-        roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved,
+        roofline = {"kernel": dom, "shapes": names, "bound": "hbm", "achieved": achieved,
                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                     "traffic": traffic, "peak_source": src,
                     "tflops": flops / (ms * 1e-3) / 1e12, "us_per_launch": ms * 1e3,

@@ -254,12 +254,15 @@ def gemm(epi: int, a, w, c, *, res=None, stats_in=None, colsum=None, stats_out=N
     _check(rc, "jc_gemm")
 
 
-def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=None) -> None:
+def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=None, ws=None,
+              counters=None) -> None:
+    """o = softmax(q k^T / 8) v per head (jc_attention). ws / counters: split-KV scratch sized for
+    16 key ranges (allocated here when not given)."""
     import torch
     n = qkv.shape[0]
     chunks = kv_chunks
-    ws = cnt = None
-    if kv_chunks != 1:
+    cnt = counters
+    if kv_chunks != 1 and (ws is None or cnt is None):
         probe = 16 if kv_chunks == 0 else kv_chunks
         ws = torch.empty(max(lib().jc_attention_ws_floats(n, heads, probe), 1), dtype=torch.float32,
                          device=qkv.device)
