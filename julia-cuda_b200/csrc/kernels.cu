@@ -304,14 +304,21 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     GemmConfig c;
     const uint32_t tiles_m = (m + GEMM_BM - 1) / GEMM_BM;
-    c.bn = (n % 128 == 0 && tiles_m * (n / 128) >= (uint32_t)sms) ? 128 : 64;
-    if (n % c.bn) c.bn = 32;
-    const uint32_t ctas = tiles_m * (n / c.bn);
-    // Split-K measured slower than one CTA per tile for every encoder shape at 72-1024 tokens
-    // (the partial round trip costs more than the shorter K loop saves), so it stays at 1.
+    // The narrowest tile whose grid still fits one CTA per SM: a CTA's time is its operand stream
+    // ((128 + tile width) x k), so narrower tiles are faster until the grid no longer fits in one
+    // wave (measured: 32 columns for the 768-wide GEMMs at 72-293 tokens, 64 at 1024; 64 for the
+    // 2304-wide ones up to 293 tokens, 128 at 1024).
+    c.bn = 0;
+    for (int bn : {32, 64, 128})
+        if (n % bn == 0 && tiles_m * (n / bn) <= (uint32_t)sms) {
+            c.bn = bn;
+            break;
+        }
+    if (c.bn == 0) c.bn = n % 128 == 0 ? 128 : (n % 64 == 0 ? 64 : 32);
+    // Split-K (workspace or cluster) measured slower than one CTA per tile for every encoder
+    // shape at 72-1024 tokens (the partial exchange costs more than the shorter K loop saves).
     c.splits = 1;
     (void)k;
-    (void)ctas;
     set_gemm_depth(c, m, n, sms);
     return c;
 }
