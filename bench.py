@@ -277,22 +277,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layer-fused", action="store_true")
     args = ap.parse_args()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    replicas = importlib.import_module("julia-cuda_b200.replicas")
+    rank, world, local = replicas.rank_env()
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return
 
     import torch
-    import torch.distributed as dist
     if args.warmup < 3:
         args.warmup = 3
     torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    replicas.init(world, "nccl", device=torch.device("cuda", local))
     jc = importlib.import_module("julia-cuda_b200")
     cfg = jc.default_config(max_positions=1024)
     eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
@@ -306,8 +301,7 @@ def main():
 
     def barrier():
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        replicas.barrier(world)
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
@@ -328,11 +322,8 @@ def main():
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_s = sum(step_ms) / 1e3
     assert jc.device_error() == 0
-    if world > 1:
-        t = torch.tensor([total_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_s = float(t.item())
-    value = world * args.steps / total_s
+    total_s = replicas.max_over_ranks(total_s, world, device="cuda")
+    value = replicas.job_rate(args.steps, total_s, world)
     ms_per_step = total_s * 1e3 / args.steps
 
     # e2e through julia_cuda_run: host arrays in, logits out, copies inside the timed region.
@@ -350,11 +341,8 @@ def main():
         gpu_ms.append(float(ms[0]))
     barrier()
     e2e_total = sum(e2e_times)
-    if world > 1:
-        t = torch.tensor([e2e_total], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_total = float(t.item())
-    e2e_value = world * args.steps / e2e_total
+    e2e_total = replicas.max_over_ranks(e2e_total, world, device="cuda")
+    e2e_value = replicas.job_rate(args.steps, e2e_total, world)
 
     roofline = kernels = None
     cpu = None
@@ -419,8 +407,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     eng.close()
-    if world > 1:
-        dist.destroy_process_group()
+    replicas.finalize(world)
 
 
 if __name__ == "__main__":
