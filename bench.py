@@ -62,6 +62,7 @@ def request(rank, vocab):
 def cpu_forward_sample(budget_s=20.0, max_runs=5):
     """The oracle's f32 forward at config 0 on all host threads; returns (s/request, runs, cores)."""
     from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     c = O.config(max_positions=1024)
     raw = O.init_random(c, SEED)
     ids, markers = request(0, c.vocab)
@@ -236,6 +237,7 @@ def reference_arm(args, rank, world):
         return
     per, runs, cores = None, 0, None
     from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     c = O.config(max_positions=1024)
     raw = O.init_random(c, SEED)
     ids, markers = request(0, c.vocab)

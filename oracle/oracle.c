@@ -48,6 +48,14 @@ int or_num_threads(void) {
 #endif
 }
 
+void or_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* layout and random init */
 

@@ -139,6 +139,9 @@ void or_f16_round_array(const float *src, uint16_t *dst, size_t n);
 float or_gelu(float x);
 
 int or_num_threads(void);
+/* Threads the oracle's parallel loops use from now on (OpenMP; launchers such as torchrun set
+ * OMP_NUM_THREADS=1 for every rank). */
+void or_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -88,6 +88,8 @@ def lib():
         L.or_gelu.argtypes = [f32]
         L.or_gelu.restype = f32
         L.or_num_threads.restype = i32
+        L.or_set_num_threads.argtypes = [i32]
+        L.or_set_num_threads.restype = None
         _lib = L
     return _lib
 
@@ -252,3 +254,7 @@ def gelu(x: float) -> float:
 
 def num_threads() -> int:
     return lib().or_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    lib().or_set_num_threads(n)
