@@ -162,7 +162,7 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
         st = torch.rand(2 * n, device="cuda") + 1.0
         st[1::2] += 800.0
         cs = torch.randn(N, device="cuda")
-        rope = torch.from_numpy(O.rope_table(160000.0, n)).cuda()
+        rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
         bias = torch.randn(N, device="cuda")
         so = torch.zeros(2 * n, device="cuda")
         ws, cnt = jc.gemm_scratch(n, N, K)

@@ -147,7 +147,7 @@ int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_
  * calls). splits = -2 or -4 splits K across a thread-block cluster of that many CTAs instead, which
  * reduce their partials through distributed shared memory (64- or 128-column tiles; no workspace,
  * ws / counters unused; same result bits as that many workspace splits). stats_in / stats_out:
- * [m][2] f32 (sum, sum of squares). rope: [>= m][32][2] (cos, sin).
+ * [m][2] f32 (sum, sum of squares). rope: 16 x m float4 (cos, sin of two pairs; jc_prep_rope_gemm).
  * zero / zero_len: a float buffer to clear on the way. Replaces src/gemm.rs:254-392. */
 int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t *w, uint16_t *c,
             const uint16_t *res, float *ws, uint32_t *counters, const float *stats_in,
@@ -210,6 +210,10 @@ void jc_prep_interleave_geglu_f16(const uint16_t *w, uint32_t n, uint32_t k, uin
 void jc_prep_interleave_geglu_f32(const float *w, uint32_t n, uint32_t k, float *out);
 /* RoPE (cos, sin) table [n][32][2] in f32. */
 void jc_prep_rope_table(float theta, uint32_t n, float *out);
+/* The layout jc_gemm's rope argument takes, from a [>= m][32][2] table: float4 out[16][m] with
+ * out[g][r] = (cos, sin) of pairs 2g and 2g + 1 of row r (pair-group major, so the rows a warp
+ * handles are contiguous). The reference keeps its table row-major (src/prep.rs:88-118). */
+void jc_prep_rope_gemm(const float *table, uint32_t m, float *out);
 
 #ifdef __cplusplus
 }

@@ -116,6 +116,7 @@ def lib():
         "jc_prep_interleave_geglu_f16": ([P, u32, u32, P], None),
         "jc_prep_interleave_geglu_f32": ([P, u32, u32, P], None),
         "jc_prep_rope_table": ([f32, u32, P], None),
+        "jc_prep_rope_gemm": ([P, u32, P], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -225,6 +226,15 @@ def prep_rope_table(theta: float, n: int) -> np.ndarray:
     t = np.zeros((n, 32, 2), np.float32)
     lib().jc_prep_rope_table(theta, n, _np_ptr(t))
     return t
+
+
+def prep_rope_gemm(table: np.ndarray, m: int) -> np.ndarray:
+    """jc_gemm's RoPE argument (float4 [16][m]) from a [>= m][32][2] (cos, sin) table."""
+    t = np.ascontiguousarray(table, np.float32)
+    assert t.shape[0] >= m and t.shape[1:] == (32, 2)
+    out = np.zeros((16, m, 4), np.float32)
+    lib().jc_prep_rope_gemm(_np_ptr(t), m, _np_ptr(out))
+    return out
 
 
 # ------------------------------------------------------------------------------------------------

@@ -536,4 +536,8 @@ void jc_prep_interleave_geglu_f32(const float *w, uint32_t n, uint32_t k, float 
 
 void jc_prep_rope_table(float theta, uint32_t n, float *out) { jc::rope_table(theta, n, out); }
 
+void jc_prep_rope_gemm(const float *table, uint32_t m, float *out) {
+    jc::rope_table_gemm(table, m, m, out);
+}
+
 }  // extern "C"

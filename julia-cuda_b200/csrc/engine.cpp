@@ -92,6 +92,19 @@ bool Engine::init(const float *raw, std::string *why) {
     if (!cu(cudaMemcpy(w16, hw.f16.data(), hw.f16.size() * 2, cudaMemcpyHostToDevice), "upload") ||
         !cu(cudaMemcpy(w32, hw.f32.data(), hw.f32.size() * 4, cudaMemcpyHostToDevice), "upload"))
         return false;
+    {
+        // The GEMM epilogue's RoPE tables (global then local theta), pair-group major with one
+        // float4 per (pair group, position), from the arena's [positions][32][2] tables.
+        const PreparedLayout &P = hw.layout;
+        rope_rows = (uint32_t)max_length;
+        std::vector<float> t((size_t)2 * 16 * rope_rows * 4);
+        rope_table_gemm(hw.f32.data() + P.rope_global.off, rope_rows, rope_rows, t.data());
+        rope_table_gemm(hw.f32.data() + P.rope_local.off, rope_rows, rope_rows,
+                        t.data() + (size_t)16 * rope_rows * 4);
+        if (!dalloc((void **)&rope_t, t.size() * 4) ||
+            !cu(cudaMemcpy(rope_t, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "upload"))
+            return false;
+    }
     hw.f16.clear();
     hw.f16.shrink_to_fit();
     hw.f32.clear();
@@ -211,6 +224,7 @@ Step Engine::gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32
     g.stats_out = stats_out;
     g.zero = zero;
     g.rope = rope;
+    g.rope_stride = rope_rows;
     g.bias = bias;
     g.zero_len = zero_len;
     g.m = m;
@@ -256,7 +270,7 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
     for (int l = 0; l < cfg.n_layers; l++) {
         const LayerSpans &ls = P.layers[l];
         const LayerMaps &lm = lmaps[l];
-        const float *rope = w32 + (ls.global ? P.rope_global.off : P.rope_local.off);
+        const float *rope = rope_t + (ls.global ? 0 : (size_t)16 * rope_rows * 4);
         // qkv: LayerNorm folded (from layer 1) + RoPE; clears stats_a for wo.
         steps.push_back(gemm_step(ls.has_ln ? (JC_EPI_LN | JC_EPI_ROPE) : JC_EPI_ROPE, m_x, lm.wqkv,
                                   w16 + ls.wqkv.off, n, 3 * D, D, qkv, nullptr, stats_b,
@@ -383,6 +397,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             g.k = p.k;
             g.eps = p.eps;
             g.rope = p.rope;
+            g.rope_stride = p.rope_stride;
             g.bias = p.bias;
             return launch_gemm(g, c, s, true);
         }

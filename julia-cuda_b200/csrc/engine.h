@@ -102,6 +102,9 @@ class Engine {
     HostWeights hw;  // layout only after upload (arenas freed)
     uint16_t *w16 = nullptr;
     float *w32 = nullptr;
+    // RoPE tables in the GEMM epilogue's layout (global, then local), rope_rows positions each
+    float *rope_t = nullptr;
+    uint32_t rope_rows = 0;
     __half *x = nullptr, *qkv = nullptr, *o = nullptr, *mb = nullptr, *hx = nullptr,
            *xs = nullptr, *ys = nullptr;
     float *stats_a = nullptr, *stats_b = nullptr, *stats_s = nullptr;

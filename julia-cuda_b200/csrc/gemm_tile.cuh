@@ -241,9 +241,11 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
     float4 ropev[ROPE_V];
     if constexpr ((EPI & JC_EPI_ROPE) != 0) {
         if (valid) {
-            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope + (size_t)r * 64 + 2 * pair0);
+            // Pair-group-major table: consecutive rows (the lanes of a warp) are consecutive
+            // float4s, so each load instruction reads one contiguous 512-byte run.
+            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + (size_t)(pair0 / 2) * p.rope_stride + r;
 #pragma unroll
-            for (int i = 0; i < GT / 2; i++) ropev[i] = __ldg(t4 + i);
+            for (int i = 0; i < GT / 2; i++) ropev[i] = __ldg(t4 + (size_t)i * p.rope_stride);
         }
     }
 

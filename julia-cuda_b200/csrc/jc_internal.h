@@ -62,6 +62,7 @@ struct GemmArgs {
     float eps = 0.f;
     const float *rope = nullptr;
     const float *bias = nullptr;
+    uint32_t rope_stride = 0;  // rows of the pair-group-major RoPE table; 0: m
 };
 
 struct GemmConfig {

@@ -251,6 +251,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.zero = g.zero;
     p.rope = g.rope;
     p.bias = g.bias;
+    p.rope_stride = g.rope_stride ? g.rope_stride : g.m;
     p.zero_len = g.zero_len;
     p.m = g.m;
     p.n = g.n;

@@ -220,6 +220,13 @@ void rope_table(float theta, uint32_t n, float *out) {
         }
 }
 
+void rope_table_gemm(const float *table, uint32_t rows, uint32_t stride, float *out) {
+    for (uint32_t g = 0; g < 16; g++)
+        for (uint32_t r = 0; r < stride; r++)
+            for (uint32_t e = 0; e < 4; e++)
+                out[((size_t)g * stride + r) * 4 + e] = r < rows ? table[(size_t)r * 64 + 4 * g + e] : 0.f;
+}
+
 namespace {
 struct Arena16 {
     std::vector<uint16_t> data;

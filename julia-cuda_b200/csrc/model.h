@@ -42,6 +42,9 @@ void fold_layernorm_bias(const float *w, const float *gamma, const float *beta, 
 template <typename T>
 void interleave_geglu(const T *w, uint32_t n, uint32_t k, T *out);
 void rope_table(float theta, uint32_t n, float *out);
+// The GEMM epilogue's layout of a RoPE table: float4 out[16][stride] with out[g][r] = (cos, sin) of
+// pairs 2g and 2g + 1 of row r, from the natural [rows][32][2] table (rows <= stride).
+void rope_table_gemm(const float *table, uint32_t rows, uint32_t stride, float *out);
 
 // The prepared weights: f16 matrices in one arena and f32 vectors in another, every span
 // 128-byte aligned (the reference's two-arena layout, src/weights.rs:19-140).

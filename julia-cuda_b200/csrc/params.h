@@ -20,8 +20,9 @@ struct GemmParams {
     const float *colsum;
     float *stats_out;
     float *zero;
-    const float *rope;
+    const float *rope;      // float4 [16][rope_stride]: (cos, sin) of pairs 2g, 2g + 1 of row r
     const float *bias;
+    uint32_t rope_stride;   // rows of the RoPE table (>= m)
     uint32_t zero_len, m, n, k;
     float eps;
 };

@@ -92,6 +92,13 @@ def test_prep_interleave_geglu_layout(jc):
     assert np.array_equal(jc.prep_interleave_geglu(w)[:, 0], (rows * 3).astype(np.uint16))
 
 
+def test_prep_rope_gemm_layout(jc, O):
+    """jc_gemm's RoPE argument: float4 [16][m], entry (g, r) = (cos, sin) of pairs 2g, 2g + 1."""
+    t = O.rope_table(10000.0, 50)
+    g = jc.prep_rope_gemm(t, 37)
+    assert np.array_equal(g, t[:37].reshape(37, 16, 4).transpose(1, 0, 2))
+
+
 def test_choose_gemm_fills_the_b200(jc):
     bn, sp = ctypes.c_int(), ctypes.c_int()
     for (m, n, k) in [(293, 2304, 768), (293, 768, 768), (293, 768, 1152), (1024, 2304, 768),

@@ -81,7 +81,8 @@ def run_gemm_case(jc, O, name, m, n, k, bn=0, splits=0, seed=0):
     zero = torch.ones(2 * m + 5, dtype=torch.float32, device="cuda")
     jc.gemm(epi, cuda_u16(a), cuda_u16(w_dev), c, res=c if epi & jc.EPI_RES else None,
             stats_in=cuda_f32(stats_in), colsum=cuda_f32(cs_dev), stats_out=stats_out, zero=zero,
-            eps=1e-5, rope=cuda_f32(rope), bias=cuda_f32(bias), bn=bn, splits=splits)
+            eps=1e-5, rope=cuda_f32(jc.prep_rope_gemm(rope, m)), bias=cuda_f32(bias), bn=bn,
+            splits=splits)
     torch.cuda.synchronize()
     assert jc.device_error() == 0
     got = host_u16(c)
