@@ -268,6 +268,50 @@ def reference_arm(args, rank, world):
 
 
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
+SERVING_METRIC = "requests/s (config 3 serving: log-normal lengths around 293 tokens, 4 markers)"
+
+
+def serving_arm(args, rank, world, local, replicas):
+    """Config 3: a seeded set of requests (log-normal lengths, mean 293, clipped to [32, 1024])
+    partitioned over the ranks by longest processing time, each rank serving its share through
+    julia_cuda_run (batches of up to 16, host arrays in and out) on its own GPU. Throughput =
+    all requests / the slowest rank's wall time."""
+    import torch
+    torch.cuda.set_device(local)
+    replicas.init(world, "nccl", device=torch.device("cuda", local))
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
+    reqs = replicas.serving_requests(args.requests, SEED, cfg.vocab)
+    mine = [reqs[i] for i in replicas.shard_lpt([len(r[0]) for r in reqs], world)[rank]]
+    # Warm-up: one request of every length this rank will see, so each shape's CUDA graph is
+    # captured before the timed pass (a long-running server keeps them).
+    seen = {}
+    for r in mine:
+        seen.setdefault(len(r[0]), r)
+    warm = list(seen.values())
+    for i in range(0, len(warm), 16):
+        eng.run(warm[i:i + 16])
+    replicas.barrier(world)
+    t0 = time.perf_counter()
+    gpu_ms = 0.0
+    for i in range(0, len(mine), 16):
+        _, ms = eng.run(mine[i:i + 16])
+        gpu_ms += float(np.sum(ms))
+    wall = time.perf_counter() - t0
+    slowest = replicas.max_over_ranks(wall, world, device="cuda")
+    if rank == 0:
+        tokens = sum(len(r[0]) for r in reqs)
+        print(json.dumps({
+            "metric": SERVING_METRIC, "value": args.requests / slowest, "unit": "requests/s",
+            "n_gpus": world, "requests": args.requests, "tokens": tokens,
+            "wall_s": slowest, "gpu_ms_rank0": gpu_ms, "higher_is_better": True,
+            "scaling": "strong", "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
+            "config": {"workload": "config3: log-normal lengths (sigma 0.5, mean 293, [32, 1024]), "
+                                   "4 markers, qtype 0, seed 1234", "partition": "LPT by cost",
+                       "path": "julia_cuda_run, per-step kernels, batches of 16"}}), flush=True)
+    eng.close()
+    replicas.finalize(world)
 
 
 def main():
@@ -278,11 +322,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layer-fused", action="store_true")
+    ap.add_argument("--serving", action="store_true",
+                    help="config 3 instead of the headline: a seeded request set served end to end")
+    ap.add_argument("--requests", type=int, default=4096)
     args = ap.parse_args()
     replicas = importlib.import_module("julia-cuda_b200.replicas")
     rank, world, local = replicas.rank_env()
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.serving:
+        serving_arm(args, rank, world, local, replicas)
         return
 
     import torch

@@ -6,7 +6,7 @@
 
 namespace jc {
 
-static constexpr int GRAPH_CACHE = 64;
+static constexpr int GRAPH_CACHE = 1024;  // every request length up to 1024 tokens
 
 Engine *Engine::create(const jc_model_config &cfg, const float *raw, size_t max_length,
                        int device, std::string *why) {
@@ -557,11 +557,11 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
             if (graphs[old].descs) cudaFree(graphs[old].descs);
             graphs.erase(old);
         }
+        graph_lru.push_front(key);
+        entry.lru = graph_lru.begin();
         it = graphs.emplace(key, entry).first;
-        graph_lru.push_front(key);
     } else {
-        graph_lru.remove(key);
-        graph_lru.push_front(key);
+        graph_lru.splice(graph_lru.begin(), graph_lru, it->second.lru);
     }
     return cuda_ok(cudaGraphLaunch(it->second.exec, s), "graph launch");
 }

@@ -81,6 +81,7 @@ class Engine {
     struct GraphEntry {
         cudaGraphExec_t exec = nullptr;
         void *descs = nullptr;
+        std::list<GraphKey>::iterator lru;  // this key's place in graph_lru
     };
     Engine() = default;
     bool init(const float *raw, std::string *why);

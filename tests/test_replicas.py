@@ -98,3 +98,17 @@ def test_reference_arm_runs_on_rank_zero_only(capsys):
         steps, warmup = 1, 0
     bench.reference_arm(Args, 1, 2)
     assert capsys.readouterr().out == ""
+
+
+def test_lpt_partition_balances_request_costs():
+    rep = importlib.import_module("julia-cuda_b200.replicas")
+    import random
+    rng = random.Random(0)
+    lengths = [max(32, min(1024, int(rng.lognormvariate(5.55, 0.5)))) for _ in range(500)]
+    for world in (1, 2, 4, 8):
+        parts = rep.shard_lpt(lengths, world)
+        assert sorted(i for p in parts for i in p) == list(range(len(lengths)))
+        loads = [sum(rep.request_cost(lengths[i]) for i in p) for p in parts]
+        # LPT: no rank exceeds the mean by more than the largest single request
+        assert max(loads) - sum(loads) / world <= max(rep.request_cost(n) for n in lengths)
+    assert rep.shard_lpt([10, 300, 20], 2) == [[1], [0, 2]]
