@@ -19,6 +19,13 @@ embed -> logits. With --gpus N (torchrun), every rank runs its own engine on its
 
 --impl reference: the reference's own CPU path cannot be built here (Rust / julia-rs absent), so
 the reference arm times the oracle's f32 restatement of it on all host cores.
+
+Other BASELINE configs (extra lines, not the headline):
+  --sweep                               configs 1-2: each GEMM epilogue at M in {72, 293, 448, 1024}
+                                        and attention at {128, 512, 1024} tokens, alone
+  --serving [--requests 4096]           config 3: a seeded log-normal request set through
+                                        julia_cuda_run, LPT-partitioned over the ranks
+  --seq 1024 --head-length 512 --mode 2 config 4: the whole model in one cooperative launch
 """
 import argparse
 import importlib
@@ -52,26 +59,30 @@ def peaks():
         return FALLBACK_PEAKS, "fallback"
 
 
-def request(rank, vocab):
+def request(rank, vocab, n=SEQ, head=0):
+    """A seeded request of n tokens; its markers lie in the head's rows (the first `head` rows
+    when the head is limited, else anywhere)."""
     rng = np.random.default_rng(1000 + rank)
-    ids = rng.integers(0, vocab, SEQ).astype(np.uint32)
-    markers = np.sort(rng.choice(SEQ, MARKERS, replace=False)).astype(np.uint32)
+    ids = rng.integers(0, vocab, n).astype(np.uint32)
+    span = head if 0 < head < n else n
+    markers = np.sort(rng.choice(span, MARKERS, replace=False)).astype(np.uint32)
     return ids, markers
 
 
-def cpu_forward_sample(budget_s=20.0, max_runs=5):
-    """The oracle's f32 forward at config 0 on all host threads; returns (s/request, runs, cores)."""
+def cpu_forward_sample(budget_s=20.0, max_runs=5, n=SEQ, head=0):
+    """The oracle's f32 forward (config 0, or n tokens with the head on `head` rows) on all host
+    threads; returns (s/request, runs, cores)."""
     from oracle import oracle as O
     O.set_num_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     c = O.config(max_positions=1024)
     raw = O.init_random(c, SEED)
-    ids, markers = request(0, c.vocab)
+    ids, markers = request(0, c.vocab, n, head)
     O.forward_f32(c, raw, ids[:32], markers[:1] % 32, 0)  # warm the thread pool
     times = []
     t_all = time.perf_counter()
     while len(times) < max_runs and (time.perf_counter() - t_all) < budget_s:
         t0 = time.perf_counter()
-        O.forward_f32(c, raw, ids, markers, 0)
+        O.forward_f32(c, raw, ids, markers, 0, head_rows=head)
         times.append(time.perf_counter() - t0)
     return statistics.mean(times), len(times), O.num_threads()
 
@@ -145,15 +156,18 @@ def gemm_shapes(cfg, n):
             ("head_l2", "biasresstats", D, F, HL)]
 
 
-def time_kernels(jc, torch, cfg, flush, reps=30):
-    """Each GEMM shape and attention of the forward pass alone (timed(): its launches in a CUDA
-    graph on the launching stream, L2 flushed before every launch). Returns {name: (avg ms,
-    launches per forward, algorithmic bytes, flops)}."""
+def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=True):
+    """Each GEMM shape and attention of the forward pass alone at n tokens (timed(): its launches
+    in a CUDA graph on the launching stream, L2 flushed before every launch); `gemms` limits the
+    GEMM shapes by name. Returns {name: (avg ms, launches per forward, algorithmic bytes,
+    flops)}."""
     from oracle import oracle as O
-    n = SEQ
     out = {}
     stream = torch.cuda.current_stream()
+    torch.manual_seed(n)
     for name, epi_name, N, K, count in gemm_shapes(cfg, n):
+        if gemms is not None and name not in gemms:
+            continue
         epi = jc.EPILOGUES[epi_name]
         a = torch.randn(n, K, device="cuda").half()
         w = (torch.randn(N, K, device="cuda") * 0.02).half()
@@ -175,6 +189,8 @@ def time_kernels(jc, torch, cfg, flush, reps=30):
             (8 * n + 4 * N if epi & jc.EPI_LN else 0) + (4 * N if epi & jc.EPI_BIAS else 0) + \
             (256 * n if epi & jc.EPI_ROPE else 0) + (8 * n if epi & jc.EPI_STATS else 0)
         out[name] = (ms, count, bytes_, 2.0 * n * N * K)
+    if not attention:
+        return out
     heads = cfg.n_heads
     qkv = torch.randn(n, 3 * heads * 64, device="cuda").half()
     o = torch.zeros(n, heads * 64, device="cuda").half()
@@ -229,6 +245,37 @@ def timed(torch, stream, flush, launch, reps):
         del with_k, flush_only
     torch.cuda.synchronize()
     return ms
+
+
+def sweep_arm(args, rank, local):
+    """BASELINE configs 1 and 2, each kernel alone with a cold L2 (timed()): the four encoder
+    GEMMs with their fused epilogues at M in {72, 293, 448, 1024} tokens, and attention (12 heads
+    x d64, global with split-KV and the +-64 window) at {128, 512, 1024} tokens. One JSON line
+    per case: device time, algorithmic GB/s and TFLOP/s, and their fractions of the measured
+    HBM copy bandwidth and burst dense-f16/bf16 tensor throughput."""
+    if rank != 0:
+        return
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    pk, src = peaks()
+    rows = []
+    for n in (72, 293, 448, 1024):
+        rows += [("config1", n, k, v) for k, v in time_kernels(
+            jc, torch, cfg, flush, n=n, gemms=("qkv", "wo", "wi", "wo_mlp"),
+            attention=False).items()]
+    for n in (128, 512, 1024):
+        rows += [("config2", n, k, v) for k, v in time_kernels(
+            jc, torch, cfg, flush, n=n, gemms=()).items()]
+    assert jc.device_error() == 0
+    for conf, n, name, (ms, _, bytes_, flops) in rows:
+        gbs, tfs = bytes_ / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / 1e12
+        print(json.dumps({"sweep": conf, "kernel": name, "tokens": n, "us": ms * 1e3,
+                          "gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "tflops": tfs,
+                          "tensor_frac": tfs / pk["bf16_tflops"], "peak_source": src,
+                          "l2": "flushed before every launch"}), flush=True)
 
 
 def reference_arm(args, rank, world):
@@ -321,10 +368,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layer-fused", action="store_true")
+    ap.add_argument("--layer-fused", action="store_true", help="same as --mode 1")
+    ap.add_argument("--mode", type=int, default=0, choices=[0, 1, 2],
+                    help="0 per-step kernels, 1 persistent kernel per layer, 2 whole model")
+    ap.add_argument("--seq", type=int, default=SEQ, help="tokens per request (config 4: 1024)")
+    ap.add_argument("--head-length", type=int, default=0,
+                    help="head on the first rows only (config 4: 512); 0 = every row")
     ap.add_argument("--serving", action="store_true",
                     help="config 3 instead of the headline: a seeded request set served end to end")
     ap.add_argument("--requests", type=int, default=4096)
+    ap.add_argument("--sweep", action="store_true",
+                    help="configs 1-2 instead of the headline: each GEMM and attention alone")
     args = ap.parse_args()
     replicas = importlib.import_module("julia-cuda_b200.replicas")
     rank, world, local = replicas.rank_env()
@@ -333,6 +387,9 @@ def main():
         return
     if args.serving:
         serving_arm(args, rank, world, local, replicas)
+        return
+    if args.sweep:
+        sweep_arm(args, rank, local)
         return
 
     import torch
@@ -343,13 +400,16 @@ def main():
     jc = importlib.import_module("julia-cuda_b200")
     cfg = jc.default_config(max_positions=1024)
     eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
-    ids, markers = request(rank, cfg.vocab)
-    ids_d = torch.from_numpy(ids.view(np.int32)).cuda()
-    mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
     logits = torch.zeros(MARKERS, dtype=torch.float32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
-    fused = args.layer_fused
+    fused = 1 if args.layer_fused else args.mode
+    n_tok = args.seq
+    if args.head_length:
+        eng.set_head_length(args.head_length)
+    ids, markers = request(rank, cfg.vocab, n_tok, args.head_length)
+    ids_d = torch.from_numpy(ids.view(np.int32)).cuda()
+    mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
 
     def barrier():
         torch.cuda.synchronize()
@@ -400,7 +460,7 @@ def main():
     cpu = None
     if rank == 0:
         pk, src = peaks()
-        kt = time_kernels(jc, torch, cfg, flush)
+        kt = time_kernels(jc, torch, cfg, flush, n=n_tok)
         # The dominant kernel is a compiled kernel (one epilogue instantiation), whose launches in
         # a forward pass may have several shapes: per-launch averages over them.
         groups = {}
@@ -419,7 +479,7 @@ def main():
         try:
             with open(TRAFFIC) as f:
                 tr = json.load(f)
-            if all(n in tr for n in names):
+            if n_tok == SEQ and all(n in tr for n in names):
                 traffic = sum(tr[n] * kt[n][1] for n in names) / count
         except Exception:
             pass
@@ -432,26 +492,38 @@ def main():
                        "gbs": v[2] / (v[0] * 1e-3) / 1e9, "tflops": v[3] / (v[0] * 1e-3) / 1e12}
                    for k, v in kt.items()}
         if world == 1 and not args.no_cpu_baseline:
-            per, runs, cores = cpu_forward_sample()
+            per, runs, cores = cpu_forward_sample(n=n_tok, head=args.head_length)
             cpu = {"value": 1.0 / per, "unit": "requests/s", "cores": cores, "kind": "port",
-                   "sample": f"{runs} full 293-token requests, f32 restatement of the reference's "
-                             f"CPU path (julia-rs), OpenMP"}
-    launches = eng.launches_per_forward(SEQ, MARKERS, fused) * args.steps
+                   "sample": f"{runs} full {n_tok}-token requests, f32 restatement of the "
+                             f"reference's CPU path (julia-rs), OpenMP"}
+    launches = eng.launches_per_forward(n_tok, MARKERS, fused) * args.steps
+    paths = {0: "per-step kernels, CUDA graph + PDL", 1: "persistent kernel per encoder layer",
+             2: "whole-model persistent kernel (one cooperative launch)"}
+    if n_tok == SEQ and not args.head_length:
+        metric = METRIC
+        workload = ("config0: 293-token request, 4 markers, batch 1 per engine; hidden 768, "
+                    "12 heads, 22 layers, 2 head layers, scorer 384")
+    else:
+        metric = (f"requests/s (embed->logits, {n_tok}-token requests, head on "
+                  f"{args.head_length or n_tok} rows, batch 1 per engine)")
+        workload = (f"{'config4: ' if n_tok == 1024 and args.head_length == 512 else ''}"
+                    f"{n_tok}-token request, head on rows [0, {args.head_length or n_tok}), "
+                    f"4 markers inside them, batch 1 per engine; hidden 768, 12 heads, 22 layers")
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "requests/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": "requests/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "us_per_request": ms_per_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
-            "config": {"workload": "config0: 293-token request, 4 markers, batch 1 per engine; "
-                                   "hidden 768, 12 heads, 22 layers, 2 head layers, scorer 384",
-                       "global_batch": world, "seq_len": SEQ, "parallelism": f"replicas x{world}",
+            "config": {"workload": workload, "global_batch": world, "seq_len": n_tok,
+                       "head_rows": args.head_length or n_tok,
+                       "parallelism": f"replicas x{world}",
                        "l2": "flushed (256 MiB write) before every timed step",
-                       "path": "persistent layer kernel" if fused else "per-step kernels, CUDA graph + PDL"},
+                       "path": paths[fused]},
             "e2e": {"value": e2e_value, "unit": "requests/s",
                     "us_per_request": e2e_total / args.steps * 1e6,
                     "gpu_ms_per_request": statistics.mean(gpu_ms),
-                    "h2d_bytes_per_step": SEQ * 4 + MARKERS * 4,
+                    "h2d_bytes_per_step": n_tok * 4 + MARKERS * 4,
                     "d2h_bytes_per_step": MARKERS * 4},
             "gpu_launches": launches,
             "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,

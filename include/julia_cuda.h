@@ -119,6 +119,16 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
 int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint32_t *code,
                                      char *err, size_t err_len);
 
+/* Limits the head to the first `rows` rows of every later request (0: all rows, the default
+ * and the reference's GPU behaviour, src/forward.rs:432-436): the final LayerNorm, the head
+ * layers (their attention over those rows only) and the marker gather run on rows
+ * [0, min(n, rows)), the encoder on all n. Markers must lie inside: julia_cuda_run rejects
+ * others, and on the device path a marker outside records device error 6 (JC_DEV_BAD_INDEX,
+ * read by jc_device_error; julia_cuda_run reports it) and is not read. Stands in for
+ * julia-rs's head_length (passed to `sequence`, src/engine.rs:165), whose semantics are not in
+ * the reference. Returns 0, or -1 for a NULL engine. */
+int julia_cuda_set_head_length(JcEngine *engine, size_t rows);
+
 /* How many kernels one forward pass launches (for launch accounting). */
 int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,
                                     int layer_fused);

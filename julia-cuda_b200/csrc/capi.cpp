@@ -212,6 +212,12 @@ int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_
     return 0;
 }
 
+int julia_cuda_set_head_length(JcEngine *engine, size_t rows) {
+    if (!engine) return -1;
+    engine->e->head_length = rows;
+    return 0;
+}
+
 int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,
                                     int layer_fused) {
     if (!engine) return -1;
@@ -308,9 +314,11 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                                              std::to_string(ids[at_id + j]) + " is past the vocabulary");
                     return -1;
                 }
+            const size_t head = e->head_rows((uint32_t)lens[i]);
             for (size_t j = 0; j < n_markers[i]; j++)
-                if (markers[at_mk + j] >= lens[i]) {
-                    report(err, err_len, "sequence " + std::to_string(i) + ": a marker is past the sequence");
+                if (markers[at_mk + j] >= head) {
+                    report(err, err_len, "sequence " + std::to_string(i) + ": a marker is past the " +
+                                             (head < lens[i] ? "head's rows" : "sequence"));
                     return -1;
                 }
             at_id += lens[i];

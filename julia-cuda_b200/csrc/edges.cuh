@@ -115,13 +115,18 @@ __global__ void __launch_bounds__(128) norm_add_kernel(const __half *x, uint32_t
 // out[i] = x[rows[i]] and its two statistics (one warp per gathered row).
 __global__ void __launch_bounds__(128) gather_rows_kernel(const __half *x, const float *stats,
                                                           uint32_t d, const uint32_t *rows,
-                                                          uint32_t k, __half *out,
-                                                          float *out_stats) {
+                                                          uint32_t k, uint32_t limit,
+                                                          __half *out, float *out_stats) {
     const uint32_t i = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     pdl_wait();
     pdl_launch_dependents();
     if (i >= k) return;
     const uint32_t r = rows[i];
+    if (r >= limit) {
+        // A marker past the rows the head computed: recorded, and the row is left unread.
+        if (lane == 0) dev_fail(JC_DEV_BAD_INDEX);
+        return;
+    }
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)r * d);
     uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)i * d);
     for (uint32_t j = lane; j < d / 8; j += 32) dst[j] = src[j];

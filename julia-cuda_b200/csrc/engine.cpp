@@ -248,10 +248,10 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
         st.layer = layer;
         return st;
     };
-    auto attn_step = [&](uint32_t window, int layer) {
+    auto attn_step = [&](uint32_t rows, uint32_t window, int layer) {
         Step st;
         st.d.kind = PH_ATTN;
-        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, n, (uint32_t)cfg.n_heads, window};
+        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, rows, (uint32_t)cfg.n_heads, window};
         st.layer = layer;
         return st;
     };
@@ -276,7 +276,7 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
                                   w16 + ls.wqkv.off, n, 3 * D, D, qkv, nullptr, stats_b,
                                   ls.has_ln ? w32 + ls.qkv_colsum.off : nullptr, nullptr, stats_a,
                                   2 * n, rope, nullptr, cfg.norm_eps, l));
-        steps.push_back(attn_step(ls.global ? 0 : (uint32_t)cfg.window, l));
+        steps.push_back(attn_step(n, ls.global ? 0 : (uint32_t)cfg.window, l));
         // wo: x += o . Wo^T, row statistics into stats_a.
         steps.push_back(gemm_step(JC_EPI_RES | JC_EPI_STATS, m_o, lm.wo, w16 + ls.wo.off, n, D, D,
                                   x, x, nullptr, nullptr, stats_a, nullptr, 0, nullptr, nullptr,
@@ -298,7 +298,9 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
             steps.push_back(st);
         }
     }
-    // Head input: final LayerNorm + type embedding, statistics into stats_a.
+    // Head input: final LayerNorm + type embedding, statistics into stats_a. The head runs on
+    // the first nh rows (all of them unless a head length is set).
+    const uint32_t nh = head_rows(n);
     {
         Step st = row_step(PH_NORM_ADD, -2);
         RowParams &r = st.d.r;
@@ -307,7 +309,7 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
         r.add = w32 + P.type_emb.off + (size_t)qtype * D;
         r.out = hx;
         r.stats = stats_a;
-        r.n = n;
+        r.n = nh;
         r.d = D;
         r.eps = cfg.norm_eps;
         steps.push_back(st);
@@ -316,18 +318,18 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
     for (size_t l = 0; l < P.head.size(); l++) {
         const HeadSpans &h = P.head[l];
         const HeadMaps &hm = hmaps_head[l];
-        steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS, m_hx, hm.in, w16 + h.in_w.off, n, 3 * D, D,
+        steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS, m_hx, hm.in, w16 + h.in_w.off, nh, 3 * D, D,
                                   qkv, nullptr, stats_a, w32 + h.in_colsum.off, nullptr, stats_b,
-                                  2 * n, nullptr, w32 + h.in_b.off, heps, -2));
-        steps.push_back(attn_step(0, -2));
+                                  2 * nh, nullptr, w32 + h.in_b.off, heps, -2));
+        steps.push_back(attn_step(nh, 0, -2));
         steps.push_back(gemm_step(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, m_o, hm.out,
-                                  w16 + h.out_w.off, n, D, D, hx, hx, nullptr, nullptr, stats_b,
+                                  w16 + h.out_w.off, nh, D, D, hx, hx, nullptr, nullptr, stats_b,
                                   nullptr, 0, nullptr, w32 + h.out_b.off, 0.f, -2));
         steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_RELU, m_hx, hm.l1, w16 + h.l1_w.off,
-                                  n, F, D, mb, nullptr, stats_b, w32 + h.l1_colsum.off, nullptr,
-                                  stats_a, 2 * n, nullptr, w32 + h.l1_b.off, heps, -2));
+                                  nh, F, D, mb, nullptr, stats_b, w32 + h.l1_colsum.off, nullptr,
+                                  stats_a, 2 * nh, nullptr, w32 + h.l1_b.off, heps, -2));
         steps.push_back(gemm_step(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, m_f, hm.l2,
-                                  w16 + h.l2_w.off, n, D, F, hx, hx, nullptr, nullptr, stats_a,
+                                  w16 + h.l2_w.off, nh, D, F, hx, hx, nullptr, nullptr, stats_a,
                                   nullptr, 0, nullptr, w32 + h.l2_b.off, 0.f, -2));
     }
     if (k == 0) return steps;
@@ -342,6 +344,7 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
         r.stats = stats_s;
         r.n = k;
         r.d = D;
+        r.limit = nh;
         steps.push_back(st);
     }
     steps.push_back(gemm_step(JC_EPI_LN | JC_EPI_BIAS | JC_EPI_GELU, m_xs, m_s1,
@@ -421,8 +424,8 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             return launch_norm_add(d.r.x, d.r.n, d.r.d, d.r.gamma, d.r.add, d.r.eps, d.r.out,
                                    d.r.stats, s, true);
         case PH_GATHER:
-            return launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n, d.r.out,
-                                      d.r.stats, s, true);
+            return launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n, d.r.limit,
+                                      d.r.out, d.r.stats, s, true);
         case PH_SCORE:
             return launch_score(d.r.x, d.r.d, d.r.w, d.r.b, d.r.rows, d.r.n, d.r.logits, s, true);
         case PH_COPY:
@@ -508,7 +511,7 @@ int Engine::launches_per_forward(uint32_t n, uint32_t k, int mode) const {
 }
 
 bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s) {
-    GraphKey key{n, k, qtype, mode};
+    GraphKey key{n, k, qtype, mode, head_rows(n)};
     auto it = graphs.find(key);
     if (it == graphs.end()) {
         if (n == 0 || n > max_length || k > max_length || qtype >= (uint32_t)cfg.n_qtypes ||

@@ -26,11 +26,12 @@ enum : int { MODE_STEPS = 0, MODE_LAYER = 1, MODE_MODEL = 2 };
 struct GraphKey {
     uint32_t n, k, qtype;
     int mode;
+    uint32_t head;  // rows the head runs on
     bool operator==(const GraphKey &o) const {
-        return n == o.n && k == o.k && qtype == o.qtype && mode == o.mode;
+        return n == o.n && k == o.k && qtype == o.qtype && mode == o.mode && head == o.head;
     }
     bool operator<(const GraphKey &o) const {
-        return std::tie(n, k, qtype, mode) < std::tie(o.n, o.k, o.qtype, o.mode);
+        return std::tie(n, k, qtype, mode, head) < std::tie(o.n, o.k, o.qtype, o.mode, o.head);
     }
 };
 
@@ -67,6 +68,12 @@ class Engine {
     std::string name;
     cudaStream_t stream = nullptr;
     uint64_t barrier_timeout_ns = 2000000000ull;
+    // The head (final LayerNorm, head layers, marker gather) runs on rows [0, head_length) of a
+    // longer sequence; 0 = every row (the reference's GPU head). Markers must lie inside.
+    size_t head_length = 0;
+    uint32_t head_rows(uint32_t n) const {
+        return head_length && head_length < n ? (uint32_t)head_length : n;
+    }
 
     // inputs / outputs of one request (device)
     uint32_t *ids = nullptr, *markers = nullptr, *iota = nullptr;

@@ -116,8 +116,10 @@ bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma
 bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,
                   uint32_t k, float *logits, cudaStream_t s, bool pdl);
 // Gathers the marker rows of x and their statistics (for the scorer, which only needs those).
+// A marker >= limit records JC_DEV_BAD_INDEX and is not read.
 bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
-                        uint32_t k, __half *out, float *out_stats, cudaStream_t s, bool pdl);
+                        uint32_t k, uint32_t limit, __half *out, float *out_stats, cudaStream_t s,
+                        bool pdl);
 
 // The device error word: read (and clear) it.
 bool read_device_error(unsigned int *code);

@@ -439,14 +439,15 @@ bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma
 }
 
 bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
-                        uint32_t k, __half *out, float *out_stats, cudaStream_t s, bool pdl) {
+                        uint32_t k, uint32_t limit, __half *out, float *out_stats, cudaStream_t s,
+                        bool pdl) {
     if (k == 0) return true;
     if (d % 8) {
         set_error("gather: width must be a multiple of 8");
         return false;
     }
     return launch_ex(gather_rows_kernel, dim3((k + 3) / 4), dim3(128), 0, s, pdl, "gather launch",
-                     x, stats, d, rows, k, out, out_stats);
+                     x, stats, d, rows, k, limit, out, out_stats);
 }
 
 bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,

@@ -56,6 +56,7 @@ struct RowParams {
     const __half *w;
     uint32_t n, d;
     float eps, b;
+    uint32_t limit;  // marker gather: rows a marker may name (the head's rows)
 };
 
 // How a phase's items wait for an earlier phase: DEP_ROWS, the earlier phase's row block(s) that

@@ -231,6 +231,10 @@ __device__ __noinline__ void row_op(uint32_t kind, const RowParams &r, uint32_t 
                r.stats + 2 * i, lane);
     } else if (kind == PH_GATHER) {
         const uint32_t src = r.rows[i];
+        if (src >= r.limit) {
+            if (lane == 0) dev_fail(JC_DEV_BAD_INDEX);
+            return;
+        }
         const uint4 *s4 = reinterpret_cast<const uint4 *>(r.x + (size_t)src * r.d);
         uint4 *d4 = reinterpret_cast<uint4 *>(r.out + (size_t)i * r.d);
         for (uint32_t j = lane; j < r.d / 8; j += 32) d4[j] = s4[j];

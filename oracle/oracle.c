@@ -317,17 +317,19 @@ void or_attention_f32(const float *qkv, float *o, int n, int heads, int window) 
 /* ------------------------------------------------------------------------------------------ */
 /* f32 model */
 
-int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, int n,
-                   const uint32_t *markers, int n_markers, int qtype, float *logits,
-                   float *trace_x) {
+int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x) {
     or_layout L;
     if (or_layout_of(c, &L) || n <= 0 || n > c->max_positions || qtype < 0 ||
         qtype >= c->n_qtypes)
         return -1;
     for (int i = 0; i < n; i++)
         if (ids[i] >= (uint32_t)c->vocab) return -1;
+    /* the head runs on rows [0, nh) (all rows unless head_rows limits it) */
+    const int nh = head_rows > 0 && head_rows < n ? head_rows : n;
     for (int i = 0; i < n_markers; i++)
-        if (markers[i] >= (uint32_t)n) return -1;
+        if (markers[i] >= (uint32_t)nh) return -1;
     const int D = c->d_model, I = c->inter, F = c->head_ff, S = c->scorer_hidden;
     const int H = c->n_heads;
     float *x = malloc((size_t)n * D * 4), *h = malloc((size_t)n * D * 4);
@@ -364,19 +366,19 @@ int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, in
     }
 
     /* head input: final LN (encoder eps) + type embedding */
-    layernorm_rows(x, n, D, raw + L.final_norm.off, NULL, c->norm_eps, h);
+    layernorm_rows(x, nh, D, raw + L.final_norm.off, NULL, c->norm_eps, h);
     const float *te = raw + L.type_emb.off + (size_t)qtype * D;
-    for (int i = 0; i < n; i++)
+    for (int i = 0; i < nh; i++)
         for (int j = 0; j < D; j++) x[(size_t)i * D + j] = h[(size_t)i * D + j] + te[j];
     for (int l = 0; l < c->n_head_layers; l++) {
-        layernorm_rows(x, n, D, raw + L.h_norm1_w[l].off, raw + L.h_norm1_b[l].off, c->head_eps, h);
-        matmul_f32(h, n, D, raw + L.h_in_w[l].off, 3 * D, qkv, raw + L.h_in_b[l].off, 0);
-        or_attention_f32(qkv, o, n, H, 0);
-        matmul_f32(o, n, D, raw + L.h_out_w[l].off, D, x, raw + L.h_out_b[l].off, 1);
-        layernorm_rows(x, n, D, raw + L.h_norm2_w[l].off, raw + L.h_norm2_b[l].off, c->head_eps, h);
-        matmul_f32(h, n, D, raw + L.h_l1_w[l].off, F, hh, raw + L.h_l1_b[l].off, 0);
-        for (size_t i = 0; i < (size_t)n * F; i++) hh[i] = hh[i] > 0 ? hh[i] : 0;
-        matmul_f32(hh, n, F, raw + L.h_l2_w[l].off, D, x, raw + L.h_l2_b[l].off, 1);
+        layernorm_rows(x, nh, D, raw + L.h_norm1_w[l].off, raw + L.h_norm1_b[l].off, c->head_eps, h);
+        matmul_f32(h, nh, D, raw + L.h_in_w[l].off, 3 * D, qkv, raw + L.h_in_b[l].off, 0);
+        or_attention_f32(qkv, o, nh, H, 0);
+        matmul_f32(o, nh, D, raw + L.h_out_w[l].off, D, x, raw + L.h_out_b[l].off, 1);
+        layernorm_rows(x, nh, D, raw + L.h_norm2_w[l].off, raw + L.h_norm2_b[l].off, c->head_eps, h);
+        matmul_f32(h, nh, D, raw + L.h_l1_w[l].off, F, hh, raw + L.h_l1_b[l].off, 0);
+        for (size_t i = 0; i < (size_t)nh * F; i++) hh[i] = hh[i] > 0 ? hh[i] : 0;
+        matmul_f32(hh, nh, F, raw + L.h_l2_w[l].off, D, x, raw + L.h_l2_b[l].off, 1);
     }
     /* scorer on the marker rows */
     float *z = malloc((size_t)(n_markers ? n_markers : 1) * D * 4);
@@ -390,6 +392,12 @@ int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, in
     free(z); free(zn); free(y);
     free(x); free(h); free(qkv); free(o); free(hh); free(mm); free(rg); free(rl);
     return 0;
+}
+
+int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                   const uint32_t *markers, int n_markers, int qtype, float *logits,
+                   float *trace_x) {
+    return or_forward_f32_head(c, raw, ids, n, markers, n_markers, qtype, 0, logits, trace_x);
 }
 
 /* ------------------------------------------------------------------------------------------ */
@@ -668,17 +676,18 @@ void or_ref_gemm_plan(int n, int cols, int k, int sms, int per_sm, int *bm_out, 
 /* ------------------------------------------------------------------------------------------ */
 /* the whole f16-emulated forward pass */
 
-int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, int n,
-                   const uint32_t *markers, int n_markers, int qtype, float *logits,
-                   float *trace_x, int bugs) {
+int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x, int bugs) {
     or_layout L;
     if (or_layout_of(c, &L) || n <= 0 || n > c->max_positions || qtype < 0 ||
         qtype >= c->n_qtypes)
         return -1;
     for (int i = 0; i < n; i++)
         if (ids[i] >= (uint32_t)c->vocab) return -1;
+    const int nh = head_rows > 0 && head_rows < n ? head_rows : n;
     for (int i = 0; i < n_markers; i++)
-        if (markers[i] >= (uint32_t)n) return -1;
+        if (markers[i] >= (uint32_t)nh) return -1;
     const int D = c->d_model, I = c->inter, F = c->head_ff, S = c->scorer_hidden, H = c->n_heads;
     const size_t nD = (size_t)n * D;
     uint16_t *x = malloc(nD * 2), *qkv = malloc(nD * 3 * 2), *o = malloc(nD * 2);
@@ -740,32 +749,32 @@ int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, in
 
     /* head input: st_a feeds in_proj and the scorer, st_b feeds linear1 */
     uint16_t *hx = malloc(nD * 2);
-    or_emu_norm_add(x, raw + L.final_norm.off, raw + L.type_emb.off + (size_t)qtype * D, n, D,
+    or_emu_norm_add(x, raw + L.final_norm.off, raw + L.type_emb.off + (size_t)qtype * D, nh, D,
                     c->norm_eps, hx, st_a);
     for (int l = 0; l < c->n_head_layers; l++) {
         or_fold_layernorm_bias(raw + L.h_in_w[l].off, raw + L.h_norm1_w[l].off,
                                raw + L.h_norm1_b[l].off, raw + L.h_in_b[l].off, 3 * D, D, w16,
                                colsum, bias);
-        or_emu_gemm(OR_LN | OR_BIAS, hx, w16, qkv, n, 3 * D, D, st_a, colsum, c->head_eps, NULL,
+        or_emu_gemm(OR_LN | OR_BIAS, hx, w16, qkv, nh, 3 * D, D, st_a, colsum, c->head_eps, NULL,
                     bias, NULL);
-        or_emu_attention(qkv, o, n, H, 0);
+        or_emu_attention(qkv, o, nh, H, 0);
         or_f16_round_array(raw + L.h_out_w[l].off, w16, (size_t)D * D);
         memset(st_b, 0, (size_t)2 * n * 4);
-        or_emu_gemm(OR_BIAS | OR_RES | OR_STATS, o, w16, hx, n, D, D, NULL, NULL, 0, NULL,
+        or_emu_gemm(OR_BIAS | OR_RES | OR_STATS, o, w16, hx, nh, D, D, NULL, NULL, 0, NULL,
                     raw + L.h_out_b[l].off, st_b);
         or_fold_layernorm_bias(raw + L.h_l1_w[l].off, raw + L.h_norm2_w[l].off,
                                raw + L.h_norm2_b[l].off, raw + L.h_l1_b[l].off, F, D, w16, colsum,
                                bias);
-        or_emu_gemm(OR_LN | OR_BIAS | OR_RELU, hx, w16, m, n, F, D, st_b, colsum, c->head_eps,
+        or_emu_gemm(OR_LN | OR_BIAS | OR_RELU, hx, w16, m, nh, F, D, st_b, colsum, c->head_eps,
                     NULL, bias, NULL);
         or_f16_round_array(raw + L.h_l2_w[l].off, w16, (size_t)D * F);
         memset(st_a, 0, (size_t)2 * n * 4);
-        or_emu_gemm(OR_BIAS | OR_RES | OR_STATS, m, w16, hx, n, D, F, NULL, NULL, 0, NULL,
+        or_emu_gemm(OR_BIAS | OR_RES | OR_STATS, m, w16, hx, nh, D, F, NULL, NULL, 0, NULL,
                     raw + L.h_l2_b[l].off, st_a);
     }
     or_fold_layernorm_bias(raw + L.s_lin1_w.off, raw + L.s_norm_w.off, raw + L.s_norm_b.off,
                            raw + L.s_lin1_b.off, S, D, w16, colsum, bias);
-    or_emu_gemm(OR_LN | OR_BIAS | OR_GELU, hx, w16, y, n, S, D, st_a, colsum, c->head_eps, NULL,
+    or_emu_gemm(OR_LN | OR_BIAS | OR_GELU, hx, w16, y, nh, S, D, st_a, colsum, c->head_eps, NULL,
                 bias, NULL);
     uint16_t *w2 = malloc((size_t)S * 2);
     or_f16_round_array(raw + L.s_lin2_w.off, w2, (size_t)S);
@@ -774,4 +783,11 @@ int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, in
     free(x); free(qkv); free(o); free(m); free(y); free(st_a); free(st_b); free(rg); free(rl);
     free(w16); free(colsum); free(bias); free(wtmp);
     return 0;
+}
+
+int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                   const uint32_t *markers, int n_markers, int qtype, float *logits,
+                   float *trace_x, int bugs) {
+    return or_forward_emu_head(c, raw, ids, n, markers, n_markers, qtype, 0, logits, trace_x,
+                               bugs);
 }

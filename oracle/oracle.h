@@ -82,6 +82,12 @@ void or_fill_normal(float *dst, size_t n, uint64_t seed, float mean, float std);
 int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, int n,
                    const uint32_t *markers, int n_markers, int qtype, float *logits,
                    float *trace_x);
+/* The same with the head on rows [0, head_rows) only (0: all rows): the final LayerNorm, the
+ * head layers (their attention over those rows) and the marker rows; markers must be below
+ * head_rows. BASELINE config 4's long-context request (1024 tokens, head on 512 rows). */
+int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x);
 
 /* The f16 emulation of the GPU path (same folds, roundings and statistics as the kernels) over the
  * same raw weights; same outputs as or_forward_f32. trace_x gets the f16 residual stream after each
@@ -90,6 +96,9 @@ int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, in
 int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, int n,
                    const uint32_t *markers, int n_markers, int qtype, float *logits,
                    float *trace_x, int bugs);
+int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x, int bugs);
 
 /* ---- f16-arithmetic emulation of single kernels (inputs/outputs are f16 bit patterns) ---- */
 /* Epilogue flags, as the GEMM family's. */

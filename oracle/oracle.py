@@ -66,10 +66,10 @@ def lib():
         L.or_raw_size.restype = sz
         L.or_init_random.argtypes = [cfgp, u64, P]
         L.or_fill_normal.argtypes = [P, sz, u64, f32, f32]
-        L.or_forward_f32.argtypes = [cfgp, P, P, i32, P, i32, i32, P, P]
-        L.or_forward_f32.restype = i32
-        L.or_forward_emu.argtypes = [cfgp, P, P, i32, P, i32, i32, P, P, i32]
-        L.or_forward_emu.restype = i32
+        L.or_forward_f32_head.argtypes = [cfgp, P, P, i32, P, i32, i32, i32, P, P]
+        L.or_forward_f32_head.restype = i32
+        L.or_forward_emu_head.argtypes = [cfgp, P, P, i32, P, i32, i32, i32, P, P, i32]
+        L.or_forward_emu_head.restype = i32
         L.or_emu_gemm.argtypes = [i32, P, P, P, i32, i32, i32, P, P, f32, P, P, P]
         L.or_emu_attention.argtypes = [P, P, i32, i32, i32]
         L.or_attention_f32.argtypes = [P, P, i32, i32, i32]
@@ -117,25 +117,26 @@ def normal(shape, seed: int, mean=0.0, std=1.0) -> np.ndarray:
     return a
 
 
-def forward_f32(c: Config, raw, ids, markers, qtype=0, trace=False):
+def forward_f32(c: Config, raw, ids, markers, qtype=0, trace=False, head_rows=0):
+    """head_rows > 0: the head on the first head_rows rows only (or_forward_f32_head)."""
     ids = np.ascontiguousarray(ids, np.uint32)
     markers = np.ascontiguousarray(markers, np.uint32)
     logits = np.zeros(max(len(markers), 1), np.float32)
     tr = np.zeros((c.n_layers, len(ids), c.d_model), np.float32) if trace else None
-    rc = lib().or_forward_f32(ctypes.byref(c), _p(raw), _p(ids), len(ids), _p(markers),
-                              len(markers), qtype, _p(logits), _p(tr))
+    rc = lib().or_forward_f32_head(ctypes.byref(c), _p(raw), _p(ids), len(ids), _p(markers),
+                                   len(markers), qtype, head_rows, _p(logits), _p(tr))
     if rc:
         raise ValueError("oracle: bad forward arguments")
     return (logits[:len(markers)], tr) if trace else logits[:len(markers)]
 
 
-def forward_emu(c: Config, raw, ids, markers, qtype=0, trace=False, bugs=0):
+def forward_emu(c: Config, raw, ids, markers, qtype=0, trace=False, bugs=0, head_rows=0):
     ids = np.ascontiguousarray(ids, np.uint32)
     markers = np.ascontiguousarray(markers, np.uint32)
     logits = np.zeros(max(len(markers), 1), np.float32)
     tr = np.zeros((c.n_layers, len(ids), c.d_model), np.float32) if trace else None
-    rc = lib().or_forward_emu(ctypes.byref(c), _p(raw), _p(ids), len(ids), _p(markers),
-                              len(markers), qtype, _p(logits), _p(tr), bugs)
+    rc = lib().or_forward_emu_head(ctypes.byref(c), _p(raw), _p(ids), len(ids), _p(markers),
+                                   len(markers), qtype, head_rows, _p(logits), _p(tr), bugs)
     if rc:
         raise ValueError("oracle: bad forward arguments")
     return (logits[:len(markers)], tr) if trace else logits[:len(markers)]

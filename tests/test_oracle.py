@@ -126,6 +126,31 @@ def test_oracle_f32_matches_torch(O, n, window, qtype):
         assert rel_err(tr[l], trw[l]) < 1e-5
 
 
+@pytest.mark.parametrize("n,head_rows", [(70, 40), (70, 70), (70, 200)])
+def test_oracle_head_rows_matches_torch(O, n, head_rows):
+    """The head limited to the first head_rows rows: the oracle's f32 path
+    against the torch restatement, the emulation within the f16 bar, and markers past the head's
+    rows rejected."""
+    c = small(O)
+    raw = O.init_random(c, 4)
+    rng = np.random.default_rng(n + head_rows)
+    ids = rng.integers(0, c.vocab, n)
+    markers = [0, 17, min(n, head_rows) - 1]
+    got = O.forward_f32(c, raw, ids, markers, 1, head_rows=head_rows)
+    want = torch_ref.forward(c, raw, ids, markers, 1, head_rows=head_rows)
+    assert np.max(np.abs(got - want)) < 2e-5
+    emu = O.forward_emu(c, raw, ids, markers, 1, head_rows=head_rows)
+    assert np.max(np.abs(emu - got)) < 3e-2
+    if head_rows >= n:
+        assert np.array_equal(got, O.forward_f32(c, raw, ids, markers, 1))
+    else:
+        assert np.max(np.abs(got - O.forward_f32(c, raw, ids, markers, 1))) > 1e-6
+        with pytest.raises(ValueError):
+            O.forward_f32(c, raw, ids, [head_rows], 1, head_rows=head_rows)
+        with pytest.raises(ValueError):
+            O.forward_emu(c, raw, ids, [head_rows], 1, head_rows=head_rows)
+
+
 def test_oracle_reference_width(O):
     """The reference's own width (384 / 6 heads, scorer D -> D), torch vs oracle."""
     c = O.reference_width_config(n_layers=2, vocab=300, head_ff=256, max_positions=128)

@@ -114,7 +114,9 @@ def attention(q, k, v, heads, window):
     return (p @ vh).transpose(0, 1).reshape(n, heads * 64)
 
 
-def forward(c, raw, ids, markers, qtype=0, trace=False):
+def forward(c, raw, ids, markers, qtype=0, trace=False, head_rows=0):
+    """head_rows > 0: the head (final norm, head layers, marker rows) sees only the first
+    head_rows rows of the encoder's output."""
     W = raw_tensors(c, raw)
     D, H, I = c.d_model, c.n_heads, c.inter
     n = len(ids)
@@ -137,6 +139,8 @@ def forward(c, raw, ids, markers, qtype=0, trace=False):
         m = gelu_as(hh[:, :I]) * hh[:, I:]
         x = x + m @ W[f"wo_mlp{l}"].T
         tr.append(x.clone())
+    if 0 < head_rows < n:
+        x = x[:head_rows]
     x = ln64(x, W["final_norm"], None, c.norm_eps) + W["type_emb"][qtype]
     for l in range(c.n_head_layers):
         h = ln64(x, W[f"n1w{l}"], W[f"n1b{l}"], c.head_eps)
