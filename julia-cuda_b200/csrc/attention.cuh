@@ -190,22 +190,38 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
         }
 
         // Mask, scale and the online softmax. Row h of this lane: elements 2h, 2h+1 of each tile.
+        // A tile every key of which every query of this warp may see (inside the sequence and,
+        // in a window layer, within the window of the warp's first and last query) needs no mask.
         const uint32_t k0 = kb_of(j) * 64;
+        const uint32_t wq0 = q0 + qw * 16;
+        const bool interior = k0 + 64 <= n &&
+                              (window == 0 || (k0 + 63 <= wq0 + window && wq0 + 15 <= k0 + window));
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             float m = -INFINITY;
+            if (interior) {
 #pragma unroll
-            for (int jt = 0; jt < 8; jt++)
+                for (int jt = 0; jt < 8; jt++)
 #pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const uint32_t key = k0 + 8 * jt + 2 * t + e;
-                    const uint32_t qq = qrow[h];
-                    const uint32_t dist = qq > key ? qq - key : key - qq;
-                    const bool ok = key < n && (window == 0 || dist <= window);
-                    const float v = ok ? s[jt][2 * h + e] * scale : -INFINITY;
-                    s[jt][2 * h + e] = v;
-                    m = fmaxf(m, v);
-                }
+                    for (int e = 0; e < 2; e++) {
+                        const float v = s[jt][2 * h + e] * scale;
+                        s[jt][2 * h + e] = v;
+                        m = fmaxf(m, v);
+                    }
+            } else {
+#pragma unroll
+                for (int jt = 0; jt < 8; jt++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const uint32_t key = k0 + 8 * jt + 2 * t + e;
+                        const uint32_t qq = qrow[h];
+                        const uint32_t dist = qq > key ? qq - key : key - qq;
+                        const bool ok = key < n && (window == 0 || dist <= window);
+                        const float v = ok ? s[jt][2 * h + e] * scale : -INFINITY;
+                        s[jt][2 * h + e] = v;
+                        m = fmaxf(m, v);
+                    }
+            }
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
             const float m_new = fmaxf(mx[h], m);
@@ -367,8 +383,10 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
     }
 }
 
+// Two CTAs per SM (at most 128 registers a thread), so the 64-query shape's grid at 1024 tokens
+// (16 query tiles x 12 heads) is resident in one wave.
 template <int QW, int KS>
-__global__ void __launch_bounds__(32 * QW * KS) attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(32 * QW * KS, 2) attention_kernel(const AttnParams p) {
     extern __shared__ __align__(128) uint8_t att_smem[];
     attention_task<QW, KS>(p, att_smem, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z, true);
 }

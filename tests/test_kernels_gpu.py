@@ -200,6 +200,19 @@ def test_attention(jc, O, n, window):
         assert e1 < 2e-3 and e2 < 4e-3, f"n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
 
 
+@pytest.mark.parametrize("n,window", [(300, 8), (300, 100), (1024, 200), (700, 31)])
+def test_attention_other_windows(jc, O, n, window):
+    """Windows narrower and wider than a 64-key tile: the tiles wholly inside every query's
+    window skip the mask, the others keep it."""
+    heads = 12
+    qkv = O.f16(O.normal((n, 3 * heads * 64), 7 * n + window))
+    want = O.emu_attention(qkv, n, heads, window)
+    o = torch.zeros(n, heads * 64, dtype=torch.float16, device="cuda")
+    jc.attention(cuda_u16(qkv), o, heads, window)
+    torch.cuda.synchronize()
+    assert rel_err(O.f32(host_u16(o)), O.f32(want)) < 2e-3
+
+
 def test_attention_reference_width(jc, O):
     """Six heads (the reference's 384-wide model)."""
     n, heads = 363, 6
