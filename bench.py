@@ -262,13 +262,14 @@ def sweep_arm(args, rank, local):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     pk, src = peaks()
     rows = []
-    for n in (72, 293, 448, 1024):
-        rows += [("config1", n, k, v) for k, v in time_kernels(
-            jc, torch, cfg, flush, n=n, gemms=("qkv", "wo", "wi", "wo_mlp"),
-            attention=False).items()]
-    for n in (128, 512, 1024):
-        rows += [("config2", n, k, v) for k, v in time_kernels(
-            jc, torch, cfg, flush, n=n, gemms=()).items()]
+    with ClockSampler(local) as clk:
+        for n in (72, 293, 448, 1024):
+            rows += [("config1", n, k, v) for k, v in time_kernels(
+                jc, torch, cfg, flush, n=n, gemms=("qkv", "wo", "wi", "wo_mlp"),
+                attention=False).items()]
+        for n in (128, 512, 1024):
+            rows += [("config2", n, k, v) for k, v in time_kernels(
+                jc, torch, cfg, flush, n=n, gemms=()).items()]
     assert jc.device_error() == 0
     for conf, n, name, (ms, _, bytes_, flops) in rows:
         gbs, tfs = bytes_ / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / 1e12
@@ -276,6 +277,7 @@ def sweep_arm(args, rank, local):
                           "gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "tflops": tfs,
                           "tensor_frac": tfs / pk["bf16_tflops"], "peak_source": src,
                           "l2": "flushed before every launch"}), flush=True)
+    print(json.dumps({"sweep": "clocks", "clocks": clk.summary()}), flush=True)
 
 
 def reference_arm(args, rank, world):
