@@ -187,6 +187,13 @@ int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, u
                  uint32_t kv_chunks, float *ws, uint32_t *counters, void *stream);
 size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 size_t jc_attention_counters(uint32_t n, uint32_t heads);
+/* Which attention kernel serves a launch: the tcgen05 kernel (128-query tiles, S and P.V in
+ * TMEM) for global attention from 768 tokens by default (JC_ATTN_TC_MIN), never for sliding
+ * windows by default (JC_ATTN_TC_MIN_WINDOW); the mma.sync kernel otherwise. Sets the shortest
+ * global and window sequence lengths for the tcgen05 kernel (1: every launch; 0xFFFFFFFF:
+ * never) for later launches and later-captured engine graphs, and returns the previous ones in
+ * place. A tuning and test hook. */
+void jc_attention_tc_min(uint32_t *global_min, uint32_t *window_min);
 
 /* x[i] = LayerNorm(table[ids[i]]) * gamma, f16; stats (optional) [n][2]. Replaces
  * kernels/src/main.rs:47-103 + src/lib.rs:164-219. */

@@ -107,6 +107,7 @@ def lib():
         "jc_attention": ([P, P, u32, u32, u32, u32, P, P, P], i32),
         "jc_attention_ws_floats": ([u32, u32, u32], sz),
         "jc_attention_counters": ([u32, u32], sz),
+        "jc_attention_tc_min": ([P, P], None),
         "jc_embed": ([P, u32, P, P, u32, f32, P, P, P], i32),
         "jc_norm_add": ([P, u32, u32, P, P, f32, P, P, P], i32),
         "jc_score": ([P, u32, P, f32, P, u32, P, P], i32),
@@ -282,6 +283,14 @@ def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=No
     rc = lib().jc_attention(_t_ptr(qkv), _t_ptr(o), n, heads, window, chunks, _t_ptr(ws),
                             _t_ptr(cnt), _stream(stream))
     _check(rc, "jc_attention")
+
+
+def attention_tc_min(global_min: int, window_min: int) -> tuple:
+    """Sets the shortest global / sliding-window sequence for the tcgen05 attention kernel
+    (jc_attention_tc_min); returns the previous pair."""
+    g, w = ctypes.c_uint32(global_min), ctypes.c_uint32(window_min)
+    lib().jc_attention_tc_min(ctypes.byref(g), ctypes.byref(w))
+    return g.value, w.value
 
 
 def embed(ids, table, gamma, x, eps=1e-5, stats=None, stream=None) -> None:

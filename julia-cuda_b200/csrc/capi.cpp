@@ -465,6 +465,10 @@ size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
 
 size_t jc_attention_counters(uint32_t n, uint32_t heads) { return jc::attn_counters(n, heads); }
 
+void jc_attention_tc_min(uint32_t *global_min, uint32_t *window_min) {
+    if (global_min && window_min) jc::swap_attn_tc_min(global_min, window_min);
+}
+
 int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, uint32_t window,
                  uint32_t kv_chunks, float *ws, uint32_t *counters, void *stream) {
     return guarded(nullptr, 0, [&]() -> int {

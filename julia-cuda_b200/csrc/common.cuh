@@ -135,6 +135,23 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 2-D tiled store of the box at smem `src` to (x = column, y = row) of the tensor; elements
+// outside the tensor are not written. x * sizeof(element) must be a multiple of 16 bytes and
+// neither coordinate negative (callers pass tile origins). Completes as a bulk async group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t x,
+                                             int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the bulk stores committed so far have read their shared memory.
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // programmatic dependent launch (no-ops when the launch has no PDL attribute)
 

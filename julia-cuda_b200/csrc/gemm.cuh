@@ -106,12 +106,12 @@ __device__ __forceinline__ void store_halves(__half *dst, const uint32_t *in) {
     }
 }
 
-// Stores G values at dst, after adding the residual (already in registers as G/2 half2 words),
-// and accumulates the statistics of the values as stored (f16), as the next LayerNorm sees them.
+// Packs G values into G/2 half2 words after adding the residual (already in registers as G/2
+// half2 words), and accumulates the statistics of the values as stored (f16), as the next
+// LayerNorm sees them.
 template <int G, uint32_t EPI>
-__device__ __forceinline__ void store_group(const float *v, __half *dst, const uint32_t *resw,
-                                            float &s, float &q) {
-    uint32_t out[G / 2];
+__device__ __forceinline__ void pack_group(const float *v, const uint32_t *resw, uint32_t *out,
+                                           float &s, float &q) {
 #pragma unroll
     for (int j = 0; j < G / 2; j++) {
         float lo = v[2 * j], hi = v[2 * j + 1];
@@ -128,7 +128,24 @@ __device__ __forceinline__ void store_group(const float *v, __half *dst, const u
             q = fmaf(f.y, f.y, q);
         }
     }
-    store_halves<G>(dst, out);
+}
+
+// G f16 values (G/2 words) of tile row `row` at tile-local output column `oc` into the staging
+// area of the TMA stores: boxes of BW columns x 128 rows, 16-byte chunk c of a row at chunk
+// c ^ (row % 8) (BW 64, 128-byte swizzle) or c ^ ((row / 2) % 4) (BW 32, 64-byte swizzle), the
+// layout the tensor map's swizzle mode reads; a warp's 32 rows then spread over all banks.
+template <int G, int BW>
+__device__ __forceinline__ void stage_halves(uint8_t *stage, uint32_t row, uint32_t oc,
+                                             const uint32_t *in) {
+    static_assert(G % 8 == 0 && (BW == 64 || BW == 32), "16-byte chunks in 64- or 32-column boxes");
+    constexpr uint32_t ROWB = BW * 2;
+    uint8_t *box_row = stage + (oc / BW) * (GEMM_BM * ROWB) + row * ROWB;
+    const uint32_t c0 = (oc % BW) / 8;
+    const uint32_t sw = BW == 64 ? (row & 7) : ((row >> 1) & 3);
+#pragma unroll
+    for (int j = 0; j < G / 8; j++)
+        *reinterpret_cast<uint4 *>(box_row + (((c0 + j) ^ sw) << 4)) =
+            make_uint4(in[4 * j], in[4 * j + 1], in[4 * j + 2], in[4 * j + 3]);
 }
 
 // The epilogue of one thread's share of a chunk of 2 * HALF columns starting at global column c0:
@@ -136,14 +153,19 @@ __device__ __forceinline__ void store_group(const float *v, __half *dst, const u
 // 64-column chunks RoPE and GeGLU need: v[j] and v[G + j] are then a RoPE pair (i, i + 32) of one
 // head, or a GeGLU input and its gate). cs / bs: the tile's column sums / biases in shared memory
 // (tile-local, the tile starting at n0); resw: the residual of those columns (G/2 + G/2 words);
-// ropev: (cos, sin) of pairs pair0 .. pair0 + G, two per float4.
-template <int G, int HALF, uint32_t EPI>
+// ropev: (cos, sin) of pairs pair0 .. pair0 + G, two per float4. stage: the TMA-store staging
+// area (boxes of BW output columns; tr = the row inside the tile), or nullptr to store directly.
+template <int G, int HALF, uint32_t EPI, int BW>
 __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v, uint32_t r,
+                                                   uint32_t tr, uint8_t *stage,
                                                    bool valid, uint32_t n0, uint32_t c0,
                                                    uint32_t pair0, float mean, float rstd,
                                                    const float *cs, const float *bs,
                                                    const uint32_t *resw, const float4 *ropev,
                                                    float &s, float &q) {
+    // Staging needs whole 16-byte chunks in 32- or 64-column boxes (every launch the host allows
+    // TMA stores for; the other instantiations store directly).
+    constexpr bool STAGE_OK = (BW == 32 || BW == 64) && G % 8 == 0;
     const uint32_t la = c0 - n0 + pair0, lb = la + HALF;
     if constexpr ((EPI & JC_EPI_LN) != 0) {
 #pragma unroll
@@ -194,13 +216,29 @@ __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v
             for (int j = 0; j < G / 2; j++)
                 out[j] = pack_half2(gelu_as(v[2 * j]) * v[G + 2 * j],
                                     gelu_as(v[2 * j + 1]) * v[G + 2 * j + 1]);
+            if constexpr (STAGE_OK) {
+                if (stage) {
+                    stage_halves<G, BW>(stage, tr, (c0 - n0) / 2 + pair0, out);
+                    return;
+                }
+            }
             store_halves<G>(p.c + (size_t)r * (p.n / 2) + c0 / 2 + pair0, out);
         }
     } else {
         if (valid) {
+            uint32_t oa[G / 2], ob[G / 2];
+            pack_group<G, EPI>(v, resw, oa, s, q);
+            pack_group<G, EPI>(v + G, resw + G / 2, ob, s, q);
+            if constexpr (STAGE_OK) {
+                if (stage) {
+                    stage_halves<G, BW>(stage, tr, la, oa);
+                    stage_halves<G, BW>(stage, tr, lb, ob);
+                    return;
+                }
+            }
             __half *row = p.c + (size_t)r * p.n + n0;
-            store_group<G, EPI>(v, row + la, resw, s, q);
-            store_group<G, EPI>(v + G, row + lb, resw + G / 2, s, q);
+            store_halves<G>(row + la, oa);
+            store_halves<G>(row + lb, ob);
         }
     }
 }

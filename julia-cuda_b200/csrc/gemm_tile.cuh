@@ -102,21 +102,23 @@ __device__ __forceinline__ void gemm_issue_a(const GemmParams &p, const GemmSmem
 
 // v[0, G) = columns [ta, ta + G) and v[G, 2G) = columns [tb, tb + G) of this thread's TMEM lane,
 // each summed over the NI accumulators (BN columns apart) in accumulator order, so the result does
-// not depend on timing. The first two accumulators are read with one wait.
+// not depend on timing. Every accumulator's columns are requested before the one wait.
 template <int G, int NI, int BN>
 __device__ __forceinline__ void acc_ld2(uint32_t ta, uint32_t tb, float *v) {
     tmem_ld<G>(ta, v);
     tmem_ld<G>(tb, v + G);
     if constexpr (NI > 1) {
-        float t[2 * G];
+        float t[NI - 1][2 * G];
 #pragma unroll
         for (int j = 1; j < NI; j++) {
-            tmem_ld<G>(ta + j * BN, t);
-            tmem_ld<G>(tb + j * BN, t + G);
-            tc_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 2 * G; c++) v[c] += t[c];
+            tmem_ld<G>(ta + j * BN, t[j - 1]);
+            tmem_ld<G>(tb + j * BN, t[j - 1] + G);
         }
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 1; j < NI; j++)
+#pragma unroll
+            for (int c = 0; c < 2 * G; c++) v[c] += t[j - 1][c];
     } else {
         tc_wait_ld();
     }
@@ -344,6 +346,12 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         __threadfence();
     }
 
+    // Output through TMA stores (single-GEMM kernel): the tile is staged in the stage memory,
+    // free now that every MMA has completed, in boxes of BW columns.
+    constexpr int W_OUT = (EPI & JC_EPI_GEGLU) ? BN / 2 : BN;
+    constexpr int BW = W_OUT < 64 ? W_OUT : 64;
+    constexpr bool CAN_STAGE = CS == 1 && (BW == 32 || BW == 64) && GT % 8 == 0;
+    uint8_t *stage = (CAN_STAGE && p.map_c) ? sv.stages : nullptr;
     if (run_epilogue) {
         float s = 0.f, q = 0.f;
 #pragma unroll
@@ -392,7 +400,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
                     }
                 }
             }
-            gemm_epilogue_part<GT, HALF, EPI>(p, v, r, valid, n0, n0 + ci * CH, pair0, mean, rstd,
+            gemm_epilogue_part<GT, HALF, EPI, BW>(p, v, r, row, stage, valid, n0, n0 + ci * CH, pair0, mean, rstd,
                                               sv.cs_s, sv.bs_s, resw + ((EPI & JC_EPI_RES) ? ci * GT : 0),
                                               ropev, s, q);
         }
@@ -403,6 +411,21 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
             if (!half && valid) {
                 const float2 o = sv.row_part[row];
                 red_add_f32x2(p.stats_out + 2 * (size_t)r, s + o.x, q + o.y);
+            }
+        }
+        if (stage) {
+            // Every thread's staging writes are visible to the TMA (async proxy) before one
+            // thread stores the boxes (rows past m are not written) and waits until they have
+            // been read out of shared memory.
+            fence_proxy_async();
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                const int32_t out0 = (int32_t)((EPI & JC_EPI_GEGLU) ? n0 / 2 : n0);
+#pragma unroll
+                for (int b = 0; b < W_OUT / BW; b++)
+                    tma_store_2d(p.map_c, stage + b * GEMM_BM * BW * 2, out0 + b * BW, (int32_t)m0);
+                bulk_commit();
+                bulk_wait_read();
             }
         }
     }
@@ -417,6 +440,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
 struct GemmKernelParams {
     CUtensorMap map_a;
     CUtensorMap map_w;
+    CUtensorMap map_c;  // valid when p.store_tma
     GemmParams p;
 };
 
@@ -429,6 +453,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     GemmParams p = kp.p;
     p.map_a = &kp.map_a;
     p.map_w = &kp.map_w;
+    p.map_c = p.store_tma ? &kp.map_c : nullptr;
     const GemmSmemView<BN, STAGES> sv(base);
     if (threadIdx.x == 32) {
         tma_prefetch_desc(p.map_a);

@@ -104,6 +104,9 @@ size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 size_t attn_counters(uint32_t n, uint32_t heads);
 bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms);
+// The shortest global / sliding-window sequences for the tensor-core attention: sets both,
+// returns the old values in place.
+void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min);
 
 // ---------------------------------------------------------------------------------------------
 // memory-bound edges

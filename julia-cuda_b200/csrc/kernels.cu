@@ -9,6 +9,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "edges.cuh"
 #include "gemm.cuh"
 #include "jc_internal.h"
@@ -241,6 +242,27 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     GemmParams &p = kp.p;
     p.map_a = nullptr;  // the kernel points these at its own copies
     p.map_w = nullptr;
+    p.map_c = nullptr;
+    p.store_tma = 0;
+    if (cfg.cluster == 1) {
+        // The output through TMA stores: c as (columns, m rows), boxes of up to 64 columns x 128
+        // rows with the swizzle the epilogue stages in; rows past m are not written.
+        const bool geglu = g.epi & JC_EPI_GEGLU;
+        const uint32_t n_out = geglu ? g.n / 2 : g.n, w_out = geglu ? cfg.bn / 2 : cfg.bn;
+        const uint32_t bw = w_out < 64 ? w_out : 64;
+        auto fn = encode_fn();
+        if (fn && (reinterpret_cast<uintptr_t>(g.c) & 15) == 0 && (n_out * 2) % 16 == 0) {
+            cuuint64_t dims[2] = {n_out, g.m};
+            cuuint64_t strides[1] = {(cuuint64_t)n_out * 2};
+            cuuint32_t box[2] = {bw, (cuuint32_t)GEMM_BM};
+            cuuint32_t es[2] = {1, 1};
+            const CUresult r = fn(&kp.map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.c, dims, strides,
+                                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                  bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            p.store_tma = r == CUDA_SUCCESS ? 1u : 0u;
+        }
+    }
     p.c = g.c;
     p.res = g.res;
     p.ws = g.ws;
@@ -346,18 +368,68 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // ---------------------------------------------------------------------------------------------
 // attention
 
-// Two shapes: up to 512 tokens, 32-query CTAs whose 4 key groups each take every 4th key tile
-// (the most CTAs and the shortest per-warp key loop); longer, 64-query CTAs with 2 key groups.
+// Three shapes. The tensor-core kernel (attention_tc.cuh: 128-query CTAs, tcgen05) for global
+// attention from ATTN_TC_MIN tokens (its single MMA thread serialises ~130 cycles a
+// instruction, so it only pays once the key loop is long; sliding-window layers and shorter
+// sequences measured faster on the mma.sync kernel); below, the mma.sync kernel: up to 512 tokens
+// 32-query CTAs whose 4 key groups each take every 4th key tile (the most CTAs and the shortest
+// per-warp key loop), else 64-query CTAs with 2 key groups.
 struct AttnVariant {
     int qw, ks;
+    bool tc;
 };
-static AttnVariant attn_variant(uint32_t n) { return n <= 512 ? AttnVariant{2, 4} : AttnVariant{4, 2}; }
+static uint32_t env_u32(const char *name, uint32_t dflt) {
+    const char *e = getenv(name);
+    return e ? (uint32_t)strtoul(e, nullptr, 10) : dflt;
+}
+// A/B knobs: the shortest global / sliding-window sequence for the tensor-core kernel.
+static std::atomic<uint32_t> g_attn_tc_min{env_u32("JC_ATTN_TC_MIN", 768u)};
+static std::atomic<uint32_t> g_attn_tc_min_window{env_u32("JC_ATTN_TC_MIN_WINDOW", 0xFFFFFFFFu)};
+void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
+    *global_min = g_attn_tc_min.exchange(*global_min);
+    *window_min = g_attn_tc_min_window.exchange(*window_min);
+}
+static AttnVariant attn_variant(uint32_t n, uint32_t window) {
+    if (n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load()))
+        return AttnVariant{0, 0, true};
+    return n <= 512 ? AttnVariant{2, 4, false} : AttnVariant{4, 2, false};
+}
 
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
     if (kv_chunks <= 1) return 0;
-    const AttnVariant v = attn_variant(n);
-    const uint32_t qt = 16 * v.qw;
-    return (size_t)((n + qt - 1) / qt) * heads * kv_chunks * ATTN_PART * 32 * v.qw;
+    // Enough for whichever kernel serves any length up to n.
+    size_t need = 0;
+    for (uint32_t qt : {32u, 64u})
+        need = std::max(need, (size_t)((n + qt - 1) / qt) * heads * kv_chunks * ATTN_PART * qt * 2);
+    need = std::max(need, (size_t)((n + ATC_QT - 1) / ATC_QT) * heads * kv_chunks * ATC_PART * ATC_QT);
+    return need;
+}
+
+static bool launch_attn_tc(const AttnParams &p, uint32_t chunks, cudaStream_t s, bool pdl) {
+    static std::atomic<uint64_t> smem_set{0};
+    if (!ensure_smem(attention_tc_kernel, AtcSmem::ALLOC, smem_set)) return false;
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+        return false;
+    }
+    AttnTcParams kp;
+    kp.p = p;
+    // qkv as (64 columns of a head, n rows, 3 x heads head blocks): zero fill past row n.
+    cuuint64_t dims[3] = {64, p.n, 3ull * p.heads};
+    cuuint64_t strides[2] = {3ull * p.heads * 64 * 2, 128};
+    cuuint32_t box[3] = {64, 64, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(&kp.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(p.qkv), dims,
+                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("attention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+        return false;
+    }
+    dim3 grid((p.n + ATC_QT - 1) / ATC_QT, p.heads, chunks);
+    return launch_ex(attention_tc_kernel, grid, dim3(ATC_THREADS), AtcSmem::ALLOC, s, pdl,
+                     "attention launch", kp);
 }
 
 size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32) * heads; }
@@ -386,19 +458,30 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         return false;
     }
     AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window};
-    const AttnVariant v = attn_variant(a.n);
+    const AttnVariant v = attn_variant(a.n, a.window);
+    if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     if (v.qw == 2) return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);
     return launch_attn_inst<4, 2>(p, a.kv_chunks, s, pdl);
 }
 
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) {
+    const AttnVariant v = attn_variant(n, window);
+    const uint32_t key_tiles = (n + 63) / 64;
+    if (v.tc) {
+        // Up to two CTAs per SM (the tensor-core kernel's residency), at least two key tiles a
+        // range: each extra resident CTA brings another independent MMA chain.
+        const uint32_t tiles = ((n + ATC_QT - 1) / ATC_QT) * heads;
+        const uint32_t reach = window ? (ATC_QT + 2 * window + 63) / 64 : key_tiles;
+        uint32_t c = 2 * (uint32_t)sms / (tiles ? tiles : 1);
+        c = std::min(c, reach / 2);
+        c = std::min(c, 8u);
+        return c < 1 ? 1 : c;
+    }
     // Split the keys across CTAs only when a (query tile, head) grid leaves most SMs idle and each
     // key group would still walk several key tiles.
     if (window > 0) return 1;
-    const AttnVariant v = attn_variant(n);
     const uint32_t qt = 16 * v.qw;
     const uint32_t tiles = ((n + qt - 1) / qt) * heads;
-    const uint32_t key_tiles = (n + 63) / 64;
     if (2 * tiles >= (uint32_t)sms || key_tiles <= (uint32_t)(2 * v.ks)) return 1;
     uint32_t c = (uint32_t)sms / (tiles ? tiles : 1);
     if (c > key_tiles / v.ks) c = key_tiles / v.ks;

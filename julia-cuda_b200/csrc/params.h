@@ -12,6 +12,7 @@ namespace jc {
 struct GemmParams {
     const CUtensorMap *map_a;
     const CUtensorMap *map_w;
+    const CUtensorMap *map_c;  // output tile through TMA stores (nullptr: direct stores)
     __half *c;
     const __half *res;
     float *ws;
@@ -25,6 +26,7 @@ struct GemmParams {
     uint32_t rope_stride;   // rows of the RoPE table (>= m)
     uint32_t zero_len, m, n, k;
     float eps;
+    uint32_t store_tma;     // single-GEMM kernel: the launch carries map_c
 };
 
 struct AttnParams {

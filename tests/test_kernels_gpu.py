@@ -200,6 +200,34 @@ def test_attention(jc, O, n, window):
         assert e1 < 2e-3 and e2 < 4e-3, f"n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
 
 
+@pytest.fixture(params=["mma", "tc"])
+def attn_kernel(request, jc):
+    """Both attention kernels at every length: the mma.sync one (threshold above every length)
+    and the tcgen05 one (threshold 1)."""
+    t = 0xFFFFFFFF if request.param == "mma" else 1
+    old = jc.attention_tc_min(t, t)
+    yield request.param
+    jc.attention_tc_min(*old)
+
+
+@pytest.mark.parametrize("n", [1, 2, 63, 65, 129, 200, 293, 1024])
+@pytest.mark.parametrize("window", [0, 64])
+def test_attention_both_kernels(jc, O, attn_kernel, n, window):
+    heads = 12
+    qkv = O.f16(O.normal((n, 3 * heads * 64), 3 * n + window))
+    want = O.emu_attention(qkv, n, heads, window)
+    f32 = O.attention_f32(O.f32(qkv), n, heads, window)
+    for chunks in ([1, 0, 3] if window == 0 else [1, 2]):
+        o = torch.full((n, heads * 64), float("nan"), dtype=torch.float16, device="cuda")
+        jc.attention(cuda_u16(qkv), o, heads, window, kv_chunks=chunks)
+        torch.cuda.synchronize()
+        assert jc.device_error() == 0
+        got = O.f32(host_u16(o))
+        e1, e2 = rel_err(got, O.f32(want)), rel_err(got, f32)
+        assert e1 < 2e-3 and e2 < 4e-3, \
+            f"{attn_kernel} n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
+
+
 @pytest.mark.parametrize("n,window", [(300, 8), (300, 100), (1024, 200), (700, 31)])
 def test_attention_other_windows(jc, O, n, window):
     """Windows narrower and wider than a 64-key tile: the tiles wholly inside every query's
