@@ -188,7 +188,7 @@ int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, u
 size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 size_t jc_attention_counters(uint32_t n, uint32_t heads);
 /* Which attention kernel serves a launch: the tcgen05 kernel (128-query tiles, S and P.V in
- * TMEM) for global attention from 768 tokens by default (JC_ATTN_TC_MIN), never for sliding
+ * TMEM) for global attention from 832 tokens by default (JC_ATTN_TC_MIN), never for sliding
  * windows by default (JC_ATTN_TC_MIN_WINDOW); the mma.sync kernel otherwise. Sets the shortest
  * global and window sequence lengths for the tcgen05 kernel (1: every launch; 0xFFFFFFFF:
  * never) for later launches and later-captured engine graphs, and returns the previous ones in

@@ -9,16 +9,19 @@
 // finish). Six warps:
 //   - warp 4 lane 0 streams Q once and the K and V tiles of each key tile through a 3-deep ring
 //     with TMA (qkv seen as (64 columns, rows, 3 x heads 64-column blocks), 128B swizzle, zero
-//     fill past n; no multicast);
-//   - warp 5 lane 0 issues the MMAs: S_j = Q K_j^T (M 128 queries, N 64 keys, K 64 dims) into one
-//     of two TMEM buffers, then PV_{j-1} = P_{j-1} V_{j-1} (M 128, N 64 dims, K 64 keys, V read
-//     MN-major straight from its TMA tile) into one of two more; S_{j+1} is issued before PV_j so
-//     the tensor core works on the next scores while the softmax runs;
+//     fill past n; no multicast), and issues PV_j = P_j V_j (M 128, N 64 dims, K 64 keys, V read
+//     MN-major straight from its TMA tile) into one of two TMEM buffers as soon as the softmax
+//     has written P_j;
+//   - warp 5 lane 0 issues S_j = Q K_j^T (M 128 queries, N 64 keys, K 64 dims) into one of two
+//     more as soon as K_j has landed and the softmax has read S_{j-2}: the S and PV products are
+//     two independent MMA chains;
 //   - warps 0-3, one query row per thread (TMEM lane = row): read S_j from TMEM, mask, scale, keep
 //     the running maximum and sum, write P_j = exp2(s - max) rounded to f16 into shared memory in
-//     the 128B-swizzled K-major layout the MMA reads, then fold the previous tile's PV into f32
-//     register accumulators (o = o * alpha + PV), so no accumulator is rescaled in TMEM.
-// Every wait is bounded (records a JC_DEV_TIMEOUT_* code and gives up).
+//     the 128B-swizzled K-major layout the MMA reads, then fold PV_{j-1} into f32 register
+//     accumulators (o = o * alpha + PV), so no accumulator is rescaled in TMEM.
+// The exponentials (16 per clock per SM) bound the softmax: the maximum and the sum are tree
+// reductions and the scale rides in the exponent's FMA. Every wait is bounded (records a
+// JC_DEV_TIMEOUT_* code and gives up).
 #pragma once
 #include "common.cuh"
 #include "params.h"
@@ -50,6 +53,13 @@ struct AttnTcParams {
 // Barrier among the 128 softmax threads (warps 0-3) only.
 __device__ __forceinline__ void group_bar_atc() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// 2^x on the special-function unit (PTX ex2.approx.ftz; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -75,8 +85,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + AtcSmem::BAR);
     uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = kv_full + ATC_STAGES;
     uint64_t *s_full = kv_empty + ATC_STAGES, *s_free = s_full + 2, *p_full = s_free + 2;
-    uint64_t *pv_full = p_full + 2, *pv_free = pv_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pv_free + 2);
+    uint64_t *pv_full = p_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pv_full + 2);
     uint32_t *last_flag = tmem_slot + 1;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -99,14 +109,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
         mbar_init(q_full, 1);
         for (int s = 0; s < ATC_STAGES; s++) {
             mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&kv_empty[s], 2);  // the S and the PV issuer each release a stage
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&s_full[b], 1);
             mbar_init(&s_free[b], 4);
             mbar_init(&p_full[b], 4);
             mbar_init(&pv_full[b], 1);
-            mbar_init(&pv_free[b], 4);
         }
         fence_barrier_init();
     }
@@ -123,36 +132,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
         if (lane == 0 && T > 0) {
             const int32_t hq = (int32_t)head, hk = (int32_t)(p.heads + head),
                           hv = (int32_t)(2 * p.heads + head);
-            mbar_arrive_expect_tx(q_full, 2 * AtcSmem::TILE);
-            tma_load_3d(base + AtcSmem::Q, &kp.map, q_full, 0, (int32_t)q0, hq);
-            tma_load_3d(base + AtcSmem::Q + AtcSmem::TILE, &kp.map, q_full, 0, (int32_t)q0 + 64, hq);
-            uint32_t issued = 0;
-            for (uint32_t j = 0; j < T; j++) {
-                const uint32_t s = j % ATC_STAGES, round = j / ATC_STAGES;
-                if (round > 0 && !mbar_wait(&kv_empty[s], (round - 1) & 1, JC_DEV_TIMEOUT_EMPTY)) break;
+            auto load_kv = [&](uint32_t j) {
+                const uint32_t s = j % ATC_STAGES;
                 uint8_t *st = base + AtcSmem::KV + s * 2 * AtcSmem::TILE;
                 mbar_arrive_expect_tx(&kv_full[s], 2 * AtcSmem::TILE);
                 const int32_t k0 = (int32_t)((kb0 + j) * ATC_KT);
                 tma_load_3d(st, &kp.map, &kv_full[s], 0, k0, hk);
                 tma_load_3d(st + AtcSmem::TILE, &kp.map, &kv_full[s], 0, k0, hv);
-                issued = j + 1;
-            }
-            // No copy may land after the CTA has left: wait (bounded) for the last ones.
-            mbar_wait(q_full, 0, JC_DEV_TIMEOUT_FULL);
-            for (uint32_t j = issued > (uint32_t)ATC_STAGES ? issued - ATC_STAGES : 0; j < issued; j++)
-                mbar_wait(&kv_full[j % ATC_STAGES], (j / ATC_STAGES) & 1, JC_DEV_TIMEOUT_FULL);
-        }
-    } else if (warp == 5) {
-        if (lane == 0 && T > 0) {
-            constexpr uint32_t idesc_s = umma_idesc_f16(ATC_QT, ATC_KT);
-            constexpr uint32_t idesc_o = umma_idesc_f16(ATC_QT, 64) | (1u << 16);  // B MN-major
-            const uint32_t q_a = smem_u32(base + AtcSmem::Q);
-            bool ok = mbar_wait(q_full, 0, JC_DEV_TIMEOUT_FULL);
-            auto issue_pv = [&](uint32_t i) -> bool {
-                const uint32_t b = i & 1, s = i % ATC_STAGES;
-                if (!mbar_wait(&p_full[b], (i >> 1) & 1, JC_DEV_TIMEOUT_FULL)) return false;
-                if (i >= 2 && !mbar_wait(&pv_free[b], ((i - 2) >> 1) & 1, JC_DEV_TIMEOUT_EMPTY))
-                    return false;
+            };
+            mbar_arrive_expect_tx(q_full, 2 * AtcSmem::TILE);
+            tma_load_3d(base + AtcSmem::Q, &kp.map, q_full, 0, (int32_t)q0, hq);
+            tma_load_3d(base + AtcSmem::Q + AtcSmem::TILE, &kp.map, q_full, 0, (int32_t)q0 + 64, hq);
+            uint32_t issued = 0;
+            for (; issued < T && issued < (uint32_t)ATC_STAGES; issued++) load_kv(issued);
+            constexpr uint32_t idesc_o = umma_idesc_f16(ATC_QT, 64) | (1u << 16);  // B (V) MN-major
+            for (uint32_t j = 0; j < T; j++) {
+                const uint32_t b = j & 1, s = j % ATC_STAGES;
+                // P_j written (every softmax thread had folded PV_{j-2}, whose buffer PV_j reuses,
+                // before writing it) and V_j landed.
+                if (!mbar_wait(&p_full[b], (j >> 1) & 1, JC_DEV_TIMEOUT_FULL) ||
+                    !mbar_wait(&kv_full[s], (j / ATC_STAGES) & 1, JC_DEV_TIMEOUT_FULL))
+                    break;
                 tc_fence_after();
                 const uint32_t p_a = smem_u32(base + AtcSmem::P + b * 2 * AtcSmem::TILE);
                 const uint32_t v_a = smem_u32(base + AtcSmem::KV + s * 2 * AtcSmem::TILE + AtcSmem::TILE);
@@ -163,15 +163,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
                                umma_desc_sw128_mn(v_a + kk * 2048), idesc_o, kk > 0);
                 tc_commit(&pv_full[b]);
                 tc_commit(&kv_empty[s]);
-                return true;
-            };
+                // Stage s takes tile j + STAGES once both products of tile j have read it.
+                if (issued < T) {
+                    if (!mbar_wait(&kv_empty[s], (j / ATC_STAGES) & 1, JC_DEV_TIMEOUT_EMPTY)) break;
+                    load_kv(issued++);
+                }
+            }
+            // No copy may land after the CTA has left: wait (bounded) for the last ones.
+            mbar_wait(q_full, 0, JC_DEV_TIMEOUT_FULL);
+            for (uint32_t j = issued > (uint32_t)ATC_STAGES ? issued - ATC_STAGES : 0; j < issued; j++)
+                mbar_wait(&kv_full[j % ATC_STAGES], (j / ATC_STAGES) & 1, JC_DEV_TIMEOUT_FULL);
+        }
+    } else if (warp == 5) {
+        if (lane == 0 && T > 0) {
+            constexpr uint32_t idesc_s = umma_idesc_f16(ATC_QT, ATC_KT);
+            const uint32_t q_a = smem_u32(base + AtcSmem::Q);
+            bool ok = mbar_wait(q_full, 0, JC_DEV_TIMEOUT_FULL);
             for (uint32_t j = 0; ok && j < T; j++) {
                 const uint32_t b = j & 1, s = j % ATC_STAGES;
                 if (!mbar_wait(&kv_full[s], (j / ATC_STAGES) & 1, JC_DEV_TIMEOUT_FULL) ||
-                    (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) >> 1) & 1, JC_DEV_TIMEOUT_EMPTY))) {
-                    ok = false;
+                    (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) >> 1) & 1, JC_DEV_TIMEOUT_EMPTY)))
                     break;
-                }
                 tc_fence_after();
                 const uint32_t k_a = smem_u32(base + AtcSmem::KV + s * 2 * AtcSmem::TILE);
 #pragma unroll
@@ -179,9 +191,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
                     tc_mma_f16(tmem + b * 64, umma_desc_sw128(q_a) + 2 * kk,
                                umma_desc_sw128(k_a) + 2 * kk, idesc_s, kk > 0);
                 tc_commit(&s_full[b]);
-                if (j >= 1) ok = issue_pv(j - 1);
+                tc_commit(&kv_empty[s]);
             }
-            if (ok) issue_pv(T - 1);
         }
     } else {
         // Softmax: thread = query row of the tile = TMEM lane.
@@ -198,84 +209,84 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
             const uint32_t b = i & 1;
             if (!mbar_wait(&pv_full[b], (i >> 1) & 1, JC_DEV_TIMEOUT_MMA)) return false;
             tc_fence_after();
-            float v[64];
-            tmem_ld<16>(lane_base + 128 + b * 64, v);
-            tmem_ld<16>(lane_base + 128 + b * 64 + 16, v + 16);
-            tmem_ld<16>(lane_base + 128 + b * 64 + 32, v + 32);
-            tmem_ld<16>(lane_base + 128 + b * 64 + 48, v + 48);
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pv_free[b]);
 #pragma unroll
-            for (int e = 0; e < 64; e++) o[e] = fmaf(o[e], a, v[e]);
+            for (int h = 0; h < 2; h++) {  // in halves: 32 more registers, not 64
+                float v[32];
+                tmem_ld<16>(lane_base + 128 + b * 64 + 32 * h, v);
+                tmem_ld<16>(lane_base + 128 + b * 64 + 32 * h + 16, v + 16);
+                tc_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; e++) o[32 * h + e] = fmaf(o[32 * h + e], a, v[e]);
+            }
+            tc_fence_before();
             return true;
         };
         for (uint32_t j = 0; j < T; j++) {
             const uint32_t b = j & 1;
-            if (!mbar_wait(&s_full[b], (j >> 1) & 1, JC_DEV_TIMEOUT_MMA)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            float s[64];
-            tmem_ld<16>(lane_base + b * 64, s);
-            tmem_ld<16>(lane_base + b * 64 + 16, s + 16);
-            tmem_ld<16>(lane_base + b * 64 + 32, s + 32);
-            tmem_ld<16>(lane_base + b * 64 + 48, s + 48);
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[b]);
+            float alpha = 1.f;
+            if (ok) ok = mbar_wait(&s_full[b], (j >> 1) & 1, JC_DEV_TIMEOUT_MMA);
+            if (ok) {
+                tc_fence_after();
+                float sc[64];
+                tmem_ld<16>(lane_base + b * 64, sc);
+                tmem_ld<16>(lane_base + b * 64 + 16, sc + 16);
+                tmem_ld<16>(lane_base + b * 64 + 32, sc + 32);
+                tmem_ld<16>(lane_base + b * 64 + 48, sc + 48);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[b]);
 
-            // Mask (unless every key of the tile is visible to every row of this warp), scale,
-            // running maximum.
-            const uint32_t k0 = (kb0 + j) * ATC_KT;
-            const bool interior = k0 + ATC_KT <= n &&
-                                  (window == 0 || (k0 + ATC_KT - 1 <= wq0 + window && wq0 + 31 <= k0 + window));
-            float mt = -INFINITY;
-            if (interior) {
+                // Mask (unless every key of the tile is visible to every row of this warp), then
+                // the tile's maximum in a tree (the scale is positive: max(s) * scale is the
+                // maximum of the scaled scores).
+                const uint32_t k0 = (kb0 + j) * ATC_KT;
+                const bool interior = k0 + ATC_KT <= n &&
+                                      (window == 0 || (k0 + ATC_KT - 1 <= wq0 + window && wq0 + 31 <= k0 + window));
+                if (!interior) {
+                    // This row sees keys [q - window, q + window] (all keys when global) below n:
+                    // columns [clo, chi) of the tile.
+                    const int lo_key = window ? (int)q - (int)window : 0;
+                    const int hi_key = window ? min((int)q + (int)window, (int)n - 1) : (int)n - 1;
+                    const int clo = lo_key - (int)k0, chi = hi_key - (int)k0 + 1;
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    s[c] *= scale;
-                    mt = fmaxf(mt, s[c]);
+                    for (int c = 0; c < 64; c++) sc[c] = (c >= clo && c < chi) ? sc[c] : -INFINITY;
                 }
-            } else {
+                float m8[8];
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const uint32_t key = k0 + c;
-                    const uint32_t dist = q > key ? q - key : key - q;
-                    const bool vis = key < n && (window == 0 || dist <= window);
-                    s[c] = vis ? s[c] * scale : -INFINITY;
-                    mt = fmaxf(mt, s[c]);
+                for (int c = 0; c < 8; c++) m8[c] = fmaxf(sc[c], sc[c + 8]);
+#pragma unroll
+                for (int c = 16; c < 64; c++) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
+                const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale;
+                const float m_new = fmaxf(mx, mt);
+                const float bse = m_new == -INFINITY ? 0.f : m_new;
+                alpha = ex2_approx(mx - bse);
+                mx = m_new;
+                // P row into the K-major 128B-swizzled tile, a 16-byte chunk (8 keys) at a time:
+                // chunk c at chunk c ^ (row % 8).
+                uint8_t *prow = base + AtcSmem::P + b * 2 * AtcSmem::TILE + row * 128;
+                float r8[8];
+#pragma unroll
+                for (uint32_t c = 0; c < 8; c++) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float a0 = ex2_approx(fmaf(sc[8 * c + 2 * e], scale, -bse));
+                        const float a1 = ex2_approx(fmaf(sc[8 * c + 2 * e + 1], scale, -bse));
+                        r8[2 * (e & 1) + (c & 1) * 4 + (e >> 1)] =
+                            c < 2 ? a0 + a1 : r8[2 * (e & 1) + (c & 1) * 4 + (e >> 1)] + (a0 + a1);
+                        pk[e] = pack_half2(a0, a1);
+                    }
+                    *reinterpret_cast<uint4 *>(prow + ((c ^ (row & 7)) << 4)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
+                lsum = lsum * alpha + (((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7])));
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[b]);
             }
-            const float m_new = fmaxf(mx, mt);
-            const float bse = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = exp2f(mx - bse);
-            mx = m_new;
-            float rs = 0.f;
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < 32; c++) {
-                const float a0 = exp2f(s[2 * c] - bse), a1 = exp2f(s[2 * c + 1] - bse);
-                rs += a0 + a1;
-                pk[c] = pack_half2(a0, a1);
-            }
-            lsum = lsum * alpha + rs;
-            // P row into the K-major 128B-swizzled tile: 16-byte chunk c at chunk c ^ (row % 8).
-            uint8_t *prow = base + AtcSmem::P + b * 2 * AtcSmem::TILE + row * 128;
-#pragma unroll
-            for (uint32_t c = 0; c < 8; c++)
-                *reinterpret_cast<uint4 *>(prow + ((c ^ (row & 7)) << 4)) =
-                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[b]);
-            if (j >= 1 && !fold(j - 1, alpha_prev)) {
-                ok = false;
-                break;
-            }
+            if (j >= 1 && ok) ok = fold(j - 1, alpha_prev);
             alpha_prev = alpha;
         }
         if (ok && T > 0) ok = fold(T - 1, alpha_prev);

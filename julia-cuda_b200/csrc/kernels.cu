@@ -383,7 +383,7 @@ static uint32_t env_u32(const char *name, uint32_t dflt) {
     return e ? (uint32_t)strtoul(e, nullptr, 10) : dflt;
 }
 // A/B knobs: the shortest global / sliding-window sequence for the tensor-core kernel.
-static std::atomic<uint32_t> g_attn_tc_min{env_u32("JC_ATTN_TC_MIN", 768u)};
+static std::atomic<uint32_t> g_attn_tc_min{env_u32("JC_ATTN_TC_MIN", 832u)};
 static std::atomic<uint32_t> g_attn_tc_min_window{env_u32("JC_ATTN_TC_MIN_WINDOW", 0xFFFFFFFFu)};
 void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
     *global_min = g_attn_tc_min.exchange(*global_min);
@@ -468,14 +468,22 @@ uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) 
     const AttnVariant v = attn_variant(n, window);
     const uint32_t key_tiles = (n + 63) / 64;
     if (v.tc) {
-        // Up to two CTAs per SM (the tensor-core kernel's residency), at least two key tiles a
-        // range: each extra resident CTA brings another independent MMA chain.
+        // Up to two CTAs per SM (the kernel's residency: each brings two more independent MMA
+        // chains), at least two key tiles a range: the range count that minimises waves x key
+        // tiles per range, ties to fewer ranges (whose merge is cheaper).
         const uint32_t tiles = ((n + ATC_QT - 1) / ATC_QT) * heads;
-        const uint32_t reach = window ? (ATC_QT + 2 * window + 63) / 64 : key_tiles;
-        uint32_t c = 2 * (uint32_t)sms / (tiles ? tiles : 1);
-        c = std::min(c, reach / 2);
-        c = std::min(c, 8u);
-        return c < 1 ? 1 : c;
+        const uint32_t reach = std::min(key_tiles, window ? (ATC_QT + 2 * window + 63) / 64 + 1 : key_tiles);
+        uint32_t best = 1, best_cost = ~0u;
+        for (uint32_t c = 1; c <= 8; c++) {
+            if (c > 1 && reach < 2 * c) break;
+            const uint32_t waves = (tiles * c + 2 * (uint32_t)sms - 1) / (2 * (uint32_t)sms);
+            const uint32_t cost = waves * ((reach + c - 1) / c);
+            if (cost < best_cost) {
+                best_cost = cost;
+                best = c;
+            }
+        }
+        return best;
     }
     // Split the keys across CTAs only when a (query tile, head) grid leaves most SMs idle and each
     // key group would still walk several key tiles.
