@@ -334,14 +334,13 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
             for (size_t i = c0; i < c1; i++) {
                 const int slot = (int)(i - c0);
                 const size_t n = lens[i], k = n_markers[i];
-                std::memcpy(e->h_ids + slot * L, ids + at_id, n * 4);
-                std::memcpy(e->h_markers + slot * L, markers + at_mk, k * 4);
+                // ids at [0, n) and markers at [L, L + k) of the slot, as on the device: one copy.
+                uint32_t *stage = e->h_ids + slot * 2 * L;
+                std::memcpy(stage, ids + at_id, n * 4);
+                std::memcpy(stage + L, markers + at_mk, k * 4);
                 mk_at[slot] = at_mk;
-                bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, e->h_ids + slot * L, n * 4,
-                                                      cudaMemcpyHostToDevice, s), "ids") &&
-                          (k == 0 || jc::cuda_ok(cudaMemcpyAsync(e->markers, e->h_markers + slot * L,
-                                                                 k * 4, cudaMemcpyHostToDevice, s),
-                                                 "markers")) &&
+                bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, stage, (k ? L + k : n) * 4,
+                                                      cudaMemcpyHostToDevice, s), "ids and markers") &&
                           jc::cuda_ok(cudaEventRecord(e->ev_start[slot], s), "event") &&
                           e->launch_forward((uint32_t)n, (uint32_t)k, qtypes[i], layer_fused, s) &&
                           jc::cuda_ok(cudaEventRecord(e->ev_end[slot], s), "event") &&
@@ -356,12 +355,13 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                 at_id += n;
                 at_mk += k;
             }
-            if (!jc::cuda_ok(cudaStreamSynchronize(s), "run")) {
+            if (!jc::enqueue_device_error_read(e->h_err, s) ||
+                !jc::cuda_ok(cudaStreamSynchronize(s), "run")) {
                 report(err, err_len, std::string("run: ") + jc::last_error());
                 return -1;
             }
             std::string why;
-            if (!e->check_device_error(&why)) {
+            if (!e->check_device_error_copy(&why)) {
                 report(err, err_len, "run: " + why);
                 return -1;
             }

@@ -40,8 +40,8 @@ Engine::~Engine() {
     }
     for (void *p : allocations) cudaFree(p);
     if (h_ids) cudaFreeHost(h_ids);
-    if (h_markers) cudaFreeHost(h_markers);
     if (h_logits) cudaFreeHost(h_logits);
+    if (h_err) cudaFreeHost(h_err);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -119,9 +119,10 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&hx, rows * D * 2) && dalloc((void **)&xs, rows * D * 2) &&
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
-              dalloc((void **)&ids, L * 4) && dalloc((void **)&markers, L * 4) &&
+              dalloc((void **)&ids, 2 * L * 4) &&
               dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4);
     if (!ok) return false;
+    markers = ids + L;
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
     const size_t widest = std::max({3 * D, 2 * I, F, S});
     gemm_ws_cap = rows * widest * 8;
@@ -182,9 +183,9 @@ bool Engine::init(const float *raw, std::string *why) {
         return false;
     persist_grid = (uint32_t)(sms * std::max(0, persist_blocks_per_sm()));
 
-    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * L * 4), "cudaMallocHost") ||
-        !cu(cudaMallocHost((void **)&h_markers, QUEUE * L * 4), "cudaMallocHost") ||
-        !cu(cudaMallocHost((void **)&h_logits, QUEUE * L * 4), "cudaMallocHost"))
+    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * 2 * L * 4), "cudaMallocHost") ||
+        !cu(cudaMallocHost((void **)&h_logits, QUEUE * L * 4), "cudaMallocHost") ||
+        !cu(cudaMallocHost((void **)&h_err, sizeof(unsigned int)), "cudaMallocHost"))
         return false;
     for (int i = 0; i < QUEUE; i++)
         if (!cu(cudaEventCreate(&ev_start[i]), "cudaEventCreate") ||
@@ -552,6 +553,12 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
             if (entry.descs) cudaFree(entry.descs);
             return false;
         }
+        // Upload once now, so later launches do not carry the graph's upload.
+        if (!cuda_ok(cudaGraphUpload(entry.exec, s), "graph upload")) {
+            cudaGraphExecDestroy(entry.exec);
+            if (entry.descs) cudaFree(entry.descs);
+            return false;
+        }
         if ((int)graphs.size() >= GRAPH_CACHE) {
             GraphKey old = graph_lru.back();
             graph_lru.pop_back();
@@ -567,6 +574,19 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
         graph_lru.splice(graph_lru.begin(), graph_lru, it->second.lru);
     }
     return cuda_ok(cudaGraphLaunch(it->second.exec, s), "graph launch");
+}
+
+bool Engine::check_device_error_copy(std::string *why) {
+    const unsigned int code = *h_err;
+    if (!code) return true;
+    if (!clear_device_error()) {
+        *why = last_error();
+        return false;
+    }
+    cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4);
+    cudaDeviceSynchronize();
+    *why = std::string("device error: ") + device_error_name(code);
+    return false;
 }
 
 bool Engine::check_device_error(std::string *why) {

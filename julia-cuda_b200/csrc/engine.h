@@ -80,8 +80,13 @@ class Engine {
     float *logits = nullptr;
     // pinned staging for julia_cuda_run
     static constexpr int QUEUE = 16;
-    uint32_t *h_ids = nullptr, *h_markers = nullptr;  // QUEUE slots of max_length
+    // QUEUE slots of 2 x max_length words: the ids, then the markers (the device buffers `ids`
+    // and `markers` are one allocation in the same layout, so a request is one copy)
+    uint32_t *h_ids = nullptr;
     float *h_logits = nullptr;
+    unsigned int *h_err = nullptr;  // the device error word, copied after each queue of requests
+    // The error word copied into h_err (the stream has synchronised since): 0, or the reason.
+    bool check_device_error_copy(std::string *why);
     cudaEvent_t ev_start[QUEUE] = {}, ev_end[QUEUE] = {};
 
    private:

@@ -126,6 +126,10 @@ bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const u
 
 // The device error word: read (and clear) it.
 bool read_device_error(unsigned int *code);
+// Queues a copy of the device error word into pinned host memory on stream s (read it after the
+// stream has synchronised), and clears it (synchronous).
+bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s);
+bool clear_device_error();
 const char *device_error_name(unsigned int code);
 
 // ---------------------------------------------------------------------------------------------

@@ -35,6 +35,17 @@ bool read_device_error(unsigned int *code) {
     return true;
 }
 
+bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s) {
+    return cuda_ok(cudaMemcpyFromSymbolAsync(pinned, g_dev_error, sizeof(unsigned int), 0,
+                                             cudaMemcpyDeviceToHost, s),
+                   "read error word");
+}
+
+bool clear_device_error() {
+    unsigned int zero = 0;
+    return cuda_ok(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(zero)), "clear error word");
+}
+
 const char *device_error_name(unsigned int code) {
     switch (code) {
         case 0: return "none";
