@@ -372,28 +372,52 @@ class Engine:
         lib().julia_cuda_device(self._h, buf, 256)
         return buf.value.decode()
 
+    def _staging(self, n_ids: int, n_mk: int, b: int):
+        """Per-engine argument arrays for julia_cuda_run, grown on demand; their addresses are
+        taken once (numpy's .ctypes costs microseconds a call, a sizeable share of a request)."""
+        st = getattr(self, "_st", None)
+        if st is None or st["ids"].size < n_ids or st["mk"].size < max(n_mk, 1) or st["lens"].size < b:
+            cap = lambda x, old: max(x, 2 * old)  # noqa: E731
+            old = st or {"ids": np.zeros(0), "mk": np.zeros(0), "lens": np.zeros(0)}
+            st = {"ids": np.zeros(cap(n_ids, old["ids"].size), np.uint32),
+                  "mk": np.zeros(cap(max(n_mk, 1), old["mk"].size), np.uint32),
+                  "logits": np.zeros(cap(max(n_mk, 1), old["mk"].size), np.float32)}
+            nb = cap(b, old["lens"].size)
+            st.update(lens=np.zeros(nb, np.uint64), nmk=np.zeros(nb, np.uint64),
+                      qt=np.zeros(nb, np.uint32), gpu_ms=np.zeros(nb, np.float32),
+                      err=ctypes.create_string_buffer(1024))
+            st["ptr"] = {k: v.ctypes.data for k, v in st.items() if isinstance(v, np.ndarray)}
+            self._st = st
+        return st
+
     def run(self, seqs, layer_fused: int = 0):
         """seqs: list of (ids, markers, qtype). Returns (list of logits arrays, gpu_ms array).
         layer_fused: 0 per-step kernels, 1 one persistent launch per layer, 2 whole model."""
-        ids = np.ascontiguousarray(np.concatenate([np.asarray(s[0], np.uint32) for s in seqs]))
-        lens = np.array([len(s[0]) for s in seqs], np.uint64)
-        mk = [np.asarray(s[1], np.uint32) for s in seqs]
-        markers = np.ascontiguousarray(np.concatenate(mk) if mk else np.zeros(0, np.uint32))
-        nmk = np.array([len(m) for m in mk], np.uint64)
-        qt = np.array([s[2] for s in seqs], np.uint32)
-        logits = np.zeros(max(int(nmk.sum()), 1), np.float32)
-        gpu_ms = np.zeros(len(seqs), np.float32)
-        err = ctypes.create_string_buffer(1024)
-        rc = lib().julia_cuda_run(self._h, len(seqs), _np_ptr(ids), _np_ptr(lens),
-                                  _np_ptr(markers), _np_ptr(nmk), _np_ptr(qt), int(layer_fused),
-                                  _np_ptr(logits), _np_ptr(gpu_ms), err, 1024)
+        b = len(seqs)
+        n_ids = sum(len(s[0]) for s in seqs)
+        n_mk = sum(len(s[1]) for s in seqs)
+        st = self._staging(n_ids, n_mk, b)
+        at_i = at_m = 0
+        for i, (ids, mk, qt) in enumerate(seqs):
+            n, k = len(ids), len(mk)
+            st["ids"][at_i:at_i + n] = ids
+            st["mk"][at_m:at_m + k] = mk
+            st["lens"][i], st["nmk"][i], st["qt"][i] = n, k, qt
+            at_i += n
+            at_m += k
+        ptr = st["ptr"]
+        rc = lib().julia_cuda_run(self._h, b, ptr["ids"], ptr["lens"], ptr["mk"], ptr["nmk"],
+                                  ptr["qt"], int(layer_fused), ptr["logits"], ptr["gpu_ms"],
+                                  st["err"], 1024)
         if rc != 0:
-            raise JuliaCudaError(err.value.decode(errors="replace"))
+            raise JuliaCudaError(st["err"].value.decode(errors="replace"))
         out, at = [], 0
-        for k in nmk:
-            out.append(logits[at:at + int(k)].copy())
-            at += int(k)
-        return out, gpu_ms
+        logits = st["logits"]
+        for s in seqs:
+            k = len(s[1])
+            out.append(logits[at:at + k].copy())
+            at += k
+        return out, st["gpu_ms"][:b].copy()
 
     def forward_device(self, ids, markers, qtype: int, logits, trace=None, layer_fused=False,
                        stream=None) -> None:
