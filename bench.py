@@ -280,6 +280,48 @@ def sweep_arm(args, rank, local):
     print(json.dumps({"sweep": "clocks", "clocks": clk.summary()}), flush=True)
 
 
+def one_kernel_arm(args, local):
+    """Launches one kernel of the forward pass (a GEMM shape or an attention mode) at --seq tokens,
+    --warmup + --steps times with the inputs of time_kernels, then synchronises: a small, fixed
+    workload for ncu captures (`-k regex:<kernel> -s <warmup> -c <n>`). Prints what it ran."""
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    from oracle import oracle as O
+    cfg = jc.default_config(max_positions=1024)
+    n = args.seq
+    torch.manual_seed(n)
+    shapes = {name: (epi, N, K) for name, epi, N, K, _ in gemm_shapes(cfg, n)}
+    if args.one in shapes:
+        epi_name, N, K = shapes[args.one]
+        epi = jc.EPILOGUES[epi_name]
+        a = torch.randn(n, K, device="cuda").half()
+        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        c = torch.randn(n, N // 2 if epi & jc.EPI_GEGLU else N, device="cuda").half()
+        st = torch.rand(2 * n, device="cuda") + 1.0
+        st[1::2] += 800.0
+        cs, bias, so = torch.randn(N, device="cuda"), torch.randn(N, device="cuda"), torch.zeros(2 * n, device="cuda")
+        rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
+        ws, cnt = jc.gemm_scratch(n, N, K)
+
+        def launch():
+            jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st, colsum=cs,
+                    stats_out=so, rope=rope, bias=bias, ws=ws, counters=cnt)
+    else:
+        window = {"attn_global": 0, "attn_window": cfg.window}[args.one]
+        heads = cfg.n_heads
+        qkv = torch.randn(n, 3 * heads * 64, device="cuda").half()
+        o = torch.zeros(n, heads * 64, device="cuda").half()
+
+        def launch():
+            jc.attention(qkv, o, heads, window)
+    for _ in range(args.warmup + args.steps):
+        launch()
+    torch.cuda.synchronize()
+    assert jc.device_error() == 0
+    print(json.dumps({"one": args.one, "tokens": n, "launches": args.warmup + args.steps}), flush=True)
+
+
 def reference_arm(args, rank, world):
     """The reference's CPU path (restated: the oracle's f32 forward) on all host cores."""
     if rank != 0:
@@ -381,6 +423,9 @@ def main():
     ap.add_argument("--requests", type=int, default=4096)
     ap.add_argument("--sweep", action="store_true",
                     help="configs 1-2 instead of the headline: each GEMM and attention alone")
+    ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
+                                      "attn_global", "attn_window"],
+                    help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")
     args = ap.parse_args()
     replicas = importlib.import_module("julia-cuda_b200.replicas")
     rank, world, local = replicas.rank_env()
@@ -392,6 +437,10 @@ def main():
         return
     if args.sweep:
         sweep_arm(args, rank, local)
+        return
+    if args.one:
+        if rank == 0:
+            one_kernel_arm(args, local)
         return
 
     import torch
