@@ -375,20 +375,33 @@ def serving_arm(args, rank, world, local, replicas):
     eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
     reqs = replicas.serving_requests(args.requests, SEED, cfg.vocab)
     mine = [reqs[i] for i in replicas.shard_lpt([len(r[0]) for r in reqs], world)[rank]]
-    # Warm-up: one request of every length this rank will see, so each shape's CUDA graph is
-    # captured before the timed pass (a long-running server keeps them).
-    seen = {}
-    for r in mine:
-        seen.setdefault(len(r[0]), r)
-    warm = list(seen.values())
-    for i in range(0, len(warm), 16):
-        eng.run(warm[i:i + 16])
+    batch = 16
+    if args.pack:
+        # Requests packed into forwards of up to --pack tokens (julia_cuda_set_packing); one
+        # call queues up to 16 forwards.
+        eng.set_packing(args.pack)
+        batch = 64
+        warm = mine  # the pack shapes this share makes
+    else:
+        # One request of every length this rank will see.
+        seen = {}
+        for r in mine:
+            seen.setdefault(len(r[0]), r)
+        warm = list(seen.values())
+    # Warm-up: every CUDA graph shape the timed pass needs is captured first (a long-running
+    # server keeps them).
+    for i in range(0, len(warm), batch):
+        eng.run(warm[i:i + batch])
     replicas.barrier(world)
     t0 = time.perf_counter()
     gpu_ms = 0.0
-    for i in range(0, len(mine), 16):
-        _, ms = eng.run(mine[i:i + 16])
-        gpu_ms += float(np.sum(ms))
+    for i in range(0, len(mine), batch):
+        _, ms = eng.run(mine[i:i + batch])
+        prev = None
+        for v in ms:  # the requests of a packed forward are consecutive and report its time
+            if not args.pack or v != prev:
+                gpu_ms += float(v)
+            prev = v
     wall = time.perf_counter() - t0
     slowest = replicas.max_over_ranks(wall, world, device="cuda")
     if rank == 0:
@@ -400,7 +413,9 @@ def serving_arm(args, rank, world, local, replicas):
             "scaling": "strong", "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
             "config": {"workload": "config3: log-normal lengths (sigma 0.5, mean 293, [32, 1024]), "
                                    "4 markers, qtype 0, seed 1234", "partition": "LPT by cost",
-                       "path": "julia_cuda_run, per-step kernels, batches of 16"}}), flush=True)
+                       "path": "julia_cuda_run, per-step kernels, " + (
+                           f"requests packed into forwards of up to {args.pack} tokens, {batch} a call"
+                           if args.pack else "one forward per request, 16 a call")}}), flush=True)
     eng.close()
     replicas.finalize(world)
 
@@ -421,6 +436,8 @@ def main():
     ap.add_argument("--serving", action="store_true",
                     help="config 3 instead of the headline: a seeded request set served end to end")
     ap.add_argument("--requests", type=int, default=4096)
+    ap.add_argument("--pack", type=int, default=0,
+                    help="--serving: pack requests into forwards of up to this many tokens")
     ap.add_argument("--sweep", action="store_true",
                     help="configs 1-2 instead of the headline: each GEMM and attention alone")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",

@@ -129,6 +129,16 @@ int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint
  * the reference. Returns 0, or -1 for a NULL engine. */
 int julia_cuda_set_head_length(JcEngine *engine, size_t rows);
 
+/* Packs requests for throughput: julia_cuda_run then runs consecutive requests of one question
+ * type as one forward of up to `rows` tokens (at most the engine's max_length; 0, the default,
+ * runs each request alone as the reference does). Inside a packed forward every request attends
+ * only to its own tokens and its RoPE positions start at 0, so each request's logits are its
+ * own; gpu_ms reports the packed forward's time for each of its requests. Not combined with a
+ * head length (requests then run alone). Returns 0, or -1 for a NULL engine or rows above
+ * max_length. No counterpart in the reference (its engine runs requests one by one,
+ * src/engine.rs:170-196). */
+int julia_cuda_set_packing(JcEngine *engine, size_t rows);
+
 /* How many kernels one forward pass launches (for launch accounting). */
 int julia_cuda_launches_per_forward(const JcEngine *engine, uint32_t n, uint32_t n_markers,
                                     int layer_fused);

@@ -97,6 +97,7 @@ def lib():
         "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
         "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
         "julia_cuda_set_head_length": ([P, sz], i32),
+        "julia_cuda_set_packing": ([P, sz], i32),
         "julia_cuda_barrier_timeout_probe": ([P, u64, P, P, sz], i32),
         "julia_cuda_engine_config": ([P, cfgp, P, P, P], i32),
         "jc_gemm": ([u32, i32, i32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32, f32, P, P, P],
@@ -428,6 +429,11 @@ class Engine:
                                              1024)
         if rc != 0:
             raise JuliaCudaError(err.value.decode(errors="replace"))
+
+    def set_packing(self, rows: int) -> None:
+        """run() packs consecutive requests into forwards of up to `rows` tokens (0: off)."""
+        if lib().julia_cuda_set_packing(self._h, rows) != 0:
+            raise JuliaCudaError("set_packing: no engine, or rows above max_length")
 
     def set_head_length(self, rows: int) -> None:
         """The head runs on the first `rows` rows of later requests (0: all rows)."""

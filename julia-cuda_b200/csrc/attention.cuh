@@ -116,14 +116,13 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
     const uint32_t q0 = q_tile * QT;
     const uint32_t n = p.n, window = p.window;
 
-    // Key tiles some query of this CTA can reach, this CTA's range of them, this group's share.
-    const uint32_t nb = (n + 63) / 64;
-    uint32_t kb_lo = 0, kb_hi = nb;
-    if (window > 0) {
-        kb_lo = (q0 > window ? q0 - window : 0) / 64;
-        const uint32_t last_q = min(q0 + QT - 1, n - 1);
-        kb_hi = min(last_q + window, n - 1) / 64 + 1;
-    }
+    // Key tiles some query of this CTA can reach (the spans of its first and last query bound
+    // those of the others), this CTA's range of them, this group's share.
+    int lo_first, hi_first, lo_last, hi_last;
+    key_span(p.seg, n, window, q0, lo_first, hi_first);
+    key_span(p.seg, n, window, min(q0 + QT - 1, n - 1), lo_last, hi_last);
+    const uint32_t kb_lo = (uint32_t)max(lo_first, 0) / 64;
+    const uint32_t kb_hi = (uint32_t)max(hi_last, lo_first) / 64 + 1;
     const uint32_t span = kb_hi - kb_lo;
     const uint32_t kb0 = kb_lo + chunk * span / chunks, kb1 = kb_lo + (chunk + 1) * span / chunks;
     const uint32_t my_n = kb1 > kb0 + grp ? (kb1 - kb0 - grp + KS - 1) / KS : 0;
@@ -155,6 +154,12 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
 
     const float scale = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
     const uint32_t qrow[2] = {q0 + qw * 16 + g, q0 + qw * 16 + g + 8};
+    // This lane's two rows' key spans, and the keys every row of the warp sees.
+    int row_lo[2], row_hi[2], w_lo, w_hi, unused;
+    key_span(p.seg, n, window, qrow[0], row_lo[0], row_hi[0]);
+    key_span(p.seg, n, window, qrow[1], row_lo[1], row_hi[1]);
+    key_span(p.seg, n, window, q0 + qw * 16 + 15, w_lo, unused);
+    key_span(p.seg, n, window, q0 + qw * 16, unused, w_hi);
     float mx[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
     float acc[8][4];
 #pragma unroll
@@ -190,12 +195,10 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
         }
 
         // Mask, scale and the online softmax. Row h of this lane: elements 2h, 2h+1 of each tile.
-        // A tile every key of which every query of this warp may see (inside the sequence and,
-        // in a window layer, within the window of the warp's first and last query) needs no mask.
+        // A tile every key of which every query of this warp may see (inside the spans of the
+        // warp's first and last query, which bound the others') needs no mask.
         const uint32_t k0 = kb_of(j) * 64;
-        const uint32_t wq0 = q0 + qw * 16;
-        const bool interior = k0 + 64 <= n &&
-                              (window == 0 || (k0 + 63 <= wq0 + window && wq0 + 15 <= k0 + window));
+        const bool interior = (int)k0 >= w_lo && (int)k0 + 63 <= w_hi;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             float m = -INFINITY;
@@ -213,10 +216,8 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
                 for (int jt = 0; jt < 8; jt++)
 #pragma unroll
                     for (int e = 0; e < 2; e++) {
-                        const uint32_t key = k0 + 8 * jt + 2 * t + e;
-                        const uint32_t qq = qrow[h];
-                        const uint32_t dist = qq > key ? qq - key : key - qq;
-                        const bool ok = key < n && (window == 0 || dist <= window);
+                        const int key = (int)(k0 + 8 * jt + 2 * t + e);
+                        const bool ok = key >= row_lo[h] && key <= row_hi[h];
                         const float v = ok ? s[jt][2 * h + e] * scale : -INFINITY;
                         s[jt][2 * h + e] = v;
                         m = fmaxf(m, v);

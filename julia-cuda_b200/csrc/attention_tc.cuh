@@ -93,14 +93,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
     const uint32_t q_tile = blockIdx.x, head = blockIdx.y, chunk = blockIdx.z, chunks = gridDim.z;
     const uint32_t q0 = q_tile * ATC_QT, n = p.n, window = p.window;
 
-    // The key tiles some query of this CTA can reach, and this CTA's range of them.
-    const uint32_t nb = (n + ATC_KT - 1) / ATC_KT;
-    uint32_t kb_lo = 0, kb_hi = nb;
-    if (window > 0) {
-        kb_lo = (q0 > window ? q0 - window : 0) / ATC_KT;
-        const uint32_t last_q = min(q0 + ATC_QT - 1, n - 1);
-        kb_hi = min(last_q + window, n - 1) / ATC_KT + 1;
-    }
+    // The key tiles some query of this CTA can reach (the spans of its first and last query
+    // bound the others'), and this CTA's range of them.
+    int lo_first, hi_first, lo_last, hi_last;
+    key_span(p.seg, n, window, q0, lo_first, hi_first);
+    key_span(p.seg, n, window, min(q0 + ATC_QT - 1, n - 1), lo_last, hi_last);
+    const uint32_t kb_lo = (uint32_t)max(lo_first, 0) / ATC_KT;
+    const uint32_t kb_hi = (uint32_t)max(hi_last, lo_first) / ATC_KT + 1;
     const uint32_t span = kb_hi - kb_lo;
     const uint32_t kb0 = kb_lo + chunk * span / chunks;
     const uint32_t T = kb_lo + (chunk + 1) * span / chunks - kb0;
@@ -198,7 +197,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
         // Softmax: thread = query row of the tile = TMEM lane.
         const uint32_t row = threadIdx.x, q = q0 + row;
         const uint32_t lane_base = tmem + ((warp * 32) << 16);
-        const uint32_t wq0 = q0 + warp * 32;
+        // This row's key span, and the keys every row of the warp sees.
+        int row_lo, row_hi, w_lo, w_hi, unused;
+        key_span(p.seg, n, window, q, row_lo, row_hi);
+        key_span(p.seg, n, window, q0 + warp * 32 + 31, w_lo, unused);
+        key_span(p.seg, n, window, q0 + warp * 32, unused, w_hi);
         const float scale = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
         float o[64];
 #pragma unroll
@@ -241,14 +244,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
                 // the tile's maximum in a tree (the scale is positive: max(s) * scale is the
                 // maximum of the scaled scores).
                 const uint32_t k0 = (kb0 + j) * ATC_KT;
-                const bool interior = k0 + ATC_KT <= n &&
-                                      (window == 0 || (k0 + ATC_KT - 1 <= wq0 + window && wq0 + 31 <= k0 + window));
+                const bool interior = (int)k0 >= w_lo && (int)k0 + ATC_KT - 1 <= w_hi;
                 if (!interior) {
-                    // This row sees keys [q - window, q + window] (all keys when global) below n:
-                    // columns [clo, chi) of the tile.
-                    const int lo_key = window ? (int)q - (int)window : 0;
-                    const int hi_key = window ? min((int)q + (int)window, (int)n - 1) : (int)n - 1;
-                    const int clo = lo_key - (int)k0, chi = hi_key - (int)k0 + 1;
+                    // This row sees keys [row_lo, row_hi]: columns [clo, chi) of the tile.
+                    const int clo = row_lo - (int)k0, chi = row_hi - (int)k0 + 1;
 #pragma unroll
                     for (int c = 0; c < 64; c++) sc[c] = (c >= clo && c < chi) ? sc[c] : -INFINITY;
                 }

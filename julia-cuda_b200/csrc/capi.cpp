@@ -212,6 +212,12 @@ int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_
     return 0;
 }
 
+int julia_cuda_set_packing(JcEngine *engine, size_t rows) {
+    if (!engine || rows > engine->e->max_length) return -1;
+    engine->e->pack_rows = rows;
+    return 0;
+}
+
 int julia_cuda_set_head_length(JcEngine *engine, size_t rows) {
     if (!engine) return -1;
     engine->e->head_length = rows;
@@ -326,34 +332,78 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
         }
         const size_t L = e->max_length;
         cudaStream_t s = e->stream;
+        // Forwards: each request alone, or (packing on, no head length) consecutive requests of
+        // one question type packed while their rows fit pack_rows and their markers L.
+        struct Forward {
+            size_t first, last, rows, marks, id0, mk0;
+        };
+        std::vector<Forward> fwd;
+        const bool pack = e->pack_rows > 0 && e->head_length == 0;
         at_id = at_mk = 0;
+        for (size_t i = 0; i < b; i++) {
+            Forward *f = fwd.empty() ? nullptr : &fwd.back();
+            if (pack && f && qtypes[f->first] == qtypes[i] && f->rows + lens[i] <= e->pack_rows &&
+                f->marks + n_markers[i] <= L) {
+                f->last = i + 1;
+                f->rows += lens[i];
+                f->marks += n_markers[i];
+            } else {
+                fwd.push_back(Forward{i, i + 1, lens[i], n_markers[i], at_id, at_mk});
+            }
+            at_id += lens[i];
+            at_mk += n_markers[i];
+        }
         size_t out_at = 0;
-        for (size_t c0 = 0; c0 < b; c0 += jc::Engine::QUEUE) {
-            const size_t c1 = std::min(b, c0 + (size_t)jc::Engine::QUEUE);
-            size_t mk_at[jc::Engine::QUEUE];
-            for (size_t i = c0; i < c1; i++) {
-                const int slot = (int)(i - c0);
-                const size_t n = lens[i], k = n_markers[i];
-                // ids at [0, n) and markers at [L, L + k) of the slot, as on the device: one copy.
-                uint32_t *stage = e->h_ids + slot * 2 * L;
-                std::memcpy(stage, ids + at_id, n * 4);
-                std::memcpy(stage + L, markers + at_mk, k * 4);
-                mk_at[slot] = at_mk;
-                bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, stage, (k ? L + k : n) * 4,
-                                                      cudaMemcpyHostToDevice, s), "ids and markers") &&
+        for (size_t c0 = 0; c0 < fwd.size(); c0 += jc::Engine::QUEUE) {
+            const size_t c1 = std::min(fwd.size(), c0 + (size_t)jc::Engine::QUEUE);
+            for (size_t fi = c0; fi < c1; fi++) {
+                const Forward &f = fwd[fi];
+                const int slot = (int)(fi - c0);
+                const bool packed = f.last - f.first > 1;
+                // ids at [0, rows), markers at [L, L + marks) (rows of the packed forward), and
+                // for packed forwards each row's request rows at [2L, 2L + 2 rows): as on the
+                // device, so the forward's inputs are one copy.
+                // Packed forwards are padded to 64-row / 8-marker buckets (padding rows form a
+                // segment of their own, padding markers read row 0 and are dropped), so a few
+                // CUDA graphs serve every pack.
+                const size_t rows = packed ? std::min(L, (f.rows + 63) / 64 * 64) : f.rows;
+                const size_t marks = packed ? std::min(L, (f.marks + 7) / 8 * 8) : f.marks;
+                uint32_t *stage = e->h_ids + slot * 4 * L;
+                std::memcpy(stage, ids + f.id0, f.rows * 4);
+                uint32_t row = 0, mk = 0;
+                size_t m_src = f.mk0;  // request i's markers: markers[m_src, m_src + n_markers[i])
+                for (size_t i = f.first; i < f.last; i++) {
+                    const uint32_t n = (uint32_t)lens[i];
+                    for (size_t j = 0; j < n_markers[i]; j++) stage[L + mk++] = row + markers[m_src + j];
+                    m_src += n_markers[i];
+                    if (packed)
+                        for (uint32_t r = 0; r < n; r++) {
+                            stage[2 * L + 2 * (row + r)] = row;
+                            stage[2 * L + 2 * (row + r) + 1] = row + n;
+                        }
+                    row += n;
+                }
+                for (size_t r = f.rows; r < rows; r++) {
+                    stage[r] = 0;
+                    stage[2 * L + 2 * r] = (uint32_t)f.rows;
+                    stage[2 * L + 2 * r + 1] = (uint32_t)rows;
+                }
+                for (size_t j = f.marks; j < marks; j++) stage[L + j] = 0;
+                const size_t words = packed ? 2 * L + 2 * rows : (f.marks ? L + f.marks : f.rows);
+                bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, stage, words * 4, cudaMemcpyHostToDevice,
+                                                      s), "ids and markers") &&
                           jc::cuda_ok(cudaEventRecord(e->ev_start[slot], s), "event") &&
-                          e->launch_forward((uint32_t)n, (uint32_t)k, qtypes[i], layer_fused, s) &&
+                          e->launch_forward((uint32_t)rows, (uint32_t)marks, qtypes[f.first],
+                                            layer_fused, s, packed) &&
                           jc::cuda_ok(cudaEventRecord(e->ev_end[slot], s), "event") &&
-                          (k == 0 || jc::cuda_ok(cudaMemcpyAsync(e->h_logits + slot * L, e->logits,
-                                                                 k * 4, cudaMemcpyDeviceToHost, s),
-                                                 "logits"));
+                          (f.marks == 0 || jc::cuda_ok(cudaMemcpyAsync(e->h_logits + slot * L, e->logits,
+                                                                       f.marks * 4, cudaMemcpyDeviceToHost, s),
+                                                       "logits"));
                 if (!ok) {
                     cudaStreamSynchronize(s);
                     report(err, err_len, std::string("run: ") + jc::last_error());
                     return -1;
                 }
-                at_id += n;
-                at_mk += k;
             }
             if (!jc::enqueue_device_error_read(e->h_err, s) ||
                 !jc::cuda_ok(cudaStreamSynchronize(s), "run")) {
@@ -365,10 +415,10 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                 report(err, err_len, "run: " + why);
                 return -1;
             }
-            for (size_t i = c0; i < c1; i++) {
-                const int slot = (int)(i - c0);
-                const size_t k = n_markers[i];
-                for (size_t j = 0; j < k; j++) {
+            for (size_t fi = c0; fi < c1; fi++) {
+                const Forward &f = fwd[fi];
+                const int slot = (int)(fi - c0);
+                for (size_t j = 0; j < f.marks; j++) {
                     const float v = e->h_logits[slot * L + j];
                     if (!std::isfinite(v)) {
                         report(err, err_len, "run: inference returned nonfinite logits");
@@ -376,11 +426,10 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                     }
                     logits[out_at + j] = v;
                 }
-                (void)mk_at;
-                out_at += k;
+                out_at += f.marks;
                 float ms = 0.f;
                 cudaEventElapsedTime(&ms, e->ev_start[slot], e->ev_end[slot]);
-                gpu_ms[i] = ms;
+                for (size_t i = f.first; i < f.last; i++) gpu_ms[i] = ms;  // a packed forward's time
             }
         }
         return 0;

@@ -292,6 +292,24 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
 // ---------------------------------------------------------------------------------------------
 // misc
 
+// The keys query row q may see, [lo, hi] inclusive: its request's rows (seg[q] for packed
+// requests, else [0, n)) and, with a window, those within `window` of q.
+__device__ __forceinline__ void key_span(const uint2 *seg, uint32_t n, uint32_t window, uint32_t q,
+                                         int &lo, int &hi) {
+    int s0 = 0, s1 = (int)n;
+    if (seg) {
+        const uint2 sg = seg[q < n ? q : n - 1];
+        s0 = (int)sg.x;
+        s1 = (int)sg.y;
+    }
+    lo = s0;
+    hi = s1 - 1;
+    if (window) {
+        lo = max(lo, (int)q - (int)window);
+        hi = min(hi, (int)q + (int)window);
+    }
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);

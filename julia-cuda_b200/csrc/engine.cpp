@@ -119,10 +119,11 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&hx, rows * D * 2) && dalloc((void **)&xs, rows * D * 2) &&
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
-              dalloc((void **)&ids, 2 * L * 4) &&
+              dalloc((void **)&ids, 4 * L * 4) &&
               dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4);
     if (!ok) return false;
     markers = ids + L;
+    seg = reinterpret_cast<uint2 *>(ids + 2 * L);
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
     const size_t widest = std::max({3 * D, 2 * I, F, S});
     gemm_ws_cap = rows * widest * 8;
@@ -183,7 +184,7 @@ bool Engine::init(const float *raw, std::string *why) {
         return false;
     persist_grid = (uint32_t)(sms * std::max(0, persist_blocks_per_sm()));
 
-    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * 2 * L * 4), "cudaMallocHost") ||
+    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * 4 * L * 4), "cudaMallocHost") ||
         !cu(cudaMallocHost((void **)&h_logits, QUEUE * L * 4), "cudaMallocHost") ||
         !cu(cudaMallocHost((void **)&h_err, sizeof(unsigned int)), "cudaMallocHost"))
         return false;
@@ -239,7 +240,18 @@ Step Engine::gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32
 }
 
 std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
-                                      int mode) const {
+                                      int mode, bool packed) const {
+    std::vector<Step> steps = build_steps_flat(n, k, qtype, d_trace, mode);
+    if (packed)
+        for (Step &st : steps) {
+            if (st.d.kind == PH_ATTN) st.d.a.seg = seg;
+            if (st.d.kind == PH_GEMM && (st.d.epi & JC_EPI_ROPE)) st.d.g.seg = seg;
+        }
+    return steps;
+}
+
+std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype,
+                                           uint16_t *d_trace, int mode) const {
     const PreparedLayout &P = hw.layout;
     const uint32_t D = cfg.d_model, I = cfg.inter, F = cfg.head_ff, S = cfg.scorer_hidden;
     std::vector<Step> steps;
@@ -402,6 +414,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             g.eps = p.eps;
             g.rope = p.rope;
             g.rope_stride = p.rope_stride;
+            g.seg = p.seg;
             g.bias = p.bias;
             return launch_gemm(g, c, s, true);
         }
@@ -412,6 +425,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             a.n = d.a.n;
             a.heads = d.a.heads;
             a.window = d.a.window;
+            a.seg = d.a.seg;
             a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms);
             a.ws = attn_ws;
             a.counters = attn_cnt;
@@ -511,8 +525,9 @@ int Engine::launches_per_forward(uint32_t n, uint32_t k, int mode) const {
     return 1 + 5 * cfg.n_layers + head;
 }
 
-bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s) {
-    GraphKey key{n, k, qtype, mode, head_rows(n)};
+bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s,
+                            bool packed) {
+    GraphKey key{n, k, qtype, mode, head_rows(n), packed ? 1u : 0u};
     auto it = graphs.find(key);
     if (it == graphs.end()) {
         if (n == 0 || n > max_length || k > max_length || qtype >= (uint32_t)cfg.n_qtypes ||
@@ -521,7 +536,7 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
             return false;
         }
         GraphEntry entry;
-        std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode);
+        std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode, packed);
         if (mode != MODE_STEPS) {
             plan_steps(steps, mode);
             std::vector<PhaseDesc> descs(steps.size());

@@ -26,12 +26,15 @@ enum : int { MODE_STEPS = 0, MODE_LAYER = 1, MODE_MODEL = 2 };
 struct GraphKey {
     uint32_t n, k, qtype;
     int mode;
-    uint32_t head;  // rows the head runs on
+    uint32_t head;    // rows the head runs on
+    uint32_t packed;  // several requests in one forward (their segments in the engine's seg)
     bool operator==(const GraphKey &o) const {
-        return n == o.n && k == o.k && qtype == o.qtype && mode == o.mode && head == o.head;
+        return n == o.n && k == o.k && qtype == o.qtype && mode == o.mode && head == o.head &&
+               packed == o.packed;
     }
     bool operator<(const GraphKey &o) const {
-        return std::tie(n, k, qtype, mode, head) < std::tie(o.n, o.k, o.qtype, o.mode, o.head);
+        return std::tie(n, k, qtype, mode, head, packed) <
+               std::tie(o.n, o.k, o.qtype, o.mode, o.head, o.packed);
     }
 };
 
@@ -53,7 +56,10 @@ class Engine {
     bool enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, uint16_t *d_trace,
                          cudaStream_t s);
     // Same, through a cached CUDA graph of that shape.
-    bool launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s);
+    // packed: the n rows hold several requests (rows [seg[r].x, seg[r].y) per row r of the
+    // device array `seg`); attention stays within a request and RoPE positions restart.
+    bool launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s,
+                        bool packed = false);
     int launches_per_forward(uint32_t n, uint32_t k, int mode) const;
     // Reads (and clears) the device error word; on an error also resets the grid barrier.
     bool check_device_error(std::string *why);
@@ -71,17 +77,22 @@ class Engine {
     // The head (final LayerNorm, head layers, marker gather) runs on rows [0, head_length) of a
     // longer sequence; 0 = every row (the reference's GPU head). Markers must lie inside.
     size_t head_length = 0;
+    // julia_cuda_run packs consecutive requests (same question type, no head length) into
+    // forwards of up to pack_rows tokens; 0 = one forward per request (the reference's way).
+    size_t pack_rows = 0;
     uint32_t head_rows(uint32_t n) const {
         return head_length && head_length < n ? (uint32_t)head_length : n;
     }
 
-    // inputs / outputs of one request (device)
+    // inputs / outputs of one forward (device): ids at [0, L), markers at [L, 2L) and, for
+    // packed requests, each row's request rows (uint2) at [2L, 4L) of one allocation
     uint32_t *ids = nullptr, *markers = nullptr, *iota = nullptr;
+    uint2 *seg = nullptr;
     float *logits = nullptr;
     // pinned staging for julia_cuda_run
     static constexpr int QUEUE = 16;
-    // QUEUE slots of 2 x max_length words: the ids, then the markers (the device buffers `ids`
-    // and `markers` are one allocation in the same layout, so a request is one copy)
+    // QUEUE slots of 4 x max_length words: the ids, the markers, the segments (the device buffers
+    // are one allocation in the same layout, so a forward's inputs are one copy)
     uint32_t *h_ids = nullptr;
     float *h_logits = nullptr;
     unsigned int *h_err = nullptr;  // the device error word, copied after each queue of requests
@@ -103,7 +114,9 @@ class Engine {
     // each encoder layer's steps) and the launches' item counts.
     void plan_steps(std::vector<Step> &steps, int mode) const;
     std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
-                                  int mode) const;
+                                  int mode, bool packed = false) const;
+    std::vector<Step> build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+                                       int mode) const;
     Step gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32_t m, uint32_t n,
                    uint32_t k, __half *c, const __half *res, const float *stats_in,
                    const float *colsum, float *stats_out, float *zero, uint32_t zero_len,

@@ -245,7 +245,9 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         if (valid) {
             // Pair-group-major table: consecutive rows (the lanes of a warp) are consecutive
             // float4s, so each load instruction reads one contiguous 512-byte run.
-            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + (size_t)(pair0 / 2) * p.rope_stride + r;
+            // Row r's position: r, or its offset in its request when requests are packed.
+            const uint32_t pos = p.seg ? r - p.seg[r].x : r;
+            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + (size_t)(pair0 / 2) * p.rope_stride + pos;
 #pragma unroll
             for (int i = 0; i < GT / 2; i++) ropev[i] = __ldg(t4 + (size_t)i * p.rope_stride);
         }

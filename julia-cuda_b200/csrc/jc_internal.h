@@ -63,6 +63,7 @@ struct GemmArgs {
     const float *rope = nullptr;
     const float *bias = nullptr;
     uint32_t rope_stride = 0;  // rows of the pair-group-major RoPE table; 0: m
+    const uint2 *seg = nullptr;  // packed requests: row r's request rows (RoPE position r - seg[r].x)
 };
 
 struct GemmConfig {
@@ -99,6 +100,7 @@ struct AttnArgs {
     uint32_t kv_chunks = 1;       // split-KV: key ranges per (query tile, head)
     float *ws = nullptr;          // kv_chunks > 1: partials
     uint32_t *counters = nullptr; // kv_chunks > 1: one zeroed counter per (query tile, head)
+    const uint2 *seg = nullptr;   // packed requests: row r sees only keys [seg[r].x, seg[r].y)
 };
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 size_t attn_counters(uint32_t n, uint32_t heads);

@@ -285,6 +285,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.rope = g.rope;
     p.bias = g.bias;
     p.rope_stride = g.rope_stride ? g.rope_stride : g.m;
+    p.seg = g.seg;
     p.zero_len = g.zero_len;
     p.m = g.m;
     p.n = g.n;
@@ -468,7 +469,7 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         set_error("attention: qkv and o must be 16-byte aligned");
         return false;
     }
-    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window};
+    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg};
     const AttnVariant v = attn_variant(a.n, a.window);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     if (v.qw == 2) return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);

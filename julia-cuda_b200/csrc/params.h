@@ -27,6 +27,9 @@ struct GemmParams {
     uint32_t zero_len, m, n, k;
     float eps;
     uint32_t store_tma;     // single-GEMM kernel: the launch carries map_c
+    // Packed requests (RoPE positions restart at each request): row r is position r - seg[r].x;
+    // nullptr: position r.
+    const uint2 *seg;
 };
 
 struct AttnParams {
@@ -35,6 +38,9 @@ struct AttnParams {
     float *ws;
     uint32_t *counters;
     uint32_t n, heads, window;
+    // Packed requests: row r belongs to the request occupying rows [seg[r].x, seg[r].y) and sees
+    // only its keys; nullptr: one request of n rows.
+    const uint2 *seg;
 };
 
 // Phase kinds of the persistent kernel.
