@@ -371,8 +371,10 @@ def serving_arm(args, rank, world, local, replicas):
     torch.cuda.set_device(local)
     replicas.init(world, "nccl", device=torch.device("cuda", local))
     jc = importlib.import_module("julia-cuda_b200")
-    cfg = jc.default_config(max_positions=1024)
-    eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
+    # Requests are at most 1024 tokens; a longer engine capacity only serves larger packs.
+    cap = max(1024, args.max_length)
+    cfg = jc.default_config(max_positions=cap)
+    eng = jc.Engine.load_random(cfg, SEED, max_length=cap, device=local)
     reqs = replicas.serving_requests(args.requests, SEED, cfg.vocab)
     mine = [reqs[i] for i in replicas.shard_lpt([len(r[0]) for r in reqs], world)[rank]]
     batch = 16
@@ -438,6 +440,8 @@ def main():
     ap.add_argument("--requests", type=int, default=4096)
     ap.add_argument("--pack", type=int, default=0,
                     help="--serving: pack requests into forwards of up to this many tokens")
+    ap.add_argument("--max-length", type=int, default=1024,
+                    help="--serving: the engine's row capacity (packs up to it)")
     ap.add_argument("--sweep", action="store_true",
                     help="configs 1-2 instead of the headline: each GEMM and attention alone")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
