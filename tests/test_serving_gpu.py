@@ -46,19 +46,16 @@ def served(jc, O):
 
 def test_serving_parity_gate(served):
     reqs, got, want, _ = served
-    d = np.concatenate([np.abs(g - w) for g, w in zip(got, want)])
-    mean_d, max_d = float(d.mean()), float(d.max())
-    margins = np.array([np.sort(w)[-1] - np.sort(w)[-2] for w in want])
-    agree = np.array([np.argmax(g) == np.argmax(w) for g, w in zip(got, want)])
-    decided = margins > 2 * max_d
-    hist = np.histogram(margins, bins=[0, 0.01, 0.03, 0.1, 0.3, 1, np.inf])[0]
+    scoring = importlib.import_module("julia-cuda_b200.scoring")
+    a = scoring.agreement(got, want)
     print(f"\n{len(reqs)} requests, lengths {min(len(r[0]) for r in reqs)}-"
-          f"{max(len(r[0]) for r in reqs)}: mean |dlogit| {mean_d:.4f}, max {max_d:.4f}, argmax "
-          f"agreement {agree.mean() * 100:.1f}% ({agree[decided].mean() * 100:.1f}% of the "
-          f"{decided.sum()} decided); f32 top-2 margins <0.01/<0.03/<0.1/<0.3/<1/>=1: {hist}")
-    assert mean_d <= 0.03
-    assert max_d < 0.15  # src/check.rs:560
-    assert agree[decided].all()
+          f"{max(len(r[0]) for r in reqs)}: mean |dlogit| {a['mean_abs_dlogit']:.4f}, max "
+          f"{a['max_abs_dlogit']:.4f}, argmax agreement {a['agreement'] * 100:.1f}% "
+          f"({a['decided_agreement'] * 100:.1f}% of the {a['decided']} decided); f32 top-2 "
+          f"margins <0.01/<0.03/<0.1/<0.3/<1/>=1: {a['margin_hist']}")
+    assert a["mean_abs_dlogit"] <= 0.03
+    assert a["max_abs_dlogit"] < 0.15  # src/check.rs:560
+    assert a["decided_agreement"] == 1.0
 
 
 def test_persistent_modes_serve_the_same_answers(served):
