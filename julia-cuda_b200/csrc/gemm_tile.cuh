@@ -195,8 +195,8 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
     k_range(p.k / GEMM_BK, z, splits, kb0, nkb);
 
     // Column sums and biases are weights: fetch them before waiting for the previous kernel.
-    if (threadIdx.x >= 64 && threadIdx.x < 64 + BN) {
-        const uint32_t j = threadIdx.x - 64;
+    // (threads 64 and up: warps 0 and 1 hold the TMA producer and an MMA issuer)
+    for (uint32_t j = threadIdx.x - 64; threadIdx.x >= 64 && j < (uint32_t)BN; j += GEMM_THREADS - 64) {
         if constexpr ((EPI & JC_EPI_LN) != 0) sv.cs_s[j] = __ldg(p.colsum + n0 + j);
         if constexpr ((EPI & JC_EPI_BIAS) != 0) sv.bs_s[j] = __ldg(p.bias + n0 + j);
     }

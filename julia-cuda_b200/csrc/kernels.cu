@@ -195,6 +195,7 @@ template <int BN> struct Depth;
 template <> struct Depth<32> { static constexpr int shallow = 2, deep = 5; };
 template <> struct Depth<64> { static constexpr int shallow = 2, deep = 4; };
 template <> struct Depth<128> { static constexpr int shallow = 2, deep = 3; };
+template <> struct Depth<256> { static constexpr int shallow = 2, deep = 2; };  // 96 KB stages
 
 template <int BN, int STAGES, uint32_t EPI, int CS>
 static bool launch_gemm_inst(const GemmKernelParams &p, dim3 grid, cudaStream_t s, bool pdl) {
@@ -237,7 +238,7 @@ template <int BN>
 static bool launch_gemm_bn(uint32_t epi, const GemmConfig &cfg, const GemmKernelParams &p,
                            dim3 grid, cudaStream_t s, bool pdl) {
     // Cluster split-K runs with the shallow ring: a cluster's CTAs share the tile's K loop.
-    if constexpr (BN >= 64) {
+    if constexpr (BN >= 64 && BN <= 128) {
         if (cfg.cluster == 2) return launch_gemm_depth<BN, Depth<BN>::shallow, 2>(epi, p, grid, s, pdl);
         if (cfg.cluster == 4) return launch_gemm_depth<BN, Depth<BN>::shallow, 4>(epi, p, grid, s, pdl);
     }
@@ -295,6 +296,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     switch (cfg.bn) {
         case 32: return launch_gemm_bn<32>(g.epi, cfg, kp, grid, s, pdl);
         case 64: return launch_gemm_bn<64>(g.epi, cfg, kp, grid, s, pdl);
+        case 256: return launch_gemm_bn<256>(g.epi, cfg, kp, grid, s, pdl);
         default: return launch_gemm_bn<128>(g.epi, cfg, kp, grid, s, pdl);
     }
 }
@@ -304,7 +306,8 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     const bool ln = e & JC_EPI_LN, res = e & JC_EPI_RES, stats = e & JC_EPI_STATS,
                rope = e & JC_EPI_ROPE, geglu = e & JC_EPI_GEGLU, bias = e & JC_EPI_BIAS;
     auto fail = [](const char *m) { set_error(std::string("gemm: ") + m); return false; };
-    if (cfg.bn != 32 && cfg.bn != 64 && cfg.bn != 128) return fail("tile width must be 32, 64 or 128");
+    if (cfg.bn != 32 && cfg.bn != 64 && cfg.bn != 128 && cfg.bn != 256)
+        return fail("tile width must be 32, 64, 128 or 256");
     if (g.m == 0) return fail("no rows");
     if (g.k == 0 || g.k % GEMM_BK) return fail("k must be a positive multiple of 64");
     if (g.n == 0 || g.n % cfg.bn) return fail("n must be a multiple of the tile width");
@@ -312,9 +315,9 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
         return fail("split-K must be 1..8 and at most k/64");
     if (cfg.cluster != 1 && cfg.cluster != 2 && cfg.cluster != 4)
         return fail("a split-K cluster must be 1, 2 or 4 CTAs");
-    if (cfg.cluster > 1 && (cfg.splits != 1 || cfg.bn < 64 || (uint32_t)cfg.cluster > g.k / GEMM_BK))
+    if (cfg.cluster > 1 && (cfg.splits != 1 || cfg.bn < 64 || cfg.bn > 128 || (uint32_t)cfg.cluster > g.k / GEMM_BK))
         return fail("cluster split-K needs 64- or 128-column tiles, no workspace split and k/64 >= cluster");
-    if ((rope || geglu) && cfg.bn < 64) return fail("RoPE and GeGLU need 64- or 128-column tiles");
+    if ((rope || geglu) && cfg.bn < 64) return fail("RoPE and GeGLU need 64-column tiles or wider");
     if (rope && g.n % 192) return fail("RoPE needs a qkv output (n a multiple of 3 x 64)");
     if (rope && geglu) return fail("RoPE and GeGLU do not combine");
     if ((res || stats) && geglu) return fail("residual / statistics do not combine with GeGLU");
@@ -339,17 +342,23 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     GemmConfig c;
     const uint32_t tiles_m = (m + GEMM_BM - 1) / GEMM_BM;
-    // The narrowest tile whose grid still fits one CTA per SM: a CTA's time is its operand stream
-    // ((128 + tile width) x k), so narrower tiles are faster until the grid no longer fits in one
-    // wave (measured: 32 columns for the 768-wide GEMMs at 72-293 tokens, 64 at 1024; 64 for the
-    // 2304-wide ones up to 293 tokens, 128 at 1024).
-    c.bn = 0;
-    for (int bn : {32, 64, 128})
-        if (n % bn == 0 && tiles_m * (n / bn) <= (uint32_t)sms) {
+    // A CTA's time is its operand stream ((128 + tile width) x k bytes, at what an SM ingests
+    // from L2), so a launch takes about waves x (128 + width): the width with the least of it,
+    // ties to the narrower (less epilogue a thread). Up to a wave this is the narrowest tile whose
+    // grid fits (measured: 32 columns for the 768-wide GEMMs at 72-293 tokens, 64 at 1024; 64 for
+    // the 2304-wide ones up to 448 tokens, 128 at 1024); packs of several thousand rows take
+    // 256-column tiles, which read the activation tile half as often per output column.
+    c.bn = 32;
+    uint64_t best = ~0ull;
+    for (int bn : {32, 64, 128, 256}) {
+        if (n % bn) continue;
+        const uint64_t ctas = (uint64_t)tiles_m * (n / bn);
+        const uint64_t cost = (ctas + sms - 1) / sms * (uint64_t)(GEMM_BM + bn);
+        if (cost < best) {
+            best = cost;
             c.bn = bn;
-            break;
         }
-    if (c.bn == 0) c.bn = n % 128 == 0 ? 128 : (n % 64 == 0 ? 64 : 32);
+    }
     // Split-K (workspace or cluster) measured slower than one CTA per tile for every encoder
     // shape at 72-1024 tokens (the partial exchange costs more than the shorter K loop saves).
     c.splits = 1;

@@ -107,7 +107,15 @@ def test_gemm_ragged_rows(jc, O, m):
     run_gemm_case(jc, O, "resstats", m, 768, 1152)
 
 
-@pytest.mark.parametrize("bn", [32, 64, 128])
+@pytest.mark.parametrize("name,n,k", [c for c in GEMM_CASES if c[1] % 256 == 0])
+@pytest.mark.parametrize("m", [1, 293, 3000])
+def test_gemm_256_column_tiles(jc, O, name, n, k, m):
+    """256-column tiles (two 256-wide accumulators filling TMEM; what large packs of requests
+    take) on every epilogue whose width allows them."""
+    run_gemm_case(jc, O, name, m, n, k, bn=256)
+
+
+@pytest.mark.parametrize("bn", [32, 64, 128, 256])
 @pytest.mark.parametrize("splits", [1, 2, 3, 4, 8])
 def test_gemm_tile_and_split_sweep(jc, O, bn, splits):
     """Every tile width x split-K on the resstats and lnbias shapes (the reference's
