@@ -264,7 +264,7 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
     auto attn_step = [&](uint32_t rows, uint32_t window, int layer) {
         Step st;
         st.d.kind = PH_ATTN;
-        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, rows, (uint32_t)cfg.n_heads, window};
+        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, rows, (uint32_t)cfg.n_heads, window, nullptr};
         st.layer = layer;
         return st;
     };
