@@ -60,10 +60,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Descriptor of an MN-major operand tile whose K rows are 128 bytes (64 f16 along N), swizzled
 // with the 128-byte pattern: stride byte offset = the next group of 8 K rows (1024 B); the leading
 // byte offset (the next 64-wide N block) is never used at N = 64.

@@ -71,6 +71,10 @@ struct GemmConfig {
     int splits = 1;   // split-K factor through a global workspace, 1..8
     int cluster = 1;  // split-K factor inside a thread-block cluster (1, 2 or 4; DSMEM reduction)
     bool deep = false;  // twice the pipeline stages (one CTA per SM)
+    // More tiles than SMs, 128- or 256-column tiles, no split: one CTA per SM walks the tiles
+    // with the epilogue of one under the main loop of the next (gemm_persist.cuh) on `grid` CTAs.
+    bool persistent = false;
+    uint32_t grid = 0;
 };
 
 // Floats of split-K workspace and counters a launch of this shape needs.

@@ -12,6 +12,7 @@
 #include "attention_tc.cuh"
 #include "edges.cuh"
 #include "gemm.cuh"
+#include "gemm_persist.cuh"
 #include "jc_internal.h"
 #include "persist.cuh"
 
@@ -246,6 +247,37 @@ static bool launch_gemm_bn(uint32_t epi, const GemmConfig &cfg, const GemmKernel
                     : launch_gemm_depth<BN, Depth<BN>::shallow, 1>(epi, p, grid, s, pdl);
 }
 
+template <int BN, int STAGES>
+static bool launch_gemm_persist(uint32_t epi, const GemmKernelParams &p, dim3 grid, cudaStream_t s,
+                                bool pdl) {
+    constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
+    constexpr int smem = GemmPersistShape<BN, STAGES>::SMEM_BYTES + 1024;
+    auto go = [&](auto kern, std::atomic<uint64_t> &set) {
+        if (!ensure_smem(kern, smem, set)) return false;
+        return launch_ex(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, "gemm launch", p);
+    };
+#define JC_PERSIST(E)                                                   \
+    case E: {                                                           \
+        static std::atomic<uint64_t> set{0};                            \
+        return go(gemm_persistent_kernel<BN, STAGES, E>, set);          \
+    }
+    switch (epi) {
+        JC_PERSIST(0)
+        JC_PERSIST(RS)
+        JC_PERSIST(JC_EPI_BIAS | RS)
+        JC_PERSIST(LB)
+        JC_PERSIST(LB | JC_EPI_RELU)
+        JC_PERSIST(LB | JC_EPI_GELU)
+        JC_PERSIST(JC_EPI_ROPE)
+        JC_PERSIST(JC_EPI_LN | JC_EPI_ROPE)
+        JC_PERSIST(JC_EPI_LN | JC_EPI_GEGLU)
+        default: break;
+    }
+#undef JC_PERSIST
+    set_error("gemm: no compiled kernel for epilogue " + std::to_string(epi));
+    return false;
+}
+
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     if (!check_gemm(g, cfg)) return false;
     GemmKernelParams kp;
@@ -292,6 +324,13 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.n = g.n;
     p.k = g.k;
     p.eps = g.eps;
+    if (cfg.persistent && (cfg.bn == 128 || cfg.bn == 256) && cfg.splits == 1 && cfg.cluster == 1) {
+        const uint32_t tiles = (g.n / cfg.bn) * ((g.m + GEMM_BM - 1) / GEMM_BM);
+        const dim3 pgrid(std::min(tiles, std::max(cfg.grid, 1u)));
+        kp.p.store_tma = 0;  // direct stores: the epilogue runs under the next tile's main loop
+        return cfg.bn == 128 ? launch_gemm_persist<128, 3>(g.epi, kp, pgrid, s, pdl)
+                             : launch_gemm_persist<256, 2>(g.epi, kp, pgrid, s, pdl);
+    }
     dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.cluster > 1 ? cfg.cluster : cfg.splits);
     switch (cfg.bn) {
         case 32: return launch_gemm_bn<32>(g.epi, cfg, kp, grid, s, pdl);
@@ -339,21 +378,36 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     return true;
 }
 
+// 128- and 256-column tiles of a launch past one wave run the persistent kernel, unless
+// JC_GEMM_PERSIST=0 (an A/B knob) turns it off.
+static bool persistent_width(int bn) {
+    static const char *persist = getenv("JC_GEMM_PERSIST");
+    return (bn == 128 || bn == 256) && !(persist && persist[0] == '0');
+}
+
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     GemmConfig c;
     const uint32_t tiles_m = (m + GEMM_BM - 1) / GEMM_BM;
-    // A CTA's time is its operand stream ((128 + tile width) x k bytes, at what an SM ingests
-    // from L2), so a launch takes about waves x (128 + width): the width with the least of it,
-    // ties to the narrower (less epilogue a thread). Up to a wave this is the narrowest tile whose
-    // grid fits (measured: 32 columns for the 768-wide GEMMs at 72-293 tokens, 64 at 1024; 64 for
-    // the 2304-wide ones up to 448 tokens, 128 at 1024); packs of several thousand rows take
-    // 256-column tiles, which read the activation tile half as often per output column.
+    // A CTA's time is a fixed part (set-up, first stage, epilogue, drain: about as long as
+    // streaming 256 operand rows) plus its operand stream ((128 + tile width) x k bytes, at what
+    // an SM ingests from L2), so a launch takes about waves x (256 + 128 + width): the width with
+    // the least of it, ties to the narrower (less epilogue a thread). Up to a wave this is the
+    // narrowest tile whose grid fits (measured: 32 columns for the 768-wide GEMMs at 72-293
+    // tokens, 64 at 1024; 64 for the 2304-wide ones up to 448 tokens, 128 at 1024); packs of
+    // thousands of rows take 256-column tiles (2304-wide at 3072 rows: 25.0 against 26.6 us),
+    // which read the activation tile half as often per output column. Past one wave, 128- and
+    // 256-column tiles run persistent (gemm_persist.cuh): the fixed part is paid once and each
+    // further wave costs about twice its width (measured per extra wave at k = 768: 5.0 us for
+    // 128 columns, 9.5 us for 256, against 10.6 / 15.4 us for the first).
     c.bn = 32;
     uint64_t best = ~0ull;
     for (int bn : {32, 64, 128, 256}) {
         if (n % bn) continue;
         const uint64_t ctas = (uint64_t)tiles_m * (n / bn);
-        const uint64_t cost = (ctas + sms - 1) / sms * (uint64_t)(GEMM_BM + bn);
+        const uint64_t waves = (ctas + sms - 1) / sms;
+        const uint64_t cost = waves > 1 && persistent_width(bn)
+                                  ? (256 + GEMM_BM + bn) + (waves - 1) * 2 * (uint64_t)bn
+                                  : waves * (uint64_t)(256 + GEMM_BM + bn);
         if (cost < best) {
             best = cost;
             c.bn = bn;
@@ -384,6 +438,8 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
     static const char *force = getenv("JC_GEMM_DEPTH");  // A/B knob: "deep" / "shallow"
     if (force && force[0] == 'd') c.deep = true;
     if (force && force[0] == 's') c.deep = false;
+    c.persistent = ctas > (uint32_t)sms && persistent_width(c.bn) && c.splits == 1 && c.cluster == 1;
+    c.grid = (uint32_t)sms;
 }
 
 // ---------------------------------------------------------------------------------------------

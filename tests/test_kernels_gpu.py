@@ -115,6 +115,21 @@ def test_gemm_256_column_tiles(jc, O, name, n, k, m):
     run_gemm_case(jc, O, name, m, n, k, bn=256)
 
 
+PERSISTENT_CASES = [  # (m, tile width): more tiles than SMs, so one CTA per SM walks several
+    (1200, 128), (4000, 128), (3000, 256), (6400, 128)]
+
+
+@pytest.mark.parametrize("name,n,k", GEMM_CASES)
+@pytest.mark.parametrize("m,bn", PERSISTENT_CASES)
+def test_gemm_persistent_multi_tile(jc, O, name, n, k, m, bn):
+    """Launches of more tiles than SMs run the persistent kernel (two TMEM accumulator buffers,
+    the epilogue of one tile under the main loop of the next) on every epilogue."""
+    tiles = -(-m // 128) * (n // bn) if n % bn == 0 else 0
+    if tiles <= 148 or (m >= 4000 and n > 768 and bn == 128):
+        pytest.skip("single wave (not the persistent kernel), or a case another row covers")
+    run_gemm_case(jc, O, name, m, n, k, bn=bn)
+
+
 @pytest.mark.parametrize("bn", [32, 64, 128, 256])
 @pytest.mark.parametrize("splits", [1, 2, 3, 4, 8])
 def test_gemm_tile_and_split_sweep(jc, O, bn, splits):
