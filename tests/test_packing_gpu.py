@@ -70,3 +70,22 @@ def test_packing_rejects_rows_above_max_length(jc, packed_case):
     c, raw, eng, reqs, alone, packed, ms = packed_case
     with pytest.raises(jc.JuliaCudaError):
         eng.set_packing(4096)
+
+
+def test_large_packs_run_the_persistent_gemm(jc, O):
+    """Packs of a few thousand rows: the GEMMs have more tiles than SMs (the persistent kernel,
+    RoPE positions from each row's request), the global layers the tcgen05 attention. Each
+    request's logits match running it alone."""
+    rep = importlib.import_module("julia-cuda_b200.replicas")
+    c = jc.default_config(max_positions=3072)
+    eng = jc.Engine.load_raw(c, O.init_random(oracle_cfg(O, c), 7), max_length=3072)
+    try:
+        reqs = rep.serving_requests(24, 11, c.vocab)
+        alone, _ = eng.run(reqs)
+        eng.set_packing(3072)
+        packed, ms = eng.run(reqs)
+        assert jc.device_error() == 0 and len(set(np.round(ms, 6))) < len(reqs)
+        for a, p in zip(alone, packed):
+            assert np.max(np.abs(a - p)) < 2e-3
+    finally:
+        eng.close()
