@@ -26,6 +26,8 @@ Other BASELINE configs (extra lines, not the headline):
   --serving [--requests 4096]           config 3: a seeded log-normal request set through
                                         julia_cuda_run, LPT-partitioned over the ranks
   --seq 1024 --head-length 512 --mode 2 config 4: the whole model in one cooperative launch
+  --restated                            the reference's per-step GPU kernels restated in CUDA C++
+                                        (baseline/restated) against this library, same request
 """
 import argparse
 import importlib
@@ -358,6 +360,54 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def restated_arm(args, local):
+    """The reference's per-step GPU forward, restated in CUDA C++ (baseline/restated), on the same
+    request and weights as the headline: CUDA-event time embed -> logits per request (the
+    reference's own timing), L2 flushed before every request; beside it this library's engine on
+    the same request, timed the same way (julia_cuda_run's per-request GPU time)."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "restated"))
+    import restated
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    raw = jc.init_random(cfg, SEED)
+    ref = restated.Restated(cfg, raw, max_length=1024, device=local)
+    eng = jc.Engine.load_raw(cfg, raw, max_length=1024, device=local)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    n_tok = args.seq
+    ids, markers = request(0, cfg.vocab, n_tok)
+    steps = max(1, min(args.steps, 200))
+    out = {}
+    for name, fn in (("restated", lambda: ref.run(ids, markers, 0)),
+                     ("ours", lambda: (lambda r: (r[0][0], float(r[1][0])))(eng.run([(ids, markers, 0)])))):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        ms = []
+        for _ in range(steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            logits, t = fn()
+            ms.append(t)
+        out[name] = (statistics.mean(ms), logits)
+    d = float(np.max(np.abs(out["restated"][1] - out["ours"][1])))
+    ref.close()
+    eng.close()
+    line = {
+        "metric": f"us/request (embed->logits, {n_tok} tokens, batch 1): the reference's per-step "
+                  f"kernels restated vs this library",
+        "restated_us": out["restated"][0] * 1e3, "ours_us": out["ours"][0] * 1e3,
+        "speedup": out["restated"][0] / out["ours"][0], "steps": steps,
+        "max_abs_dlogit": d, "unit": "us", "higher_is_better": False, "data": "synthetic",
+        "config": {"workload": f"config0 request ({n_tok} tokens, 4 markers), seed {SEED} weights",
+                   "l2": "flushed (256 MiB write) before every request",
+                   "restated": "mma.sync BMx64 GEMMs (BK 32, register prefetch), split-K, fragment "
+                               "epilogues, FA-2 attention, plain stream launches",
+                   "ours": "julia_cuda_run, per-step kernels, CUDA graph + PDL"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
 SERVING_METRIC = "requests/s (config 3 serving: log-normal lengths around 293 tokens, 4 markers)"
 
@@ -444,6 +494,9 @@ def main():
                     help="--serving: the engine's row capacity (packs up to it)")
     ap.add_argument("--sweep", action="store_true",
                     help="configs 1-2 instead of the headline: each GEMM and attention alone")
+    ap.add_argument("--restated", action="store_true",
+                    help="the reference's per-step kernels restated (baseline/restated) against "
+                         "this library on the headline request")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
                                       "attn_global", "attn_window"],
                     help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")
@@ -462,6 +515,10 @@ def main():
     if args.one:
         if rank == 0:
             one_kernel_arm(args, local)
+        return
+    if args.restated:
+        if rank == 0:
+            restated_arm(args, local)
         return
 
     import torch
