@@ -493,6 +493,54 @@ __global__ void __launch_bounds__(128) attention_kernel(const __half *qkv, __hal
 }
 
 // ---------------------------------------------------------------------------------------------
+// launches
+
+// gemm::choose (src/gemm.rs:153-180): the tile height from m (32 up to 200 rows, 64 up to 400,
+// else 128 on 8 warps), split-K 4 while the tiles fill at most half the SMs, at least 3 K steps
+// a split.
+struct Plan {
+    int shape;
+    uint32_t bm, splits;
+};
+
+static Plan choose(uint32_t m, uint32_t n, uint32_t k, int sms) {
+    Plan p;
+    p.shape = m <= 200 ? 0 : (m <= 400 ? 1 : 2);
+    p.bm = p.shape == 0 ? 32 : (p.shape == 1 ? 64 : 128);
+    const uint32_t tiles = (n / 64) * ((m + p.bm - 1) / p.bm);
+    p.splits = 2 * tiles > (uint32_t)sms ? 1 : 4;
+    p.splits = std::min(p.splits, std::max(k / 32 / 3, 1u));
+    return p;
+}
+
+template <uint32_t EPI>
+static void launch_gemm(const GemmP &g, int sms, cudaStream_t stream) {
+    const Plan p = choose(g.m, g.n, g.k, sms);
+    const dim3 grid(g.n / 64, (g.m + p.bm - 1) / p.bm, p.splits);
+    if (p.shape == 0)
+        gemm_kernel<1, 2, EPI><<<grid, 128, 0, stream>>>(g);
+    else if (p.shape == 1)
+        gemm_kernel<2, 2, EPI><<<grid, 128, 0, stream>>>(g);
+    else
+        gemm_kernel<2, 4, EPI><<<grid, 256, 0, stream>>>(g);
+}
+
+static bool launch_gemm_epi(uint32_t epi, const GemmP &g, int sms, cudaStream_t stream) {
+    constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
+    switch (epi) {
+        case JC_EPI_ROPE: launch_gemm<JC_EPI_ROPE>(g, sms, stream); return true;
+        case JC_EPI_LN | JC_EPI_ROPE: launch_gemm<JC_EPI_LN | JC_EPI_ROPE>(g, sms, stream); return true;
+        case JC_EPI_LN | JC_EPI_GEGLU: launch_gemm<JC_EPI_LN | JC_EPI_GEGLU>(g, sms, stream); return true;
+        case RS: launch_gemm<RS>(g, sms, stream); return true;
+        case JC_EPI_BIAS | RS: launch_gemm<JC_EPI_BIAS | RS>(g, sms, stream); return true;
+        case LB: launch_gemm<LB>(g, sms, stream); return true;
+        case LB | JC_EPI_RELU: launch_gemm<LB | JC_EPI_RELU>(g, sms, stream); return true;
+        case LB | JC_EPI_GELU: launch_gemm<LB | JC_EPI_GELU>(g, sms, stream); return true;
+        default: return false;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host: weights in the reference's layouts, buffers, the launch sequence
 
 // Wqkv rows for the fragment RoPE epilogue: in each q and k head, packed rows 2i and 2i + 1 are
@@ -675,26 +723,12 @@ struct Restated {
         return false;
     }
 
-    // gemm::choose (src/gemm.rs:153-180): the tile height from m, split-K 4 while the tiles fill
-    // at most half the SMs, at least 3 K steps a split.
     template <uint32_t EPI>
-    bool gemm(const __half *a, const Linear &w, uint32_t mm, uint32_t nn, uint32_t kk, __half *cc,
+    void gemm(const __half *a, const Linear &w, uint32_t mm, uint32_t nn, uint32_t kk, __half *cc,
               const __half *res, const float *stats_in, float *stats_out, float *zero, uint32_t zero_len,
               float eps, const float *rope) {
-        GemmP g{a, w.w, cc, res, ws, counters, stats_in, w.colsum, stats_out, zero, zero_len, mm, nn, kk, eps, rope, w.bias};
-        const int shape = mm <= 200 ? 0 : (mm <= 400 ? 1 : 2);
-        const uint32_t bm = shape == 0 ? 32 : (shape == 1 ? 64 : 128);
-        const uint32_t tiles = (nn / 64) * ((mm + bm - 1) / bm);
-        uint32_t splits = 2 * tiles > (uint32_t)sms ? 1 : 4;
-        splits = std::min(splits, std::max(kk / 32 / 3, 1u));
-        const dim3 grid(nn / 64, (mm + bm - 1) / bm, splits);
-        if (shape == 0)
-            gemm_kernel<1, 2, EPI><<<grid, 128, 0, stream>>>(g);
-        else if (shape == 1)
-            gemm_kernel<2, 2, EPI><<<grid, 128, 0, stream>>>(g);
-        else
-            gemm_kernel<2, 4, EPI><<<grid, 256, 0, stream>>>(g);
-        return true;
+        const GemmP g{a, w.w, cc, res, ws, counters, stats_in, w.colsum, stats_out, zero, zero_len, mm, nn, kk, eps, rope, w.bias};
+        launch_gemm<EPI>(g, sms, stream);
     }
 
     void attention(const __half *q, __half *out, uint32_t n, uint32_t window) {
@@ -802,5 +836,35 @@ int jc_restated_run(void *h, const uint32_t *ids, size_t n, const uint32_t *mark
 }
 
 void jc_restated_free(void *h) { delete static_cast<rs::Restated *>(h); }
+
+size_t jc_restated_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int sms) {
+    const rs::Plan p = rs::choose(m, n, k, sms);
+    return p.splits > 1 ? (size_t)(n / 64) * ((m + p.bm - 1) / p.bm) * p.splits * p.bm * 64 : 0;
+}
+
+size_t jc_restated_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int sms) {
+    const rs::Plan p = rs::choose(m, n, k, sms);
+    return p.splits > 1 ? (size_t)(n / 64) * ((m + p.bm - 1) / p.bm) : 0;
+}
+
+int jc_restated_gemm(uint32_t epi, const void *a, const void *w, void *c, const void *res, float *ws,
+                     uint32_t *counters, const float *stats_in, const float *colsum, float *stats_out,
+                     float *zero, uint32_t zero_len, uint32_t m, uint32_t n, uint32_t k, float eps,
+                     const float *rope, const float *bias, int sms, void *stream) {
+    if (m < 1 || n % 64 || k % 32 || k < 32 || !a || !w || !c || sms < 1) return -1;
+    if (jc_restated_gemm_ws_floats(m, n, k, sms) && (!ws || !counters)) return -1;
+    const rs::GemmP g{static_cast<const __half *>(a), static_cast<const __half *>(w), static_cast<__half *>(c),
+                      static_cast<const __half *>(res), ws, counters, stats_in, colsum, stats_out, zero,
+                      zero_len, m, n, k, eps, rope, bias};
+    if (!rs::launch_gemm_epi(epi, g, sms, static_cast<cudaStream_t>(stream))) return -1;
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+int jc_restated_attention(const void *qkv, void *o, uint32_t n, uint32_t window, uint32_t d, void *stream) {
+    if (n < 1 || d % 64 || !qkv || !o) return -1;
+    rs::attention_kernel<<<dim3((n + 63) / 64, d / 64), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half *>(qkv), static_cast<__half *>(o), n, window, d);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
 
 }  // extern "C"

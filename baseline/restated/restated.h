@@ -24,6 +24,19 @@ int jc_restated_run(void *handle, const uint32_t *ids, size_t n, const uint32_t 
 
 void jc_restated_free(void *handle);
 
+/* One restated GEMM on device pointers (the reference's gemm_* kernel arguments, kernels/src/
+ * main.rs:1043-1066, tile and split by gemm::choose with `sms` SMs; epi one of the eight JC_EPI_*
+ * combinations of the forward; the rope table natural [rows][32][2]), queued on `stream`. With
+ * split-K, ws and counters sized by the two functions below (counters zeroed). 0 or -1. */
+size_t jc_restated_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int sms);
+size_t jc_restated_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int sms);
+int jc_restated_gemm(uint32_t epi, const void *a, const void *w, void *c, const void *res, float *ws,
+                     uint32_t *counters, const float *stats_in, const float *colsum, float *stats_out,
+                     float *zero, uint32_t zero_len, uint32_t m, uint32_t n, uint32_t k, float eps,
+                     const float *rope, const float *bias, int sms, void *stream);
+/* The restated attention (qkv [n, 3d] f16, o [n, d] f16, window 0 = global) on `stream`. */
+int jc_restated_attention(const void *qkv, void *o, uint32_t n, uint32_t window, uint32_t d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

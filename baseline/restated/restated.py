@@ -27,6 +27,15 @@ def lib():
                                       ctypes.c_size_t]
         L.jc_restated_free.restype = None
         L.jc_restated_free.argtypes = [ctypes.c_void_p]
+        u32, P = ctypes.c_uint32, ctypes.c_void_p
+        for f in ("jc_restated_gemm_ws_floats", "jc_restated_gemm_counters"):
+            getattr(L, f).restype = ctypes.c_size_t
+            getattr(L, f).argtypes = [u32, u32, u32, ctypes.c_int]
+        L.jc_restated_gemm.restype = ctypes.c_int
+        L.jc_restated_gemm.argtypes = [u32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32,
+                                       ctypes.c_float, P, P, ctypes.c_int, P]
+        L.jc_restated_attention.restype = ctypes.c_int
+        L.jc_restated_attention.argtypes = [P, P, u32, u32, u32, P]
         _lib = L
     return _lib
 
@@ -61,3 +70,40 @@ class Restated:
         if self.h:
             lib().jc_restated_free(self.h)
             self.h = None
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def gemm_scratch(torch, m, n, k, sms):
+    """Split-K workspace and zeroed counters for one restated GEMM shape (None when unsplit)."""
+    wf = lib().jc_restated_gemm_ws_floats(m, n, k, sms)
+    if not wf:
+        return None, None
+    cnt = lib().jc_restated_gemm_counters(m, n, k, sms)
+    return (torch.empty(wf, dtype=torch.float32, device="cuda"),
+            torch.zeros(cnt, dtype=torch.int32, device="cuda"))
+
+
+def gemm(torch, epi, a, w, c, sms, res=None, ws=None, counters=None, stats_in=None, colsum=None,
+         stats_out=None, zero=None, eps=1e-5, rope=None, bias=None):
+    """One restated GEMM on torch tensors, queued on torch's current stream. rope: the natural
+    [rows][32][2] f32 table."""
+    m, k = a.shape
+    n = w.shape[0]
+    rc = lib().jc_restated_gemm(epi, _p(a), _p(w), _p(c), _p(res), _p(ws), _p(counters),
+                                _p(stats_in), _p(colsum), _p(stats_out), _p(zero),
+                                0 if zero is None else zero.numel(), m, n, k, eps, _p(rope),
+                                _p(bias), sms, torch.cuda.current_stream().cuda_stream)
+    if rc != 0:
+        raise RuntimeError("restated gemm: bad arguments or launch failure")
+
+
+def attention(torch, qkv, o, window):
+    """The restated attention (one key range, as the reference's per-step launch)."""
+    n, d = o.shape
+    rc = lib().jc_restated_attention(_p(qkv), _p(o), n, window, d,
+                                     torch.cuda.current_stream().cuda_stream)
+    if rc != 0:
+        raise RuntimeError("restated attention: bad arguments or launch failure")

@@ -158,11 +158,22 @@ def gemm_shapes(cfg, n):
             ("head_l2", "biasresstats", D, F, HL)]
 
 
-def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=True):
+def restated_module():
+    """baseline/restated's binding when its library is built, else None."""
+    d = os.path.join(ROOT, "baseline", "restated")
+    if not os.path.exists(os.path.join(d, "librestated.so")):
+        return None
+    sys.path.insert(0, d)
+    import restated
+    return restated
+
+
+def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=True, restated=None):
     """Each GEMM shape and attention of the forward pass alone at n tokens (timed(): its launches
     in a CUDA graph on the launching stream, L2 flushed before every launch); `gemms` limits the
     GEMM shapes by name. Returns {name: (avg ms, launches per forward, algorithmic bytes,
-    flops)}."""
+    flops)}; with `restated` (baseline/restated's binding), also {name + "@restated": ...}: the
+    reference's kernel for the same shape on the same inputs, timed the same way."""
     from oracle import oracle as O
     out = {}
     stream = torch.cuda.current_stream()
@@ -191,6 +202,17 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
             (8 * n + 4 * N if epi & jc.EPI_LN else 0) + (4 * N if epi & jc.EPI_BIAS else 0) + \
             (256 * n if epi & jc.EPI_ROPE else 0) + (8 * n if epi & jc.EPI_STATS else 0)
         out[name] = (ms, count, bytes_, 2.0 * n * N * K)
+        if restated is not None:
+            sms = torch.cuda.get_device_properties(0).multi_processor_count
+            rws, rcnt = restated.gemm_scratch(torch, n, N, K, sms)
+            rtab = torch.from_numpy(O.rope_table(160000.0, n)).cuda()
+
+            def launch_ref():
+                restated.gemm(torch, epi, a, w, c, sms, res=c if epi & jc.EPI_RES else None,
+                              ws=rws, counters=rcnt, stats_in=st, colsum=cs, stats_out=so,
+                              rope=rtab, bias=bias)
+            out[name + "@restated"] = (timed(torch, stream, flush, launch_ref, reps), count,
+                                       bytes_, 2.0 * n * N * K)
     if not attention:
         return out
     heads = cfg.n_heads
@@ -208,6 +230,9 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
                                          for i in range(n)) / n
         out[name] = (ms, count, 2 * (n * 3 * heads * 64 + n * heads * 64),
                      4.0 * n * keys * heads * 64)
+        if restated is not None:
+            ms_r = timed(torch, stream, flush, lambda: restated.attention(torch, qkv, o, window), reps)
+            out[name + "@restated"] = (ms_r,) + out[name][1:]
     return out
 
 
@@ -263,22 +288,31 @@ def sweep_arm(args, rank, local):
     cfg = jc.default_config(max_positions=1024)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     pk, src = peaks()
+    rs = restated_module()
     rows = []
     with ClockSampler(local) as clk:
         for n in (72, 293, 448, 1024):
             rows += [("config1", n, k, v) for k, v in time_kernels(
                 jc, torch, cfg, flush, n=n, gemms=("qkv", "wo", "wi", "wo_mlp"),
-                attention=False).items()]
+                attention=False, restated=rs).items()]
         for n in (128, 512, 1024):
             rows += [("config2", n, k, v) for k, v in time_kernels(
-                jc, torch, cfg, flush, n=n, gemms=()).items()]
+                jc, torch, cfg, flush, n=n, gemms=(), restated=rs).items()]
     assert jc.device_error() == 0
+    ref_us = {(n, name.split("@")[0]): v[0] * 1e3 for _, n, name, v in rows if "@" in name}
     for conf, n, name, (ms, _, bytes_, flops) in rows:
+        if "@" in name:
+            continue
         gbs, tfs = bytes_ / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / 1e12
-        print(json.dumps({"sweep": conf, "kernel": name, "tokens": n, "us": ms * 1e3,
-                          "gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "tflops": tfs,
-                          "tensor_frac": tfs / pk["bf16_tflops"], "peak_source": src,
-                          "l2": "flushed before every launch"}), flush=True)
+        line = {"sweep": conf, "kernel": name, "tokens": n, "us": ms * 1e3,
+                "gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"], "tflops": tfs,
+                "tensor_frac": tfs / pk["bf16_tflops"], "peak_source": src,
+                "l2": "flushed before every launch"}
+        if (n, name) in ref_us:
+            # The reference's kernel (restated, baseline/restated) on the same inputs.
+            line["restated_us"] = ref_us[(n, name)]
+            line["speedup_vs_restated"] = ref_us[(n, name)] / (ms * 1e3)
+        print(json.dumps(line), flush=True)
     print(json.dumps({"sweep": "clocks", "clocks": clk.summary()}), flush=True)
 
 

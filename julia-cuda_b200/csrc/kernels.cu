@@ -445,12 +445,16 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // ---------------------------------------------------------------------------------------------
 // attention
 
-// Three shapes. The tensor-core kernel (attention_tc.cuh: 128-query CTAs, tcgen05) for global
+// Two kernels. The tensor-core kernel (attention_tc.cuh: 128-query CTAs, tcgen05) for global
 // attention from ATTN_TC_MIN tokens (its single MMA thread serialises ~130 cycles a
 // instruction, so it only pays once the key loop is long; sliding-window layers and shorter
-// sequences measured faster on the mma.sync kernel); below, the mma.sync kernel: up to 512 tokens
-// 32-query CTAs whose 4 key groups each take every 4th key tile (the most CTAs and the shortest
-// per-warp key loop), else 64-query CTAs with 2 key groups.
+// sequences measured faster on the mma.sync kernel); otherwise the mma.sync kernel with 32-query
+// CTAs: 4 key groups up to 384 tokens (256 threads, 132 KB of shared memory), else 2 key groups
+// (128 threads, 68 KB: up to three CTAs an SM, spread by spread_smem). Measured alone (cold L2,
+// us, global / window), 2 groups against 4 (one CTA an SM: 512 tokens take two waves) and 64 x 2:
+// 128 tokens 4.30 / 4.47 (4.76 / 4.97), 293: 6.77 / 5.98 (6.88 / 5.95), 512: 9.85 / 7.17 (13.36 /
+// 9.98), 768: 13.04 / 7.54 (64 x 2: 14.08 / 7.32), 1024 window 8.43 (9.35); 64 x 1 and 32 x 1
+// were slower throughout. In the 293-token forward 4 groups measured 660.8 against 662.7 us.
 struct AttnVariant {
     int qw, ks;
     bool tc;
@@ -469,7 +473,11 @@ void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
 static AttnVariant attn_variant(uint32_t n, uint32_t window) {
     if (n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load()))
         return AttnVariant{0, 0, true};
-    return n <= 512 ? AttnVariant{2, 4, false} : AttnVariant{4, 2, false};
+    // A/B knob: JC_ATTN_SHAPE=<query warps><key groups>, e.g. "41".
+    static const char *force = getenv("JC_ATTN_SHAPE");
+    if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '4')
+        return AttnVariant{force[0] - '0', force[1] - '0', false};
+    return n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
 }
 
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
@@ -511,14 +519,40 @@ static bool launch_attn_tc(const AttnParams &p, uint32_t chunks, cudaStream_t s,
 
 size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32) * heads; }
 
+// The dynamic shared memory a launch of `ctas` CTAs (each needing `need` bytes) requests so that
+// an SM holds at most ceil(ctas / SMs) of them. Under programmatic dependent launch a grid's CTAs
+// are placed while the previous kernel still holds most SMs: small CTAs would pack several to
+// each of the few free SMs and run there in turn (a 120-CTA attention grid at 293 tokens on ~40
+// SMs), instead of spreading over the SMs the previous kernel frees. One CTA more than the cap
+// must not fit in an SM's shared memory (less the per-CTA reservation).
+static int spread_smem(int need, uint32_t ctas) {
+    static const int3 dev = []() {
+        int d = 0, per_sm = 0, reserved = 0, sms = 0;
+        cudaGetDevice(&d);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d);
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, d);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+        return make_int3(per_sm, reserved, sms);
+    }();
+    if (dev.x <= 0 || dev.z <= 0) return need;
+    const uint32_t cap = (ctas + (uint32_t)dev.z - 1) / (uint32_t)dev.z;
+    const int spread = ((dev.x / (int)(cap + 1) - dev.y + 1) + 127) / 128 * 128;
+    return std::min(std::max(need, spread), dev.x - dev.y);
+}
+
 template <int QW, int KS>
 static bool launch_attn_inst(const AttnParams &p, uint32_t chunks, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
     using S = AttnShape<QW, KS>;
     auto kern = attention_kernel<QW, KS>;
-    if (!ensure_smem(kern, S::SMEM, smem_set)) return false;
+    // Permission for any request spread_smem makes (at most an SM's memory less the reservation).
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (!ensure_smem(kern, std::max(optin, S::SMEM), smem_set)) return false;
     dim3 grid((p.n + S::QT - 1) / S::QT, p.heads, chunks);
-    return launch_ex(kern, grid, dim3(S::THREADS), S::SMEM, s, pdl, "attention launch", p);
+    const int smem = std::min(spread_smem(S::SMEM, grid.x * grid.y * grid.z), std::max(optin, S::SMEM));
+    return launch_ex(kern, grid, dim3(S::THREADS), smem, s, pdl, "attention launch", p);
 }
 
 bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
@@ -537,8 +571,16 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
     AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg};
     const AttnVariant v = attn_variant(a.n, a.window);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
-    if (v.qw == 2) return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);
-    return launch_attn_inst<4, 2>(p, a.kv_chunks, s, pdl);
+    switch (v.qw * 10 + v.ks) {
+        case 24: return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);
+        case 42: return launch_attn_inst<4, 2>(p, a.kv_chunks, s, pdl);
+        case 41: return launch_attn_inst<4, 1>(p, a.kv_chunks, s, pdl);
+        case 22: return launch_attn_inst<2, 2>(p, a.kv_chunks, s, pdl);
+        case 21: return launch_attn_inst<2, 1>(p, a.kv_chunks, s, pdl);
+        default:
+            set_error("attention: no compiled shape for these query warps / key groups");
+            return false;
+    }
 }
 
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) {
