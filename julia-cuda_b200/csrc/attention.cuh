@@ -6,11 +6,12 @@
 // split inside the CTA: a CTA takes 16 * QW queries of one head and runs QW x KS warps; warp group
 // g (QW warps, 16 queries each) streams key tiles g, g + KS, g + 2 KS, ... of the CTA's key range
 // through its own double-buffered, XOR-swizzled shared-memory slots with cp.async, keeping S and
-// the running max / sum in registers (online softmax in exp2), rounding P to f16 for the P.V
-// product and O in f32. The KS partial results meet in shared memory and are merged in group
-// order, so the output does not depend on timing. Sequences of a few hundred tokens therefore run
-// at most a couple of dependent key-tile steps per warp. d = 64 tiles are too small for 128-row
-// tcgen05 tiles at these lengths, so the products use the 16x8x16 tensor-core MMA.
+// the running max / sum in registers (online softmax in exp2 on the special-function unit),
+// rounding P to f16 for the P.V product and O in f32. The KS partial results meet in shared
+// memory and are merged in group order, so the output does not depend on timing. Sequences of a
+// few hundred tokens therefore run at most a couple of dependent key-tile steps per warp.
+// d = 64 tiles are too small for 128-row tcgen05 tiles at these lengths, so the products use
+// the 16x8x16 tensor-core MMA.
 //
 // Sliding-window CTAs only visit the key tiles some query of theirs can reach. For long global
 // sequences the key range can also be split across CTAs (gridDim.z ranges): each range stores
@@ -227,14 +228,14 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
             const float m_new = fmaxf(mx[h], m);
             const float base = m_new == -INFINITY ? 0.f : m_new;
-            const float alpha = exp2f(mx[h] - base);
+            const float alpha = ex2_approx(mx[h] - base);
             mx[h] = m_new;
             float rs = 0.f;
 #pragma unroll
             for (int jt = 0; jt < 8; jt++) {
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const float pv = exp2f(s[jt][2 * h + e] - base);
+                    const float pv = ex2_approx(s[jt][2 * h + e] - base);
                     s[jt][2 * h + e] = pv;
                     rs += pv;
                 }

@@ -53,12 +53,6 @@ struct AttnTcParams {
 // Barrier among the 128 softmax threads (warps 0-3) only.
 __device__ __forceinline__ void group_bar_atc() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// 2^x on the special-function unit (PTX ex2.approx.ftz; 2^-inf = 0).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 // Descriptor of an MN-major operand tile whose K rows are 128 bytes (64 f16 along N), swizzled
 // with the 128-byte pattern: stride byte offset = the next group of 8 K rows (1024 B); the leading

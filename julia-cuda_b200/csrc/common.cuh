@@ -327,6 +327,13 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
 // GELU(x) = x * Phi(x) with Phi from the Abramowitz & Stegun 7.1.26 erf approximation (the
 // formula julia-rs and the reference kernels use; kernels/src/gemm.rs:139-150). The reciprocal is
 // the hardware approximation (a couple of ulp; the result's error stays near 1e-7 relative).
+// 2^x on the special-function unit (PTX ex2.approx.ftz; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float gelu_as(float x) {
     float t = __fdividef(1.0f, 1.0f + 0.2316419f * fabsf(x));
     float p = 0.5f * 1.061405429f;
