@@ -449,9 +449,9 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // attention from ATTN_TC_MIN tokens (its single MMA thread serialises ~130 cycles a
 // instruction, so it only pays once the key loop is long; sliding-window layers and shorter
 // sequences measured faster on the mma.sync kernel); otherwise the mma.sync kernel with 32-query
-// CTAs: 4 key groups up to 384 tokens (256 threads, 132 KB of shared memory), else 2 key groups
-// (128 threads, 68 KB: up to three CTAs an SM, spread by spread_smem). Measured alone (cold L2,
-// us, global / window), 2 groups against 4 (one CTA an SM: 512 tokens take two waves) and 64 x 2:
+// CTAs: 4 key groups from 193 to 384 tokens (256 threads, 132 KB of shared memory), else 2 key
+// groups (128 threads, 68 KB: up to three CTAs an SM, spread by spread_smem). Measured alone (cold
+// L2, us, global / window), 2 groups against 4 (one CTA an SM: 512 tokens take two waves) and 64 x 2:
 // 128 tokens 4.30 / 4.47 (4.76 / 4.97), 293: 6.77 / 5.98 (6.88 / 5.95), 512: 9.85 / 7.17 (13.36 /
 // 9.98), 768: 13.04 / 7.54 (64 x 2: 14.08 / 7.32), 1024 window 8.43 (9.35); 64 x 1 and 32 x 1
 // were slower throughout. In the 293-token forward 4 groups measured 660.8 against 662.7 us.
@@ -477,7 +477,7 @@ static AttnVariant attn_variant(uint32_t n, uint32_t window) {
     static const char *force = getenv("JC_ATTN_SHAPE");
     if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '4')
         return AttnVariant{force[0] - '0', force[1] - '0', false};
-    return n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
+    return n > 192 && n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
 }
 
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
