@@ -108,6 +108,11 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait (bounded) for its first sample, so that a
+            # short timed region still has samples from inside it.
+            t0 = time.perf_counter()
+            while not self.rows and time.perf_counter() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
