@@ -386,9 +386,10 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
 }
 
 // Two CTAs per SM (at most 128 registers a thread), so the 64-query shape's grid at 1024 tokens
-// (16 query tiles x 12 heads) is resident in one wave.
+// (16 query tiles x 12 heads) is resident in one wave; five key groups (320 threads, 164 KB of
+// shared memory) fit one CTA an SM whatever the registers, so they are not capped.
 template <int QW, int KS>
-__global__ void __launch_bounds__(32 * QW * KS, 2) attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(32 * QW * KS, KS > 4 ? 1 : 2) attention_kernel(const AttnParams p) {
     extern __shared__ __align__(128) uint8_t att_smem[];
     attention_task<QW, KS>(p, att_smem, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z, true);
 }

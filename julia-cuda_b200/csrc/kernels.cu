@@ -455,6 +455,9 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // 128 tokens 4.30 / 4.47 (4.76 / 4.97), 293: 6.77 / 5.98 (6.88 / 5.95), 512: 9.85 / 7.17 (13.36 /
 // 9.98), 768: 13.04 / 7.54 (64 x 2: 14.08 / 7.32), 1024 window 8.43 (9.35); 64 x 1 and 32 x 1
 // were slower throughout. In the 293-token forward 4 groups measured 660.8 against 662.7 us.
+// Global attention over exactly five key tiles (257-320 tokens) takes 5 groups of one tile each
+// (320 threads, 164 KB), so no group waits at the merge for a second tile: 293 tokens 6.78 ->
+// 6.30 us alone, forward 662.9 -> 656.9 us.
 struct AttnVariant {
     int qw, ks;
     bool tc;
@@ -475,8 +478,10 @@ static AttnVariant attn_variant(uint32_t n, uint32_t window) {
         return AttnVariant{0, 0, true};
     // A/B knob: JC_ATTN_SHAPE=<query warps><key groups>, e.g. "41".
     static const char *force = getenv("JC_ATTN_SHAPE");
-    if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '4')
+    if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '5')
         return AttnVariant{force[0] - '0', force[1] - '0', false};
+    // Global attention over exactly five key tiles: one tile for each of five key groups.
+    if (window == 0 && n > 256 && n <= 320) return AttnVariant{2, 5, false};
     return n > 192 && n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
 }
 
@@ -577,6 +582,7 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         case 41: return launch_attn_inst<4, 1>(p, a.kv_chunks, s, pdl);
         case 22: return launch_attn_inst<2, 2>(p, a.kv_chunks, s, pdl);
         case 21: return launch_attn_inst<2, 1>(p, a.kv_chunks, s, pdl);
+        case 25: return launch_attn_inst<2, 5>(p, a.kv_chunks, s, pdl);
         default:
             set_error("attention: no compiled shape for these query warps / key groups");
             return false;
