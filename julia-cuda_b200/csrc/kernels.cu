@@ -457,7 +457,10 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
 // were slower throughout. In the 293-token forward 4 groups measured 660.8 against 662.7 us.
 // Global attention over exactly five key tiles (257-320 tokens) takes 5 groups of one tile each
 // (320 threads, 164 KB), so no group waits at the merge for a second tile: 293 tokens 6.78 ->
-// 6.30 us alone, forward 662.9 -> 656.9 us.
+// 6.30 us alone, forward 662.9 -> 656.9 us. Window layers from 193 to 768 tokens take 3 groups (a
+// 32-query CTA reaches at most three key tiles; 192 threads, 100 KB): 293 tokens 5.92 -> 5.45 us,
+// 512: 7.08 -> 6.3 us alone, forward 655.6 -> 650.0 us; at 1024 tokens the grid would take two
+// waves of two CTAs an SM (10.5 against 8.2 us).
 struct AttnVariant {
     int qw, ks;
     bool tc;
@@ -482,6 +485,9 @@ static AttnVariant attn_variant(uint32_t n, uint32_t window) {
         return AttnVariant{force[0] - '0', force[1] - '0', false};
     // Global attention over exactly five key tiles: one tile for each of five key groups.
     if (window == 0 && n > 256 && n <= 320) return AttnVariant{2, 5, false};
+    // A 32-query CTA of a +-64 window reaches at most three key tiles: three groups of one tile,
+    // while the grid (12 heads) stays within two 100 KB CTAs an SM.
+    if (window > 0 && window <= 64 && n > 192 && n <= 768) return AttnVariant{2, 3, false};
     return n > 192 && n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
 }
 
@@ -583,6 +589,7 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         case 22: return launch_attn_inst<2, 2>(p, a.kv_chunks, s, pdl);
         case 21: return launch_attn_inst<2, 1>(p, a.kv_chunks, s, pdl);
         case 25: return launch_attn_inst<2, 5>(p, a.kv_chunks, s, pdl);
+        case 23: return launch_attn_inst<2, 3>(p, a.kv_chunks, s, pdl);
         default:
             set_error("attention: no compiled shape for these query warps / key groups");
             return false;
