@@ -71,6 +71,33 @@ def request(rank, vocab, n=SEQ, head=0):
     return ids, markers
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), for the CPU baselines."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def headline_config(world, n_tok=SEQ, head_length=0):
+    """The headline's workload, printed identically by both arms (this library's and the
+    reference's), so the two lines describe the same configuration."""
+    if n_tok == SEQ and not head_length:
+        workload = ("config0: 293-token request, 4 markers, batch 1 per engine; hidden 768, "
+                    "12 heads, 22 layers, 2 head layers, scorer 384")
+    else:
+        workload = (f"{'config4: ' if n_tok == 1024 and head_length == 512 else ''}"
+                    f"{n_tok}-token request, head on rows [0, {head_length or n_tok}), "
+                    f"4 markers inside them, batch 1 per engine; hidden 768, 12 heads, 22 layers")
+    return {"workload": workload, "global_batch": world, "seq_len": n_tok,
+            "head_rows": head_length or n_tok, "parallelism": f"replicas x{world}",
+            "l2": "flushed (256 MiB write) before every timed step"}
+
+
 def cpu_forward_sample(budget_s=20.0, max_runs=5, n=SEQ, head=0):
     """The oracle's f32 forward (config 0, or n tokens with the head on `head` rows) on all host
     threads; returns (s/request, runs, cores)."""
@@ -372,27 +399,38 @@ def reference_arm(args, rank, world):
     O.set_num_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     c = O.config(max_positions=1024)
     raw = O.init_random(c, SEED)
-    ids, markers = request(0, c.vocab)
-    for _ in range(min(args.warmup, 1)):
-        O.forward_f32(c, raw, ids, markers, 0)
-    steps = max(1, min(args.steps, 20))
+    n_tok = args.seq
+    ids, markers = request(0, c.vocab, n_tok, args.head_length)
+    warmup = max(args.warmup, 3)  # as this library's arm
+    for _ in range(warmup):
+        O.forward_f32(c, raw, ids, markers, 0, head_rows=args.head_length)
+    # Every step is one whole request; at ~0.2 s a request on the host, the timed steps stop
+    # after 90 s of them (the line reports how many ran).
     t0 = time.perf_counter()
-    for _ in range(steps):
-        O.forward_f32(c, raw, ids, markers, 0)
+    steps = 0
+    while steps < max(args.steps, 1) and (steps == 0 or time.perf_counter() - t0 < 90.0):
+        O.forward_f32(c, raw, ids, markers, 0, head_rows=args.head_length)
+        steps += 1
     el = time.perf_counter() - t0
     per = el / steps
     cores = O.num_threads()
     v = 1.0 / per
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "requests/s",
-        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 1),
+        "impl": "reference", "metric": METRIC if n_tok == SEQ and not args.head_length else
+        f"requests/s (embed->logits, {n_tok}-token requests, head on "
+        f"{args.head_length or n_tok} rows, batch 1 per engine)",
+        "value": v, "unit": "requests/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": per * 1e3, "us_per_request": per * 1e6, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config0: 293-token request, batch 1, hidden 768, 22 layers + head",
-                   "global_batch": 1, "seq_len": SEQ, "parallelism": "host threads"},
+        "config": headline_config(world, n_tok, args.head_length),
+        "path": "the reference's f32 CPU path (julia-rs), restated in C (oracle/oracle.c), "
+                "OpenMP over all host threads, rank 0 only",
         "cpu_baseline": {"value": v, "unit": "requests/s", "cores": cores, "kind": "port",
-                         "sample": f"{steps} full requests (f32 restatement of julia-rs; the Rust "
-                                   f"reference and julia-rs cannot be built here)"},
+                         "cpu_model": cpu_model(),
+                         "sample": f"{steps} full {n_tok}-token requests (f32 restatement of "
+                                   f"julia-rs; the Rust reference and julia-rs cannot be built "
+                                   f"here)"},
         "e2e": {"value": v, "unit": "requests/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -447,30 +485,62 @@ def restated_arm(args, local):
     print(json.dumps(line), flush=True)
 
 
+def restated_headline(jc, torch, cfg, eng, ids, markers, flush, steps, local):
+    """The reference's per-step GPU forward restated (baseline/restated) and this engine on the
+    headline's request and weights, each timed per request with CUDA events embed -> logits (the
+    reference's own timing) after an L2 flush, alternating so both see the same clocks. Returns
+    the headline keys, or {} when the restated library is not built."""
+    rs = restated_module()
+    if rs is None:
+        return {"restated_us_per_request": None}
+    raw = jc.init_random(cfg, SEED)
+    ref = rs.Restated(cfg, raw, max_length=1024, device=local)
+    try:
+        for _ in range(3):
+            ref.run(ids, markers, 0)
+            eng.run([(ids, markers, 0)])
+        r_ms, o_ms = [], []
+        d = 0.0
+        for _ in range(max(1, min(steps, 200))):
+            flush.zero_()
+            torch.cuda.synchronize()
+            lr, t = ref.run(ids, markers, 0)
+            r_ms.append(t)
+            flush.zero_()
+            torch.cuda.synchronize()
+            lo, t2 = eng.run([(ids, markers, 0)])
+            o_ms.append(float(t2[0]))
+            d = max(d, float(np.max(np.abs(lr - lo[0]))))
+    finally:
+        ref.close()
+    r_us, o_us = statistics.mean(r_ms) * 1e3, statistics.mean(o_ms) * 1e3
+    return {"restated_us_per_request": r_us, "ours_us_per_request_same_timing": o_us,
+            "speedup_vs_restated": r_us / o_us, "restated_max_abs_dlogit": d,
+            "restated_samples": len(r_ms)}
+
+
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
 SERVING_METRIC = "requests/s (config 3 serving: log-normal lengths around 293 tokens, 4 markers)"
 
 
-def serving_arm(args, rank, world, local, replicas):
-    """Config 3: a seeded set of requests (log-normal lengths, mean 293, clipped to [32, 1024])
-    partitioned over the ranks by longest processing time, each rank serving its share through
-    julia_cuda_run (batches of up to 16, host arrays in and out) on its own GPU. Throughput =
-    all requests / the slowest rank's wall time."""
-    import torch
-    torch.cuda.set_device(local)
-    replicas.init(world, "nccl", device=torch.device("cuda", local))
-    jc = importlib.import_module("julia-cuda_b200")
+def serve_config3(requests, pack, max_length, rank, world, local, replicas, jc):
+    """Config 3 on every rank: a seeded set of `requests` requests (log-normal lengths, mean 293,
+    clipped to [32, 1024]) partitioned over the ranks by longest processing time, each rank
+    serving its share through julia_cuda_run (host arrays in and out) on its own GPU, packed into
+    forwards of up to `pack` tokens (0: one forward per request). Every rank takes the same
+    collective steps. Returns (requests/s = all requests / the slowest rank's wall time, the
+    ranks' wall times, rank 0's summed GPU ms, total tokens)."""
     # Requests are at most 1024 tokens; a longer engine capacity only serves larger packs.
-    cap = max(1024, args.max_length)
+    cap = max(1024, max_length, pack)
     cfg = jc.default_config(max_positions=cap)
     eng = jc.Engine.load_random(cfg, SEED, max_length=cap, device=local)
-    reqs = replicas.serving_requests(args.requests, SEED, cfg.vocab)
+    reqs = replicas.serving_requests(requests, SEED, cfg.vocab)
     mine = [reqs[i] for i in replicas.shard_lpt([len(r[0]) for r in reqs], world)[rank]]
     batch = 16
-    if args.pack:
-        # Requests packed into forwards of up to --pack tokens (julia_cuda_set_packing); one
+    if pack:
+        # Requests packed into forwards of up to `pack` tokens (julia_cuda_set_packing); one
         # call queues up to 16 forwards.
-        eng.set_packing(args.pack)
+        eng.set_packing(pack)
         batch = 64
         warm = mine  # the pack shapes this share makes
     else:
@@ -490,24 +560,39 @@ def serving_arm(args, rank, world, local, replicas):
         _, ms = eng.run(mine[i:i + batch])
         prev = None
         for v in ms:  # the requests of a packed forward are consecutive and report its time
-            if not args.pack or v != prev:
+            if not pack or v != prev:
                 gpu_ms += float(v)
             prev = v
     wall = time.perf_counter() - t0
-    slowest = replicas.max_over_ranks(wall, world, device="cuda")
+    assert eng.device_error() == 0
+    eng.close()
+    walls = replicas.all_over_ranks(wall, world, device="cuda")
+    return requests / max(walls), walls, gpu_ms, sum(len(r[0]) for r in reqs)
+
+
+def serving_arm(args, rank, world, local, replicas):
+    """Config 3 alone (serve_config3), one JSON line."""
+    import torch
+    torch.cuda.set_device(local)
+    replicas.init(world, "nccl", device=torch.device("cuda", local))
+    jc = importlib.import_module("julia-cuda_b200")
+    rate, walls, gpu_ms, tokens = serve_config3(args.requests, args.pack, args.max_length, rank,
+                                                world, local, replicas, jc)
+    slowest = max(walls)
+    batch = 64 if args.pack else 16
     if rank == 0:
-        tokens = sum(len(r[0]) for r in reqs)
         print(json.dumps({
-            "metric": SERVING_METRIC, "value": args.requests / slowest, "unit": "requests/s",
+            "metric": SERVING_METRIC, "value": rate, "unit": "requests/s",
             "n_gpus": world, "requests": args.requests, "tokens": tokens,
-            "wall_s": slowest, "gpu_ms_rank0": gpu_ms, "higher_is_better": True,
+            "wall_s": slowest, "rank_wall_s": walls,
+            "imbalance": max(walls) / (sum(walls) / len(walls)) - 1.0,
+            "gpu_ms_rank0": gpu_ms, "higher_is_better": True,
             "scaling": "strong", "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
             "config": {"workload": "config3: log-normal lengths (sigma 0.5, mean 293, [32, 1024]), "
                                    "4 markers, qtype 0, seed 1234", "partition": "LPT by cost",
                        "path": "julia_cuda_run, per-step kernels, " + (
                            f"requests packed into forwards of up to {args.pack} tokens, {batch} a call"
                            if args.pack else "one forward per request, 16 a call")}}), flush=True)
-    eng.close()
     replicas.finalize(world)
 
 
@@ -536,6 +621,11 @@ def main():
     ap.add_argument("--restated", action="store_true",
                     help="the reference's per-step kernels restated (baseline/restated) against "
                          "this library on the headline request")
+    ap.add_argument("--serving-requests", type=int, default=4096,
+                    help="headline: config 3 served after the timed region on every rank with "
+                         "this many requests (0: skip)")
+    ap.add_argument("--serving-pack", type=int, default=6144,
+                    help="headline: the config-3 pass's pack size in tokens (0: unpacked)")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
                                       "attn_global", "attn_window"],
                     help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")
@@ -587,7 +677,7 @@ def main():
     for _ in range(args.warmup):
         eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=fused, stream=stream)
     torch.cuda.synchronize()
-    assert jc.device_error() == 0
+    assert eng.device_error() == 0
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
@@ -601,7 +691,7 @@ def main():
         barrier()
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_s = sum(step_ms) / 1e3
-    assert jc.device_error() == 0
+    assert eng.device_error() == 0
     total_s = replicas.max_over_ranks(total_s, world, device="cuda")
     value = replicas.job_rate(args.steps, total_s, world)
     ms_per_step = total_s * 1e3 / args.steps
@@ -624,8 +714,31 @@ def main():
     e2e_total = replicas.max_over_ranks(e2e_total, world, device="cuda")
     e2e_value = replicas.job_rate(args.steps, e2e_total, world)
 
-    roofline = kernels = None
+    # The box-level workload on the same ranks, after the headline: every rank
+    # serves its LPT share of the seeded request set, packed, through julia_cuda_run.
+    serving = None
+    if args.serving_requests > 0:
+        rate, walls, gpu_ms3, tokens3 = serve_config3(args.serving_requests, args.serving_pack,
+                                                      args.serving_pack, rank, world, local,
+                                                      replicas, jc)
+        serving = {"metric": SERVING_METRIC, "value": rate, "unit": "requests/s",
+                   "requests": args.serving_requests, "tokens": tokens3, "wall_s": max(walls),
+                   "rank_wall_s": walls,
+                   "imbalance": max(walls) / (sum(walls) / len(walls)) - 1.0,
+                   "gpu_ms_rank0": gpu_ms3, "scaling": "strong",
+                   "config": {"workload": "config3: log-normal lengths (sigma 0.5, mean 293, "
+                                          "[32, 1024]), 4 markers, qtype 0, seed 1234",
+                              "partition": "LPT by cost",
+                              "path": f"julia_cuda_run, per-step kernels, requests packed into "
+                                      f"forwards of up to {args.serving_pack} tokens"
+                              if args.serving_pack else
+                              "julia_cuda_run, per-step kernels, one forward per request"}}
+
+    roofline = kernels = restated_line = None
     cpu = None
+    if rank == 0 and n_tok == SEQ and not args.head_length and fused == 0:
+        restated_line = restated_headline(jc, torch, cfg, eng, ids, markers, flush, args.steps,
+                                          local)
     if rank == 0:
         pk, src = peaks()
         kt = time_kernels(jc, torch, cfg, flush, n=n_tok)
@@ -662,6 +775,7 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             per, runs, cores = cpu_forward_sample(n=n_tok, head=args.head_length)
             cpu = {"value": 1.0 / per, "unit": "requests/s", "cores": cores, "kind": "port",
+                   "cpu_model": cpu_model(),
                    "sample": f"{runs} full {n_tok}-token requests, f32 restatement of the "
                              f"reference's CPU path (julia-rs), OpenMP"}
     launches = eng.launches_per_forward(n_tok, MARKERS, fused) * args.steps
@@ -669,25 +783,17 @@ def main():
              2: "whole-model persistent kernel (one cooperative launch)"}
     if n_tok == SEQ and not args.head_length:
         metric = METRIC
-        workload = ("config0: 293-token request, 4 markers, batch 1 per engine; hidden 768, "
-                    "12 heads, 22 layers, 2 head layers, scorer 384")
     else:
         metric = (f"requests/s (embed->logits, {n_tok}-token requests, head on "
                   f"{args.head_length or n_tok} rows, batch 1 per engine)")
-        workload = (f"{'config4: ' if n_tok == 1024 and args.head_length == 512 else ''}"
-                    f"{n_tok}-token request, head on rows [0, {args.head_length or n_tok}), "
-                    f"4 markers inside them, batch 1 per engine; hidden 768, 12 heads, 22 layers")
     if rank == 0:
         line = {
             "metric": metric, "value": value, "unit": "requests/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "us_per_request": ms_per_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 storage, f32 accumulation", "data": "synthetic",
-            "config": {"workload": workload, "global_batch": world, "seq_len": n_tok,
-                       "head_rows": args.head_length or n_tok,
-                       "parallelism": f"replicas x{world}",
-                       "l2": "flushed (256 MiB write) before every timed step",
-                       "path": paths[fused]},
+            "config": headline_config(world, n_tok, args.head_length),
+            "path": paths[fused],
             "e2e": {"value": e2e_value, "unit": "requests/s",
                     "us_per_request": e2e_total / args.steps * 1e6,
                     "gpu_ms_per_request": statistics.mean(gpu_ms),
@@ -697,6 +803,13 @@ def main():
             "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
+        if restated_line:
+            # The 3x target's denominator: the reference's per-step GPU kernels (restated in CUDA
+            # C++, baseline/restated) on the same request and weights, same L2 flush, after the
+            # headline's timed region.
+            line.update(restated_line)
+        if serving:
+            line["serving"] = serving
         print(json.dumps(line), flush=True)
     eng.close()
     replicas.finalize(world)

@@ -50,9 +50,12 @@ typedef struct jc_model_config {
 /* The kernel tier this library was built for ("sm_100a"), static. Replaces src/capi.rs:56-62. */
 const char *julia_cuda_tier(void);
 
-/* Opens a checkpoint directory and uploads it to GPU 0 (src/capi.rs:64-85). Reads the raw model
- * format below from `dir/jc_config.bin` + `dir/jc_weights.f32` (written by
- * julia_cuda_save_raw); `max_length` 0 means the model's max_positions. */
+/* Opens a checkpoint directory and uploads it to GPU 0 (src/capi.rs:64-85). The reference's
+ * layout (src/checkpoint.rs:27-62): dir/model.safetensors + dir/encoder/config.json (the
+ * ModernBERT encoder's Hugging Face config) + dir/julia_config.json (the head and scorer), read as
+ * julia_cuda_read_checkpoint documents; or, when there is no model.safetensors, the raw model
+ * format below from dir/jc_config.bin + dir/jc_weights.f32 (julia_cuda_save_raw). `max_length` 0
+ * means the model's max_positions. */
 JcEngine *julia_cuda_load(const char *dir, size_t max_length, char *err, size_t err_len);
 
 /* Frees an engine (NULL is fine). Replaces src/capi.rs:87-96. */
@@ -95,6 +98,40 @@ void julia_cuda_init_random(const jc_model_config *cfg, uint64_t seed, float *ra
 int julia_cuda_save_raw(const char *dir, const jc_model_config *cfg, const float *raw,
                         char *err, size_t err_len);
 
+/* Reads a checkpoint directory (model.safetensors + encoder/config.json + julia_config.json) on the
+ * host into *cfg and the raw format (raw_cap floats at raw; raw NULL: only *cfg and *raw_len).
+ * Tensors are F32, F16 or BF16, named as the public layouts they come from: the encoder as Hugging
+ * Face ModernBERT (`<prefix>embeddings.tok_embeddings.weight`, `<prefix>embeddings.norm.weight`,
+ * `<prefix>layers.{i}.attn_norm.weight` (i > 0), `.attn.Wqkv.weight`, `.attn.Wo.weight`,
+ * `.mlp_norm.weight`, `.mlp.Wi.weight` (GELU inputs, then gates), `.mlp.Wo.weight`,
+ * `<prefix>final_norm.weight`; the prefix "model.", "encoder.model.", "encoder." or none, found by
+ * probing), the head layers as torch.nn.TransformerEncoderLayer (`head.layers.{i}.norm1.weight`,
+ * `.norm1.bias`, `.self_attn.in_proj_weight`, `.self_attn.in_proj_bias`,
+ * `.self_attn.out_proj.weight`, `.self_attn.out_proj.bias`, `.norm2.weight`, `.norm2.bias`,
+ * `.linear1.weight`, `.linear1.bias`, `.linear2.weight`, `.linear2.bias`), `type_emb.weight`
+ * [n_qtypes, D] and `scorer.{norm,lin1,lin2}.{weight,bias}`. The reference reads the head and
+ * scorer names through julia-rs (not available here), so an optional dir/jc_names.json overrides
+ * any of them: {"encoder_prefix": "...", "names": {"<name above, encoder names without the
+ * prefix>": "<name in the file>"}}. encoder/config.json gives hidden_size, intermediate_size,
+ * num_hidden_layers, vocab_size (required), num_attention_heads, norm_eps, local_attention (the
+ * window's full span), global_attn_every_n_layers, max_position_embeddings, global_rope_theta and
+ * local_rope_theta; julia_config.json (optional) head_layers, head_ff, scorer_hidden, n_qtypes and
+ * head_eps, each otherwise taken from the tensors' shapes (or the benchmark model's default).
+ * Every shape is checked. Returns 0, or -1 with the reason. No counterpart in the reference's C
+ * ABI (its Engine::load does this internally, src/engine.rs:118-150). */
+int julia_cuda_read_checkpoint(const char *dir, jc_model_config *cfg, float *raw, size_t raw_cap,
+                               size_t *raw_len, char *err, size_t err_len);
+/* Writes cfg + raw as such a directory under the default names (dtype 0 F32, 1 F16, 2 BF16). */
+int julia_cuda_save_checkpoint(const char *dir, const jc_model_config *cfg, const float *raw,
+                               int dtype, char *err, size_t err_len);
+/* The load-time preparation alone, on the host (src/weights.rs:143-238, src/prep.rs): the f16
+ * arena (bit patterns) and the f32 arena an engine of max_length rows (0: max_positions) uploads.
+ * *f16_len / *f32_len receive their sizes; f16 / f32 may be NULL to ask only for them. */
+int julia_cuda_prepare_host(const jc_model_config *cfg, const float *raw, size_t raw_len,
+                            size_t max_length, uint16_t *f16, size_t f16_cap, float *f32,
+                            size_t f32_cap, size_t *f16_len, size_t *f32_len, char *err,
+                            size_t err_len);
+
 /* Builds an engine on GPU `device` from raw weights (prepared on the host: LayerNorm folds,
  * GeGLU interleave, f16 conversion, RoPE tables), buffers for sequences up to max_length. */
 JcEngine *julia_cuda_load_raw(const jc_model_config *cfg, const float *raw, size_t raw_len,
@@ -112,12 +149,34 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
                               int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
                               char *err, size_t err_len);
 
+/* julia_cuda_forward_device with every stage traced (the reference's --check traces the encoder
+ * step by step and the head from the encoder's output, src/check.rs:177-224, :484-548, :564-596).
+ * Any trace pointer may be NULL. d_trace: the residual stream after each encoder layer
+ * [n_layers][n][D]; d_head_trace: the head's stream [n_head_layers + 1][nh][D], its input (final
+ * LayerNorm + type embedding), then after each head layer, nh = the head's rows (n unless
+ * julia_cuda_set_head_length limits them); d_scorer_trace: the scorer's hidden layer after GELU
+ * for each marker [n_markers][scorer_hidden]. All f16. Slower: no CUDA graph. Returns 0 or -1. */
+int julia_cuda_forward_trace(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                             const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                             int layer_fused, float *d_logits, uint16_t *d_trace,
+                             uint16_t *d_head_trace, uint16_t *d_scorer_trace, void *stream,
+                             char *err, size_t err_len);
+
 /* Failure detection: runs the persistent kernel with a grid barrier that waits for one CTA more
  * than the grid has, so every wait must give up after timeout_ns; writes the device error code it
  * recorded (JC_DEV_TIMEOUT_GRID = 4) and leaves the engine usable. No counterpart in the
  * reference (its grid barrier spins forever, kernels/src/gemm.rs:444-463). */
 int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint32_t *code,
                                      char *err, size_t err_len);
+
+/* Waits for the engine's stream, then reads and clears the engine's own device error word into
+ * *code (0: none; JC_DEV_* codes as jc_device_error). Every kernel an engine launches records
+ * device-side timeouts in this word, not in the module's word that jc_device_error reads, so two
+ * engines on one GPU (or an engine beside bare jc_* calls) each see only their own errors. On an
+ * error it also re-zeroes the engine's persistent-kernel, split-K and split-KV counters.
+ * julia_cuda_run checks the word itself after every queue of requests; callers of
+ * julia_cuda_forward_device read it here. Returns 0, or -1. No counterpart in the reference. */
+int julia_cuda_device_error(JcEngine *engine, uint32_t *code, char *err, size_t err_len);
 
 /* Limits the head to the first `rows` rows of every later request (0: all rows, the default
  * and the reference's GPU behaviour, src/forward.rs:432-436): the final LayerNorm, the head
@@ -164,7 +223,8 @@ int julia_cuda_engine_config(const JcEngine *engine, jc_model_config *cfg, size_
 /* c = epilogue(a . w^T): a [m, k] f16, w [n, k] f16, c [m, n] f16 ([m, n/2] for GEGLU), k a
  * multiple of 64. bn (32/64/128) and splits (1..8) of 0 choose automatically. ws / counters: the
  * split-K workspace (jc_gemm_ws_floats floats, jc_gemm_counters zeroed u32, kept zero between
- * calls). splits = -2 or -4 splits K across a thread-block cluster of that many CTAs instead, which
+ * calls; after jc_device_error reports a timeout the caller must zero the counters again: a split
+ * that gave up never arrives, so its tile's counter stays non-zero). splits = -2 or -4 splits K across a thread-block cluster of that many CTAs instead, which
  * reduce their partials through distributed shared memory (64- or 128-column tiles; no workspace,
  * ws / counters unused; same result bits as that many workspace splits). stats_in / stats_out:
  * [m][2] f32 (sum, sum of squares). rope: 16 x m float4 (cos, sin of two pairs; jc_prep_rope_gemm).
@@ -192,7 +252,8 @@ int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *sp
 /* o = softmax(q k^T / 8) v per 64-wide head, qkv [n, 3*heads*64] (q | k | v, natural order),
  * o [n, heads*64]; window 0 = global, else keys with |q - k| <= window. kv_chunks > 1 splits the
  * keys into ranges (needs ws / counters, jc_attention_ws_floats / jc_attention_counters; counters
- * zero, kept zero); 0 chooses. Replaces kernels/src/main.rs:303-542 and src/attn.rs:20-56. */
+ * zero, kept zero, and to be zeroed again by the caller after jc_device_error reports a timeout);
+ * 0 chooses. Replaces kernels/src/main.rs:303-542 and src/attn.rs:20-56. */
 int jc_attention(const uint16_t *qkv, uint16_t *o, uint32_t n, uint32_t heads, uint32_t window,
                  uint32_t kv_chunks, float *ws, uint32_t *counters, void *stream);
 size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
@@ -218,7 +279,9 @@ int jc_score(const uint16_t *y, uint32_t d, const uint16_t *w, float b, const ui
 
 /* The last error message of this thread. */
 const char *jc_last_error(void);
-/* Reads and clears the device error word of the current device (0: none). */
+/* Reads and clears the module's device error word on the current device (0: none): the word the
+ * per-kernel entry points (jc_gemm, jc_attention, jc_gemm_noalloc, ...) record device-side
+ * timeouts in. Engines keep their own (julia_cuda_device_error). */
 int jc_device_error(uint32_t *code);
 
 /* ============================== host weight preparation ============================== */

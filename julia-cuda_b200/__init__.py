@@ -95,11 +95,16 @@ def lib():
         "julia_cuda_load_raw": ([cfgp, P, sz, sz, i32, P, sz], P),
         "julia_cuda_load_random": ([cfgp, u64, sz, i32, P, sz], P),
         "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
+        "julia_cuda_forward_trace": ([P, P, u32, P, u32, u32, i32, P, P, P, P, P, P, sz], i32),
         "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
         "julia_cuda_set_head_length": ([P, sz], i32),
         "julia_cuda_set_packing": ([P, sz], i32),
         "julia_cuda_barrier_timeout_probe": ([P, u64, P, P, sz], i32),
+        "julia_cuda_device_error": ([P, P, P, sz], i32),
         "julia_cuda_engine_config": ([P, cfgp, P, P, P], i32),
+        "julia_cuda_read_checkpoint": ([ch, cfgp, P, sz, P, P, sz], i32),
+        "julia_cuda_save_checkpoint": ([ch, cfgp, P, i32, P, sz], i32),
+        "julia_cuda_prepare_host": ([cfgp, P, sz, sz, P, sz, P, sz, P, P, P, sz], i32),
         "jc_gemm": ([u32, i32, i32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32, f32, P, P, P],
                     i32),
         "jc_gemm_ws_floats": ([u32, u32, u32, i32, i32], sz),
@@ -181,6 +186,46 @@ def raw_offsets(cfg: Config) -> np.ndarray:
     if n < 0:
         raise JuliaCudaError(last_error())
     return out[:n]
+
+
+def read_checkpoint(directory: str):
+    """(Config, raw f32 weights) of a checkpoint directory (julia_cuda_read_checkpoint)."""
+    cfg = Config()
+    n = ctypes.c_size_t(0)
+    err = ctypes.create_string_buffer(1024)
+    if lib().julia_cuda_read_checkpoint(directory.encode(), ctypes.byref(cfg), None, 0,
+                                        ctypes.byref(n), err, 1024) != 0:
+        raise JuliaCudaError(err.value.decode(errors="replace"))
+    raw = np.empty(n.value, np.float32)
+    if lib().julia_cuda_read_checkpoint(directory.encode(), ctypes.byref(cfg), _np_ptr(raw),
+                                        raw.size, None, err, 1024) != 0:
+        raise JuliaCudaError(err.value.decode(errors="replace"))
+    return cfg, raw
+
+
+def save_checkpoint(directory: str, cfg: Config, raw: np.ndarray, dtype: int = 0) -> None:
+    """Writes a checkpoint directory (julia_cuda_save_checkpoint; dtype 0 F32, 1 F16, 2 BF16)."""
+    raw = np.ascontiguousarray(raw, np.float32)
+    err = ctypes.create_string_buffer(1024)
+    if lib().julia_cuda_save_checkpoint(directory.encode(), ctypes.byref(cfg), _np_ptr(raw), dtype,
+                                        err, 1024) != 0:
+        raise JuliaCudaError(err.value.decode(errors="replace"))
+
+
+def prepare_host(cfg: Config, raw: np.ndarray, max_length: int = 0):
+    """The prepared f16 (bit patterns) and f32 arenas an engine uploads (julia_cuda_prepare_host)."""
+    raw = np.ascontiguousarray(raw, np.float32)
+    n16, n32 = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    err = ctypes.create_string_buffer(1024)
+    args = (ctypes.byref(cfg), _np_ptr(raw), raw.size, max_length)
+    if lib().julia_cuda_prepare_host(*args, None, 0, None, 0, ctypes.byref(n16), ctypes.byref(n32),
+                                     err, 1024) != 0:
+        raise JuliaCudaError(err.value.decode(errors="replace"))
+    a16, a32 = np.empty(n16.value, np.uint16), np.empty(n32.value, np.float32)
+    if lib().julia_cuda_prepare_host(*args, _np_ptr(a16), a16.size, _np_ptr(a32), a32.size, None,
+                                     None, err, 1024) != 0:
+        raise JuliaCudaError(err.value.decode(errors="replace"))
+    return a16, a32
 
 
 def init_random(cfg: Config, seed: int) -> np.ndarray:
@@ -430,6 +475,19 @@ class Engine:
         if rc != 0:
             raise JuliaCudaError(err.value.decode(errors="replace"))
 
+    def forward_trace(self, ids, markers, qtype: int, logits, trace=None, head_trace=None,
+                      scorer_trace=None, layer_fused=False, stream=None) -> None:
+        """forward_device with the head and the scorer traced too (julia_cuda_forward_trace):
+        trace [n_layers][n][D], head_trace [n_head_layers + 1][nh][D], scorer_trace
+        [n_markers][scorer_hidden], f16 device tensors, each optional."""
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_forward_trace(self._h, _t_ptr(ids), ids.numel(), _t_ptr(markers),
+                                            markers.numel(), qtype, int(layer_fused),
+                                            _t_ptr(logits), _t_ptr(trace), _t_ptr(head_trace),
+                                            _t_ptr(scorer_trace), _stream(stream), err, 1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+
     def set_packing(self, rows: int) -> None:
         """run() packs consecutive requests into forwards of up to `rows` tokens (0: off)."""
         if lib().julia_cuda_set_packing(self._h, rows) != 0:
@@ -450,6 +508,16 @@ class Engine:
         err = ctypes.create_string_buffer(1024)
         rc = lib().julia_cuda_barrier_timeout_probe(self._h, timeout_ns, ctypes.byref(code), err,
                                                    1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        return code.value
+
+    def device_error(self) -> int:
+        """Waits for the engine's stream and reads (and clears) the engine's own device error
+        word (julia_cuda_device_error; 0: none)."""
+        code = ctypes.c_uint32(0)
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_device_error(self._h, ctypes.byref(code), err, 1024)
         if rc != 0:
             raise JuliaCudaError(err.value.decode(errors="replace"))
         return code.value

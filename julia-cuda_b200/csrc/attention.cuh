@@ -390,6 +390,7 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
 // shared memory) fit one CTA an SM whatever the registers, so they are not capped.
 template <int QW, int KS>
 __global__ void __launch_bounds__(32 * QW * KS, KS > 4 ? 1 : 2) attention_kernel(const AttnParams p) {
+    dev_err_bind(p.err);
     extern __shared__ __align__(128) uint8_t att_smem[];
     attention_task<QW, KS>(p, att_smem, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z, true);
 }

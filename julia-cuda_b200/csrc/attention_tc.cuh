@@ -68,6 +68,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr) {
 }
 
 __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __grid_constant__ AttnTcParams kp) {
+    dev_err_bind(kp.p.err);
     extern __shared__ uint8_t atc_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(atc_raw) + 1023) &
                                                 ~uintptr_t(1023));

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/julia_cuda.h"
+#include "checkpoint.h"
 #include "engine.h"
 #include "jc_internal.h"
 #include "model.h"
@@ -120,6 +121,76 @@ int julia_cuda_save_raw(const char *dir, const jc_model_config *cfg, const float
     });
 }
 
+int julia_cuda_read_checkpoint(const char *dir, jc_model_config *cfg, float *raw, size_t raw_cap,
+                               size_t *raw_len, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!dir || !cfg) {
+            report(err, err_len, "read_checkpoint: null directory or config");
+            return -1;
+        }
+        std::vector<float> r;
+        std::string why;
+        if (!jc::read_checkpoint(dir, cfg, &r, &why)) {
+            report(err, err_len, "read_checkpoint: " + why);
+            return -1;
+        }
+        if (raw_len) *raw_len = r.size();
+        if (raw) {
+            if (raw_cap < r.size()) {
+                report(err, err_len, "read_checkpoint: raw holds " + std::to_string(raw_cap) +
+                                         " floats, the model needs " + std::to_string(r.size()));
+                return -1;
+            }
+            std::memcpy(raw, r.data(), r.size() * 4);
+        }
+        return 0;
+    });
+}
+
+int julia_cuda_save_checkpoint(const char *dir, const jc_model_config *cfg, const float *raw,
+                               int dtype, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        std::string why;
+        if (!dir || !cfg || !raw) {
+            report(err, err_len, "save_checkpoint: null argument");
+            return -1;
+        }
+        if (!jc::write_checkpoint(dir, *cfg, raw, dtype, &why)) {
+            report(err, err_len, "save_checkpoint: " + why);
+            return -1;
+        }
+        return 0;
+    });
+}
+
+int julia_cuda_prepare_host(const jc_model_config *cfg, const float *raw, size_t raw_len,
+                            size_t max_length, uint16_t *f16, size_t f16_cap, float *f32,
+                            size_t f32_cap, size_t *f16_len, size_t *f32_len, char *err,
+                            size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        std::string why;
+        if (!cfg || !raw || !jc::check_config(*cfg, &why) || raw_len != jc::raw_layout(*cfg).total) {
+            report(err, err_len, "prepare: " + (why.empty() ? std::string("bad arguments") : why));
+            return -1;
+        }
+        const size_t L = max_length ? max_length : (size_t)cfg->max_positions;
+        jc::HostWeights hw;
+        if (!jc::prepare_weights(*cfg, raw, (uint32_t)L, &hw, &why)) {
+            report(err, err_len, "prepare: " + why);
+            return -1;
+        }
+        if (f16_len) *f16_len = hw.f16.size();
+        if (f32_len) *f32_len = hw.f32.size();
+        if ((f16 && f16_cap < hw.f16.size()) || (f32 && f32_cap < hw.f32.size())) {
+            report(err, err_len, "prepare: the output arrays are too small");
+            return -1;
+        }
+        if (f16) std::memcpy(f16, hw.f16.data(), hw.f16.size() * 2);
+        if (f32) std::memcpy(f32, hw.f32.data(), hw.f32.size() * 4);
+        return 0;
+    });
+}
+
 JcEngine *julia_cuda_load_raw(const jc_model_config *cfg, const float *raw, size_t raw_len,
                               size_t max_length, int device, char *err, size_t err_len) {
     return guarded(err, err_len, [&]() -> JcEngine * {
@@ -165,11 +236,24 @@ JcEngine *julia_cuda_load(const char *dir, size_t max_length, char *err, size_t 
             report(err, err_len, "load: null directory");
             return nullptr;
         }
+        if (jc::has_checkpoint(dir)) {
+            // The reference's checkpoint layout: model.safetensors + encoder/config.json +
+            // julia_config.json (src/checkpoint.rs:27-62).
+            jc_model_config cfg;
+            std::vector<float> raw;
+            std::string why;
+            if (!jc::read_checkpoint(dir, &cfg, &raw, &why)) {
+                report(err, err_len, "load: " + why);
+                return nullptr;
+            }
+            return julia_cuda_load_raw(&cfg, raw.data(), raw.size(), max_length, 0, err, err_len);
+        }
         jc_model_config cfg;
         std::ifstream c(std::string(dir) + "/jc_config.bin", std::ios::binary);
         if (!c.read(reinterpret_cast<char *>(&cfg), sizeof(cfg))) {
             report(err, err_len, std::string("load: no model at ") + dir +
-                                     " (jc_config.bin + jc_weights.f32, see julia_cuda_save_raw)");
+                                     " (model.safetensors + encoder/config.json + "
+                                     "julia_config.json, or jc_config.bin + jc_weights.f32)");
             return nullptr;
         }
         std::string why;
@@ -246,10 +330,30 @@ int julia_cuda_barrier_timeout_probe(JcEngine *engine, uint64_t timeout_ns, uint
     });
 }
 
-int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
-                              const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
-                              int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
-                              char *err, size_t err_len) {
+int julia_cuda_device_error(JcEngine *engine, uint32_t *code, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!engine || !code) {
+            report(err, err_len, "device_error: null engine or code");
+            return -1;
+        }
+        if (!set_device(engine->e->device, err, err_len)) return -1;
+        unsigned int c = 0;
+        if (!engine->e->take_device_error(&c)) {
+            report(err, err_len, std::string("device_error: ") + jc::last_error());
+            return -1;
+        }
+        *code = c;
+        return 0;
+    });
+}
+
+}  // extern "C"
+
+// The device-pointer forward, optionally traced (julia_cuda_forward_device / _trace).
+static int forward_on_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                             const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                             int layer_fused, float *d_logits, const jc::Trace &tr, void *stream,
+                             char *err, size_t err_len) {
     return guarded(err, err_len, [&]() -> int {
         if (!engine) {
             report(err, err_len, "forward: null engine");
@@ -271,8 +375,9 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
             report(err, err_len, jc::last_error());
             return -1;
         }
-        const bool ok = d_trace ? e->enqueue_forward(n, n_markers, qtype, layer_fused, d_trace, s)
-                                : e->launch_forward(n, n_markers, qtype, layer_fused, s);
+        const bool traced = tr.enc || tr.head || tr.scorer;
+        const bool ok = traced ? e->enqueue_forward(n, n_markers, qtype, layer_fused, tr, s)
+                               : e->launch_forward(n, n_markers, qtype, layer_fused, s);
         if (!ok) {
             report(err, err_len, std::string("forward: ") + jc::last_error());
             return -1;
@@ -285,6 +390,31 @@ int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t 
         }
         return 0;
     });
+}
+
+extern "C" {
+
+int julia_cuda_forward_device(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                              const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                              int layer_fused, float *d_logits, uint16_t *d_trace, void *stream,
+                              char *err, size_t err_len) {
+    jc::Trace tr;
+    tr.enc = d_trace;
+    return forward_on_device(engine, d_ids, n, d_markers, n_markers, qtype, layer_fused, d_logits,
+                             tr, stream, err, err_len);
+}
+
+int julia_cuda_forward_trace(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                             const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                             int layer_fused, float *d_logits, uint16_t *d_trace,
+                             uint16_t *d_head_trace, uint16_t *d_scorer_trace, void *stream,
+                             char *err, size_t err_len) {
+    jc::Trace tr;
+    tr.enc = d_trace;
+    tr.head = d_head_trace;
+    tr.scorer = d_scorer_trace;
+    return forward_on_device(engine, d_ids, n, d_markers, n_markers, qtype, layer_fused, d_logits,
+                             tr, stream, err, err_len);
 }
 
 int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const size_t *lens,
@@ -405,7 +535,7 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                     return -1;
                 }
             }
-            if (!jc::enqueue_device_error_read(e->h_err, s) ||
+            if (!jc::enqueue_device_error_read(e->h_err, s, e->dev_err) ||
                 !jc::cuda_ok(cudaStreamSynchronize(s), "run")) {
                 report(err, err_len, std::string("run: ") + jc::last_error());
                 return -1;
@@ -443,7 +573,7 @@ const char *jc_last_error(void) { return jc::last_error(); }
 
 int jc_device_error(uint32_t *code) {
     unsigned int c = 0;
-    if (!jc::read_device_error(&c)) return -1;
+    if (!jc::read_device_error(&c, nullptr)) return -1;
     if (code) *code = c;
     return 0;
 }

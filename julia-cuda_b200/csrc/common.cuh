@@ -14,11 +14,23 @@
 
 namespace jc {
 
-// The module-wide error word: 0, or the first JC_DEV_* code a kernel recorded. (All kernels live
-// in one translation unit, kernels.cu, so this is the only definition.)
+// The module-wide error word: 0, or the first JC_DEV_* code a kernel recorded. It serves the
+// per-kernel entry points (jc_gemm, jc_attention, ...), which have no engine; an engine passes
+// its own word in every launch's parameters, so two engines on one GPU (or an engine beside bare
+// jc_* calls) never see or clear each other's errors. (All kernels live in one translation unit,
+// kernels.cu, so this is the only definition.)
 __device__ unsigned int g_dev_error = 0;
 
-__device__ __forceinline__ void dev_fail(unsigned int code) { atomicCAS(&g_dev_error, 0u, code); }
+// The word the running CTA records errors into. Every kernel that can record an error binds it
+// first thing (dev_err_bind, by every thread: each writes the same value, so no barrier is
+// needed before its own later reads).
+__shared__ unsigned int *s_dev_err;
+
+__device__ __forceinline__ void dev_err_bind(unsigned int *word) {
+    s_dev_err = word ? word : &g_dev_error;
+}
+
+__device__ __forceinline__ void dev_fail(unsigned int code) { atomicCAS(s_dev_err, 0u, code); }
 
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;

@@ -116,7 +116,9 @@ __global__ void __launch_bounds__(128) norm_add_kernel(const __half *x, uint32_t
 __global__ void __launch_bounds__(128) gather_rows_kernel(const __half *x, const float *stats,
                                                           uint32_t d, const uint32_t *rows,
                                                           uint32_t k, uint32_t limit,
-                                                          __half *out, float *out_stats) {
+                                                          __half *out, float *out_stats,
+                                                          unsigned int *err) {
+    dev_err_bind(err);
     const uint32_t i = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     pdl_wait();
     pdl_launch_dependents();

@@ -120,8 +120,9 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
               dalloc((void **)&ids, 4 * L * 4) &&
-              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4);
-    if (!ok) return false;
+              dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4) &&
+              dalloc((void **)&dev_err, 16);
+    if (!ok || !cu(cudaMemset(dev_err, 0, 16), "memset")) return false;
     markers = ids + L;
     seg = reinterpret_cast<uint2 *>(ids + 2 * L);
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
@@ -176,7 +177,7 @@ bool Engine::init(const float *raw, std::string *why) {
                        cudaMemcpyHostToDevice),
             "upload tensor maps"))
         return false;
-    scratch_cap = 16 + 6 * (size_t)cfg.n_layers + 6 * (size_t)cfg.n_head_layers + 8;
+    scratch_cap = 16 + 6 * (size_t)cfg.n_layers + 7 * (size_t)cfg.n_head_layers + 10;
     if (!dalloc((void **)&scratch_descs, scratch_cap * sizeof(PhaseDesc))) return false;
     flow_blocks = (uint32_t)(rows / FLOW_BLOCK);
     const size_t words = flow_counter_words((uint32_t)scratch_cap, flow_blocks);
@@ -233,15 +234,16 @@ Step Engine::gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32
     g.n = n;
     g.k = k;
     g.eps = eps;
+    g.err = dev_err;
     st.map_a = map_a;
     st.w = w;
     st.layer = layer;
     return st;
 }
 
-std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
                                       int mode, bool packed) const {
-    std::vector<Step> steps = build_steps_flat(n, k, qtype, d_trace, mode);
+    std::vector<Step> steps = build_steps_flat(n, k, qtype, tr, mode);
     if (packed)
         for (Step &st : steps) {
             if (st.d.kind == PH_ATTN) st.d.a.seg = seg;
@@ -251,7 +253,8 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, ui
 }
 
 std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype,
-                                           uint16_t *d_trace, int mode) const {
+                                           const Trace &tr, int mode) const {
+    uint16_t *d_trace = tr.enc;
     const PreparedLayout &P = hw.layout;
     const uint32_t D = cfg.d_model, I = cfg.inter, F = cfg.head_ff, S = cfg.scorer_hidden;
     std::vector<Step> steps;
@@ -261,10 +264,23 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
         st.layer = layer;
         return st;
     };
+    // A copy of `rows` rows of `width` columns into a trace buffer (a row phase in the persistent
+    // kernel, a device-to-device copy otherwise).
+    auto copy_step = [&](const __half *src, uint16_t *dst, uint32_t rows, uint32_t width, int layer) {
+        Step st;
+        st.d.kind = PH_COPY;
+        st.layer = layer;
+        st.d.r.x = src;
+        st.d.r.out = reinterpret_cast<__half *>(dst);
+        st.d.r.n = rows;
+        st.d.r.d = width;
+        return st;
+    };
     auto attn_step = [&](uint32_t rows, uint32_t window, int layer) {
         Step st;
         st.d.kind = PH_ATTN;
-        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, rows, (uint32_t)cfg.n_heads, window, nullptr};
+        st.d.a = AttnParams{qkv, o, attn_ws, attn_cnt, rows, (uint32_t)cfg.n_heads, window, nullptr,
+                            dev_err};
         st.layer = layer;
         return st;
     };
@@ -327,6 +343,7 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
         r.eps = cfg.norm_eps;
         steps.push_back(st);
     }
+    if (tr.head) steps.push_back(copy_step(hx, tr.head, nh, D, -2));
     const float heps = cfg.head_eps;
     for (size_t l = 0; l < P.head.size(); l++) {
         const HeadSpans &h = P.head[l];
@@ -344,6 +361,7 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
         steps.push_back(gemm_step(JC_EPI_BIAS | JC_EPI_RES | JC_EPI_STATS, m_f, hm.l2,
                                   w16 + h.l2_w.off, nh, D, F, hx, hx, nullptr, nullptr, stats_a,
                                   nullptr, 0, nullptr, w32 + h.l2_b.off, 0.f, -2));
+        if (tr.head) steps.push_back(copy_step(hx, tr.head + (l + 1) * (size_t)nh * D, nh, D, -2));
     }
     if (k == 0) return steps;
     // Scorer on the marker rows only (rows do not interact after the head's last attention).
@@ -364,6 +382,7 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
                               w16 + P.s_lin1_w.off, k, S, D, ys, nullptr, stats_s,
                               w32 + P.s_lin1_colsum.off, nullptr, nullptr, 0, nullptr,
                               w32 + P.s_lin1_b.off, heps, -2));
+    if (tr.scorer) steps.push_back(copy_step(ys, tr.scorer, k, S, -2));
     {
         Step st = row_step(PH_SCORE, -2);
         RowParams &r = st.d.r;
@@ -416,6 +435,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             g.rope_stride = p.rope_stride;
             g.seg = p.seg;
             g.bias = p.bias;
+            g.err = p.err;
             return launch_gemm(g, c, s, true);
         }
         case PH_ATTN: {
@@ -429,6 +449,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms);
             a.ws = attn_ws;
             a.counters = attn_cnt;
+            a.err = d.a.err;
             if (attn_ws_floats(a.n, a.heads, a.kv_chunks) > attn_ws_cap) a.kv_chunks = 1;
             return launch_attention(a, s, true);
         }
@@ -440,7 +461,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
                                    d.r.stats, s, true);
         case PH_GATHER:
             return launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n, d.r.limit,
-                                      d.r.out, d.r.stats, s, true);
+                                      d.r.out, d.r.stats, s, true, dev_err);
         case PH_SCORE:
             return launch_score(d.r.x, d.r.d, d.r.w, d.r.b, d.r.rows, d.r.n, d.r.logits, s, true);
         case PH_COPY:
@@ -463,7 +484,7 @@ bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const Phase
     };
     if (mode == MODE_MODEL)
         return launch_persist(descs, (uint32_t)steps.size(), steps[0].flow_total, flow_ctr,
-                              flow_blocks, persist_grid, barrier_timeout_ns, s);
+                              flow_blocks, persist_grid, barrier_timeout_ns, s, dev_err);
     size_t i = 0;
     while (i < steps.size()) {
         const int layer = steps[i].layer;
@@ -471,7 +492,7 @@ bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const Phase
             size_t j = i;
             while (j < steps.size() && steps[j].layer == layer) j++;
             if (!launch_persist(descs + i, (uint32_t)(j - i), steps[i].flow_total, flow_ctr,
-                                flow_blocks, persist_grid, barrier_timeout_ns, s))
+                                flow_blocks, persist_grid, barrier_timeout_ns, s, dev_err))
                 return false;
             i = j;
         } else {
@@ -486,7 +507,7 @@ bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const Phase
 }
 
 bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
-                             uint16_t *d_trace, cudaStream_t s) {
+                             const Trace &tr, cudaStream_t s) {
     if (n == 0 || n > max_length || k > max_length || qtype >= (uint32_t)cfg.n_qtypes) {
         set_error("engine: sequence length, marker count or question type out of range");
         return false;
@@ -499,7 +520,7 @@ bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
         set_error("engine: the persistent kernel cannot be resident on this GPU");
         return false;
     }
-    std::vector<Step> steps = build_steps(n, k, qtype, d_trace, mode);
+    std::vector<Step> steps = build_steps(n, k, qtype, tr, mode);
     if (mode != MODE_STEPS) {
         plan_steps(steps, mode);
         if (steps.size() > scratch_cap) {
@@ -514,7 +535,7 @@ bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
             return false;
         // The copy above is from pageable memory, so it is staged before this call returns.
     }
-    return enqueue_steps(steps, mode, scratch_descs, d_trace, n, s);
+    return enqueue_steps(steps, mode, scratch_descs, tr.enc, n, s);
 }
 
 int Engine::launches_per_forward(uint32_t n, uint32_t k, int mode) const {
@@ -536,7 +557,7 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
             return false;
         }
         GraphEntry entry;
-        std::vector<Step> steps = build_steps(n, k, qtype, nullptr, mode, packed);
+        std::vector<Step> steps = build_steps(n, k, qtype, Trace{}, mode, packed);
         if (mode != MODE_STEPS) {
             plan_steps(steps, mode);
             std::vector<PhaseDesc> descs(steps.size());
@@ -591,30 +612,45 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
     return cuda_ok(cudaGraphLaunch(it->second.exec, s), "graph launch");
 }
 
+bool Engine::reset_after_error() {
+    // A wait that gave up leaves its kernel's counters mid-way: the persistent kernel's
+    // dependency counters, and the arrival counters of split-K tiles and split-KV query tiles (a
+    // split that timed out never arrives, so a later launch would take the wrong CTA for the
+    // last one). Start them all afresh.
+    return clear_device_error(dev_err) &&
+           cuda_ok(cudaMemsetAsync(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4,
+                                   stream),
+                   "reset counters") &&
+           cuda_ok(cudaMemsetAsync(gemm_cnt, 0, gemm_cnt_cap * 4, stream), "reset counters") &&
+           cuda_ok(cudaMemsetAsync(attn_cnt, 0, attn_cnt_cap * 4, stream), "reset counters") &&
+           cuda_ok(cudaStreamSynchronize(stream), "reset counters");
+}
+
 bool Engine::check_device_error_copy(std::string *why) {
     const unsigned int code = *h_err;
     if (!code) return true;
-    if (!clear_device_error()) {
+    if (!reset_after_error()) {
         *why = last_error();
         return false;
     }
-    cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4);
-    cudaDeviceSynchronize();
     *why = std::string("device error: ") + device_error_name(code);
     return false;
 }
 
+bool Engine::take_device_error(unsigned int *code) {
+    *code = 0;
+    if (!cuda_ok(cudaStreamSynchronize(stream), "sync") || !read_device_error(code, dev_err))
+        return false;
+    return *code == 0 || reset_after_error();
+}
+
 bool Engine::check_device_error(std::string *why) {
     unsigned int code = 0;
-    if (!read_device_error(&code)) {
+    if (!take_device_error(&code)) {
         *why = last_error();
         return false;
     }
     if (code) {
-        // A timed-out dependency wait can leave the persistent kernel's counters mid-way: start
-        // them afresh.
-        cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4);
-        cudaDeviceSynchronize();
         *why = std::string("device error: ") + device_error_name(code);
         return false;
     }
@@ -640,18 +676,17 @@ bool Engine::barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code) {
     const uint32_t total = plan_flow(descs.data(), 2);
     descs[0].extra = 1;
     unsigned int before = 0;
-    if (!read_device_error(&before)) return false;
+    if (!read_device_error(&before, dev_err)) return false;
     if (!cuda_ok(cudaMemcpy(scratch_descs, descs.data(), 2 * sizeof(PhaseDesc), cudaMemcpyHostToDevice),
                  "phase upload") ||
-        !launch_persist(scratch_descs, 2, total, flow_ctr, flow_blocks, persist_grid, timeout_ns, stream) ||
+        !launch_persist(scratch_descs, 2, total, flow_ctr, flow_blocks, persist_grid, timeout_ns, stream,
+                        dev_err) ||
         !cuda_ok(cudaStreamSynchronize(stream), "probe"))
         return false;
     unsigned int c = 0;
-    if (!read_device_error(&c)) return false;
+    if (!read_device_error(&c, dev_err)) return false;
     *code = c;
-    return cuda_ok(cudaMemset(flow_ctr, 0, flow_counter_words((uint32_t)scratch_cap, flow_blocks) * 4),
-                   "reset counters") &&
-           cuda_ok(cudaDeviceSynchronize(), "reset counters");
+    return reset_after_error();
 }
 
 void Engine::plan_steps(std::vector<Step> &steps, int mode) const {

@@ -38,6 +38,14 @@ struct GraphKey {
     }
 };
 
+// Where a traced forward copies its intermediate results (device, f16; nullptr: not traced):
+// enc [n_layers][n][D] the residual stream after each encoder layer; head [n_head_layers + 1][nh]
+// [D] the head's stream (its input, then after each head layer; nh = the head's rows); scorer
+// [k][scorer_hidden] the scorer's hidden layer (after GELU) of each marker.
+struct Trace {
+    uint16_t *enc = nullptr, *head = nullptr, *scorer = nullptr;
+};
+
 struct Step {
     PhaseDesc d{};      // device-ready descriptor (tensor-map pointers into the device map array)
     int map_a = -1;     // host copy of the A operand's tensor map (index)
@@ -53,7 +61,7 @@ class Engine {
     ~Engine();
 
     // Queues one sequence whose ids / markers are already in the engine's buffers.
-    bool enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, uint16_t *d_trace,
+    bool enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, const Trace &tr,
                          cudaStream_t s);
     // Same, through a cached CUDA graph of that shape.
     // packed: the n rows hold several requests (rows [seg[r].x, seg[r].y) per row r of the
@@ -61,8 +69,12 @@ class Engine {
     bool launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cudaStream_t s,
                         bool packed = false);
     int launches_per_forward(uint32_t n, uint32_t k, int mode) const;
-    // Reads (and clears) the device error word; on an error also resets the grid barrier.
+    // Reads (and clears) this engine's device error word; on an error also resets every counter
+    // its kernels keep (persistent-kernel dependencies, split-K and split-KV arrivals), since a
+    // wait that gave up can leave them mid-way.
     bool check_device_error(std::string *why);
+    // The same, returning the code (0: none) instead of a message.
+    bool take_device_error(unsigned int *code);
     // Runs the persistent kernel with a grid barrier that waits for one CTA too many, so it must
     // time out after timeout_ns; returns the device error code it recorded.
     bool barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code);
@@ -96,6 +108,10 @@ class Engine {
     uint32_t *h_ids = nullptr;
     float *h_logits = nullptr;
     unsigned int *h_err = nullptr;  // the device error word, copied after each queue of requests
+    // The engine's own device error word: every kernel it launches records device-side timeouts
+    // here (not in the module's word, which bare jc_* calls use), so engines sharing a GPU never
+    // see or clear each other's errors.
+    unsigned int *dev_err = nullptr;
     // The error word copied into h_err (the stream has synchronised since): 0, or the reason.
     bool check_device_error_copy(std::string *why);
     cudaEvent_t ev_start[QUEUE] = {}, ev_end[QUEUE] = {};
@@ -113,9 +129,9 @@ class Engine {
     // Fills the persistent kernel's schedule of each launch the mode makes (the whole list, or
     // each encoder layer's steps) and the launches' item counts.
     void plan_steps(std::vector<Step> &steps, int mode) const;
-    std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+    std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
                                   int mode, bool packed = false) const;
-    std::vector<Step> build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype, uint16_t *d_trace,
+    std::vector<Step> build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
                                        int mode) const;
     Step gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32_t m, uint32_t n,
                    uint32_t k, __half *c, const __half *res, const float *stats_in,
@@ -124,6 +140,9 @@ class Engine {
     bool run_step(const Step &st, cudaStream_t s);
     bool enqueue_steps(const std::vector<Step> &steps, int mode, const PhaseDesc *descs,
                        uint16_t *d_trace, uint32_t n, cudaStream_t s);
+    // After a device error: clears the error word and every counter a wait that gave up may have
+    // left non-zero (synchronous).
+    bool reset_after_error();
 
     HostWeights hw;  // layout only after upload (arenas freed)
     uint16_t *w16 = nullptr;

@@ -90,6 +90,7 @@ __device__ __forceinline__ void row_chunk_epilogue(const GemmParams &p, float *v
 template <int BN, int STAGES, uint32_t EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ GemmKernelParams kp) {
+    dev_err_bind(kp.p.err);
     using S = GemmPersistShape<BN, STAGES>;
     constexpr int NI = S::NI;
     extern __shared__ uint8_t smem_raw[];

@@ -449,6 +449,7 @@ struct GemmKernelParams {
 template <int BN, int STAGES, uint32_t EPI, int CS>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ GemmKernelParams kp) {
+    dev_err_bind(kp.p.err);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));

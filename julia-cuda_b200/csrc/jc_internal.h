@@ -64,6 +64,7 @@ struct GemmArgs {
     const float *bias = nullptr;
     uint32_t rope_stride = 0;  // rows of the pair-group-major RoPE table; 0: m
     const uint2 *seg = nullptr;  // packed requests: row r's request rows (RoPE position r - seg[r].x)
+    unsigned int *err = nullptr;  // error word for device-side timeouts (nullptr: the module's)
 };
 
 struct GemmConfig {
@@ -105,6 +106,7 @@ struct AttnArgs {
     float *ws = nullptr;          // kv_chunks > 1: partials
     uint32_t *counters = nullptr; // kv_chunks > 1: one zeroed counter per (query tile, head)
     const uint2 *seg = nullptr;   // packed requests: row r sees only keys [seg[r].x, seg[r].y)
+    unsigned int *err = nullptr;  // error word (nullptr: the module's)
 };
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 size_t attn_counters(uint32_t n, uint32_t heads);
@@ -125,17 +127,20 @@ bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma
 bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,
                   uint32_t k, float *logits, cudaStream_t s, bool pdl);
 // Gathers the marker rows of x and their statistics (for the scorer, which only needs those).
-// A marker >= limit records JC_DEV_BAD_INDEX and is not read.
+// A marker >= limit records JC_DEV_BAD_INDEX in `err` (nullptr: the module's word) and is not
+// read.
 bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
                         uint32_t k, uint32_t limit, __half *out, float *out_stats, cudaStream_t s,
-                        bool pdl);
+                        bool pdl, unsigned int *err);
 
-// The device error word: read (and clear) it.
-bool read_device_error(unsigned int *code);
-// Queues a copy of the device error word into pinned host memory on stream s (read it after the
-// stream has synchronised), and clears it (synchronous).
-bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s);
-bool clear_device_error();
+// Device error words: an engine's own (a device pointer) or, for nullptr, the module's word that
+// the per-kernel entry points record into. Reads (and clears, when set) one, synchronously.
+bool read_device_error(unsigned int *code, unsigned int *word);
+// Queues a copy of an error word into pinned host memory on stream s (read it after the stream
+// has synchronised).
+bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s, unsigned int *word);
+// Clears an error word (synchronous).
+bool clear_device_error(unsigned int *word);
 const char *device_error_name(unsigned int code);
 
 // ---------------------------------------------------------------------------------------------
@@ -153,8 +158,10 @@ uint32_t plan_flow(PhaseDesc *d, uint32_t n);
 inline size_t flow_counter_words(uint32_t n_phases, uint32_t blocks) {
     return (size_t)n_phases * blocks + 3;
 }
-// phases: device copies of plan_flow's output; timeout_ns: how long a dependency wait may last.
+// phases: device copies of plan_flow's output; timeout_ns: how long a dependency wait may last;
+// err: the error word a timeout is recorded in (nullptr: the module's).
 bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
-                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s);
+                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s,
+                    unsigned int *err);
 
 }  // namespace jc

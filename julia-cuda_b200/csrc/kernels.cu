@@ -28,22 +28,31 @@ bool cuda_ok(cudaError_t e, const char *what) {
     return false;
 }
 
-bool read_device_error(unsigned int *code) {
-    unsigned int zero = 0;
+bool read_device_error(unsigned int *code, unsigned int *word) {
+    if (word) {
+        if (!cuda_ok(cudaMemcpy(code, word, sizeof(unsigned int), cudaMemcpyDeviceToHost),
+                     "read error word"))
+            return false;
+        return *code == 0 || clear_device_error(word);
+    }
     if (!cuda_ok(cudaMemcpyFromSymbol(code, g_dev_error, sizeof(unsigned int)), "read error word"))
         return false;
-    if (*code) return cuda_ok(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(zero)), "clear error word");
-    return true;
+    return *code == 0 || clear_device_error(nullptr);
 }
 
-bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s) {
+bool enqueue_device_error_read(unsigned int *pinned, cudaStream_t s, unsigned int *word) {
+    if (word)
+        return cuda_ok(cudaMemcpyAsync(pinned, word, sizeof(unsigned int), cudaMemcpyDeviceToHost, s),
+                       "read error word");
     return cuda_ok(cudaMemcpyFromSymbolAsync(pinned, g_dev_error, sizeof(unsigned int), 0,
                                              cudaMemcpyDeviceToHost, s),
                    "read error word");
 }
 
-bool clear_device_error() {
+bool clear_device_error(unsigned int *word) {
     unsigned int zero = 0;
+    if (word)
+        return cuda_ok(cudaMemcpy(word, &zero, sizeof(zero), cudaMemcpyHostToDevice), "clear error word");
     return cuda_ok(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(zero)), "clear error word");
 }
 
@@ -324,6 +333,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.n = g.n;
     p.k = g.k;
     p.eps = g.eps;
+    p.err = g.err;
     if (cfg.persistent && (cfg.bn == 128 || cfg.bn == 256) && cfg.splits == 1 && cfg.cluster == 1) {
         const uint32_t tiles = (g.n / cfg.bn) * ((g.m + GEMM_BM - 1) / GEMM_BM);
         const dim3 pgrid(std::min(tiles, std::max(cfg.grid, 1u)));
@@ -579,7 +589,7 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         set_error("attention: qkv and o must be 16-byte aligned");
         return false;
     }
-    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg};
+    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg, a.err};
     const AttnVariant v = attn_variant(a.n, a.window);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     switch (v.qw * 10 + v.ks) {
@@ -663,14 +673,14 @@ bool launch_norm_add(const __half *x, uint32_t n, uint32_t d, const float *gamma
 
 bool launch_gather_rows(const __half *x, const float *stats, uint32_t d, const uint32_t *rows,
                         uint32_t k, uint32_t limit, __half *out, float *out_stats, cudaStream_t s,
-                        bool pdl) {
+                        bool pdl, unsigned int *err) {
     if (k == 0) return true;
     if (d % 8) {
         set_error("gather: width must be a multiple of 8");
         return false;
     }
     return launch_ex(gather_rows_kernel, dim3((k + 3) / 4), dim3(128), 0, s, pdl, "gather launch",
-                     x, stats, d, rows, k, limit, out, out_stats);
+                     x, stats, d, rows, k, limit, out, out_stats, err);
 }
 
 bool launch_score(const __half *y, uint32_t d, const __half *w, float b, const uint32_t *markers,
@@ -738,10 +748,11 @@ uint32_t plan_flow(PhaseDesc *d, uint32_t n) {
 }
 
 bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
-                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s) {
+                    uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s,
+                    unsigned int *err) {
     static std::atomic<uint64_t> smem_set{0};
     if (!ensure_smem(persist_kernel, PERSIST_SMEM, smem_set)) return false;
-    FlowParams P{phases, n_phases, total_items, blocks, ctr, timeout_ns};
+    FlowParams P{phases, n_phases, total_items, blocks, ctr, timeout_ns, err};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(PERSIST_THREADS);

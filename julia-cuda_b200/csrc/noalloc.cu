@@ -79,6 +79,15 @@ extern "C" int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t 
             jc::set_error("gemm_noalloc: n must be a multiple of the tile width");
             return -1;
         }
+        // An automatic choice (splits = 0) that would need more scratch than the fixed array
+        // holds takes fewer workspace splits instead of being refused; an explicit request is
+        // honoured or refused below.
+        while (splits == 0 && cfg.splits > 1 &&
+               (jc::gemm_ws_floats(m, n, cfg) > JC_NOALLOC_WS_FLOATS ||
+                jc::gemm_counters(m, n, cfg) > JC_NOALLOC_COUNTERS)) {
+            cfg.splits--;
+            jc::set_gemm_depth(cfg, m, n, sms);
+        }
         const size_t ws_need = jc::gemm_ws_floats(m, n, cfg);
         const size_t cnt_need = jc::gemm_counters(m, n, cfg);
         if (ws_need > JC_NOALLOC_WS_FLOATS || cnt_need > JC_NOALLOC_COUNTERS) {

@@ -30,6 +30,9 @@ struct GemmParams {
     // Packed requests (RoPE positions restart at each request): row r is position r - seg[r].x;
     // nullptr: position r.
     const uint2 *seg;
+    // The error word device-side timeouts are recorded in (an engine's own); nullptr: the
+    // module's word (jc_device_error).
+    unsigned int *err;
 };
 
 struct AttnParams {
@@ -41,6 +44,7 @@ struct AttnParams {
     // Packed requests: row r belongs to the request occupying rows [seg[r].x, seg[r].y) and sees
     // only its keys; nullptr: one request of n rows.
     const uint2 *seg;
+    unsigned int *err;  // error word (nullptr: the module's)
 };
 
 // Phase kinds of the persistent kernel.
@@ -108,6 +112,7 @@ struct FlowParams {
     uint32_t n_phases, total_items, blocks;
     uint32_t *ctr;
     uint64_t timeout_ns;
+    unsigned int *err;  // error word (nullptr: the module's)
 };
 
 }  // namespace jc

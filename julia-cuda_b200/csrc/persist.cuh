@@ -261,6 +261,7 @@ __device__ __noinline__ void row_op(uint32_t kind, const RowParams &r, uint32_t 
 }
 
 __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __grid_constant__ FlowParams F) {
+    dev_err_bind(F.err);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));

@@ -97,6 +97,18 @@ def max_over_ranks(value: float, world: int, device="cpu") -> float:
     return float(t.item())
 
 
+def all_over_ranks(value: float, world: int, device="cpu") -> list:
+    """`value` of every rank, in rank order (every rank gets the list)."""
+    if world <= 1:
+        return [float(value)]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def job_rate(units_per_rank: float, slowest_seconds: float, world: int) -> float:
     """Whole-job throughput: units done by all ranks (each did units_per_rank) over the slowest
     rank's time."""

@@ -317,9 +317,9 @@ void or_attention_f32(const float *qkv, float *o, int n, int heads, int window) 
 /* ------------------------------------------------------------------------------------------ */
 /* f32 model */
 
-int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+int or_forward_f32_full(const or_config *c, const float *raw, const uint32_t *ids, int n,
                         const uint32_t *markers, int n_markers, int qtype, int head_rows,
-                        float *logits, float *trace_x) {
+                        float *logits, float *trace_x, float *head_trace, float *scorer_trace) {
     or_layout L;
     if (or_layout_of(c, &L) || n <= 0 || n > c->max_positions || qtype < 0 ||
         qtype >= c->n_qtypes)
@@ -370,6 +370,7 @@ int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *id
     const float *te = raw + L.type_emb.off + (size_t)qtype * D;
     for (int i = 0; i < nh; i++)
         for (int j = 0; j < D; j++) x[(size_t)i * D + j] = h[(size_t)i * D + j] + te[j];
+    if (head_trace) memcpy(head_trace, x, (size_t)nh * D * 4);
     for (int l = 0; l < c->n_head_layers; l++) {
         layernorm_rows(x, nh, D, raw + L.h_norm1_w[l].off, raw + L.h_norm1_b[l].off, c->head_eps, h);
         matmul_f32(h, nh, D, raw + L.h_in_w[l].off, 3 * D, qkv, raw + L.h_in_b[l].off, 0);
@@ -379,6 +380,7 @@ int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *id
         matmul_f32(h, nh, D, raw + L.h_l1_w[l].off, F, hh, raw + L.h_l1_b[l].off, 0);
         for (size_t i = 0; i < (size_t)nh * F; i++) hh[i] = hh[i] > 0 ? hh[i] : 0;
         matmul_f32(hh, nh, F, raw + L.h_l2_w[l].off, D, x, raw + L.h_l2_b[l].off, 1);
+        if (head_trace) memcpy(head_trace + (size_t)(l + 1) * nh * D, x, (size_t)nh * D * 4);
     }
     /* scorer on the marker rows */
     float *z = malloc((size_t)(n_markers ? n_markers : 1) * D * 4);
@@ -388,10 +390,18 @@ int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *id
     layernorm_rows(z, n_markers, D, raw + L.s_norm_w.off, raw + L.s_norm_b.off, c->head_eps, zn);
     matmul_f32(zn, n_markers, D, raw + L.s_lin1_w.off, S, y, raw + L.s_lin1_b.off, 0);
     for (size_t i = 0; i < (size_t)n_markers * S; i++) y[i] = or_gelu(y[i]);
+    if (scorer_trace) memcpy(scorer_trace, y, (size_t)n_markers * S * 4);
     matmul_f32(y, n_markers, S, raw + L.s_lin2_w.off, 1, logits, raw + L.s_lin2_b.off, 0);
     free(z); free(zn); free(y);
     free(x); free(h); free(qkv); free(o); free(hh); free(mm); free(rg); free(rl);
     return 0;
+}
+
+int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x) {
+    return or_forward_f32_full(c, raw, ids, n, markers, n_markers, qtype, head_rows, logits,
+                               trace_x, NULL, NULL);
 }
 
 int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, int n,
@@ -676,9 +686,10 @@ void or_ref_gemm_plan(int n, int cols, int k, int sms, int per_sm, int *bm_out, 
 /* ------------------------------------------------------------------------------------------ */
 /* the whole f16-emulated forward pass */
 
-int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+int or_forward_emu_full(const or_config *c, const float *raw, const uint32_t *ids, int n,
                         const uint32_t *markers, int n_markers, int qtype, int head_rows,
-                        float *logits, float *trace_x, int bugs) {
+                        float *logits, float *trace_x, float *head_trace, float *scorer_trace,
+                        int bugs) {
     or_layout L;
     if (or_layout_of(c, &L) || n <= 0 || n > c->max_positions || qtype < 0 ||
         qtype >= c->n_qtypes)
@@ -751,6 +762,8 @@ int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *id
     uint16_t *hx = malloc(nD * 2);
     or_emu_norm_add(x, raw + L.final_norm.off, raw + L.type_emb.off + (size_t)qtype * D, nh, D,
                     c->norm_eps, hx, st_a);
+    if (head_trace)
+        for (size_t i = 0; i < (size_t)nh * D; i++) head_trace[i] = or_f32_from_f16(hx[i]);
     for (int l = 0; l < c->n_head_layers; l++) {
         or_fold_layernorm_bias(raw + L.h_in_w[l].off, raw + L.h_norm1_w[l].off,
                                raw + L.h_norm1_b[l].off, raw + L.h_in_b[l].off, 3 * D, D, w16,
@@ -771,11 +784,18 @@ int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *id
         memset(st_a, 0, (size_t)2 * n * 4);
         or_emu_gemm(OR_BIAS | OR_RES | OR_STATS, m, w16, hx, nh, D, F, NULL, NULL, 0, NULL,
                     raw + L.h_l2_b[l].off, st_a);
+        if (head_trace)
+            for (size_t i = 0; i < (size_t)nh * D; i++)
+                head_trace[(size_t)(l + 1) * nh * D + i] = or_f32_from_f16(hx[i]);
     }
     or_fold_layernorm_bias(raw + L.s_lin1_w.off, raw + L.s_norm_w.off, raw + L.s_norm_b.off,
                            raw + L.s_lin1_b.off, S, D, w16, colsum, bias);
     or_emu_gemm(OR_LN | OR_BIAS | OR_GELU, hx, w16, y, nh, S, D, st_a, colsum, c->head_eps, NULL,
                 bias, NULL);
+    if (scorer_trace)
+        for (int i = 0; i < n_markers; i++)
+            for (int j = 0; j < S; j++)
+                scorer_trace[(size_t)i * S + j] = or_f32_from_f16(y[(size_t)markers[i] * S + j]);
     uint16_t *w2 = malloc((size_t)S * 2);
     or_f16_round_array(raw + L.s_lin2_w.off, w2, (size_t)S);
     or_emu_score(y, w2, raw[L.s_lin2_b.off], markers, n_markers, S, logits);
@@ -783,6 +803,13 @@ int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *id
     free(x); free(qkv); free(o); free(m); free(y); free(st_a); free(st_b); free(rg); free(rl);
     free(w16); free(colsum); free(bias); free(wtmp);
     return 0;
+}
+
+int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x, int bugs) {
+    return or_forward_emu_full(c, raw, ids, n, markers, n_markers, qtype, head_rows, logits,
+                               trace_x, NULL, NULL, bugs);
 }
 
 int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, int n,

@@ -88,6 +88,14 @@ int or_forward_f32(const or_config *c, const float *raw, const uint32_t *ids, in
 int or_forward_f32_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
                         const uint32_t *markers, int n_markers, int qtype, int head_rows,
                         float *logits, float *trace_x);
+/* The same with the head traced, as the reference's --check traces it from the encoder output
+ * (src/check.rs:484-548 head_trace, :564-596 head): head_trace (if not NULL) receives the head's
+ * stream [n_head_layers + 1][nh][D] (its input after the final LayerNorm and type embedding, then
+ * after each head layer; nh = the head's rows), scorer_trace (if not NULL) the scorer's hidden
+ * layer after GELU for each marker [n_markers][scorer_hidden]. */
+int or_forward_f32_full(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x, float *head_trace, float *scorer_trace);
 
 /* The f16 emulation of the GPU path (same folds, roundings and statistics as the kernels) over the
  * same raw weights; same outputs as or_forward_f32. trace_x gets the f16 residual stream after each
@@ -99,6 +107,11 @@ int or_forward_emu(const or_config *c, const float *raw, const uint32_t *ids, in
 int or_forward_emu_head(const or_config *c, const float *raw, const uint32_t *ids, int n,
                         const uint32_t *markers, int n_markers, int qtype, int head_rows,
                         float *logits, float *trace_x, int bugs);
+/* With the head and scorer traced as or_forward_f32_full (f16 values as f32). */
+int or_forward_emu_full(const or_config *c, const float *raw, const uint32_t *ids, int n,
+                        const uint32_t *markers, int n_markers, int qtype, int head_rows,
+                        float *logits, float *trace_x, float *head_trace, float *scorer_trace,
+                        int bugs);
 
 /* ---- f16-arithmetic emulation of single kernels (inputs/outputs are f16 bit patterns) ---- */
 /* Epilogue flags, as the GEMM family's. */

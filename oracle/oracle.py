@@ -70,6 +70,10 @@ def lib():
         L.or_forward_f32_head.restype = i32
         L.or_forward_emu_head.argtypes = [cfgp, P, P, i32, P, i32, i32, i32, P, P, i32]
         L.or_forward_emu_head.restype = i32
+        L.or_forward_f32_full.argtypes = [cfgp, P, P, i32, P, i32, i32, i32, P, P, P, P]
+        L.or_forward_f32_full.restype = i32
+        L.or_forward_emu_full.argtypes = [cfgp, P, P, i32, P, i32, i32, i32, P, P, P, P, i32]
+        L.or_forward_emu_full.restype = i32
         L.or_emu_gemm.argtypes = [i32, P, P, P, i32, i32, i32, P, P, f32, P, P, P]
         L.or_emu_attention.argtypes = [P, P, i32, i32, i32]
         L.or_attention_f32.argtypes = [P, P, i32, i32, i32]
@@ -128,6 +132,32 @@ def forward_f32(c: Config, raw, ids, markers, qtype=0, trace=False, head_rows=0)
     if rc:
         raise ValueError("oracle: bad forward arguments")
     return (logits[:len(markers)], tr) if trace else logits[:len(markers)]
+
+
+def forward_traced(c: Config, raw, ids, markers, qtype=0, head_rows=0, emulate=False, bugs=0):
+    """The f32 model (or, emulate=True, the f16 emulation) with every stage traced:
+    (logits, encoder stream [n_layers][n][D], head stream [n_head_layers + 1][nh][D] (its input,
+    then after each head layer), scorer hidden layer after GELU [n_markers][scorer_hidden])."""
+    ids = np.ascontiguousarray(ids, np.uint32)
+    markers = np.ascontiguousarray(markers, np.uint32)
+    n = len(ids)
+    nh = head_rows if 0 < head_rows < n else n
+    logits = np.zeros(max(len(markers), 1), np.float32)
+    tr = np.zeros((c.n_layers, n, c.d_model), np.float32)
+    ht = np.zeros((c.n_head_layers + 1, nh, c.d_model), np.float32)
+    st = np.zeros((max(len(markers), 1), c.scorer_hidden), np.float32)
+    if emulate:
+        rc = lib().or_forward_emu_full(ctypes.byref(c), _p(raw), _p(ids), n, _p(markers),
+                                       len(markers), qtype, head_rows, _p(logits), _p(tr), _p(ht),
+                                       _p(st), bugs)
+    else:
+        rc = lib().or_forward_f32_full(ctypes.byref(c), _p(raw), _p(ids), n, _p(markers),
+                                       len(markers), qtype, head_rows, _p(logits), _p(tr), _p(ht),
+                                       _p(st))
+    if rc:
+        raise ValueError("oracle: bad forward arguments")
+    k = len(markers)
+    return logits[:k], tr, ht, st[:k]
 
 
 def forward_emu(c: Config, raw, ids, markers, qtype=0, trace=False, bugs=0, head_rows=0):

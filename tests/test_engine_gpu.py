@@ -1,7 +1,14 @@
 """The whole forward pass on the GPU (embed -> encoder -> head -> scorer), through the engine's C ABI,
 against the oracle: the f16 emulation of the same arithmetic (tight) and the f32 model (the
 reference's bars: chained stream within 3e-2, src/check.rs:395-402; logits max |d| < 0.15,
-src/check.rs:560; mean |d| <= 0.03 and the same argmax)."""
+src/check.rs:560; mean |d| <= 0.03 and the same argmax).
+
+Random-init logits are a few hundredths, so the absolute logit bars alone would pass a scorer
+that outputs zeros: every logit check here is also relative to the logits' own scale
+(rel_logits: max |d| / rms of the reference logits), and the head and the scorer are traced stage
+by stage (julia_cuda_forward_trace) and bounded like the encoder's layers, as the reference's
+--check bounds the head from the encoder output (src/check.rs:564-596). A planted mistake in the
+oracle (a head bias left out) must fail these bars."""
 import numpy as np
 import pytest
 
@@ -13,6 +20,86 @@ def rel_err(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def rel_logits(got, want):
+    """max |got - want| over the scale of `want` (its rms)."""
+    w = np.asarray(want, np.float64)
+    d = np.abs(np.asarray(got, np.float64) - w)
+    return float(d.max() / max(float(np.sqrt(np.mean(w * w))), 1e-30))
+
+
+# Bars relative to the logits' scale: against the f16 emulation (the same arithmetic; only the
+# order of f32 sums and atomics differs) and against the f32 model.
+LOGIT_REL_EMU = 2e-2
+LOGIT_REL_F32 = 5e-2
+# Per traced stage (encoder layer, head stage, scorer hidden layer), Frobenius-relative: against
+# the emulation at four layers (TRACE_EMU) and over the whole 22-layer chain (TRACE_EMU_CHAIN),
+# against the f32 model (the reference's chained bar, src/check.rs:395-402).
+TRACE_EMU = 5e-3
+TRACE_EMU_CHAIN = 1e-2
+TRACE_F32 = 3e-2
+
+
+def traced_forward(jc, eng, c, ids, markers, qtype, mode=0, head_rows=0):
+    """julia_cuda_forward_trace: (logits, encoder stream [L][n][D], head stream [H + 1][nh][D],
+    scorer hidden layer [k][S]) as f32 numpy arrays."""
+    n = len(ids)
+    nh = head_rows if 0 < head_rows < n else n
+    ids_t = torch.from_numpy(np.asarray(ids, np.uint32).view(np.int32)).cuda()
+    mk_t = torch.from_numpy(np.asarray(markers, np.uint32).view(np.int32)).cuda()
+    logits = torch.zeros(len(markers), dtype=torch.float32, device="cuda")
+    f16 = dict(dtype=torch.float16, device="cuda")
+    tr = torch.zeros(c.n_layers, n, c.d_model, **f16)
+    ht = torch.zeros(c.n_head_layers + 1, nh, c.d_model, **f16)
+    st = torch.zeros(len(markers), c.scorer_hidden, **f16)
+    eng.forward_trace(ids_t, mk_t, qtype, logits, trace=tr, head_trace=ht, scorer_trace=st,
+                      layer_fused=mode)
+    torch.cuda.synchronize()
+    assert eng.device_error() == 0
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    return f(logits), f(tr), f(ht), f(st)
+
+
+def check_traced(O, c, raw, ids, markers, qtype, got, emu_bar, head_rows=0, label=""):
+    """Every traced stage and the logits against the emulation and the f32 model; returns the
+    worst errors seen (printed by the caller)."""
+    logits, tr, ht, st = got
+    oc = oracle_cfg(O, c)
+    le, tre, hte, ste = O.forward_traced(oc, raw, ids, markers, qtype, head_rows=head_rows,
+                                         emulate=True)
+    lf, trf, htf, stf = O.forward_traced(oc, raw, ids, markers, qtype, head_rows=head_rows)
+    worst = {"enc_emu": 0.0, "enc_f32": 0.0, "head_emu": 0.0, "head_f32": 0.0}
+    for l in range(c.n_layers):
+        e1, e2 = rel_err(tr[l], tre[l]), rel_err(tr[l], trf[l])
+        worst["enc_emu"], worst["enc_f32"] = max(worst["enc_emu"], e1), max(worst["enc_f32"], e2)
+        assert e1 < emu_bar and e2 < TRACE_F32, f"{label} encoder layer {l}: {e1:.2e} {e2:.2e}"
+    for s in range(c.n_head_layers + 1):
+        e1, e2 = rel_err(ht[s], hte[s]), rel_err(ht[s], htf[s])
+        worst["head_emu"], worst["head_f32"] = max(worst["head_emu"], e1), max(worst["head_f32"], e2)
+        stage = "input" if s == 0 else f"layer {s - 1}"
+        assert e1 < emu_bar and e2 < TRACE_F32, f"{label} head {stage}: {e1:.2e} {e2:.2e}"
+    worst["scorer_emu"], worst["scorer_f32"] = rel_err(st, ste), rel_err(st, stf)
+    assert worst["scorer_emu"] < emu_bar and worst["scorer_f32"] < TRACE_F32, f"{label} scorer {worst}"
+    worst["logits_emu"], worst["logits_f32"] = rel_logits(logits, le), rel_logits(logits, lf)
+    assert worst["logits_emu"] < LOGIT_REL_EMU, f"{label} logits vs emulation {worst}"
+    assert worst["logits_f32"] < LOGIT_REL_F32, f"{label} logits vs f32 {worst}"
+    assert np.max(np.abs(logits - lf)) < 0.15 and np.mean(np.abs(logits - lf)) <= 0.03
+    assert np.argmax(logits) == np.argmax(lf)
+    return worst
+
+
+def raw_tensor(jc, c, raw, index):
+    """A view of tensor `index` (julia_cuda_raw_offsets order) of a raw weight array."""
+    off = jc.raw_offsets(c)
+    end = int(off[index + 1]) if index + 1 < len(off) else raw.size
+    return raw[int(off[index]):end]
+
+
+def head_l2_bias_index(jc, c):
+    """raw_offsets index of the last head layer's linear2 bias: the last of the head layers'
+    tensors, followed only by the scorer's six (norm w, b, lin1 w, b, lin2 w, b)."""
+    return len(jc.raw_offsets(c)) - 7
 
 
 def oracle_cfg(O, c):
@@ -31,7 +118,7 @@ def device_forward(jc, eng, ids, markers, qtype, n_layers, d, trace=True, mode=0
     tr = torch.zeros(n_layers, len(ids), d, dtype=torch.float16, device="cuda") if trace else None
     eng.forward_device(ids_t, mk_t, qtype, logits, trace=tr, layer_fused=mode)
     torch.cuda.synchronize()
-    assert jc.device_error() == 0
+    assert eng.device_error() == 0
     out = logits.cpu().numpy()
     return (out, tr.float().cpu().numpy()) if trace else out
 
@@ -226,8 +313,94 @@ def test_grid_barrier_timeout_is_reported(jc, small_engine):
     the engine usable."""
     c, raw, eng = small_engine
     assert eng.barrier_timeout_probe(200_000_000) == 4
-    assert jc.device_error() == 0
+    assert jc.device_error() == 0 and eng.device_error() == 0
     ids = np.arange(40, dtype=np.uint32)
     for mode in (0, 1, 2):
         outs, _ = eng.run([(ids, np.array([0, 39], np.uint32), 0)], layer_fused=mode)
         assert np.isfinite(outs[0]).all()
+
+
+def test_engines_keep_their_own_error_words(jc, O, small_engine):
+    """Two engines on one GPU: while one makes a persistent-kernel wait time out on purpose
+    (0.3 s), the other serves requests from another host thread. Each reports only its own
+    status: the probe's code, none for the serving engine, and nothing in the module's word that
+    the bare jc_* entry points use."""
+    import threading
+
+    c, raw, eng_a = small_engine
+    eng_b = jc.Engine.load_raw(c, raw, max_length=256)
+    try:
+        ids = np.arange(100, dtype=np.uint32) % c.vocab
+        req = [(ids, np.array([0, 50, 99], np.uint32), 1)]
+        want, _ = eng_b.run(req)
+        probe = {}
+
+        def run_probe():
+            probe["code"] = eng_a.barrier_timeout_probe(300_000_000)
+
+        t = threading.Thread(target=run_probe)
+        t.start()
+        served = []
+        while t.is_alive() or len(served) < 3:
+            outs, _ = eng_b.run(req, layer_fused=len(served) % 3)
+            served.append(outs[0])
+        t.join()
+        assert probe["code"] == 4
+        for got in served:
+            assert np.max(np.abs(got - want[0])) < 2e-3
+        assert eng_b.device_error() == 0
+        assert eng_a.device_error() == 0
+        assert jc.device_error() == 0
+        outs, _ = eng_a.run(req)
+        assert np.max(np.abs(outs[0] - want[0])) < 2e-3
+    finally:
+        eng_b.close()
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_traced_stages_small_model(jc, O, small_engine, mode):
+    """Every stage of the small model (4 layers) traced, against the emulation and the f32 model,
+    in each execution mode."""
+    c, raw, eng = small_engine
+    rng = np.random.default_rng(31 + mode)
+    n = 293
+    ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+    markers = np.sort(rng.choice(n, 4, replace=False)).astype(np.uint32)
+    got = traced_forward(jc, eng, c, ids, markers, mode % 3, mode=mode)
+    w = check_traced(O, c, raw, ids, markers, mode % 3, got, TRACE_EMU, label=f"mode {mode}")
+    print(f"\nsmall model, mode {mode}: " + ", ".join(f"{k} {v:.2e}" for k, v in w.items()))
+
+
+def test_traced_stages_benchmark_config(jc, O, full_engine):
+    """BASELINE config 0 (hidden 768, 22 layers, 293 tokens) traced stage by stage, and the gate's
+    sensitivity: the same comparison against an oracle whose last head layer leaves out its
+    linear2 bias (a planted mistake, on the CPU) must fail the bars."""
+    c, raw, eng = full_engine
+    rng = np.random.default_rng(293)
+    ids = rng.integers(0, c.vocab, 293).astype(np.uint32)
+    markers = np.sort(rng.choice(293, 4, replace=False)).astype(np.uint32)
+    got = traced_forward(jc, eng, c, ids, markers, 0)
+    w = check_traced(O, c, raw, ids, markers, 0, got, TRACE_EMU_CHAIN, label="config 0")
+    print("\nconfig 0: " + ", ".join(f"{k} {v:.2e}" for k, v in w.items()))
+    broken = raw.copy()
+    raw_tensor(jc, c, broken, head_l2_bias_index(jc, c))[:] = 0.0
+    with pytest.raises(AssertionError):
+        check_traced(O, c, broken, ids, markers, 0, got, TRACE_EMU_CHAIN, label="broken bias")
+
+
+def test_planted_head_bias_mistake_is_visible_in_the_logits(jc, O, full_engine):
+    """The logit bars alone (no trace) also catch the planted mistake: the engine's logits against
+    the broken oracle's are off by more than LOGIT_REL_EMU."""
+    c, raw, eng = full_engine
+    rng = np.random.default_rng(294)
+    ids = rng.integers(0, c.vocab, 293).astype(np.uint32)
+    markers = np.sort(rng.choice(293, 4, replace=False)).astype(np.uint32)
+    got = device_forward(jc, eng, ids, markers, 0, c.n_layers, c.d_model, trace=False)
+    broken = raw.copy()
+    raw_tensor(jc, c, broken, head_l2_bias_index(jc, c))[:] = 0.0
+    oc = oracle_cfg(O, c)
+    good, bad = O.forward_emu(oc, raw, ids, markers, 0), O.forward_emu(oc, broken, ids, markers, 0)
+    print(f"\nlogits vs emulation {rel_logits(got, good):.2e}, vs the broken oracle "
+          f"{rel_logits(got, bad):.2e}")
+    assert rel_logits(got, good) < LOGIT_REL_EMU
+    assert rel_logits(got, bad) > LOGIT_REL_EMU

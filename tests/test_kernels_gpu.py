@@ -1,7 +1,13 @@
 """Each sm_100a kernel, called through the C ABI (jc_*), against the oracle's emulation of the
 same f16/f32 arithmetic. Tolerances are the reference's (src/check.rs:107, :154, :382-389):
 GEMM outputs within 1e-3 relative of the emulation, row statistics 1e-4, attention 2e-3 of the
-emulation and 4e-3 of f32, embed within 1 f16 ulp."""
+emulation and 4e-3 of f32, embed within 1 f16 ulp.
+
+A norm-wide bar alone lets a few wrong elements through (one 16-column group of one row off by
+30% at 1024 rows moves the Frobenius error by about 1e-3), so every GEMM and attention output is
+also bounded element by element, as the reference prints the worst ulp beside the norm
+(src/check.rs:147-153): |got - want| <= ELEM x max(|want|, rms(want) / 10) for every element
+(ELEM_GEMM 1e-2, about ten f16 ulps; ELEM_ATTN 2e-2)."""
 import numpy as np
 import pytest
 
@@ -13,6 +19,19 @@ def rel_err(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+ELEM_GEMM = 1e-2
+ELEM_ATTN = 2e-2
+
+
+def elem_err(got, want):
+    """Worst element error relative to the element's own size, floored at a tenth of the output's
+    rms (elements near zero carry the f32 rounding of their large partial sums)."""
+    g = np.asarray(got, np.float64)
+    w = np.asarray(want, np.float64)
+    floor = 0.1 * max(float(np.sqrt(np.mean(w * w))), 1e-30)
+    return float(np.max(np.abs(g - w) / np.maximum(np.abs(w), floor))) if w.size else 0.0
 
 
 def stats_err(x16, stats):
@@ -88,7 +107,10 @@ def run_gemm_case(jc, O, name, m, n, k, bn=0, splits=0, seed=0):
     got = host_u16(c)
     assert float(zero.abs().max()) == 0.0, "the zero buffer was not cleared"
     e = rel_err(O.f32(got), O.f32(want))
-    assert e < 1e-3, f"{name} m={m} n={n} k={k} bn={bn} splits={splits}: rel err {e:.2e}"
+    el = elem_err(O.f32(got), O.f32(want))
+    assert e < 1e-3 and el < ELEM_GEMM, (
+        f"{name} m={m} n={n} k={k} bn={bn} splits={splits}: rel err {e:.2e}, worst element "
+        f"{el:.2e}, worst ulp {int(ulps(got, want).max())}")
     if epi & jc.EPI_STATS:
         se = stats_err(got, stats_out.cpu().numpy())
         assert se < 1e-4, f"{name}: stats err {se:.2e}"
@@ -220,7 +242,9 @@ def test_attention(jc, O, n, window):
         torch.cuda.synchronize()
         got = O.f32(host_u16(o))
         e1, e2 = rel_err(got, O.f32(want)), rel_err(got, f32)
-        assert e1 < 2e-3 and e2 < 4e-3, f"n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
+        el = elem_err(got, O.f32(want))
+        assert e1 < 2e-3 and e2 < 4e-3 and el < ELEM_ATTN, \
+            f"n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e} worst element {el:.2e}"
 
 
 @pytest.fixture(params=["mma", "tc"])
@@ -247,8 +271,9 @@ def test_attention_both_kernels(jc, O, attn_kernel, n, window):
         assert jc.device_error() == 0
         got = O.f32(host_u16(o))
         e1, e2 = rel_err(got, O.f32(want)), rel_err(got, f32)
-        assert e1 < 2e-3 and e2 < 4e-3, \
-            f"{attn_kernel} n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e}"
+        el = elem_err(got, O.f32(want))
+        assert e1 < 2e-3 and e2 < 4e-3 and el < ELEM_ATTN, \
+            f"{attn_kernel} n={n} window={window} chunks={chunks}: {e1:.2e} {e2:.2e} worst {el:.2e}"
 
 
 @pytest.mark.parametrize("n,window", [(300, 8), (300, 100), (1024, 200), (700, 31)])
@@ -261,7 +286,8 @@ def test_attention_other_windows(jc, O, n, window):
     o = torch.zeros(n, heads * 64, dtype=torch.float16, device="cuda")
     jc.attention(cuda_u16(qkv), o, heads, window)
     torch.cuda.synchronize()
-    assert rel_err(O.f32(host_u16(o)), O.f32(want)) < 2e-3
+    got = O.f32(host_u16(o))
+    assert rel_err(got, O.f32(want)) < 2e-3 and elem_err(got, O.f32(want)) < ELEM_ATTN
 
 
 def test_attention_reference_width(jc, O):

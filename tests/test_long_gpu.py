@@ -39,7 +39,7 @@ def test_long_request_head_on_512_rows(jc, long_case, mode):
     c, eng, ids, markers, emu, f32 = long_case
     outs, ms = eng.run([(ids, markers, 0)], layer_fused=mode)
     got = outs[0]
-    assert jc.device_error() == 0 and ms[0] > 0
+    assert eng.device_error() == 0 and ms[0] > 0
     assert np.max(np.abs(got - emu)) < 2e-3
     assert np.max(np.abs(got - f32)) < 0.15 and np.mean(np.abs(got - f32)) <= 0.03
     assert np.argmax(got) == np.argmax(f32)
@@ -71,6 +71,6 @@ def test_marker_past_the_head_rows_is_rejected(jc, long_case):
     for mode in (0, 2):
         eng.forward_device(ids_t, mk_t, 0, logits, layer_fused=mode)
         torch.cuda.synchronize()
-        assert jc.device_error() == 6
+        assert eng.device_error() == 6 and jc.device_error() == 0
     outs, _ = eng.run([(ids, markers, 0)], layer_fused=2)
     assert np.max(np.abs(outs[0] - emu)) < 2e-3

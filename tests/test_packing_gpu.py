@@ -38,7 +38,7 @@ def packed_case(jc, O):
 
 def test_packed_requests_match_running_alone(jc, packed_case):
     c, raw, eng, reqs, alone, packed, ms = packed_case
-    assert jc.device_error() == 0 and np.all(ms > 0)
+    assert eng.device_error() == 0 and np.all(ms > 0)
     for a, p in zip(alone, packed):
         assert a.shape == p.shape
         assert np.max(np.abs(a - p)) < 2e-3
@@ -84,7 +84,7 @@ def test_large_packs_run_the_persistent_gemm(jc, O):
         alone, _ = eng.run(reqs)
         eng.set_packing(3072)
         packed, ms = eng.run(reqs)
-        assert jc.device_error() == 0 and len(set(np.round(ms, 6))) < len(reqs)
+        assert eng.device_error() == 0 and len(set(np.round(ms, 6))) < len(reqs)
         for a, p in zip(alone, packed):
             assert np.max(np.abs(a - p)) < 2e-3
     finally:

@@ -39,6 +39,7 @@ def _rank_main(rank, world, port, out_dir, fail_rank):
         slowest = rep.max_over_ranks(r + 1.0, w)
         res["slowest"] = slowest
         res["rate"] = rep.job_rate(5, slowest, w)
+        res["all"] = rep.all_over_ranks(10.0 * r + 0.5, w)
         rep.barrier(w)
         res["ok"] = True
     except RuntimeError as e:
@@ -68,6 +69,7 @@ def test_two_gloo_ranks_partition_requests_and_agree_on_the_slowest_time(tmp_pat
         assert x["rank_env"] == [r, 2, r] and x["joined"] and x.get("ok"), x
         assert x["slowest"] == 2.0          # max over ranks, the same on every rank
         assert x["rate"] == 2 * 5 / 2.0     # all ranks' requests over the slowest time
+        assert x["all"] == [0.5, 10.5]      # every rank's value, in rank order
     # every request is served by exactly one rank
     assert sorted(res[0]["share"] + res[1]["share"]) == list(range(7))
     assert not set(res[0]["share"]) & set(res[1]["share"])
@@ -85,6 +87,7 @@ def test_single_process_needs_no_process_group():
     rep = importlib.import_module("julia-cuda_b200.replicas")
     assert rep.init(1, "gloo") is False
     assert rep.max_over_ranks(3.5, 1) == 3.5
+    assert rep.all_over_ranks(3.5, 1) == [3.5]
     assert rep.shard([1, 2, 3], 0, 1) == [1, 2, 3]
     assert rep.job_rate(10, 2.0, 1) == 5.0
 
@@ -95,7 +98,7 @@ def test_reference_arm_runs_on_rank_zero_only(capsys):
     bench = importlib.import_module("bench")
 
     class Args:
-        steps, warmup = 1, 0
+        steps, warmup, seq, head_length = 1, 0, 293, 0
     bench.reference_arm(Args, 1, 2)
     assert capsys.readouterr().out == ""
 
