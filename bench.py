@@ -28,6 +28,8 @@ Other BASELINE configs (extra lines, not the headline):
   --seq 1024 --head-length 512 --mode 2 config 4: the whole model in one cooperative launch
   --restated                            the reference's per-step GPU kernels restated in CUDA C++
                                         (baseline/restated) against this library, same request
+  --profile                             where a forward's time goes: per-CTA phase stamps of the
+                                        per-step kernels (julia_cuda_forward_profile), per launch
 """
 import argparse
 import importlib
@@ -519,6 +521,104 @@ def restated_headline(jc, torch, cfg, eng, ids, markers, flush, steps, local):
             "restated_samples": len(r_ms)}
 
 
+def launch_name(cfg, li):
+    """A readable name for a profiled launch (jc_launch_info as a dict)."""
+    import importlib as _il
+    jc = _il.import_module("julia-cuda_b200")
+    kind = jc.LAUNCH_KINDS.get(li["kind"], "?")
+    if kind == "gemm":
+        e, n, k = li["epi"], li["n"], li["k"]
+        D = cfg.d_model
+        if li["layer"] >= 0:
+            return {(3 * D, D): "qkv", (D, D): "wo", (2 * cfg.inter, D): "wi",
+                    (D, cfg.inter): "wo_mlp"}.get((n, k), f"gemm {n}x{k}")
+        if e & jc.EPI_GELU:
+            return "scorer lin1"
+        return {(3 * D, D): "head in_proj", (D, D): "head out_proj", (cfg.head_ff, D): "head linear1",
+                (D, cfg.head_ff): "head linear2"}.get((n, k), f"head gemm {n}x{k}")
+    if kind == "attention":
+        return "attention window" if li["k"] else ("attention global" if li["layer"] >= 0
+                                                   else "head attention")
+    return kind
+
+
+def profile_arm(args, local):
+    """Where a forward's time goes: --steps profiled forwards of the headline request (each a
+    CUDA graph with PDL, as julia_cuda_run runs it), every GEMM and attention CTA stamping
+    %globaltimer at its phases. Per launch name (medians over its launches and CTAs, us): the
+    wait for the previous kernel (entry -> inputs ready), first operand stage, main loop, epilogue
+    (results -> outputs written), drain to exit, and what the launch adds to the forward (its last
+    CTA's exit after the previous stamped launch's). One JSON line per name, then a total."""
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
+    n_tok = args.seq
+    ids, markers = request(0, cfg.vocab, n_tok)
+    ids_d = torch.from_numpy(ids.view(np.int32)).cuda()
+    mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
+    logits = torch.zeros(MARKERS, dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(max(args.warmup, 3)):
+        eng.forward_device(ids_d, mk_d, 0, logits)
+    rows = {}
+    totals = []
+    for rep in range(max(1, min(args.steps, 100))):
+        flush.zero_()
+        torch.cuda.synchronize()
+        recs, launches = eng.forward_profile(ids_d, mk_d, 0, logits, records_per_launch=512)
+        assert eng.device_error() == 0
+        prev_exit = None
+        first_entry = None
+        for li in launches:
+            if li["kind"] not in (0, 1):
+                continue
+            r = recs[li["record"]][: min(li["ctas"], 512)].astype(np.int64)
+            r = r[r[:, 0] > 0]
+            if not len(r):
+                continue
+            entry, exit_ = int(r[:, 0].min()), int(r[:, 5].max())
+            first_entry = entry if first_entry is None else first_entry
+            d = rows.setdefault(launch_name(cfg, li), {"dep": [], "first": [], "main": [], "epi": [],
+                                                        "drain": [], "added": [], "ctas": li["ctas"],
+                                                        "tile": li["tile"], "count": 0})
+            d["count"] += 1
+            ok = r[:, 1] > 0
+            d["dep"].append(float(np.median(r[ok, 1] - r[ok, 0])) / 1e3)
+            if li["kind"] == 0:
+                ok2 = (r[:, 2] > 0) & (r[:, 3] > 0) & (r[:, 4] > 0)
+                d["first"].append(float(np.median(r[ok2, 2] - r[ok2, 1])) / 1e3)
+                d["main"].append(float(np.median(r[ok2, 3] - r[ok2, 2])) / 1e3)
+                d["epi"].append(float(np.median(r[ok2, 4] - r[ok2, 3])) / 1e3)
+                d["drain"].append(float(np.median(r[ok2, 5] - r[ok2, 4])) / 1e3)
+            else:
+                ok2 = (r[:, 2] > 0) & (r[:, 3] > 0) & (r[:, 4] > 0)
+                d["first"].append(float(np.median(r[ok2, 2] - r[ok2, 1])) / 1e3)  # loads
+                d["main"].append(float(np.median(r[ok2, 3] - r[ok2, 2])) / 1e3)   # key loop
+                d["epi"].append(float(np.median(r[ok2, 4] - r[ok2, 3])) / 1e3)    # merge, store
+                d["drain"].append(float(np.median(r[ok2, 5] - r[ok2, 4])) / 1e3)
+            if prev_exit is not None:
+                d["added"].append((exit_ - prev_exit) / 1e3)
+            prev_exit = exit_
+        totals.append((prev_exit - first_entry) / 1e3)
+    eng.close()
+    med = lambda v: float(statistics.median(v)) if v else None  # noqa: E731
+    out = []
+    for name, d in rows.items():
+        line = {"profile": name, "launches_per_forward": d["count"] // max(1, min(args.steps, 100)),
+                "ctas": d["ctas"], "tile_rows": d["tile"] >> 16, "tile_cols": d["tile"] & 0xFFFF,
+                "dependency_wait_us": med(d["dep"]), "first_stage_us": med(d["first"]),
+                "main_loop_us": med(d["main"]), "epilogue_us": med(d["epi"]),
+                "drain_us": med(d["drain"]), "added_to_forward_us": med(d["added"])}
+        out.append(line)
+        print(json.dumps(line), flush=True)
+    print(json.dumps({"profile": "forward", "tokens": n_tok, "forwards": len(totals),
+                      "stamped_span_us": med(totals),
+                      "note": "first GEMM/attention CTA entry to the last one's exit (the embedding "
+                              "before and the gather / score after are not stamped)"}), flush=True)
+
+
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
 SERVING_METRIC = "requests/s (config 3 serving: log-normal lengths around 293 tokens, 4 markers)"
 
@@ -626,6 +726,8 @@ def main():
                          "this many requests (0: skip)")
     ap.add_argument("--serving-pack", type=int, default=6144,
                     help="headline: the config-3 pass's pack size in tokens (0: unpacked)")
+    ap.add_argument("--profile", action="store_true",
+                    help="per-CTA phase stamps of the per-step kernels: where a forward's time goes")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
                                       "attn_global", "attn_window"],
                     help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")
@@ -648,6 +750,10 @@ def main():
     if args.restated:
         if rank == 0:
             restated_arm(args, local)
+        return
+    if args.profile:
+        if rank == 0:
+            profile_arm(args, local)
         return
 
     import torch

@@ -162,6 +162,36 @@ int julia_cuda_forward_trace(JcEngine *engine, const uint32_t *d_ids, uint32_t n
                              uint16_t *d_head_trace, uint16_t *d_scorer_trace, void *stream,
                              char *err, size_t err_len);
 
+/* One launch of a profiled forward (julia_cuda_forward_profile), in launch order. */
+typedef struct jc_launch_info {
+    uint32_t kind;   /* 0 GEMM, 1 attention, 2 embedding, 3 head input (final LayerNorm + type
+                        embedding), 4 marker gather, 5 score, 6 trace copy */
+    uint32_t epi;    /* GEMM: epilogue flags (JC_EPI_*) */
+    uint32_t m, n, k; /* GEMM: rows, output columns, depth; attention: rows, heads, window;
+                         edges: rows, width */
+    int32_t layer;   /* encoder layer, -1 before the encoder, -2 the head and scorer */
+    uint32_t ctas;   /* CTAs launched */
+    uint32_t tile;   /* GEMM: tile rows << 16 | tile columns */
+    uint32_t record; /* its first phase-stamp record (GEMM and attention launches) */
+} jc_launch_info;
+
+/* A profiled forward of the per-step kernels (the reference's --time, src/timing.rs and
+ * src/profile.rs, with device-side stamps as kernels/src/prof.rs): the forward is captured into a
+ * CUDA graph with programmatic dependent launch exactly as julia_cuda_run runs it, every GEMM and
+ * attention CTA recording eight 64-bit words into d_prof: [0] entry, [1] inputs ready (the previous
+ * kernel done), [2] first operand stage in shared memory (GEMMs) / first tiles loaded (attention),
+ * [3] accumulator complete / key loop done, [4] outputs written, [5] exit (%globaltimer ns, 0 where a
+ * stage does not apply), [6] the SM, [7] the CTA's index. Launch i writes records [i *
+ * records_per_launch, (i + 1) * records_per_launch) (d_prof: that many records for every launch,
+ * 8 words each; CTAs past records_per_launch are not recorded). info (info_cap entries) receives
+ * each launch's description and *n_launches their count. Waits for the forward. Returns 0 or -1.
+ * The stamps cost a few global stores per CTA; a forward without a record array runs none. */
+int julia_cuda_forward_profile(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                               const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                               float *d_logits, uint64_t *d_prof, uint32_t records_per_launch,
+                               jc_launch_info *info, size_t info_cap, size_t *n_launches,
+                               void *stream, char *err, size_t err_len);
+
 /* Failure detection: runs the persistent kernel with a grid barrier that waits for one CTA more
  * than the grid has, so every wait must give up after timeout_ns; writes the device error code it
  * recorded (JC_DEV_TIMEOUT_GRID = 4) and leaves the engine usable. No counterpart in the
@@ -246,6 +276,12 @@ int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t *a, const u
                     uint32_t k, float eps, const float *rope, const float *bias, void *stream);
 size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
+/* The tile height policy of later jc_gemm / jc_gemm_noalloc calls and later-captured engine
+ * graphs: 0 automatic (64-row tiles for tiles of at most 64 columns without split-K whose 64-row
+ * grid fits one wave, else 128), 128 (always 128 rows, the default) or 64 (64 rows wherever
+ * legal). Sets *rows and returns the previous policy in place; other values are ignored. A tuning
+ * and test hook (JC_GEMM_BM sets the starting policy). */
+void jc_gemm_tile_rows(int *rows);
 /* The automatic choice (gemm::choose, src/gemm.rs:153-172, refit for the B200's SMs). */
 int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *splits);
 

@@ -39,6 +39,18 @@ class JuliaCudaError(RuntimeError):
     pass
 
 
+class LaunchInfo(ctypes.Structure):
+    """jc_launch_info: one launch of a profiled forward."""
+
+    _fields_ = [("kind", ctypes.c_uint32), ("epi", ctypes.c_uint32), ("m", ctypes.c_uint32),
+                ("n", ctypes.c_uint32), ("k", ctypes.c_uint32), ("layer", ctypes.c_int32),
+                ("ctas", ctypes.c_uint32), ("tile", ctypes.c_uint32), ("record", ctypes.c_uint32)]
+
+
+LAUNCH_KINDS = {0: "gemm", 1: "attention", 2: "embed", 3: "head input", 4: "gather", 5: "score",
+                6: "copy"}
+
+
 class Config(ctypes.Structure):
     """jc_model_config."""
 
@@ -96,6 +108,7 @@ def lib():
         "julia_cuda_load_random": ([cfgp, u64, sz, i32, P, sz], P),
         "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
         "julia_cuda_forward_trace": ([P, P, u32, P, u32, u32, i32, P, P, P, P, P, P, sz], i32),
+        "julia_cuda_forward_profile": ([P, P, u32, P, u32, u32, P, P, u32, P, sz, P, P, P, sz], i32),
         "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
         "julia_cuda_set_head_length": ([P, sz], i32),
         "julia_cuda_set_packing": ([P, sz], i32),
@@ -114,6 +127,7 @@ def lib():
         "jc_attention_ws_floats": ([u32, u32, u32], sz),
         "jc_attention_counters": ([u32, u32], sz),
         "jc_attention_tc_min": ([P, P], None),
+        "jc_gemm_tile_rows": ([P], None),
         "jc_embed": ([P, u32, P, P, u32, f32, P, P, P], i32),
         "jc_norm_add": ([P, u32, u32, P, P, f32, P, P, P], i32),
         "jc_score": ([P, u32, P, f32, P, u32, P, P], i32),
@@ -331,6 +345,14 @@ def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=No
     _check(rc, "jc_attention")
 
 
+def gemm_tile_rows(rows: int) -> int:
+    """Sets the GEMM tile height policy (0 automatic, 128, or 64 wherever legal;
+    jc_gemm_tile_rows); returns the previous one."""
+    r = ctypes.c_int(rows)
+    lib().jc_gemm_tile_rows(ctypes.byref(r))
+    return r.value
+
+
 def attention_tc_min(global_min: int, window_min: int) -> tuple:
     """Sets the shortest global / sliding-window sequence for the tcgen05 attention kernel
     (jc_attention_tc_min); returns the previous pair."""
@@ -487,6 +509,28 @@ class Engine:
                                             _t_ptr(scorer_trace), _stream(stream), err, 1024)
         if rc != 0:
             raise JuliaCudaError(err.value.decode(errors="replace"))
+
+    def forward_profile(self, ids, markers, qtype: int, logits, records_per_launch: int = 1024,
+                        stream=None):
+        """A per-step forward with per-CTA phase stamps (julia_cuda_forward_profile). Returns
+        (records uint64 [launches, records_per_launch, 8], list of launch dicts). A record holds
+        %globaltimer ns at entry, inputs ready, first stage, results complete, outputs written,
+        exit (0 where a stage does not apply), then the SM and the CTA index."""
+        import torch
+        cap = 4 * (self.cfg.n_layers + self.cfg.n_head_layers) * 6 + 64
+        prof = torch.zeros(cap * records_per_launch * 8, dtype=torch.int64, device=ids.device)
+        info = (LaunchInfo * cap)()
+        n = ctypes.c_size_t(0)
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().julia_cuda_forward_profile(self._h, _t_ptr(ids), ids.numel(), _t_ptr(markers),
+                                              markers.numel(), qtype, _t_ptr(logits),
+                                              _t_ptr(prof), records_per_launch, info, cap,
+                                              ctypes.byref(n), _stream(stream), err, 1024)
+        if rc != 0:
+            raise JuliaCudaError(err.value.decode(errors="replace"))
+        launches = [{f: getattr(info[i], f) for f, _ in LaunchInfo._fields_} for i in range(n.value)]
+        recs = prof.view(-1, records_per_launch, 8).cpu().numpy().view(np.uint64)
+        return recs, launches
 
     def set_packing(self, rows: int) -> None:
         """run() packs consecutive requests into forwards of up to `rows` tokens (0: off)."""

@@ -128,10 +128,12 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
     const uint32_t kb0 = kb_lo + chunk * span / chunks, kb1 = kb_lo + (chunk + 1) * span / chunks;
     const uint32_t my_n = kb1 > kb0 + grp ? (kb1 - kb0 - grp + KS - 1) / KS : 0;
 
+    uint64_t *rec = threadIdx.x == 0 ? prof_record(p.prof, p.prof_cap) : nullptr;
     if (standalone) {
         pdl_wait();
         pdl_launch_dependents();
     }
+    prof_stamp(rec, 1);
     __syncthreads();  // the previous task of this CTA is done with the shared memory
 
     const uint32_t qs_a = smem_u32(qs);
@@ -146,6 +148,7 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
+    prof_stamp(rec, 2);
 
     uint32_t qf[4][4];
 #pragma unroll
@@ -266,6 +269,7 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
         group_bar(1 + grp, GT);
     }
     cp_async_wait<0>();
+    prof_stamp(rec, 3);
 
     // The key groups' partials meet in shared memory (the slots are free now), merged in group
     // order by group 0.
@@ -383,6 +387,7 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
                 dst[(8 * jt + 2 * t) / 2] = pack_half2(acc[jt][2 * h] * inv, acc[jt][2 * h + 1] * inv);
         }
     }
+    prof_stamp(rec, 4);
 }
 
 // Two CTAs per SM (at most 128 registers a thread), so the 64-query shape's grid at 1024 tokens
@@ -391,8 +396,11 @@ __device__ __forceinline__ void attention_task(const AttnParams &p, uint8_t *sme
 template <int QW, int KS>
 __global__ void __launch_bounds__(32 * QW * KS, KS > 4 ? 1 : 2) attention_kernel(const AttnParams p) {
     dev_err_bind(p.err);
+    uint64_t *rec = threadIdx.x == 0 ? prof_record(p.prof, p.prof_cap) : nullptr;
+    prof_open(rec);
     extern __shared__ __align__(128) uint8_t att_smem[];
     attention_task<QW, KS>(p, att_smem, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z, true);
+    prof_stamp(rec, 5);
 }
 
 }  // namespace jc

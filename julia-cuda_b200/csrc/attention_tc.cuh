@@ -69,6 +69,8 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr) {
 
 __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __grid_constant__ AttnTcParams kp) {
     dev_err_bind(kp.p.err);
+    uint64_t *rec = threadIdx.x == 0 ? prof_record(kp.p.prof, kp.p.prof_cap) : nullptr;
+    prof_open(rec);
     extern __shared__ uint8_t atc_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(atc_raw) + 1023) &
                                                 ~uintptr_t(1023));
@@ -117,6 +119,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
     const uint32_t tmem = *tmem_slot;  // columns: S 0 / 64, PV 128 / 192
     pdl_wait();
     pdl_launch_dependents();
+    prof_stamp(rec, 1);
 
     if (warp == 4) {
         if (lane == 0 && T > 0) {
@@ -335,10 +338,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
     // Every TMEM read and MMA is done before the columns are freed.
     tc_fence_before();
     __syncthreads();
+    prof_stamp(rec, 4);
     if (warp == 5) {
         tc_fence_after();
         tmem_dealloc(tmem, 256);
     }
+    prof_stamp(rec, 5);
 }
 
 }  // namespace jc

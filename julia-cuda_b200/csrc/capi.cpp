@@ -417,6 +417,77 @@ int julia_cuda_forward_trace(JcEngine *engine, const uint32_t *d_ids, uint32_t n
                              tr, stream, err, err_len);
 }
 
+int julia_cuda_forward_profile(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                               const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                               float *d_logits, uint64_t *d_prof, uint32_t records_per_launch,
+                               jc_launch_info *info, size_t info_cap, size_t *n_launches,
+                               void *stream, char *err, size_t err_len) {
+    return guarded(err, err_len, [&]() -> int {
+        if (!engine || !d_prof || records_per_launch == 0) {
+            report(err, err_len, "profile: null engine or record array");
+            return -1;
+        }
+        jc::Engine *e = engine->e;
+        if (!set_device(e->device, err, err_len)) return -1;
+        if (n == 0 || n > e->max_length || n_markers > e->max_length) {
+            report(err, err_len, "profile: " + std::to_string(n) + " tokens / " +
+                                     std::to_string(n_markers) + " markers, limit " +
+                                     std::to_string(e->max_length));
+            return -1;
+        }
+        cudaStream_t s = (cudaStream_t)stream;
+        if (!jc::cuda_ok(cudaMemcpyAsync(e->ids, d_ids, n * 4, cudaMemcpyDeviceToDevice, s), "ids") ||
+            (n_markers && !jc::cuda_ok(cudaMemcpyAsync(e->markers, d_markers, n_markers * 4,
+                                                       cudaMemcpyDeviceToDevice, s),
+                                       "markers"))) {
+            report(err, err_len, jc::last_error());
+            return -1;
+        }
+        // The forward captured into a CUDA graph (with its programmatic dependent launches) on
+        // the engine's stream, as julia_cuda_run's forwards are, then run on `stream`.
+        std::vector<jc_launch_info> log;
+        jc::Trace tr;
+        tr.prof = d_prof;
+        tr.prof_cap = records_per_launch;
+        cudaStream_t cap = e->stream;
+        if (!jc::cuda_ok(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "begin capture")) {
+            report(err, err_len, std::string("profile: ") + jc::last_error());
+            return -1;
+        }
+        e->launch_log = &log;
+        const bool ok = e->enqueue_forward(n, n_markers, qtype, jc::MODE_STEPS, tr, cap);
+        e->launch_log = nullptr;
+        cudaGraph_t graph = nullptr;
+        cudaError_t ce = cudaStreamEndCapture(cap, &graph);
+        if (!ok || !jc::cuda_ok(ce, "end capture")) {
+            if (graph) cudaGraphDestroy(graph);
+            report(err, err_len, std::string("profile: ") + jc::last_error());
+            return -1;
+        }
+        cudaGraphExec_t exec = nullptr;
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (!jc::cuda_ok(ce, "graph instantiate")) {
+            report(err, err_len, std::string("profile: ") + jc::last_error());
+            return -1;
+        }
+        const bool ran = jc::cuda_ok(cudaGraphLaunch(exec, s), "graph launch") &&
+                         (n_markers == 0 ||
+                          jc::cuda_ok(cudaMemcpyAsync(d_logits, e->logits, n_markers * 4,
+                                                      cudaMemcpyDeviceToDevice, s),
+                                      "logits")) &&
+                         jc::cuda_ok(cudaStreamSynchronize(s), "profile");
+        cudaGraphExecDestroy(exec);
+        if (!ran) {
+            report(err, err_len, std::string("profile: ") + jc::last_error());
+            return -1;
+        }
+        if (n_launches) *n_launches = log.size();
+        for (size_t i = 0; info && i < log.size() && i < info_cap; i++) info[i] = log[i];
+        return 0;
+    });
+}
+
 int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const size_t *lens,
                    const uint32_t *markers, const size_t *n_markers, const uint32_t *qtypes,
                    int layer_fused, float *logits, float *gpu_ms, char *err, size_t err_len) {
@@ -631,7 +702,7 @@ int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t 
         g.eps = eps;
         g.rope = rope;
         g.bias = bias;
-        if (!jc::check_gemm(g, cfg) || !jc::make_tmap_f16(&g.map_a, a, m, k, 128) ||
+        if (!jc::check_gemm(g, cfg) || !jc::make_tmap_f16(&g.map_a, a, m, k, (uint32_t)cfg.bm) ||
             !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
             return -1;
         return jc::launch_gemm(g, cfg, (cudaStream_t)stream, true) ? 0 : -1;
@@ -643,6 +714,10 @@ size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
 }
 
 size_t jc_attention_counters(uint32_t n, uint32_t heads) { return jc::attn_counters(n, heads); }
+
+void jc_gemm_tile_rows(int *rows) {
+    if (rows && (*rows == 0 || *rows == 64 || *rows == 128)) jc::swap_gemm_tile_rows(rows);
+}
 
 void jc_attention_tc_min(uint32_t *global_min, uint32_t *window_min) {
     if (global_min && window_min) jc::swap_attn_tc_min(global_min, window_min);

@@ -38,6 +38,30 @@ __device__ __forceinline__ uint64_t globaltimer() {
     return t;
 }
 
+// Optional per-CTA phase stamps of a profiling run (off unless a launch passes a record array):
+// 8 words a CTA, [0] entry, [1] inputs ready (the previous kernel done), [2] first operand stage
+// in shared memory, [3] results complete (accumulator / key loop), [4] outputs written, [5] exit
+// (%globaltimer ns; 0 where a stage does not apply), [6] the SM, [7] the CTA's linear index.
+__device__ __forceinline__ uint64_t *prof_record(uint64_t *prof, uint32_t cap) {
+    if (!prof) return nullptr;
+    const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    return cta < cap ? prof + 8 * (size_t)cta : nullptr;
+}
+
+__device__ __forceinline__ void prof_stamp(uint64_t *rec, int slot) {
+    if (rec) rec[slot] = globaltimer();
+}
+
+__device__ __forceinline__ void prof_open(uint64_t *rec) {
+    if (!rec) return;
+    uint32_t sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    rec[0] = globaltimer();
+    rec[1] = rec[2] = rec[3] = rec[4] = rec[5] = 0;
+    rec[6] = sm;
+    rec[7] = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

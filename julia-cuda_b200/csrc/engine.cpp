@@ -52,6 +52,7 @@ int Engine::add_map(const void *p, uint32_t rows, uint32_t cols, uint32_t box) {
     CUtensorMap m;
     if (!make_tmap_f16(&m, p, rows, cols, box)) return -1;
     hmaps.push_back(m);
+    map_src.push_back(MapSrc{p, rows, cols});
     map_index.emplace(key, (int)hmaps.size() - 1);
     return (int)hmaps.size() - 1;
 }
@@ -244,6 +245,15 @@ Step Engine::gemm_step(uint32_t epi, int map_a, int map_w, const void *w, uint32
 std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
                                       int mode, bool packed) const {
     std::vector<Step> steps = build_steps_flat(n, k, qtype, tr, mode);
+    for (size_t i = 0; i < steps.size(); i++) {
+        Step &st = steps[i];
+        st.slot = (int)i;
+        if (tr.prof && mode == MODE_STEPS) {
+            uint64_t *rec = tr.prof + (size_t)i * tr.prof_cap * 8;
+            if (st.d.kind == PH_GEMM) st.d.g.prof = rec, st.d.g.prof_cap = tr.prof_cap;
+            if (st.d.kind == PH_ATTN) st.d.a.prof = rec, st.d.a.prof_cap = tr.prof_cap;
+        }
+    }
     if (packed)
         for (Step &st : steps) {
             if (st.d.kind == PH_ATTN) st.d.a.seg = seg;
@@ -400,6 +410,14 @@ std::vector<Step> Engine::build_steps_flat(uint32_t n, uint32_t k, uint32_t qtyp
 
 bool Engine::run_step(const Step &st, cudaStream_t s) {
     const PhaseDesc &d = st.d;
+    jc_launch_info info{};
+    info.kind = d.kind;
+    info.layer = st.layer;
+    info.record = (uint32_t)std::max(st.slot, 0);
+    auto logged = [&](bool ok) {
+        if (ok && launch_log) launch_log->push_back(info);
+        return ok;
+    };
     switch (d.kind) {
         case PH_GEMM: {
             const GemmParams &p = d.g;
@@ -413,10 +431,13 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
                 return false;
             }
             const CUtensorMap *wm = wmap(st.w, p.n, p.k, c.bn);
-            if (!wm) return false;
+            // The A operand in boxes of the tile height (the engine's maps hold 128-row boxes).
+            const MapSrc &as = map_src[st.map_a];
+            const CUtensorMap *am = c.bm == 128 ? &hmaps[st.map_a] : wmap(as.p, as.rows, as.cols, c.bm);
+            if (!wm || !am) return false;
             GemmArgs g;
             g.epi = d.epi;
-            g.map_a = hmaps[st.map_a];
+            g.map_a = *am;
             g.map_w = *wm;
             g.c = p.c;
             g.res = p.res;
@@ -436,7 +457,13 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             g.seg = p.seg;
             g.bias = p.bias;
             g.err = p.err;
-            return launch_gemm(g, c, s, true);
+            g.prof = p.prof;
+            g.prof_cap = p.prof_cap;
+            info.epi = d.epi;
+            info.m = p.m, info.n = p.n, info.k = p.k;
+            info.ctas = gemm_ctas(p.m, p.n, c);
+            info.tile = (uint32_t)c.bm << 16 | (uint32_t)c.bn;
+            return logged(launch_gemm(g, c, s, true));
         }
         case PH_ATTN: {
             AttnArgs a;
@@ -450,24 +477,35 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             a.ws = attn_ws;
             a.counters = attn_cnt;
             a.err = d.a.err;
+            a.prof = d.a.prof;
+            a.prof_cap = d.a.prof_cap;
             if (attn_ws_floats(a.n, a.heads, a.kv_chunks) > attn_ws_cap) a.kv_chunks = 1;
-            return launch_attention(a, s, true);
+            info.m = a.n, info.n = a.heads, info.k = a.window;
+            info.ctas = attention_ctas(a);
+            return logged(launch_attention(a, s, true));
         }
+        // The row-wise edges take no phase stamps: one warp per row, (rows + 3) / 4 CTAs.
         case PH_EMBED:
-            return launch_embed(d.r.rows, d.r.n, d.r.x, d.r.gamma, d.r.d, d.r.eps, d.r.out,
-                                d.r.stats, s, true);
+            info.m = d.r.n, info.n = d.r.d, info.ctas = (d.r.n + 3) / 4;
+            return logged(launch_embed(d.r.rows, d.r.n, d.r.x, d.r.gamma, d.r.d, d.r.eps, d.r.out,
+                                       d.r.stats, s, true));
         case PH_NORM_ADD:
-            return launch_norm_add(d.r.x, d.r.n, d.r.d, d.r.gamma, d.r.add, d.r.eps, d.r.out,
-                                   d.r.stats, s, true);
+            info.m = d.r.n, info.n = d.r.d, info.ctas = (d.r.n + 3) / 4;
+            return logged(launch_norm_add(d.r.x, d.r.n, d.r.d, d.r.gamma, d.r.add, d.r.eps,
+                                          d.r.out, d.r.stats, s, true));
         case PH_GATHER:
-            return launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n, d.r.limit,
-                                      d.r.out, d.r.stats, s, true, dev_err);
+            info.m = d.r.n, info.n = d.r.d, info.ctas = (d.r.n + 3) / 4;
+            return logged(launch_gather_rows(d.r.x, d.r.stats_in, d.r.d, d.r.rows, d.r.n,
+                                             d.r.limit, d.r.out, d.r.stats, s, true, dev_err));
         case PH_SCORE:
-            return launch_score(d.r.x, d.r.d, d.r.w, d.r.b, d.r.rows, d.r.n, d.r.logits, s, true);
+            info.m = d.r.n, info.n = d.r.d, info.ctas = (d.r.n + 3) / 4;
+            return logged(launch_score(d.r.x, d.r.d, d.r.w, d.r.b, d.r.rows, d.r.n, d.r.logits,
+                                       s, true));
         case PH_COPY:
-            return cuda_ok(cudaMemcpyAsync(d.r.out, d.r.x, (size_t)d.r.n * d.r.d * 2,
-                                           cudaMemcpyDeviceToDevice, s),
-                           "copy");
+            info.m = d.r.n, info.n = d.r.d;
+            return logged(cuda_ok(cudaMemcpyAsync(d.r.out, d.r.x, (size_t)d.r.n * d.r.d * 2,
+                                                  cudaMemcpyDeviceToDevice, s),
+                                  "copy"));
         default:
             set_error("engine: unknown step");
             return false;

@@ -42,8 +42,12 @@ struct GraphKey {
 // enc [n_layers][n][D] the residual stream after each encoder layer; head [n_head_layers + 1][nh]
 // [D] the head's stream (its input, then after each head layer; nh = the head's rows); scorer
 // [k][scorer_hidden] the scorer's hidden layer (after GELU) of each marker.
+// prof: a profiling run's per-CTA phase stamps, prof_cap 8-word records for each launch (launch i
+// of the forward writes records [i * prof_cap, (i + 1) * prof_cap)); per-step kernels only.
 struct Trace {
     uint16_t *enc = nullptr, *head = nullptr, *scorer = nullptr;
+    uint64_t *prof = nullptr;
+    uint32_t prof_cap = 0;
 };
 
 struct Step {
@@ -52,6 +56,7 @@ struct Step {
     const void *w = nullptr;  // GEMM weights, for the single-GEMM kernels' own maps
     int layer = -1;     // encoder layer, or -1 before the encoder, -2 after it
     uint32_t flow_total = 0;  // first step of a persistent launch: the launch's work items
+    int slot = -1;      // the step's index in its forward (its phase-stamp records, when profiled)
 };
 
 class Engine {
@@ -115,6 +120,8 @@ class Engine {
     // The error word copied into h_err (the stream has synchronised since): 0, or the reason.
     bool check_device_error_copy(std::string *why);
     cudaEvent_t ev_start[QUEUE] = {}, ev_end[QUEUE] = {};
+    // While set, every per-step launch appends what it ran (a profiling run's launch list).
+    std::vector<jc_launch_info> *launch_log = nullptr;
 
    private:
     struct GraphEntry {
@@ -161,6 +168,12 @@ class Engine {
     size_t gemm_ws_cap = 0, gemm_cnt_cap = 0, attn_ws_cap = 0, attn_cnt_cap = 0;
     // tensor maps: host copies and the device array the persistent kernel reads
     std::vector<CUtensorMap> hmaps;
+    // what each of hmaps covers (an A operand's map for another tile height is derived from it)
+    struct MapSrc {
+        const void *p;
+        uint32_t rows, cols;
+    };
+    std::vector<MapSrc> map_src;
     std::map<std::tuple<const void *, uint32_t, uint32_t, uint32_t>, int> map_index;
     CUtensorMap *dmaps = nullptr;
     int m_x = -1, m_o = -1, m_m = -1, m_f = -1, m_hx = -1, m_xs = -1;

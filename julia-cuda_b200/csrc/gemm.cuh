@@ -5,7 +5,9 @@
 // (kernels/src/gemm.rs:317-433 mainloop / split_reduce, kernels/src/main.rs:886-1147 gemm_tile
 // and its 32 instances) with one tcgen05 design:
 //
-//   - a CTA computes a 128 x BN tile (BN = 32, 64 or 128) with 256 threads;
+//   - a CTA computes a BM x BN tile (BM = 128, or 64 for narrow GEMMs at a few hundred rows: half
+//     the activation bytes a CTA ingests, which bounds the main loop; BN = 32, 64, 128 or 256)
+//     with 256 threads;
 //   - warp 0 lane 0 streams 64-deep K blocks of A and W into a ring of STAGES 128B-swizzled
 //     shared-memory stages with TMA (no multicast), each stage completing on an mbarrier;
 //   - lane 0 of warps 1..NI issue tcgen05.mma (M=128, N=BN, K=16, kind::f16), each into its own
@@ -49,11 +51,16 @@ constexpr int GEMM_THREADS = 256;
 // 64-deep k-blocks per pipeline stage: one 3-D TMA box per operand brings all of them.
 constexpr int GEMM_KPS = 2;
 
-template <int BN, int STAGES_>
+template <int BN, int STAGES_, int BM_ = GEMM_BM>
 struct GemmShape {
+    static_assert(BM_ == 128 || BM_ == 64, "128- or 64-row tiles");
     static constexpr int STAGES = STAGES_;
+    static constexpr int BM = BM_;
+    // Tile rows a warp's 32 TMEM lanes hold: an M = 128 MMA puts row r in lane r; an M = 64 one
+    // puts rows 16q..16q + 15 in lanes 32q..32q + 15 (lanes 32q + 16.. hold none).
+    static constexpr int RPW = BM_ / 4;
     static constexpr int KPS = GEMM_KPS;
-    static constexpr int A_KB = GEMM_BM * GEMM_BK * 2;  // one k-block of A: 128 rows x 128 B
+    static constexpr int A_KB = BM_ * GEMM_BK * 2;  // one k-block of A: BM rows x 128 B
     static constexpr int W_KB = BN * GEMM_BK * 2;       // one k-block of W
     static constexpr int A_BYTES = KPS * A_KB;
     static constexpr int B_BYTES = KPS * W_KB;
@@ -134,12 +141,12 @@ __device__ __forceinline__ void pack_group(const float *v, const uint32_t *resw,
 // area of the TMA stores: boxes of BW columns x 128 rows, 16-byte chunk c of a row at chunk
 // c ^ (row % 8) (BW 64, 128-byte swizzle) or c ^ ((row / 2) % 4) (BW 32, 64-byte swizzle), the
 // layout the tensor map's swizzle mode reads; a warp's 32 rows then spread over all banks.
-template <int G, int BW>
+template <int G, int BW, int BM = GEMM_BM>
 __device__ __forceinline__ void stage_halves(uint8_t *stage, uint32_t row, uint32_t oc,
                                              const uint32_t *in) {
     static_assert(G % 8 == 0 && (BW == 64 || BW == 32), "16-byte chunks in 64- or 32-column boxes");
     constexpr uint32_t ROWB = BW * 2;
-    uint8_t *box_row = stage + (oc / BW) * (GEMM_BM * ROWB) + row * ROWB;
+    uint8_t *box_row = stage + (oc / BW) * (BM * ROWB) + row * ROWB;
     const uint32_t c0 = (oc % BW) / 8;
     const uint32_t sw = BW == 64 ? (row & 7) : ((row >> 1) & 3);
 #pragma unroll
@@ -155,7 +162,7 @@ __device__ __forceinline__ void stage_halves(uint8_t *stage, uint32_t row, uint3
 // (tile-local, the tile starting at n0); resw: the residual of those columns (G/2 + G/2 words);
 // ropev: (cos, sin) of pairs pair0 .. pair0 + G, two per float4. stage: the TMA-store staging
 // area (boxes of BW output columns; tr = the row inside the tile), or nullptr to store directly.
-template <int G, int HALF, uint32_t EPI, int BW>
+template <int G, int HALF, uint32_t EPI, int BW, int BM = GEMM_BM>
 __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v, uint32_t r,
                                                    uint32_t tr, uint8_t *stage,
                                                    bool valid, uint32_t n0, uint32_t c0,
@@ -218,7 +225,7 @@ __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v
                                     gelu_as(v[2 * j + 1]) * v[G + 2 * j + 1]);
             if constexpr (STAGE_OK) {
                 if (stage) {
-                    stage_halves<G, BW>(stage, tr, (c0 - n0) / 2 + pair0, out);
+                    stage_halves<G, BW, BM>(stage, tr, (c0 - n0) / 2 + pair0, out);
                     return;
                 }
             }
@@ -231,8 +238,8 @@ __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v
             pack_group<G, EPI>(v + G, resw + G / 2, ob, s, q);
             if constexpr (STAGE_OK) {
                 if (stage) {
-                    stage_halves<G, BW>(stage, tr, la, oa);
-                    stage_halves<G, BW>(stage, tr, lb, ob);
+                    stage_halves<G, BW, BM>(stage, tr, la, oa);
+                    stage_halves<G, BW, BM>(stage, tr, lb, ob);
                     return;
                 }
             }

@@ -7,9 +7,9 @@ namespace jc {
 
 // Where a CTA's GEMM pipeline lives in shared memory: STAGES stages, then the barriers, the TMEM
 // base slot, a flag, per-row partial statistics and the tile's column sums / biases.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int BM = GEMM_BM>
 struct GemmSmemView {
-    using S = GemmShape<BN, STAGES>;
+    using S = GemmShape<BN, STAGES, BM>;
     uint8_t *stages;
     uint64_t *full, *empty, *done;
     uint32_t *tmem_slot, *last_flag;
@@ -38,8 +38,8 @@ struct GemmRun {
 };
 
 // Barrier initialisation and the TMEM accumulator; every thread calls it, returns the TMEM base.
-template <int BN, int STAGES>
-__device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES> &sv) {
+template <int BN, int STAGES, int BM = GEMM_BM>
+__device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES, BM> &sv) {
     constexpr uint32_t NI = GemmShape<BN, STAGES>::NI;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -73,11 +73,12 @@ __device__ __forceinline__ uint32_t gemm_stages(uint32_t nkb) { return (nkb + GE
 // run.it and whose k range starts at k-block kb0 (expect_tx covers A and W; the A halves follow
 // once the activations are ready). A stage's box may reach past the range (or past k): those
 // k-blocks are loaded (zeros past k) but never multiplied.
-template <int BN, int STAGES>
-__device__ __forceinline__ bool gemm_issue_w(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
+template <int BN, int STAGES, int BM = GEMM_BM>
+__device__ __forceinline__ bool gemm_issue_w(const GemmParams &p,
+                                             const GemmSmemView<BN, STAGES, BM> &sv,
                                              uint32_t it, uint32_t n0, uint32_t kb0,
                                              uint32_t first, uint32_t count) {
-    using S = GemmShape<BN, STAGES>;
+    using S = GemmShape<BN, STAGES, BM>;
     for (uint32_t i = first; i < count; i++) {
         const uint32_t g = it + i, s = g % STAGES, round = g / STAGES;
         if (round > 0 && !mbar_wait(&sv.empty[s], (round & 1) ^ 1, JC_DEV_TIMEOUT_EMPTY))
@@ -91,10 +92,11 @@ __device__ __forceinline__ bool gemm_issue_w(const GemmParams &p, const GemmSmem
 }
 
 // Producer thread only: the A half of stage i (whose W half and expect_tx are already issued).
-template <int BN, int STAGES>
-__device__ __forceinline__ void gemm_issue_a(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
+template <int BN, int STAGES, int BM = GEMM_BM>
+__device__ __forceinline__ void gemm_issue_a(const GemmParams &p,
+                                             const GemmSmemView<BN, STAGES, BM> &sv,
                                              uint32_t it, uint32_t m0, uint32_t kb0, uint32_t i) {
-    using S = GemmShape<BN, STAGES>;
+    using S = GemmShape<BN, STAGES, BM>;
     const uint32_t s = (it + i) % STAGES;
     tma_load_3d(sv.stages + s * S::STAGE_BYTES, p.map_a, &sv.full[s], 0, (int32_t)m0,
                 (int32_t)(kb0 + i * GEMM_KPS));
@@ -167,8 +169,9 @@ struct PdlGate {
     }
 };
 
-// One 128 x BN output tile (split z of `splits`; `tile` numbers it for the split counters). Every
-// thread of the CTA calls it. `prefetched`: leading stages whose W half gemm_issue_w already
+// One BM x BN output tile (split z of `splits`; `tile` numbers it for the split counters). Every
+// thread of the CTA calls it. BM = 64 (an M = 64 MMA; its rows in lanes 0-15 of each warp's TMEM
+// quadrant) serves single-CTA tiles only (no split, no cluster). `prefetched`: leading stages whose W half gemm_issue_w already
 // issued. `gate`: how the tile waits for its inputs (PdlGate, or the persistent kernel's
 // dependency counters).
 //
@@ -177,19 +180,21 @@ struct PdlGate {
 // columns [Go c, Go (c + 1)) of each 32-column half of every 64-column chunk (so RoPE pairs and
 // GeGLU input / gate pairs stay together), receives the other CTAs' partials of them into its own
 // (now idle) stage memory, sums them in rank order (deterministic) and runs the epilogue on them.
-template <int BN, int STAGES, uint32_t EPI, int CS = 1, class Gate = PdlGate>
-__device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemView<BN, STAGES> &sv,
+template <int BN, int STAGES, uint32_t EPI, int CS = 1, class Gate = PdlGate, int BM = GEMM_BM>
+__device__ __forceinline__ void gemm_tile(const GemmParams &p,
+                                          const GemmSmemView<BN, STAGES, BM> &sv,
                                           uint32_t tmem, GemmRun &run, uint32_t tile_n,
                                           uint32_t tile_m, uint32_t z, uint32_t splits,
                                           uint32_t tile, uint32_t prefetched, const Gate &gate) {
-    using S = GemmShape<BN, STAGES>;
+    using S = GemmShape<BN, STAGES, BM>;
     constexpr int CH = S::CH, NCH = S::NCH, HALF = CH / 2;
     constexpr int GT = CH / (4 * CS);  // columns per thread per half-chunk group
     constexpr int GO = 2 * GT;         // columns a cluster rank owns per half-chunk group
     static_assert(CS == 1 || CH == 64, "cluster split-K needs 64-column chunks");
+    static_assert(CS == 1 || BM == GEMM_BM, "cluster split-K runs 128-row tiles");
     static_assert(GT >= 4, "at least 4 columns per thread group");
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = tile_n * BN, m0 = tile_m * GEMM_BM;
+    const uint32_t n0 = tile_n * BN, m0 = tile_m * BM;
     const uint32_t rank = CS > 1 ? z : 0;
     uint32_t kb0, nkb;
     k_range(p.k / GEMM_BK, z, splits, kb0, nkb);
@@ -203,20 +208,27 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
 
     const uint32_t nst = gemm_stages(nkb);
     const uint32_t pre = nst < (uint32_t)STAGES ? nst : (uint32_t)STAGES;
+    // Phase stamps (profiling runs only): thread 0 (the producer) and thread 32 (the first issuer).
+    uint64_t *rec = (threadIdx.x & ~32u) == 0 ? prof_record(p.prof, p.prof_cap) : nullptr;
     bool ok = true;
     if (warp == 0 && lane == 0) {
         // TMA producer: weights of the first stages first (they do not depend on the previous
         // kernel), then the activations.
-        ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, prefetched < pre ? prefetched : pre, pre);
+        ok = gemm_issue_w<BN, STAGES, BM>(p, sv, run.it, n0, kb0, prefetched < pre ? prefetched : pre,
+                                          pre);
         gate.producer();
-        for (uint32_t i = 0; ok && i < pre; i++) gemm_issue_a<BN, STAGES>(p, sv, run.it, m0, kb0, i);
+        prof_stamp(rec, 1);
+        for (uint32_t i = 0; ok && i < pre; i++) gemm_issue_a<BN, STAGES, BM>(p, sv, run.it, m0, kb0, i);
     }
 
-    // Epilogue geometry: warp w owns rows 32(w%4)..+31 and half w/4 of the columns it handles.
+    // Epilogue geometry: warp w owns the tile rows of TMEM lanes 32(w%4)..+31 (rows 32(w%4)..+31
+    // of a 128-row tile; rows 16(w%4)..+15 of a 64-row one, in its first 16 lanes) and half w/4 of
+    // the columns it handles.
     const uint32_t quarter = warp & 3, half = warp >> 2;
-    const uint32_t row = quarter * 32 + lane;
+    const bool lane_ok = lane < (uint32_t)S::RPW;
+    const uint32_t row = quarter * S::RPW + (lane & (S::RPW - 1));
     const uint32_t r = m0 + row;
-    const bool valid = r < p.m;
+    const bool valid = lane_ok && r < p.m;
     const uint32_t pair0 = GO * rank + GT * half;  // first column of this thread's groups
     gate.all();
 
@@ -255,18 +267,19 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
 
     if (warp == 0 && lane == 0) {
         for (uint32_t i = pre; ok && i < nst; i++) {
-            ok = gemm_issue_w<BN, STAGES>(p, sv, run.it, n0, kb0, i, i + 1);
-            if (ok) gemm_issue_a<BN, STAGES>(p, sv, run.it, m0, kb0, i);
+            ok = gemm_issue_w<BN, STAGES, BM>(p, sv, run.it, n0, kb0, i, i + 1);
+            if (ok) gemm_issue_a<BN, STAGES, BM>(p, sv, run.it, m0, kb0, i);
         }
     } else if (warp >= 1 && warp <= (uint32_t)S::NI && lane == 0) {
-        // MMA issuer j = warp - 1: of each stage's 4 x kbs MMAs (128 x BN x 16 each), those whose
+        // MMA issuer j = warp - 1: of each stage's 4 x kbs MMAs (BM x BN x 16 each), those whose
         // index is j modulo NI, into accumulator j.
-        constexpr uint32_t idesc = umma_idesc_f16(GEMM_BM, BN);
+        constexpr uint32_t idesc = umma_idesc_f16(BM, BN);
         const uint32_t j = warp - 1, acc = tmem + j * BN;
         bool started = false;
         for (uint32_t i = 0; i < nst; i++) {
             const uint32_t g = run.it + i, s = g % STAGES, round = g / STAGES;
             if (!mbar_wait(&sv.full[s], round & 1, JC_DEV_TIMEOUT_FULL)) break;
+            if (i == 0 && j == 0) prof_stamp(rec, 2);
             tc_fence_after();
             const uint32_t kbs = nkb - i * GEMM_KPS < (uint32_t)GEMM_KPS ? nkb - i * GEMM_KPS : GEMM_KPS;
             uint8_t *st = sv.stages + s * S::STAGE_BYTES;
@@ -289,6 +302,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
 
     const bool mma_ok =
         __syncthreads_and(mbar_wait_sleep(sv.done, run.tiles & 1, JC_DEV_TIMEOUT_MMA)) != 0;
+    if (threadIdx.x == 0) prof_stamp(rec, 3);
     tc_fence_after();
     float mean = 0.f, rstd = 0.f;
     if constexpr ((EPI & JC_EPI_LN) != 0) {
@@ -324,15 +338,17 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
         }
         cluster_sync_all();
     } else if (splits > 1 && mma_ok) {
-        float *mine = p.ws + ((size_t)tile * splits + z) * BN * GEMM_BM;
+        float *mine = p.ws + ((size_t)tile * splits + z) * BN * BM;
 #pragma unroll
         for (int ci = 0; ci < NCH; ci++) {
             float v[2 * GT];
             acc_ld2<GT, S::NI, BN>(lane_base + ci * CH + pair0, lane_base + ci * CH + HALF + pair0, v);
+            if (lane_ok) {
 #pragma unroll
-            for (int j = 0; j < GT; j++) {
-                mine[(size_t)(ci * CH + pair0 + j) * GEMM_BM + row] = v[j];
-                mine[(size_t)(ci * CH + HALF + pair0 + j) * GEMM_BM + row] = v[GT + j];
+                for (int j = 0; j < GT; j++) {
+                    mine[(size_t)(ci * CH + pair0 + j) * BM + row] = v[j];
+                    mine[(size_t)(ci * CH + HALF + pair0 + j) * BM + row] = v[GT + j];
+                }
             }
         }
         __threadfence();
@@ -393,22 +409,22 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
 #pragma unroll
                         for (int j = 0; j < 2 * GT; j++) v[j] += t[j];
                     } else {
-                        const float *part = p.ws + ((size_t)tile * splits + zz) * BN * GEMM_BM;
+                        const float *part = p.ws + ((size_t)tile * splits + zz) * BN * BM;
 #pragma unroll
                         for (int j = 0; j < GT; j++) {
-                            v[j] += __ldcg(part + (size_t)(ca + j) * GEMM_BM + row);
-                            v[GT + j] += __ldcg(part + (size_t)(cb + j) * GEMM_BM + row);
+                            v[j] += __ldcg(part + (size_t)(ca + j) * BM + row);
+                            v[GT + j] += __ldcg(part + (size_t)(cb + j) * BM + row);
                         }
                     }
                 }
             }
-            gemm_epilogue_part<GT, HALF, EPI, BW>(p, v, r, row, stage, valid, n0, n0 + ci * CH, pair0, mean, rstd,
+            gemm_epilogue_part<GT, HALF, EPI, BW, BM>(p, v, r, row, stage, valid, n0, n0 + ci * CH, pair0, mean, rstd,
                                               sv.cs_s, sv.bs_s, resw + ((EPI & JC_EPI_RES) ? ci * GT : 0),
                                               ropev, s, q);
         }
         if constexpr ((EPI & JC_EPI_STATS) != 0) {
             // The two halves of a row meet in shared memory; one atomic pair per row per CTA.
-            if (half) sv.row_part[row] = make_float2(s, q);
+            if (half && lane_ok) sv.row_part[row] = make_float2(s, q);
             __syncthreads();
             if (!half && valid) {
                 const float2 o = sv.row_part[row];
@@ -425,7 +441,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
                 const int32_t out0 = (int32_t)((EPI & JC_EPI_GEGLU) ? n0 / 2 : n0);
 #pragma unroll
                 for (int b = 0; b < W_OUT / BW; b++)
-                    tma_store_2d(p.map_c, stage + b * GEMM_BM * BW * 2, out0 + b * BW, (int32_t)m0);
+                    tma_store_2d(p.map_c, stage + b * BM * BW * 2, out0 + b * BW, (int32_t)m0);
                 bulk_commit();
                 bulk_wait_read();
             }
@@ -434,6 +450,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p, const GemmSmemVie
     // Every TMEM read and shared-memory use of this tile is done before the next one starts.
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) prof_stamp(rec, 4);
     run.it += nst;
     run.tiles += 1;
 }
@@ -446,10 +463,12 @@ struct GemmKernelParams {
     GemmParams p;
 };
 
-template <int BN, int STAGES, uint32_t EPI, int CS>
+template <int BN, int STAGES, uint32_t EPI, int CS, int BM = GEMM_BM>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ GemmKernelParams kp) {
     dev_err_bind(kp.p.err);
+    uint64_t *rec = threadIdx.x == 0 ? prof_record(kp.p.prof, kp.p.prof_cap) : nullptr;
+    prof_open(rec);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
@@ -457,18 +476,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     p.map_a = &kp.map_a;
     p.map_w = &kp.map_w;
     p.map_c = p.store_tma ? &kp.map_c : nullptr;
-    const GemmSmemView<BN, STAGES> sv(base);
+    const GemmSmemView<BN, STAGES, BM> sv(base);
     if (threadIdx.x == 32) {
         tma_prefetch_desc(p.map_a);
         tma_prefetch_desc(p.map_w);
     }
-    const uint32_t tmem = gemm_setup<BN, STAGES>(sv);
+    const uint32_t tmem = gemm_setup<BN, STAGES, BM>(sv);
     GemmRun run;
-    gemm_tile<BN, STAGES, EPI, CS>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z, gridDim.z,
-                                   blockIdx.y * gridDim.x + blockIdx.x, 0, PdlGate{});
+    gemm_tile<BN, STAGES, EPI, CS, PdlGate, BM>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z,
+                                                gridDim.z, blockIdx.y * gridDim.x + blockIdx.x, 0,
+                                                PdlGate{});
     gemm_zero(p, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
               gridDim.x * gridDim.y * gridDim.z);
     gemm_teardown<BN, STAGES>(tmem);
+    prof_stamp(rec, 5);
 }
 
 }  // namespace jc

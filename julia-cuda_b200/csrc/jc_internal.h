@@ -39,7 +39,8 @@ bool cuda_ok(cudaError_t e, const char *what);
 // A row-major [rows, cols] f16 GEMM operand (cols a multiple of 64) seen as 3-D: (column inside a
 // 64-wide k-block, row, k-block), loaded in boxes of 64 x box_rows x GEMM_KPS with the 128-byte
 // swizzle, so one box lands as GEMM_KPS consecutive [box_rows][128 B] k-block tiles. Returns false
-// (and sets the error) on failure.
+// (and sets the error) on failure. A GEMM's A operand takes boxes of its tile height
+// (GemmConfig::bm), its W operand boxes of its tile width (GemmConfig::bn).
 bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                    uint32_t box_rows);
 
@@ -65,10 +66,13 @@ struct GemmArgs {
     uint32_t rope_stride = 0;  // rows of the pair-group-major RoPE table; 0: m
     const uint2 *seg = nullptr;  // packed requests: row r's request rows (RoPE position r - seg[r].x)
     unsigned int *err = nullptr;  // error word for device-side timeouts (nullptr: the module's)
+    uint64_t *prof = nullptr;     // profiling run: per-CTA phase stamps (8 words a CTA)
+    uint32_t prof_cap = 0;        // records available at prof
 };
 
 struct GemmConfig {
-    int bn = 64;      // output columns per CTA: 32, 64 or 128
+    int bm = 128;     // output rows per CTA: 128, or 64 (32- and 64-column tiles, no split-K)
+    int bn = 64;      // output columns per CTA: 32, 64, 128 or 256
     int splits = 1;   // split-K factor through a global workspace, 1..8
     int cluster = 1;  // split-K factor inside a thread-block cluster (1, 2 or 4; DSMEM reduction)
     bool deep = false;  // twice the pipeline stages (one CTA per SM)
@@ -92,8 +96,11 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms);
 // A caller's split-K request: > 0 that many splits through the workspace, < 0 a cluster of -splits
 // CTAs reducing through distributed shared memory (no workspace), 0 keeps the automatic choice.
 void request_splits(GemmConfig &c, int splits);
-// Picks the pipeline depth for a configuration whose tile width / splits are already set.
+// Picks the tile height and pipeline depth for a configuration whose tile width / splits are
+// already set.
 void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms);
+// The tile height policy (0 automatic, 128, or 64 wherever legal): sets it, returns the old one.
+void swap_gemm_tile_rows(int *rows);
 
 // ---------------------------------------------------------------------------------------------
 // attention: o = softmax(q k^T / 8) v per head, global or |q - k| <= window
@@ -107,8 +114,14 @@ struct AttnArgs {
     uint32_t *counters = nullptr; // kv_chunks > 1: one zeroed counter per (query tile, head)
     const uint2 *seg = nullptr;   // packed requests: row r sees only keys [seg[r].x, seg[r].y)
     unsigned int *err = nullptr;  // error word (nullptr: the module's)
+    uint64_t *prof = nullptr;     // profiling run: per-CTA phase stamps (8 words a CTA)
+    uint32_t prof_cap = 0;
 };
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
+// CTAs a launch_attention of these arguments runs.
+uint32_t attention_ctas(const AttnArgs &a);
+// CTAs a launch_gemm of this shape and configuration runs.
+uint32_t gemm_ctas(uint32_t m, uint32_t n, const GemmConfig &cfg);
 size_t attn_counters(uint32_t n, uint32_t heads);
 bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms);

@@ -72,6 +72,11 @@ const char *device_error_name(unsigned int code) {
 // ---------------------------------------------------------------------------------------------
 // launch helper: cudaLaunchKernelEx with programmatic stream serialization when `pdl`
 
+static uint32_t env_u32_early(const char *name, uint32_t dflt) {
+    const char *e = getenv(name);
+    return e ? (uint32_t)strtoul(e, nullptr, 10) : dflt;
+}
+
 // Programmatic dependent launch is on unless the environment sets JC_PDL=0 (for A/B timing).
 static bool pdl_allowed() {
     static const bool on = [] {
@@ -189,13 +194,13 @@ bool make_tmap_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t c
 
 size_t gemm_ws_floats(uint32_t m, uint32_t n, GemmConfig cfg) {
     if (cfg.splits <= 1) return 0;
-    const size_t tiles = (size_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / cfg.bn);
-    return tiles * cfg.splits * cfg.bn * GEMM_BM;
+    const size_t tiles = (size_t)((m + cfg.bm - 1) / cfg.bm) * (n / cfg.bn);
+    return tiles * cfg.splits * cfg.bn * cfg.bm;
 }
 
 size_t gemm_counters(uint32_t m, uint32_t n, GemmConfig cfg) {
     if (cfg.splits <= 1) return 0;
-    return (size_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / cfg.bn);
+    return (size_t)((m + cfg.bm - 1) / cfg.bm) * (n / cfg.bn);
 }
 
 // Stage depths: "shallow" keeps a CTA near 100 KB of shared memory so two fit on an SM (a GEMM
@@ -206,36 +211,41 @@ template <> struct Depth<32> { static constexpr int shallow = 2, deep = 5; };
 template <> struct Depth<64> { static constexpr int shallow = 2, deep = 4; };
 template <> struct Depth<128> { static constexpr int shallow = 2, deep = 3; };
 template <> struct Depth<256> { static constexpr int shallow = 2, deep = 2; };  // 96 KB stages
+// 64-row tiles (one CTA per SM): a stage holds half the activation bytes, so the ring goes deeper
+// and holds a whole 1152-deep K range of a 32-column tile (9 stages would; 8 x 24 KB fit).
+template <int BN> struct Depth64;
+template <> struct Depth64<32> { static constexpr int deep = 8; };  // 24 KB stages
+template <> struct Depth64<64> { static constexpr int deep = 6; };  // 32 KB stages
 
-template <int BN, int STAGES, uint32_t EPI, int CS>
+template <int BN, int STAGES, uint32_t EPI, int CS, int BM>
 static bool launch_gemm_inst(const GemmKernelParams &p, dim3 grid, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
-    auto kern = gemm_tc_kernel<BN, STAGES, EPI, CS>;
-    constexpr int smem = GemmShape<BN, STAGES>::SMEM_BYTES;
+    auto kern = gemm_tc_kernel<BN, STAGES, EPI, CS, BM>;
+    constexpr int smem = GemmShape<BN, STAGES, BM>::SMEM_BYTES;
     if (!ensure_smem(kern, smem, smem_set)) return false;
     return launch_ex_cluster(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, CS, "gemm launch", p);
 }
 
-template <int BN, int STAGES, int CS>
+template <int BN, int STAGES, int CS, int BM = GEMM_BM>
 static bool launch_gemm_depth(uint32_t epi, const GemmKernelParams &p, dim3 grid, cudaStream_t s,
                               bool pdl) {
     constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
     switch (epi) {
-        case 0: return launch_gemm_inst<BN, STAGES, 0, CS>(p, grid, s, pdl);
-        case RS: return launch_gemm_inst<BN, STAGES, RS, CS>(p, grid, s, pdl);
-        case JC_EPI_BIAS | RS: return launch_gemm_inst<BN, STAGES, JC_EPI_BIAS | RS, CS>(p, grid, s, pdl);
-        case LB: return launch_gemm_inst<BN, STAGES, LB, CS>(p, grid, s, pdl);
-        case LB | JC_EPI_RELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_RELU, CS>(p, grid, s, pdl);
-        case LB | JC_EPI_GELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_GELU, CS>(p, grid, s, pdl);
+        case 0: return launch_gemm_inst<BN, STAGES, 0, CS, BM>(p, grid, s, pdl);
+        case RS: return launch_gemm_inst<BN, STAGES, RS, CS, BM>(p, grid, s, pdl);
+        case JC_EPI_BIAS | RS: return launch_gemm_inst<BN, STAGES, JC_EPI_BIAS | RS, CS, BM>(p, grid, s, pdl);
+        case LB: return launch_gemm_inst<BN, STAGES, LB, CS, BM>(p, grid, s, pdl);
+        case LB | JC_EPI_RELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_RELU, CS, BM>(p, grid, s, pdl);
+        case LB | JC_EPI_GELU: return launch_gemm_inst<BN, STAGES, LB | JC_EPI_GELU, CS, BM>(p, grid, s, pdl);
         default: break;
     }
     if constexpr (BN >= 64) {
         switch (epi) {
-            case JC_EPI_ROPE: return launch_gemm_inst<BN, STAGES, JC_EPI_ROPE, CS>(p, grid, s, pdl);
+            case JC_EPI_ROPE: return launch_gemm_inst<BN, STAGES, JC_EPI_ROPE, CS, BM>(p, grid, s, pdl);
             case JC_EPI_LN | JC_EPI_ROPE:
-                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_ROPE, CS>(p, grid, s, pdl);
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_ROPE, CS, BM>(p, grid, s, pdl);
             case JC_EPI_LN | JC_EPI_GEGLU:
-                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_GEGLU, CS>(p, grid, s, pdl);
+                return launch_gemm_inst<BN, STAGES, JC_EPI_LN | JC_EPI_GEGLU, CS, BM>(p, grid, s, pdl);
             default: break;
         }
     }
@@ -247,6 +257,10 @@ static bool launch_gemm_depth(uint32_t epi, const GemmKernelParams &p, dim3 grid
 template <int BN>
 static bool launch_gemm_bn(uint32_t epi, const GemmConfig &cfg, const GemmKernelParams &p,
                            dim3 grid, cudaStream_t s, bool pdl) {
+    if constexpr (BN <= 64) {
+        // 64-row tiles: one deep ring (they are chosen where the grid fits the SMs).
+        if (cfg.bm == 64) return launch_gemm_depth<BN, Depth64<BN>::deep, 1, 64>(epi, p, grid, s, pdl);
+    }
     // Cluster split-K runs with the shallow ring: a cluster's CTAs share the tile's K loop.
     if constexpr (BN >= 64 && BN <= 128) {
         if (cfg.cluster == 2) return launch_gemm_depth<BN, Depth<BN>::shallow, 2>(epi, p, grid, s, pdl);
@@ -307,7 +321,7 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
         if (fn && (reinterpret_cast<uintptr_t>(g.c) & 15) == 0 && (n_out * 2) % 16 == 0) {
             cuuint64_t dims[2] = {n_out, g.m};
             cuuint64_t strides[1] = {(cuuint64_t)n_out * 2};
-            cuuint32_t box[2] = {bw, (cuuint32_t)GEMM_BM};
+            cuuint32_t box[2] = {bw, (cuuint32_t)cfg.bm};
             cuuint32_t es[2] = {1, 1};
             const CUresult r = fn(&kp.map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.c, dims, strides,
                                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -334,14 +348,17 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.k = g.k;
     p.eps = g.eps;
     p.err = g.err;
+    p.prof = g.prof;
+    p.prof_cap = g.prof_cap;
     if (cfg.persistent && (cfg.bn == 128 || cfg.bn == 256) && cfg.splits == 1 && cfg.cluster == 1) {
         const uint32_t tiles = (g.n / cfg.bn) * ((g.m + GEMM_BM - 1) / GEMM_BM);
         const dim3 pgrid(std::min(tiles, std::max(cfg.grid, 1u)));
         kp.p.store_tma = 0;  // direct stores: the epilogue runs under the next tile's main loop
+        kp.p.prof = nullptr;  // no phase stamps (a CTA walks several tiles)
         return cfg.bn == 128 ? launch_gemm_persist<128, 3>(g.epi, kp, pgrid, s, pdl)
                              : launch_gemm_persist<256, 2>(g.epi, kp, pgrid, s, pdl);
     }
-    dim3 grid(g.n / cfg.bn, (g.m + GEMM_BM - 1) / GEMM_BM, cfg.cluster > 1 ? cfg.cluster : cfg.splits);
+    dim3 grid(g.n / cfg.bn, (g.m + cfg.bm - 1) / cfg.bm, cfg.cluster > 1 ? cfg.cluster : cfg.splits);
     switch (cfg.bn) {
         case 32: return launch_gemm_bn<32>(g.epi, cfg, kp, grid, s, pdl);
         case 64: return launch_gemm_bn<64>(g.epi, cfg, kp, grid, s, pdl);
@@ -357,6 +374,9 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     auto fail = [](const char *m) { set_error(std::string("gemm: ") + m); return false; };
     if (cfg.bn != 32 && cfg.bn != 64 && cfg.bn != 128 && cfg.bn != 256)
         return fail("tile width must be 32, 64, 128 or 256");
+    if (cfg.bm != 128 && cfg.bm != 64) return fail("tile height must be 128 or 64");
+    if (cfg.bm == 64 && (cfg.bn > 64 || cfg.splits != 1 || cfg.cluster != 1 || cfg.persistent))
+        return fail("64-row tiles are 32 or 64 columns wide, with no split-K");
     if (g.m == 0) return fail("no rows");
     if (g.k == 0 || g.k % GEMM_BK) return fail("k must be a positive multiple of 64");
     if (g.n == 0 || g.n % cfg.bn) return fail("n must be a multiple of the tile width");
@@ -395,9 +415,27 @@ static bool persistent_width(int bn) {
     return (bn == 128 || bn == 256) && !(persist && persist[0] == '0');
 }
 
+// Tile height policy: 0 (automatic), 128 (always 128 rows) or 64 (64 rows wherever legal, even
+// past one wave); a tuning and test hook (jc_gemm_tile_rows), JC_GEMM_BM sets its start value.
+// The default is 128: in the 293-token forward 64-row tiles measured 652.6 against 646.2 us (the
+// 768-wide GEMMs alone 6.59 / 7.77 against 6.72 / 7.55 us), since a narrow tile's main loop is
+// bound by its chain of K = 16 MMAs, not by its operand bytes.
+static std::atomic<int> g_tile_rows{(int)env_u32_early("JC_GEMM_BM", 128u)};
+void swap_gemm_tile_rows(int *rows) { *rows = g_tile_rows.exchange(*rows); }
+
+// The tile height for a configuration whose width and split are set, under the automatic policy:
+// 64 rows (an M = 64 MMA) when the tile is at most 64 columns wide, unsplit, and the 64-row grid
+// still fits one wave, which halves the activation bytes a CTA ingests (a 768-wide GEMM at 293
+// tokens: 120 CTAs of 64 x 32 instead of 72 of 128 x 32).
+static int pick_bm(uint32_t m, uint32_t n, const GemmConfig &c, int sms) {
+    const int policy = g_tile_rows.load();
+    if (policy == 128 || c.bn > 64 || c.splits != 1 || c.cluster != 1) return 128;
+    const uint64_t ctas64 = (uint64_t)((m + 63) / 64) * (n / c.bn);
+    return policy == 64 || ctas64 <= (uint64_t)sms ? 64 : 128;
+}
+
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     GemmConfig c;
-    const uint32_t tiles_m = (m + GEMM_BM - 1) / GEMM_BM;
     // A CTA's time is a fixed part (set-up, first stage, epilogue, drain: about as long as
     // streaming 256 operand rows) plus its operand stream ((128 + tile width) x k bytes, at what
     // an SM ingests from L2), so a launch takes about waves x (256 + 128 + width): the width with
@@ -409,15 +447,20 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     // 256-column tiles run persistent (gemm_persist.cuh): the fixed part is paid once and each
     // further wave costs about twice its width (measured per extra wave at k = 768: 5.0 us for
     // 128 columns, 9.5 us for 256, against 10.6 / 15.4 us for the first).
+    // The tile height for each width (pick_bm) enters the same way: a 64-row tile streams
+    // 64 + width operand rows.
     c.bn = 32;
     uint64_t best = ~0ull;
     for (int bn : {32, 64, 128, 256}) {
         if (n % bn) continue;
-        const uint64_t ctas = (uint64_t)tiles_m * (n / bn);
+        GemmConfig t;
+        t.bn = bn;
+        const int bm = pick_bm(m, n, t, sms);
+        const uint64_t ctas = (uint64_t)((m + bm - 1) / bm) * (n / bn);
         const uint64_t waves = (ctas + sms - 1) / sms;
-        const uint64_t cost = waves > 1 && persistent_width(bn)
-                                  ? (256 + GEMM_BM + bn) + (waves - 1) * 2 * (uint64_t)bn
-                                  : waves * (uint64_t)(256 + GEMM_BM + bn);
+        const uint64_t cost = waves > 1 && bm == 128 && persistent_width(bn)
+                                  ? (256 + (uint64_t)bm + bn) + (waves - 1) * 2 * (uint64_t)bn
+                                  : waves * (uint64_t)(256 + bm + bn);
         if (cost < best) {
             best = cost;
             c.bn = bn;
@@ -442,13 +485,15 @@ void request_splits(GemmConfig &c, int splits) {
 }
 
 void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
+    c.bm = pick_bm(m, n, c, sms);
     // At most one CTA per SM: the pipeline depth of one CTA bounds the kernel, so go deep.
-    const uint32_t ctas = (m + GEMM_BM - 1) / GEMM_BM * (n / c.bn) * c.splits * c.cluster;
+    const uint32_t ctas = (m + c.bm - 1) / c.bm * (n / c.bn) * c.splits * c.cluster;
     c.deep = ctas <= (uint32_t)sms && c.cluster == 1;
     static const char *force = getenv("JC_GEMM_DEPTH");  // A/B knob: "deep" / "shallow"
     if (force && force[0] == 'd') c.deep = true;
     if (force && force[0] == 's') c.deep = false;
-    c.persistent = ctas > (uint32_t)sms && persistent_width(c.bn) && c.splits == 1 && c.cluster == 1;
+    c.persistent = ctas > (uint32_t)sms && persistent_width(c.bn) && c.splits == 1 && c.cluster == 1 &&
+                   c.bm == 128;
     c.grid = (uint32_t)sms;
 }
 
@@ -540,6 +585,19 @@ static bool launch_attn_tc(const AttnParams &p, uint32_t chunks, cudaStream_t s,
 
 size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32) * heads; }
 
+uint32_t attention_ctas(const AttnArgs &a) {
+    const AttnVariant v = attn_variant(a.n, a.window);
+    const uint32_t qt = v.tc ? (uint32_t)ATC_QT : 16u * (uint32_t)v.qw;
+    return (a.n + qt - 1) / qt * a.heads * a.kv_chunks;
+}
+
+uint32_t gemm_ctas(uint32_t m, uint32_t n, const GemmConfig &cfg) {
+    const uint32_t tiles = (n / cfg.bn) * ((m + cfg.bm - 1) / cfg.bm);
+    if (cfg.persistent && (cfg.bn == 128 || cfg.bn == 256) && cfg.splits == 1 && cfg.cluster == 1)
+        return std::min(tiles, std::max(cfg.grid, 1u));
+    return tiles * (uint32_t)(cfg.cluster > 1 ? cfg.cluster : cfg.splits);
+}
+
 // The dynamic shared memory a launch of `ctas` CTAs (each needing `need` bytes) requests so that
 // an SM holds at most ceil(ctas / SMs) of them. Under programmatic dependent launch a grid's CTAs
 // are placed while the previous kernel still holds most SMs: small CTAs would pack several to
@@ -566,13 +624,19 @@ static bool launch_attn_inst(const AttnParams &p, uint32_t chunks, cudaStream_t 
     static std::atomic<uint64_t> smem_set{0};
     using S = AttnShape<QW, KS>;
     auto kern = attention_kernel<QW, KS>;
-    // Permission for any request spread_smem makes (at most an SM's memory less the reservation).
-    int dev = 0, optin = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (!ensure_smem(kern, std::max(optin, S::SMEM), smem_set)) return false;
+    // Permission for any request spread_smem makes: at most a block's opt-in limit less the
+    // kernel's static shared memory (the error-word slot), which the dynamic request adds to.
+    static const int cap = [kern]() {
+        int dev = 0, optin = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, kern);
+        return optin - (int)fa.sharedSizeBytes;
+    }();
+    if (!ensure_smem(kern, std::max(cap, S::SMEM), smem_set)) return false;
     dim3 grid((p.n + S::QT - 1) / S::QT, p.heads, chunks);
-    const int smem = std::min(spread_smem(S::SMEM, grid.x * grid.y * grid.z), std::max(optin, S::SMEM));
+    const int smem = std::min(spread_smem(S::SMEM, grid.x * grid.y * grid.z), std::max(cap, S::SMEM));
     return launch_ex(kern, grid, dim3(S::THREADS), smem, s, pdl, "attention launch", p);
 }
 
@@ -589,7 +653,8 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         set_error("attention: qkv and o must be 16-byte aligned");
         return false;
     }
-    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg, a.err};
+    AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg, a.err, a.prof,
+                 a.prof_cap};
     const AttnVariant v = attn_variant(a.n, a.window);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     switch (v.qw * 10 + v.ks) {

@@ -33,6 +33,10 @@ struct GemmParams {
     // The error word device-side timeouts are recorded in (an engine's own); nullptr: the
     // module's word (jc_device_error).
     unsigned int *err;
+    // A profiling run's phase stamps: prof_cap 8-word records, one per CTA (nullptr: none; the
+    // single-GEMM kernel only).
+    uint64_t *prof;
+    uint32_t prof_cap;
 };
 
 struct AttnParams {
@@ -45,6 +49,8 @@ struct AttnParams {
     // only its keys; nullptr: one request of n rows.
     const uint2 *seg;
     unsigned int *err;  // error word (nullptr: the module's)
+    uint64_t *prof;     // phase stamps of a profiling run (nullptr: none; standalone launches)
+    uint32_t prof_cap;
 };
 
 // Phase kinds of the persistent kernel.

@@ -152,6 +152,24 @@ def test_gemm_persistent_multi_tile(jc, O, name, n, k, m, bn):
     run_gemm_case(jc, O, name, m, n, k, bn=bn)
 
 
+@pytest.fixture(params=[128, 64])
+def tile_rows(request, jc):
+    """Both GEMM tile heights: 128 rows, and 64 rows (an M = 64 MMA, its rows in the first 16
+    TMEM lanes of each warp quadrant) wherever legal."""
+    old = jc.gemm_tile_rows(request.param)
+    yield request.param
+    jc.gemm_tile_rows(old)
+
+
+@pytest.mark.parametrize("m", [1, 15, 16, 63, 64, 65, 200, 293, 448, 1024])
+def test_gemm_tile_heights(jc, O, tile_rows, m):
+    """Every epilogue at ragged row counts with 128- and 64-row tiles (32- and 64-column tiles;
+    64-row grids past one wave included)."""
+    for name, n, k in GEMM_CASES:
+        for bn in ((64,) if name in ("lnrope", "rope", "lngeglu") else (32, 64)):
+            run_gemm_case(jc, O, name, m, n, k, bn=bn)
+
+
 @pytest.mark.parametrize("bn", [32, 64, 128, 256])
 @pytest.mark.parametrize("splits", [1, 2, 3, 4, 8])
 def test_gemm_tile_and_split_sweep(jc, O, bn, splits):

@@ -21,10 +21,9 @@ pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 FIXTURE = os.path.join(HERE, "golden", "agreement_f32.npz")
-# max |delta| / rms(f32 logits) over all 4000 logits: the f16 path's deviation from the f32 model
-# on these weights is a few percent of the logits' scale at worst (the reference's chained
-# stream bar is 3e-2 per layer, src/check.rs:395-402).
-REL_MAX_F32 = 0.1
+# max |delta| / rms(f32 logits) over all 4000 logits: the f16 path's worst deviation from the f32
+# model on these weights measured 0.8% of the logits' scale on a B200.
+REL_MAX_F32 = 0.03
 
 
 def oracle_cfg(O, c):

@@ -96,8 +96,9 @@ def test_noalloc_matches_oracle_twice(noalloc, epi_name, n, k, splits):
     # the existing entry point, its scratch from the caller
     ref = u16(res) if epi & jc.EPI_RES else torch.zeros(m, n_out, dtype=torch.float16, device="cuda")
     ref_st = torch.zeros(2 * m, device="cuda")
+    bn = 64 if splits < 0 else 0  # a split-K cluster needs 64-column tiles or wider
     jc.gemm(epi, a_d, w_d, ref, res=ref if epi & jc.EPI_RES else None, stats_in=st_d,
-            colsum=cs_d, stats_out=ref_st, rope=rope_d, splits=splits)
+            colsum=cs_d, stats_out=ref_st, rope=rope_d, bn=bn, splits=splits)
     torch.cuda.synchronize()
     ref_h = host_u16(ref)
 
@@ -105,7 +106,7 @@ def test_noalloc_matches_oracle_twice(noalloc, epi_name, n, k, splits):
         got = u16(res) if epi & jc.EPI_RES else torch.full((m, n_out), float("nan"),
                                                           dtype=torch.float16, device="cuda")
         got_st = torch.zeros(2 * m, device="cuda")
-        rc = fn(epi, 0, splits, ptr(a_d), ptr(w_d), ptr(got), ptr(got) if epi & jc.EPI_RES else None,
+        rc = fn(epi, bn, splits, ptr(a_d), ptr(w_d), ptr(got), ptr(got) if epi & jc.EPI_RES else None,
                 ptr(st_d), ptr(cs_d), ptr(got_st), None, 0, m, n, k, 1e-5, ptr(rope_d), None,
                 stream)
         assert rc == 0, lib.jc_last_error()
