@@ -530,8 +530,11 @@ def launch_name(cfg, li):
         e, n, k = li["epi"], li["n"], li["k"]
         D = cfg.d_model
         if li["layer"] >= 0:
-            return {(3 * D, D): "qkv", (D, D): "wo", (2 * cfg.inter, D): "wi",
-                    (D, cfg.inter): "wo_mlp"}.get((n, k), f"gemm {n}x{k}")
+            if e & jc.EPI_ROPE:
+                return "qkv"
+            if e & jc.EPI_GEGLU:
+                return "wi"
+            return {(D, D): "wo", (D, cfg.inter): "wo_mlp"}.get((n, k), f"gemm {n}x{k}")
         if e & jc.EPI_GELU:
             return "scorer lin1"
         return {(3 * D, D): "head in_proj", (D, D): "head out_proj", (cfg.head_ff, D): "head linear1",

@@ -77,7 +77,20 @@ struct GemmShape {
     static constexpr int NCH = BN / CH;           // chunks per tile
     static constexpr int PER = 2 * G * NCH;       // columns per thread
     // stages | barriers (256 B) | row partial sums (1 KB) | column sums and biases (2 x BN floats)
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + 1024 + 8 * BN;
+    // [| cluster split-K receive buffer]
+    static constexpr int TAIL_BYTES = 256 + 1024 + 8 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + TAIL_BYTES;
+    // Cluster split-K over CS CTAs: every CTA receives, from each peer, the partial sums of the
+    // columns it owns (GO of each 32-column half of every chunk) for all 128 rows, row-major with
+    // rows padded by 4 floats (so a warp's 16-byte accesses of consecutive rows spread over the
+    // banks): [CS][NCH][128][RECV_STRIDE] floats (its own rank's slot unused).
+    template <int CS>
+    static constexpr int RECV_STRIDE = 2 * (2 * (CH / (4 * CS))) + 4;
+    template <int CS>
+    static constexpr int RECV_BYTES = CS > 1 ? CS * NCH * 128 * RECV_STRIDE<CS> * 4 : 0;
+    // Bytes a CTA receives: the partials of its columns from every peer.
+    template <int CS>
+    static constexpr uint32_t RECV_TX = CS > 1 ? (uint32_t)((CS - 1) * NCH * 128 * 2 * (2 * (CH / (4 * CS))) * 4) : 0;
     static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
 };
 

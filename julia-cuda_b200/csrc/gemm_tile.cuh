@@ -11,21 +11,24 @@ template <int BN, int STAGES, int BM = GEMM_BM>
 struct GemmSmemView {
     using S = GemmShape<BN, STAGES, BM>;
     uint8_t *stages;
-    uint64_t *full, *empty, *done;
+    uint64_t *full, *empty, *done, *recv_bar;
     uint32_t *tmem_slot, *last_flag;
     float2 *row_part;
     float *cs_s, *bs_s;
+    float *recv;  // cluster split-K partials from the peers (S::RECV_BYTES<CS>, after the tail)
     __device__ explicit GemmSmemView(uint8_t *base) {
         stages = base;
         uint8_t *tail = base + STAGES * S::STAGE_BYTES;
         full = reinterpret_cast<uint64_t *>(tail);
         empty = full + STAGES;
         done = empty + STAGES;
-        tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+        recv_bar = done + 1;
+        tmem_slot = reinterpret_cast<uint32_t *>(recv_bar + 1);
         last_flag = tmem_slot + 1;
         row_part = reinterpret_cast<float2 *>(tail + 256);
         cs_s = reinterpret_cast<float *>(tail + 256 + 1024);
         bs_s = cs_s + BN;
+        recv = reinterpret_cast<float *>(tail + S::TAIL_BYTES);
     }
 };
 
@@ -139,13 +142,6 @@ __device__ __forceinline__ void k_range(uint32_t kb_total, uint32_t z, uint32_t 
     nkb = (z + 1) * kb_total / splits - kb0;
 }
 
-// Barrier across the CTAs of a thread-block cluster (every thread of every CTA); release /
-// acquire so shared-memory writes into peers before it are visible after it.
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                     : "memory");
-}
-
 // The shared::cluster address of local shared address `a` in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t map_to_rank(uint32_t a, uint32_t rank) {
     uint32_t r;
@@ -153,8 +149,40 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t a, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// A barrier across the CTAs of a thread-block cluster (every thread of every CTA) in two halves:
+// arrive (release) early, wait (acquire) when needed.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Four floats into shared memory of another CTA of the cluster (addr, remote_bar: its
+// shared::cluster addresses), asynchronously: the 16 bytes count towards the transaction bytes of
+// that CTA's mbarrier remote_bar.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, float c, float d,
+                                            uint32_t remote_bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+        "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
+        : "memory");
+}
+
+// Cluster split-K set-up (every thread, after gemm_setup): the receive barrier armed for the bytes
+// the peers will send, its initialisation released to the cluster. The matching cluster_wait comes
+// before this CTA's first remote store, so every peer's barrier is armed by then.
+template <int BN, int STAGES, int CS>
+__device__ __forceinline__ void gemm_cluster_setup(const GemmSmemView<BN, STAGES> &sv) {
+    if constexpr (CS > 1) {
+        if (threadIdx.x == 0) {
+            mbar_init(sv.recv_bar, 1);
+            fence_barrier_init();
+            mbar_arrive_expect_tx(sv.recv_bar, GemmShape<BN, STAGES>::template RECV_TX<CS>);
+        }
+        __syncthreads();
+        cluster_arrive();
+    }
 }
 
 // How a tile waits for its inputs (the activations, statistics and residuals a previous step
@@ -312,13 +340,16 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
     }
     const uint32_t lane_base = tmem + ((quarter * 32) << 16);
     bool run_epilogue = mma_ok;
-    float *recv = reinterpret_cast<float *>(sv.stages);  // cluster partials: [CS][NCH][2 GO][128]
+    constexpr int RS = S::template RECV_STRIDE<CS>;
+    const float *recv = sv.recv;
 
     if constexpr (CS > 1) {
-        // Every CTA of the cluster is past its MMAs, so every stage memory is free.
-        cluster_sync_all();
+        // Reduce-scatter through distributed shared memory: each CTA sends every peer the
+        // partials of the columns that peer owns (its own receive buffer, so no peer's operands
+        // are overwritten), completing on the peer's receive barrier, then waits on its own.
+        cluster_wait();  // every peer's receive barrier is armed
         if (mma_ok) {
-            const uint32_t recv_s = smem_u32(recv);
+            const uint32_t recv_s = smem_u32(sv.recv), bar_s = smem_u32(sv.recv_bar);
 #pragma unroll
             for (int ci = 0; ci < NCH; ci++)
 #pragma unroll
@@ -327,16 +358,24 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
                     float t[2 * GT];
                     acc_ld2<GT, S::NI, BN>(lane_base + ci * CH + GO * o + GT * half,
                                            lane_base + ci * CH + HALF + GO * o + GT * half, t);
-                    const uint32_t base = map_to_rank(recv_s, o) +
-                                          (uint32_t)(((rank * NCH + ci) * 2 * GO) * GEMM_BM) * 4u;
+                    const uint32_t dst = map_to_rank(recv_s, o) +
+                                         (uint32_t)((((rank * NCH + ci) * 128 + row) * RS + GT * half) * 4);
+                    const uint32_t rbar = map_to_rank(bar_s, o);
 #pragma unroll
-                    for (int j = 0; j < GT; j++) {
-                        st_cluster_f32(base + ((GT * half + j) * GEMM_BM + row) * 4u, t[j]);
-                        st_cluster_f32(base + ((GO + GT * half + j) * GEMM_BM + row) * 4u, t[GT + j]);
+                    for (int j = 0; j < GT; j += 4) {
+                        st_async_v4(dst + j * 4, t[j], t[j + 1], t[j + 2], t[j + 3], rbar);
+                        st_async_v4(dst + (GO + j) * 4, t[GT + j], t[GT + j + 1], t[GT + j + 2],
+                                    t[GT + j + 3], rbar);
                     }
                 }
         }
-        cluster_sync_all();
+        // Every peer sends whatever happened to this CTA's own MMAs, so the wait always ends (or
+        // gives up, bounded) before the CTA may leave with writes into its memory in flight.
+        const bool got = mbar_wait_sleep(sv.recv_bar, 0, JC_DEV_TIMEOUT_SPLIT);
+        run_epilogue = __syncthreads_and(mma_ok && got) != 0;
+        // This CTA has sent and received everything; the kernel's last wait (gemm_cluster_exit)
+        // keeps every CTA of the cluster resident until all have.
+        cluster_arrive();
     } else if (splits > 1 && mma_ok) {
         float *mine = p.ws + ((size_t)tile * splits + z) * BN * BM;
 #pragma unroll
@@ -389,11 +428,14 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
 #pragma unroll
                         for (int j = 0; j < 2 * GT; j++) v[j] += t[j];
                     } else {
-                        const float *src = recv + (size_t)((zz * NCH + ci) * 2 * GO) * GEMM_BM;
+                        const float *src = recv + ((size_t)(zz * NCH + ci) * 128 + row) * RS + GT * half;
 #pragma unroll
-                        for (int j = 0; j < GT; j++) {
-                            v[j] += src[(GT * half + j) * GEMM_BM + row];
-                            v[GT + j] += src[(GO + GT * half + j) * GEMM_BM + row];
+                        for (int j = 0; j < GT; j += 4) {
+                            const float4 a4 = *reinterpret_cast<const float4 *>(src + j);
+                            const float4 b4 = *reinterpret_cast<const float4 *>(src + GO + j);
+                            v[j] += a4.x; v[j + 1] += a4.y; v[j + 2] += a4.z; v[j + 3] += a4.w;
+                            v[GT + j] += b4.x; v[GT + j + 1] += b4.y; v[GT + j + 2] += b4.z;
+                            v[GT + j + 3] += b4.w;
                         }
                     }
                 }
@@ -482,12 +524,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tma_prefetch_desc(p.map_w);
     }
     const uint32_t tmem = gemm_setup<BN, STAGES, BM>(sv);
+    if constexpr (CS > 1) gemm_cluster_setup<BN, STAGES, CS>(sv);
     GemmRun run;
     gemm_tile<BN, STAGES, EPI, CS, PdlGate, BM>(p, sv, tmem, run, blockIdx.x, blockIdx.y, blockIdx.z,
                                                 gridDim.z, blockIdx.y * gridDim.x + blockIdx.x, 0,
                                                 PdlGate{});
     gemm_zero(p, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
               gridDim.x * gridDim.y * gridDim.z);
+    if constexpr (CS > 1) cluster_wait();  // no CTA leaves while a peer may still write into it
     gemm_teardown<BN, STAGES>(tmem);
     prof_stamp(rec, 5);
 }

@@ -213,15 +213,22 @@ template <> struct Depth<128> { static constexpr int shallow = 2, deep = 3; };
 template <> struct Depth<256> { static constexpr int shallow = 2, deep = 2; };  // 96 KB stages
 // 64-row tiles (one CTA per SM): a stage holds half the activation bytes, so the ring goes deeper
 // and holds a whole 1152-deep K range of a 32-column tile (9 stages would; 8 x 24 KB fit).
+// Cluster split-K: each CTA's K range is 1/CS of the whole, so a short ring holds it (3 stages of a
+// 64-column tile cover K = 768 / 2), beside the receive buffer of the peers' partials.
+template <int BN> struct DepthCluster;
+template <> struct DepthCluster<64> { static constexpr int stages = 3; };
+template <> struct DepthCluster<128> { static constexpr int stages = 2; };
 template <int BN> struct Depth64;
-template <> struct Depth64<32> { static constexpr int deep = 8; };  // 24 KB stages
-template <> struct Depth64<64> { static constexpr int deep = 6; };  // 32 KB stages
+template <> struct Depth64<32> { static constexpr int shallow = 4, deep = 8; };  // 24 KB stages
+template <> struct Depth64<64> { static constexpr int shallow = 3, deep = 6; };  // 32 KB stages
 
 template <int BN, int STAGES, uint32_t EPI, int CS, int BM>
 static bool launch_gemm_inst(const GemmKernelParams &p, dim3 grid, cudaStream_t s, bool pdl) {
     static std::atomic<uint64_t> smem_set{0};
     auto kern = gemm_tc_kernel<BN, STAGES, EPI, CS, BM>;
-    constexpr int smem = GemmShape<BN, STAGES, BM>::SMEM_BYTES;
+    using Sh = GemmShape<BN, STAGES, BM>;
+    constexpr int smem = Sh::SMEM_BYTES + Sh::template RECV_BYTES<CS>;
+    static_assert(smem <= 227 * 1024, "a GEMM CTA's shared memory");
     if (!ensure_smem(kern, smem, smem_set)) return false;
     return launch_ex_cluster(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, CS, "gemm launch", p);
 }
@@ -258,13 +265,14 @@ template <int BN>
 static bool launch_gemm_bn(uint32_t epi, const GemmConfig &cfg, const GemmKernelParams &p,
                            dim3 grid, cudaStream_t s, bool pdl) {
     if constexpr (BN <= 64) {
-        // 64-row tiles: one deep ring (they are chosen where the grid fits the SMs).
-        if (cfg.bm == 64) return launch_gemm_depth<BN, Depth64<BN>::deep, 1, 64>(epi, p, grid, s, pdl);
+        if (cfg.bm == 64)
+            return cfg.deep ? launch_gemm_depth<BN, Depth64<BN>::deep, 1, 64>(epi, p, grid, s, pdl)
+                            : launch_gemm_depth<BN, Depth64<BN>::shallow, 1, 64>(epi, p, grid, s, pdl);
     }
     // Cluster split-K runs with the shallow ring: a cluster's CTAs share the tile's K loop.
     if constexpr (BN >= 64 && BN <= 128) {
-        if (cfg.cluster == 2) return launch_gemm_depth<BN, Depth<BN>::shallow, 2>(epi, p, grid, s, pdl);
-        if (cfg.cluster == 4) return launch_gemm_depth<BN, Depth<BN>::shallow, 4>(epi, p, grid, s, pdl);
+        if (cfg.cluster == 2) return launch_gemm_depth<BN, DepthCluster<BN>::stages, 2>(epi, p, grid, s, pdl);
+        if (cfg.cluster == 4) return launch_gemm_depth<BN, DepthCluster<BN>::stages, 4>(epi, p, grid, s, pdl);
     }
     return cfg.deep ? launch_gemm_depth<BN, Depth<BN>::deep, 1>(epi, p, grid, s, pdl)
                     : launch_gemm_depth<BN, Depth<BN>::shallow, 1>(epi, p, grid, s, pdl);
@@ -434,6 +442,8 @@ static int pick_bm(uint32_t m, uint32_t n, const GemmConfig &c, int sms) {
     return policy == 64 || ctas64 <= (uint64_t)sms ? 64 : 128;
 }
 
+static uint32_t tiles_m_of(uint32_t m) { return (m + GEMM_BM - 1) / GEMM_BM; }
+
 GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     GemmConfig c;
     // A CTA's time is a fixed part (set-up, first stage, epilogue, drain: about as long as
@@ -469,7 +479,17 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     // Split-K (workspace or cluster) measured slower than one CTA per tile for every encoder
     // shape at 72-1024 tokens (the partial exchange costs more than the shorter K loop saves).
     c.splits = 1;
-    (void)k;
+    // A/B knob JC_GEMM_CLUSTER=2|4: one-wave shapes as cluster split-K (64-column tiles, else
+    // 128), each CTA keeping at least two k-blocks.
+    static const uint32_t force_cluster = env_u32_early("JC_GEMM_CLUSTER", 0u);
+    if (force_cluster == 2 || force_cluster == 4)
+        for (int bn : {64, 128})
+            if (n % bn == 0 && (uint64_t)tiles_m_of(m) * (n / bn) * force_cluster <= (uint64_t)sms &&
+                k / GEMM_BK >= 2 * force_cluster) {
+                c.bn = bn;
+                c.cluster = (int)force_cluster;
+                break;
+            }
     set_gemm_depth(c, m, n, sms);
     return c;
 }
