@@ -350,6 +350,49 @@ def sweep_arm(args, rank, local):
     print(json.dumps({"sweep": "clocks", "clocks": clk.summary()}), flush=True)
 
 
+def tile_sweep_arm(args, local):
+    """Every tile width (32 / 64 / 128 / 256 columns, 128-row tiles, no split) of each encoder
+    GEMM (qkv, wo, wi, wo_mlp) at M in {72, 293, 448, 1024} tokens, each timed alone as
+    time_kernels does (a CUDA graph of L2-flushed launches, CUDA events): the measured sweep the
+    tile-width cost model is pinned to (tests/golden/gemm_tile_sweep.json). One JSON line per case.
+    Shapes past one wave of 128- and 256-column tiles run the persistent GEMM, as in production."""
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    from oracle import oracle as O
+    cfg = jc.default_config(max_positions=1024)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    old_rows = jc.gemm_tile_rows(128)
+    try:
+        for n in (72, 293, 448, 1024):
+            torch.manual_seed(n)
+            for name, epi_name, N, K, _ in gemm_shapes(cfg, n)[:4]:
+                epi = jc.EPILOGUES[epi_name]
+                a = torch.randn(n, K, device="cuda").half()
+                w = (torch.randn(N, K, device="cuda") * 0.02).half()
+                n_out = N // 2 if epi & jc.EPI_GEGLU else N
+                c = torch.randn(n, n_out, device="cuda").half()
+                st = torch.rand(2 * n, device="cuda") + 1.0
+                st[1::2] += 800.0
+                cs = torch.randn(N, device="cuda")
+                rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
+                so = torch.zeros(2 * n, device="cuda")
+                for bn in (32, 64, 128, 256):
+                    if N % bn or ((epi & (jc.EPI_ROPE | jc.EPI_GEGLU)) and bn < 64):
+                        continue
+
+                    def launch():
+                        jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st,
+                                colsum=cs, stats_out=so, rope=rope, bn=bn, splits=1)
+                    ms = timed(torch, stream, flush, launch, 30)
+                    print(json.dumps({"tile_sweep": name, "m": n, "n": N, "k": K, "bn": bn,
+                                      "us": round(ms * 1e3, 3)}), flush=True)
+    finally:
+        jc.gemm_tile_rows(old_rows)
+    assert jc.device_error() == 0
+
+
 def one_kernel_arm(args, local):
     """Launches one kernel of the forward pass (a GEMM shape or an attention mode) at --seq tokens,
     --warmup + --steps times with the inputs of time_kernels, then synchronises: a small, fixed
@@ -729,6 +772,8 @@ def main():
                          "this many requests (0: skip)")
     ap.add_argument("--serving-pack", type=int, default=6144,
                     help="headline: the config-3 pass's pack size in tokens (0: unpacked)")
+    ap.add_argument("--tile-sweep", action="store_true",
+                    help="every tile width of each encoder GEMM at configs 1's row counts, alone")
     ap.add_argument("--profile", action="store_true",
                     help="per-CTA phase stamps of the per-step kernels: where a forward's time goes")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
@@ -757,6 +802,10 @@ def main():
     if args.profile:
         if rank == 0:
             profile_arm(args, local)
+        return
+    if args.tile_sweep:
+        if rank == 0:
+            tile_sweep_arm(args, local)
         return
 
     import torch

@@ -276,6 +276,14 @@ int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t *a, const u
                     uint32_t k, float eps, const float *rope, const float *bias, void *stream);
 size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
+/* The persistent kernel's plan (the reference's LayerPlan / gemm_plan / phase_cost,
+ * src/forward.rs:738-806, refit to the B200): the tile width (32 or 64 columns) a GEMM phase of m x
+ * n x k with epilogue `epi` takes on a grid of `grid` CTAs, and the cost model behind it, the
+ * phase's time in us (tiles in waves, a tile 0.8 us of first stage and drain, 0.163 us per
+ * 64-deep k-block, 0.70 us of epilogue per 32 columns; -1 for a width that does not divide n).
+ * Host only. */
+int jc_persist_tile(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid);
+double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
 /* The tile height policy of later jc_gemm / jc_gemm_noalloc calls and later-captured engine
  * graphs: 0 automatic (64-row tiles for tiles of at most 64 columns without split-K whose 64-row
  * grid fits one wave, else 128), 128 (always 128 rows, the default) or 64 (64 rows wherever

@@ -128,6 +128,8 @@ def lib():
         "jc_attention_counters": ([u32, u32], sz),
         "jc_attention_tc_min": ([P, P], None),
         "jc_gemm_tile_rows": ([P], None),
+        "jc_persist_tile": ([u32, u32, u32, u32, u32], i32),
+        "jc_gemm_phase_us": ([u32, u32, u32, i32, u32], ctypes.c_double),
         "jc_embed": ([P, u32, P, P, u32, f32, P, P, P], i32),
         "jc_norm_add": ([P, u32, u32, P, P, f32, P, P, P], i32),
         "jc_score": ([P, u32, P, f32, P, u32, P, P], i32),

@@ -715,6 +715,15 @@ size_t jc_attention_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks) {
 
 size_t jc_attention_counters(uint32_t n, uint32_t heads) { return jc::attn_counters(n, heads); }
 
+int jc_persist_tile(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid) {
+    return (int)jc::persist_tile_width(m, n, k, epi, grid ? grid : 1);
+}
+
+double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) {
+    if (bn <= 0 || n % (uint32_t)bn) return -1.0;
+    return jc::gemm_phase_us(m, n, k, bn, grid ? grid : 1);
+}
+
 void jc_gemm_tile_rows(int *rows) {
     if (rows && (*rows == 0 || *rows == 64 || *rows == 128)) jc::swap_gemm_tile_rows(rows);
 }

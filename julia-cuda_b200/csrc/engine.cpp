@@ -711,7 +711,7 @@ bool Engine::barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code) {
         d.r.n = 1;
         d.r.d = (uint32_t)cfg.d_model;
     }
-    const uint32_t total = plan_flow(descs.data(), 2);
+    const uint32_t total = plan_flow(descs.data(), 2, persist_grid);
     descs[0].extra = 1;
     unsigned int before = 0;
     if (!read_device_error(&before, dev_err)) return false;
@@ -738,7 +738,7 @@ void Engine::plan_steps(std::vector<Step> &steps, int mode) const {
         }
         std::vector<PhaseDesc> d(j - i);
         for (size_t t = i; t < j; t++) d[t - i] = steps[t].d;
-        const uint32_t total = plan_flow(d.data(), (uint32_t)(j - i));
+        const uint32_t total = plan_flow(d.data(), (uint32_t)(j - i), persist_grid);
         for (size_t t = i; t < j; t++) {
             steps[t].d = d[t - i];
             steps[t].flow_total = t == i ? total : 0;

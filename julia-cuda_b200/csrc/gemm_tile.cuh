@@ -5,8 +5,11 @@
 
 namespace jc {
 
-// Where a CTA's GEMM pipeline lives in shared memory: STAGES stages, then the barriers, the TMEM
-// base slot, a flag, per-row partial statistics and the tile's column sums / biases.
+// Where a CTA's GEMM pipeline lives in shared memory: STAGES stages, then the tail: the barriers,
+// the TMEM base slot, a flag, per-row partial statistics and the tile's column sums / biases. The
+// tail normally follows the stages; a CTA that runs tiles of two widths (the persistent kernel)
+// places both views' tails at one offset past the larger stage area, their barriers bar_off bytes
+// apart inside it.
 template <int BN, int STAGES, int BM = GEMM_BM>
 struct GemmSmemView {
     using S = GemmShape<BN, STAGES, BM>;
@@ -16,10 +19,11 @@ struct GemmSmemView {
     float2 *row_part;
     float *cs_s, *bs_s;
     float *recv;  // cluster split-K partials from the peers (S::RECV_BYTES<CS>, after the tail)
-    __device__ explicit GemmSmemView(uint8_t *base) {
+    __device__ explicit GemmSmemView(uint8_t *base, uint32_t tail_at = STAGES * S::STAGE_BYTES,
+                                     uint32_t bar_off = 0) {
         stages = base;
-        uint8_t *tail = base + STAGES * S::STAGE_BYTES;
-        full = reinterpret_cast<uint64_t *>(tail);
+        uint8_t *tail = base + tail_at;
+        full = reinterpret_cast<uint64_t *>(tail + bar_off);
         empty = full + STAGES;
         done = empty + STAGES;
         recv_bar = done + 1;
@@ -40,9 +44,9 @@ struct GemmRun {
     uint32_t tiles = 0;
 };
 
-// Barrier initialisation and the TMEM accumulator; every thread calls it, returns the TMEM base.
+// A view's barriers (thread 0; the caller's next CTA barrier publishes them).
 template <int BN, int STAGES, int BM = GEMM_BM>
-__device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES, BM> &sv) {
+__device__ __forceinline__ void gemm_init_barriers(const GemmSmemView<BN, STAGES, BM> &sv) {
     constexpr uint32_t NI = GemmShape<BN, STAGES>::NI;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -52,6 +56,12 @@ __device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES, BM
         mbar_init(sv.done, NI);
         fence_barrier_init();
     }
+}
+
+// Barrier initialisation and the TMEM accumulator; every thread calls it, returns the TMEM base.
+template <int BN, int STAGES, int BM = GEMM_BM>
+__device__ __forceinline__ uint32_t gemm_setup(const GemmSmemView<BN, STAGES, BM> &sv) {
+    gemm_init_barriers<BN, STAGES, BM>(sv);
     if ((threadIdx.x >> 5) == 0) tmem_alloc(sv.tmem_slot, GemmShape<BN, STAGES>::TMEM_COLS);
     tc_fence_before();
     __syncthreads();

@@ -162,10 +162,16 @@ const char *device_error_name(unsigned int code);
 struct PhaseDesc;
 // Resident CTAs of the persistent kernel per SM (0 on error).
 int persist_blocks_per_sm();
-// Fills the dataflow schedule of a launch's phases d[0, n) (rows, items, first item, dependencies
-// on the phases before it in the same launch; PhaseDesc::extra set to 0) and returns the launch's
-// item count. Its GEMM phases run 64-column tiles, so their n is a multiple of 64.
-uint32_t plan_flow(PhaseDesc *d, uint32_t n);
+// Fills the dataflow schedule of a launch's phases d[0, n) on `grid` CTAs (each GEMM phase's tile
+// width, rows, items, first item, dependencies on the phases before it in the same launch;
+// PhaseDesc::extra set to 0) and returns the launch's item count. GEMM phases run 64- or
+// 32-column tiles (persist_tile_width), so their n is a multiple of 32 (64 for RoPE and GeGLU).
+uint32_t plan_flow(PhaseDesc *d, uint32_t n, uint32_t grid);
+// The plan's cost model (us, B200): one 128-row tile of width bn over depth k, a phase of m x n x
+// k on `grid` CTAs, and the persistent kernel's tile width for a GEMM phase.
+double gemm_tile_us(uint32_t k, int bn);
+double gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
+uint32_t persist_tile_width(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid);
 // Counter words a launch of n_phases phases over `blocks` 128-row blocks needs (zeroed once; the
 // kernel leaves them zero).
 inline size_t flow_counter_words(uint32_t n_phases, uint32_t blocks) {

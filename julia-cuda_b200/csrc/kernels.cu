@@ -793,13 +793,43 @@ int persist_blocks_per_sm() {
     return per_sm;
 }
 
-uint32_t plan_flow(PhaseDesc *d, uint32_t n) {
+// The in-forward time (us) of one 128-row GEMM tile of width bn over depth k, as the phase stamps
+// of the per-step kernels measure it on a B200 (profiles/forward_293_phase_stamps.md): first
+// stage and drain 0.8 us, the main loop 0.163 us per 64-deep k-block whatever the tile's width
+// (the chain of K = 16 MMAs its four issuer warps run), the epilogue 0.70 us per 32 columns a
+// row holds. The B200 restatement of the reference's per-task cost (src/forward.rs:783-806:
+// 5 us a task plus 0.35 us a K step on 68 SMs).
+double gemm_tile_us(uint32_t k, int bn) {
+    return 0.8 + 0.163 * (double)((k + GEMM_BK - 1) / GEMM_BK) + 0.70 * (double)bn / 32.0;
+}
+
+// A phase's time on `grid` CTAs: its tiles in waves.
+double gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) {
+    const uint64_t tiles = (uint64_t)((m + GEMM_BM - 1) / GEMM_BM) * (n / (uint32_t)bn);
+    const uint64_t waves = (tiles + grid - 1) / std::max(grid, 1u);
+    return (double)waves * gemm_tile_us(k, bn);
+}
+
+// The persistent kernel's tile width for a GEMM phase (the B200 counterpart of the reference's
+// gemm_plan, src/forward.rs:761-769): 64 or 32 columns, whichever phase_us finds cheaper on the
+// launch's grid (ties to 64); RoPE and GeGLU keep 64 (their column pairs span a 64-wide chunk).
+uint32_t persist_tile_width(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid) {
+    if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) || n % PERSIST_BN_NARROW) return PERSIST_BN;
+    if (n % PERSIST_BN) return PERSIST_BN_NARROW;
+    return gemm_phase_us(m, n, k, PERSIST_BN_NARROW, grid) < gemm_phase_us(m, n, k, PERSIST_BN, grid)
+               ? PERSIST_BN_NARROW
+               : PERSIST_BN;
+}
+
+uint32_t plan_flow(PhaseDesc *d, uint32_t n, uint32_t grid) {
     uint32_t first = 0;
     for (uint32_t i = 0; i < n; i++) {
         PhaseDesc &p = d[i];
+        p.bn = 0;
         if (p.kind == PH_GEMM) {
             p.rows = p.g.m;
-            p.items = (p.g.m + GEMM_BM - 1) / GEMM_BM * (p.g.n / PERSIST_BN);
+            p.bn = persist_tile_width(p.g.m, p.g.n, p.g.k, p.epi, grid);
+            p.items = (p.g.m + GEMM_BM - 1) / GEMM_BM * (p.g.n / p.bn);
         } else if (p.kind == PH_ATTN) {
             p.rows = p.a.n;
             p.items = (p.a.n + FLOW_CHUNK - 1) / FLOW_CHUNK * p.a.heads;

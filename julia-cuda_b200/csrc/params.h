@@ -97,6 +97,7 @@ constexpr uint32_t FLOW_ROWS = 8;    // rows per item of the row-wise phases (on
 
 struct PhaseDesc {
     uint32_t kind, epi;
+    uint32_t bn;  // GEMM phases: the persistent kernel's tile width (64, or 32), set by plan_flow
     GemmParams g;
     AttnParams a;
     RowParams r;

@@ -29,9 +29,23 @@
 
 namespace jc {
 
+// GEMM phases run 64-column tiles, or 32-column ones where the plan (plan_flow) finds them
+// cheaper: both share the stage memory; each has its own barriers and pipeline position.
 constexpr int PERSIST_BN = 64;
 constexpr int PERSIST_STAGES = 4;
+constexpr int PERSIST_BN_NARROW = 32;
+constexpr int PERSIST_STAGES_NARROW = 4;
 using PersistGemm = GemmShape<PERSIST_BN, PERSIST_STAGES>;
+using PersistGemmNarrow = GemmShape<PERSIST_BN_NARROW, PERSIST_STAGES_NARROW>;
+constexpr uint32_t PERSIST_TAIL = PERSIST_STAGES * PersistGemm::STAGE_BYTES;
+constexpr uint32_t PERSIST_NARROW_BAR_OFF = 128;  // the narrow view's barriers in the shared tail
+static_assert(PERSIST_STAGES_NARROW * PersistGemmNarrow::STAGE_BYTES <= (int)PERSIST_TAIL,
+              "the narrow tiles' stages fit the wide ones' stage memory");
+static_assert(PERSIST_NARROW_BAR_OFF + 8 * (2 * PERSIST_STAGES_NARROW + 3) <= 256 &&
+                  8 * (2 * PERSIST_STAGES + 3) <= (int)PERSIST_NARROW_BAR_OFF,
+              "both views' barriers fit the tail's barrier block");
+static_assert(PersistGemm::NI * PERSIST_BN >= PersistGemmNarrow::NI * PERSIST_BN_NARROW,
+              "the narrow tiles' accumulators fit the TMEM allocated for the wide ones");
 using PersistAttn = AttnShape<2, 4>;
 constexpr int PERSIST_THREADS = 256;
 constexpr int PERSIST_SMEM = PersistGemm::SMEM_BYTES;
@@ -61,7 +75,7 @@ __device__ __forceinline__ uint32_t block_items(const PhaseDesc &d, uint32_t b) 
     const uint32_t r1 = min(r0 + FLOW_BLOCK, d.rows);
     uint32_t c;
     if (d.kind == PH_GEMM)
-        c = d.g.n / PERSIST_BN;
+        c = d.g.n / d.bn;
     else if (d.kind == PH_ATTN)
         c = (r1 - r0 + FLOW_CHUNK - 1) / FLOW_CHUNK * d.a.heads;
     else
@@ -121,18 +135,42 @@ struct FlowGate {
 // One GEMM tile of the current phase. Everything the tile code reads repeatedly is a local value
 // here (parameters copied out of shared memory, the shared-memory view rebuilt from its base, the
 // pipeline position passed in and returned), so it stays in registers across the tile's fences.
-template <uint32_t EPI>
+template <uint32_t EPI, int BN = PERSIST_BN>
 __device__ __noinline__ uint2 flow_gemm_tile(const FlowParams *F, const PhaseDesc *d, uint8_t *base,
                                              uint32_t tmem, uint2 pos, uint32_t tm, uint32_t tn,
                                              uint32_t *ok_s) {
+    constexpr int STAGES = BN == PERSIST_BN ? PERSIST_STAGES : PERSIST_STAGES_NARROW;
     const GemmParams g = d->g;
-    const GemmSmemView<PERSIST_BN, PERSIST_STAGES> sv(base);
+    const GemmSmemView<BN, STAGES> sv(base, PERSIST_TAIL, BN == PERSIST_BN ? 0 : PERSIST_NARROW_BAR_OFF);
     GemmRun run;
     run.it = pos.x;
     run.tiles = pos.y;
     const FlowGate gate{F, d, tm * GEMM_BM, min((tm + 1) * GEMM_BM, d->rows), ok_s};
-    gemm_tile<PERSIST_BN, PERSIST_STAGES, EPI>(g, sv, tmem, run, tn, tm, 0, 1, 0, 0, gate);
+    gemm_tile<BN, STAGES, EPI>(g, sv, tmem, run, tn, tm, 0, 1, 0, 0, gate);
     return make_uint2(run.it, run.tiles);
+}
+
+// A narrow (32-column) tile of the epilogues that allow one (not RoPE or GeGLU, whose pairs span
+// 64 columns). pos: the narrow view's pipeline position.
+__device__ __forceinline__ uint2 flow_gemm_narrow(const FlowParams *F, const PhaseDesc *d, uint8_t *base,
+                                                  uint32_t tmem, uint2 pos, uint32_t tm, uint32_t tn,
+                                                  uint32_t *ok_s) {
+    constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
+    constexpr int NB = PERSIST_BN_NARROW;
+    switch (d->epi) {
+        case RS: return flow_gemm_tile<RS, NB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case JC_EPI_BIAS | RS: return flow_gemm_tile<JC_EPI_BIAS | RS, NB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB: return flow_gemm_tile<LB, NB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB | JC_EPI_RELU: return flow_gemm_tile<LB | JC_EPI_RELU, NB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        case LB | JC_EPI_GELU: return flow_gemm_tile<LB | JC_EPI_GELU, NB>(F, d, base, tmem, pos, tm, tn, ok_s);
+        default:
+            if (threadIdx.x == 0) {
+                dev_fail(JC_DEV_BAD_INDEX);
+                *ok_s = 0u;
+            }
+            __syncthreads();
+            return pos;
+    }
 }
 
 __device__ __forceinline__ uint2 flow_gemm(const FlowParams *F, const PhaseDesc *d, uint8_t *base,
@@ -269,8 +307,11 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
     // The current item's descriptor: read from shared memory, not global memory (the item's code
     // reads its parameters many times, across fences that would force global reloads).
     __shared__ __align__(16) PhaseDesc desc_s;
+    gemm_init_barriers<PERSIST_BN_NARROW, PERSIST_STAGES_NARROW>(
+        GemmSmemView<PERSIST_BN_NARROW, PERSIST_STAGES_NARROW>(base, PERSIST_TAIL, PERSIST_NARROW_BAR_OFF));
     const uint32_t tmem = gemm_setup<PERSIST_BN, PERSIST_STAGES>(GemmSmemView<PERSIST_BN, PERSIST_STAGES>(base));
-    uint2 pos = make_uint2(0, 0);  // the GEMM pipeline's position (GemmRun) across tiles
+    // The two GEMM pipelines' positions (GemmRun) across tiles: 64-column and 32-column tiles.
+    uint2 pos = make_uint2(0, 0), pos_narrow = make_uint2(0, 0);
     pdl_wait();
     pdl_launch_dependents();
     uint32_t *work = F.ctr + F.n_phases * F.blocks;  // then the exit counter, the abort flag
@@ -298,10 +339,13 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
         const uint32_t local = item - d.first_item;
         uint32_t block;
         if (d.kind == PH_GEMM) {
-            const uint32_t tiles_n = d.g.n / PERSIST_BN;
+            const uint32_t tiles_n = d.g.n / d.bn;
             const uint32_t tm = local / tiles_n, tn = local % tiles_n;
             block = tm;
-            pos = flow_gemm(&F, &desc_s, base, tmem, pos, tm, tn, &ok_s);
+            if (d.bn == PERSIST_BN_NARROW)
+                pos_narrow = flow_gemm_narrow(&F, &desc_s, base, tmem, pos_narrow, tm, tn, &ok_s);
+            else
+                pos = flow_gemm(&F, &desc_s, base, tmem, pos, tm, tn, &ok_s);
             // The first tile of a row block clears that block's rows of the statistics buffer a
             // later GEMM adds into (its readers are done: they precede this tile's inputs).
             if (tn == 0 && d.g.zero)
