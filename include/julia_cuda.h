@@ -280,7 +280,8 @@ size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
  * src/forward.rs:738-806, refit to the B200): the tile width (32 or 64 columns) a GEMM phase of m x
  * n x k with epilogue `epi` takes on a grid of `grid` CTAs, and the cost model behind it, the
  * phase's time in us (tiles in waves, a tile 0.8 us of first stage and drain, 0.163 us per
- * 64-deep k-block, 0.70 us of epilogue per 32 columns; -1 for a width that does not divide n).
+ * 64-deep k-block, 0.70 us of epilogue per 32 columns; -1 for a width other than 32, 64, 128 or
+ * 256, or one that does not divide n).
  * Host only. */
 int jc_persist_tile(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid);
 double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);

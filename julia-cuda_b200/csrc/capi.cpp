@@ -720,7 +720,7 @@ int jc_persist_tile(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t g
 }
 
 double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) {
-    if (bn <= 0 || n % (uint32_t)bn) return -1.0;
+    if ((bn != 32 && bn != 64 && bn != 128 && bn != 256) || n % (uint32_t)bn) return -1.0;
     return jc::gemm_phase_us(m, n, k, bn, grid ? grid : 1);
 }
 

@@ -66,4 +66,5 @@ def test_phase_cost_model(jc):
     assert lib.jc_gemm_phase_us(293, 768, 1152, 32, SMS) == pytest.approx(one + 0.163 * 6, rel=1e-9)
     # 1024 rows of 32-column tiles: 8 x 24 = 192 tiles, two waves on 148 CTAs
     assert lib.jc_gemm_phase_us(1024, 768, 768, 32, SMS) == pytest.approx(2 * one, rel=1e-9)
-    assert lib.jc_gemm_phase_us(293, 768, 768, 48, SMS) == -1.0
+    assert lib.jc_gemm_phase_us(293, 768, 768, 48, SMS) == -1.0  # not a tile width
+    assert lib.jc_gemm_phase_us(293, 800, 768, 64, SMS) == -1.0  # does not divide n
