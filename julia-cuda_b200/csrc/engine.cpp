@@ -168,6 +168,28 @@ bool Engine::init(const float *raw, std::string *why) {
         *why = last_error();
         return false;
     }
+    // The persistent kernel's narrow (32-column) phases read their weights in 32-row boxes: every
+    // weight matrix of an epilogue that may run narrow also gets that map (plan_steps picks the
+    // map of the width the plan chose, so a box always matches its stage slot).
+    {
+        std::vector<std::tuple<const void *, uint32_t, uint32_t>> narrow;
+        for (const LayerSpans &ls : P.layers) {
+            narrow.emplace_back(w16 + ls.wo.off, D, D);
+            narrow.emplace_back(w16 + ls.wo_mlp.off, D, I);
+        }
+        for (const HeadSpans &h : P.head) {
+            narrow.emplace_back(w16 + h.in_w.off, 3 * D, D);
+            narrow.emplace_back(w16 + h.out_w.off, D, D);
+            narrow.emplace_back(w16 + h.l1_w.off, F, D);
+            narrow.emplace_back(w16 + h.l2_w.off, D, F);
+        }
+        narrow.emplace_back(w16 + P.s_lin1_w.off, S, D);
+        for (const auto &t : narrow)
+            if (add_map(std::get<0>(t), std::get<1>(t), std::get<2>(t), 32) < 0) {
+                *why = last_error();
+                return false;
+            }
+    }
     for (auto &lm : lmaps)
         if (lm.wqkv < 0 || lm.wo < 0 || lm.wi < 0 || lm.wo_mlp < 0) {
             *why = last_error();
@@ -560,7 +582,7 @@ bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
     }
     std::vector<Step> steps = build_steps(n, k, qtype, tr, mode);
     if (mode != MODE_STEPS) {
-        plan_steps(steps, mode);
+        if (!plan_steps(steps, mode)) return false;
         if (steps.size() > scratch_cap) {
             set_error("engine: too many phases");
             return false;
@@ -597,7 +619,7 @@ bool Engine::launch_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode, cu
         GraphEntry entry;
         std::vector<Step> steps = build_steps(n, k, qtype, Trace{}, mode, packed);
         if (mode != MODE_STEPS) {
-            plan_steps(steps, mode);
+            if (!plan_steps(steps, mode)) return false;
             std::vector<PhaseDesc> descs(steps.size());
             for (size_t i = 0; i < steps.size(); i++) descs[i] = steps[i].d;
             if (!cuda_ok(cudaMalloc(&entry.descs, descs.size() * sizeof(PhaseDesc)), "cudaMalloc") ||
@@ -727,7 +749,7 @@ bool Engine::barrier_timeout_probe(uint64_t timeout_ns, uint32_t *code) {
     return reset_after_error();
 }
 
-void Engine::plan_steps(std::vector<Step> &steps, int mode) const {
+bool Engine::plan_steps(std::vector<Step> &steps, int mode) const {
     size_t i = 0;
     while (i < steps.size()) {
         size_t j = steps.size();
@@ -742,9 +764,20 @@ void Engine::plan_steps(std::vector<Step> &steps, int mode) const {
         for (size_t t = i; t < j; t++) {
             steps[t].d = d[t - i];
             steps[t].flow_total = t == i ? total : 0;
+            PhaseDesc &pd = steps[t].d;
+            if (pd.kind == PH_GEMM) {
+                // The weights' map with boxes as tall as the tile width the plan chose.
+                auto it = map_index.find(std::make_tuple(steps[t].w, pd.g.n, pd.g.k, pd.bn));
+                if (it == map_index.end()) {
+                    set_error("engine: no " + std::to_string(pd.bn) + "-row weight map for a planned phase");
+                    return false;
+                }
+                pd.g.map_w = dmaps + it->second;
+            }
         }
         i = j;
     }
+    return true;
 }
 
 }  // namespace jc

@@ -135,7 +135,9 @@ class Engine {
     const CUtensorMap *wmap(const void *p, uint32_t rows, uint32_t cols, int bn);
     // Fills the persistent kernel's schedule of each launch the mode makes (the whole list, or
     // each encoder layer's steps) and the launches' item counts.
-    void plan_steps(std::vector<Step> &steps, int mode) const;
+    // Each GEMM phase's weights map matches the tile width the plan chose; false (error set) if
+    // the engine holds no such map.
+    bool plan_steps(std::vector<Step> &steps, int mode) const;
     std::vector<Step> build_steps(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
                                   int mode, bool packed = false) const;
     std::vector<Step> build_steps_flat(uint32_t n, uint32_t k, uint32_t qtype, const Trace &tr,
