@@ -393,6 +393,56 @@ def tile_sweep_arm(args, local):
     assert jc.device_error() == 0
 
 
+def persist_sweep_arm(args, local):
+    """The persistent kernel's tile plan against the widths it chooses between: the whole-model
+    (mode 2) and per-layer (mode 1) forward at 72, 293, 448 and 1024 tokens (4 markers), with
+    every phase that allows it at 64 columns, at 32, and as planned (jc_persist_tile_policy 64 /
+    32 / 0), each on a fresh engine (plans are made at a graph's first launch), timed as the
+    headline is (CUDA events around each graph replay, L2 flushed between). The measured sweep the
+    plan is pinned to (tests/golden/persist_tile_sweep.json). One JSON line per case."""
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    cfg = jc.default_config(max_positions=1024)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    logits = torch.zeros(MARKERS, dtype=torch.float32, device="cuda")
+    old = jc.persist_tile_policy(0)
+    try:
+        for policy in (64, 32, 0):
+            jc.persist_tile_policy(policy)
+            eng = jc.Engine.load_random(cfg, SEED, max_length=1024, device=local)
+            try:
+                for n in (72, 293, 448, 1024):
+                    ids, markers = request(0, cfg.vocab, n)
+                    ids_d = torch.from_numpy(ids.view(np.int32)).cuda()
+                    mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
+                    for mode in (1, 2):
+                        for _ in range(max(args.warmup, 3)):
+                            eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=mode,
+                                               stream=stream)
+                        torch.cuda.synchronize()
+                        ms = []
+                        for _ in range(args.steps):
+                            flush.zero_()
+                            e0 = torch.cuda.Event(enable_timing=True)
+                            e1 = torch.cuda.Event(enable_timing=True)
+                            e0.record(stream)
+                            eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=mode,
+                                               stream=stream)
+                            e1.record(stream)
+                            e1.synchronize()
+                            ms.append(e0.elapsed_time(e1))
+                        assert eng.device_error() == 0
+                        print(json.dumps({"persist_sweep": mode, "m": n, "policy": policy,
+                                          "us": round(float(np.median(ms)) * 1e3, 1)}),
+                              flush=True)
+            finally:
+                eng.close()
+    finally:
+        jc.persist_tile_policy(old)
+
+
 def one_kernel_arm(args, local):
     """Launches one kernel of the forward pass (a GEMM shape or an attention mode) at --seq tokens,
     --warmup + --steps times with the inputs of time_kernels, then synchronises: a small, fixed
@@ -774,6 +824,9 @@ def main():
                     help="headline: the config-3 pass's pack size in tokens (0: unpacked)")
     ap.add_argument("--tile-sweep", action="store_true",
                     help="every tile width of each encoder GEMM at configs 1's row counts, alone")
+    ap.add_argument("--persist-sweep", action="store_true",
+                    help="the persistent forward at 64-, 32-column and planned tiles, configs 1's "
+                         "row counts")
     ap.add_argument("--profile", action="store_true",
                     help="per-CTA phase stamps of the per-step kernels: where a forward's time goes")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
@@ -806,6 +859,10 @@ def main():
     if args.tile_sweep:
         if rank == 0:
             tile_sweep_arm(args, local)
+        return
+    if args.persist_sweep:
+        if rank == 0:
+            persist_sweep_arm(args, local)
         return
 
     import torch

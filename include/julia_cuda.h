@@ -278,13 +278,19 @@ size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits)
 size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 /* The persistent kernel's plan (the reference's LayerPlan / gemm_plan / phase_cost,
  * src/forward.rs:738-806, refit to the B200): the tile width (32 or 64 columns) a GEMM phase of m x
- * n x k with epilogue `epi` takes on a grid of `grid` CTAs, and the cost model behind it, the
- * phase's time in us (tiles in waves, a tile 0.8 us of first stage and drain, 0.163 us per
- * 64-deep k-block, 0.70 us of epilogue per 32 columns; -1 for a width other than 32, 64, 128 or
- * 256, or one that does not divide n).
- * Host only. */
+ * n x k with epilogue `epi` takes on a grid of `grid` CTAs, and the cost model behind it:
+ * jc_gemm_phase_us, a launch's time in us (tiles in waves, a tile 0.8 us of first stage and drain,
+ * 0.163 us per 64-deep k-block, 0.70 us of epilogue per 32 columns; the per-step kernels' model),
+ * and jc_persist_phase_us, that plus 0.19 us for each item of a row block (what a persistent phase
+ * pays for its items' reports). Both give -1 for a width they do not take or that does not divide
+ * n. jc_persist_tile_policy sets the persistent kernel's width policy (0 the plan, 32 or 64 for
+ * every phase that allows it) for later-planned launches and returns the previous one in place,
+ * or -1 (and changes nothing) for any other value (a tuning and test hook; JC_PERSIST_BN sets the
+ * starting policy). Host only. */
 int jc_persist_tile(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid);
 double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
+double jc_persist_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
+void jc_persist_tile_policy(int *bn);
 /* The tile height policy of later jc_gemm / jc_gemm_noalloc calls and later-captured engine
  * graphs: 0 automatic (64-row tiles for tiles of at most 64 columns without split-K whose 64-row
  * grid fits one wave, else 128), 128 (always 128 rows, the default) or 64 (64 rows wherever

@@ -130,6 +130,8 @@ def lib():
         "jc_gemm_tile_rows": ([P], None),
         "jc_persist_tile": ([u32, u32, u32, u32, u32], i32),
         "jc_gemm_phase_us": ([u32, u32, u32, i32, u32], ctypes.c_double),
+        "jc_persist_phase_us": ([u32, u32, u32, i32, u32], ctypes.c_double),
+        "jc_persist_tile_policy": ([P], None),
         "jc_embed": ([P, u32, P, P, u32, f32, P, P, P], i32),
         "jc_norm_add": ([P, u32, u32, P, P, f32, P, P, P], i32),
         "jc_score": ([P, u32, P, f32, P, u32, P, P], i32),
@@ -352,6 +354,15 @@ def gemm_tile_rows(rows: int) -> int:
     jc_gemm_tile_rows); returns the previous one."""
     r = ctypes.c_int(rows)
     lib().jc_gemm_tile_rows(ctypes.byref(r))
+    return r.value
+
+
+def persist_tile_policy(bn: int) -> int:
+    """Sets the persistent kernel's tile width policy (0 the plan, 32 or 64;
+    jc_persist_tile_policy) for later-planned launches; returns the previous one (-1: not a
+    policy, nothing changed)."""
+    r = ctypes.c_int(bn)
+    lib().jc_persist_tile_policy(ctypes.byref(r))
     return r.value
 
 

@@ -724,6 +724,19 @@ double jc_gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t gri
     return jc::gemm_phase_us(m, n, k, bn, grid ? grid : 1);
 }
 
+double jc_persist_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) {
+    if ((bn != 32 && bn != 64) || n % (uint32_t)bn) return -1.0;
+    return jc::persist_phase_us(m, n, k, bn, grid ? grid : 1);
+}
+
+void jc_persist_tile_policy(int *bn) {
+    if (!bn) return;
+    if (*bn == 0 || *bn == 32 || *bn == 64)
+        jc::swap_persist_tile_policy(bn);
+    else
+        *bn = -1;  // not a policy: nothing changed
+}
+
 void jc_gemm_tile_rows(int *rows) {
     if (rows && (*rows == 0 || *rows == 64 || *rows == 128)) jc::swap_gemm_tile_rows(rows);
 }

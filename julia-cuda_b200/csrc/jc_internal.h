@@ -171,7 +171,10 @@ uint32_t plan_flow(PhaseDesc *d, uint32_t n, uint32_t grid);
 // k on `grid` CTAs, and the persistent kernel's tile width for a GEMM phase.
 double gemm_tile_us(uint32_t k, int bn);
 double gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
+double persist_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid);
 uint32_t persist_tile_width(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid);
+// The persistent kernel's tile width policy (0 the plan, 64 or 32): sets it, returns the old one.
+void swap_persist_tile_policy(int *bn);
 // Counter words a launch of n_phases phases over `blocks` 128-row blocks needs (zeroed once; the
 // kernel leaves them zero).
 inline size_t flow_counter_words(uint32_t n_phases, uint32_t blocks) {

@@ -810,13 +810,31 @@ double gemm_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) 
     return (double)waves * gemm_tile_us(k, bn);
 }
 
+// A phase of the persistent kernel: phase_us plus what its items cost a row block's completion.
+// Every item of a row block reports to the block's counter and the next phase's items of that
+// block wait for all of them: each item adds about 0.19 us (fitted to the whole-model forward at
+// 293 tokens: 32-column phases for the 768-wide GEMMs measured 1067.8 against 991.7 us with
+// 64-column ones, +1.55 us a phase where the tile time alone predicts -0.70 us, for 12 more items
+// a row block).
+double persist_phase_us(uint32_t m, uint32_t n, uint32_t k, int bn, uint32_t grid) {
+    return gemm_phase_us(m, n, k, bn, grid) + 0.19 * (double)(n / (uint32_t)bn);
+}
+
+// Tile width policy of the persistent kernel: 0 (the plan), 64 or 32 (every phase that allows
+// it); a tuning and test hook (jc_persist_tile_policy), JC_PERSIST_BN sets its start value.
+static std::atomic<int> g_persist_bn{(int)env_u32_early("JC_PERSIST_BN", 0u)};
+void swap_persist_tile_policy(int *bn) { *bn = g_persist_bn.exchange(*bn); }
+
 // The persistent kernel's tile width for a GEMM phase (the B200 counterpart of the reference's
-// gemm_plan, src/forward.rs:761-769): 64 or 32 columns, whichever phase_us finds cheaper on the
-// launch's grid (ties to 64); RoPE and GeGLU keep 64 (their column pairs span a 64-wide chunk).
+// gemm_plan, src/forward.rs:761-769): 64 or 32 columns, whichever persist_phase_us finds cheaper
+// on the launch's grid (ties to 64); RoPE and GeGLU keep 64 (their column pairs span a 64-wide
+// chunk).
 uint32_t persist_tile_width(uint32_t m, uint32_t n, uint32_t k, uint32_t epi, uint32_t grid) {
     if ((epi & (JC_EPI_ROPE | JC_EPI_GEGLU)) || n % PERSIST_BN_NARROW) return PERSIST_BN;
     if (n % PERSIST_BN) return PERSIST_BN_NARROW;
-    return gemm_phase_us(m, n, k, PERSIST_BN_NARROW, grid) < gemm_phase_us(m, n, k, PERSIST_BN, grid)
+    const int policy = g_persist_bn.load();
+    if (policy == PERSIST_BN || policy == PERSIST_BN_NARROW) return (uint32_t)policy;
+    return persist_phase_us(m, n, k, PERSIST_BN_NARROW, grid) < persist_phase_us(m, n, k, PERSIST_BN, grid)
                ? PERSIST_BN_NARROW
                : PERSIST_BN;
 }

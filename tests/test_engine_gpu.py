@@ -296,6 +296,38 @@ def test_persistent_modes(jc, O, small_engine, mode, n, qtype):
     assert np.max(np.abs(graphed - steps)) < 1e-3
 
 
+@pytest.mark.parametrize("policy", [32, 64])
+@pytest.mark.parametrize("mode", [1, 2])
+def test_persistent_tile_widths(jc, O, policy, mode):
+    """Every GEMM phase that allows it at one tile width (jc_persist_tile_policy: 32 or 64
+    columns; RoPE and GeGLU phases stay 64): the persistent kernel against the emulation and the
+    per-step kernels, on a fresh engine (its plans are made under the policy)."""
+    c = small_cfg(jc)
+    raw = O.init_random(oracle_cfg(O, c), 21)
+    old = jc.persist_tile_policy(policy)
+    try:
+        eng = jc.Engine.load_raw(c, raw, max_length=1024)
+        try:
+            for n in (65, 293):
+                rng = np.random.default_rng(n + policy)
+                ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+                markers = np.unique(rng.integers(0, n, 4)).astype(np.uint32)
+                got, tr = device_forward(jc, eng, ids, markers, 0, c.n_layers, c.d_model, mode=mode)
+                emu, tr_emu = O.forward_emu(oracle_cfg(O, c), raw, ids, markers, 0, trace=True)
+                for l in range(c.n_layers):
+                    assert rel_err(tr[l], tr_emu[l]) < 5e-3, f"layer {l} vs emulation"
+                assert np.max(np.abs(got - emu)) < 2e-3
+                graphed = device_forward(jc, eng, ids, markers, 0, c.n_layers, c.d_model,
+                                         trace=False, mode=mode)
+                steps = device_forward(jc, eng, ids, markers, 0, c.n_layers, c.d_model,
+                                       trace=False)
+                assert np.max(np.abs(graphed - steps)) < 1e-3
+        finally:
+            eng.close()
+    finally:
+        assert jc.persist_tile_policy(old) == policy
+
+
 @pytest.mark.parametrize("mode", [1, 2])
 def test_persistent_benchmark_config(jc, O, full_engine, mode):
     c, raw, eng = full_engine

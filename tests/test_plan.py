@@ -1,10 +1,13 @@
-"""The tile plan against measured sweeps (the reference's plan_matches_the_sweeps,
-src/forward.rs:815-823, for the B200): the cost model behind the persistent kernel's per-phase
-tile width (jc_persist_tile / jc_gemm_phase_us) and the per-step kernels' choice (jc_choose_gemm)
-must pick, for every encoder GEMM at BASELINE config 1's row counts on 148 SMs, a width whose
-measured time is within a few percent of the fastest measured width. The measurements are
-committed in tests/golden/gemm_tile_sweep.json (`python bench.py --tile-sweep` on a B200). CPU
-only: the plan is host code."""
+"""The tile plans against measured sweeps (the reference's plan_matches_the_sweeps,
+src/forward.rs:815-823, for the B200), CPU only (the plans are host code):
+
+- the per-step kernels' choice (jc_choose_gemm) must pick, for every encoder GEMM at BASELINE
+  config 1's row counts on 148 SMs, a width whose measured time alone is within 5% of the fastest
+  (tests/golden/gemm_tile_sweep.json, `python bench.py --tile-sweep` on a B200);
+- the persistent kernel's plan (jc_persist_tile over jc_persist_phase_us) must give a whole
+  persistent forward within 3% of the faster of its two forced widths at those row counts, in
+  both persistent modes (tests/golden/persist_tile_sweep.json, `python bench.py --persist-sweep`),
+  and the plan's own width choices must be the ones the sweep's planned runs used."""
 import ctypes
 import json
 import os
@@ -15,6 +18,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 SWEEP = os.path.join(HERE, "golden", "gemm_tile_sweep.json")
 EPI = {"qkv": 20, "wo": 9, "wi": 6, "wo_mlp": 9}
 SMS = 148
+
+
+PERSIST = os.path.join(HERE, "golden", "persist_tile_sweep.json")
 
 
 @pytest.fixture(scope="module")
@@ -31,18 +37,30 @@ def test_sweep_covers_config_1(sweep):
     assert {(g, m) for g, m, _, _ in sweep} == {(g, m) for g in EPI for m in (72, 293, 448, 1024)}
 
 
-def test_persistent_plan_matches_the_sweep(jc, sweep):
-    """The persistent kernel's width (32 or 64 columns) is the faster measured one, or within 5%
-    of it."""
+@pytest.fixture(scope="module")
+def persist_sweep():
+    with open(PERSIST) as f:
+        data = json.load(f)
+    return {(c["mode"], c["m"], c["policy"]): c["us"] for c in data["cases"]}
+
+
+def test_persistent_plan_matches_the_sweep(persist_sweep):
+    """A planned persistent forward is within 3% of the faster forced width, in both modes."""
+    for mode in (1, 2):
+        for m in (72, 293, 448, 1024):
+            t = {p: persist_sweep[(mode, m, p)] for p in (0, 32, 64)}
+            assert t[0] <= 1.03 * min(t[32], t[64]), (mode, m, t)
+
+
+def test_persistent_plan_is_the_swept_one(jc, sweep):
+    """The plan behind the sweep's planned runs: RoPE and GeGLU phases at 64 columns, the
+    768-wide phases at the width persist_phase_us prefers, which at these row counts is 64 (each
+    item of a 32-column phase adds its report to the row block's completion)."""
     lib = jc.lib()
-    for (g, m, n, k), us in sweep.items():
-        widths = {bn: t for bn, t in us.items() if bn in (32, 64)}
-        if len(widths) < 2:
-            assert lib.jc_persist_tile(m, n, k, EPI[g], SMS) == 64
-            continue
-        pick = lib.jc_persist_tile(m, n, k, EPI[g], SMS)
-        best = min(widths.values())
-        assert widths[pick] <= 1.05 * best, (g, m, pick, widths)
+    for (g, m, n, k) in sweep:
+        assert lib.jc_persist_tile(m, n, k, EPI[g], SMS) == 64, (g, m)
+        if g in ("wo", "wo_mlp"):
+            assert lib.jc_persist_phase_us(m, n, k, 64, SMS) < lib.jc_persist_phase_us(m, n, k, 32, SMS)
 
 
 def test_per_step_choice_matches_the_sweep(jc, sweep):
@@ -68,3 +86,22 @@ def test_phase_cost_model(jc):
     assert lib.jc_gemm_phase_us(1024, 768, 768, 32, SMS) == pytest.approx(2 * one, rel=1e-9)
     assert lib.jc_gemm_phase_us(293, 768, 768, 48, SMS) == -1.0  # not a tile width
     assert lib.jc_gemm_phase_us(293, 800, 768, 64, SMS) == -1.0  # does not divide n
+    # a persistent phase adds 0.19 us per item of a row block
+    assert lib.jc_persist_phase_us(293, 768, 768, 32, SMS) == pytest.approx(one + 0.19 * 24, rel=1e-9)
+    assert lib.jc_persist_phase_us(293, 768, 768, 128, SMS) == -1.0  # not a persistent width
+
+
+def test_tile_policy_hook(jc):
+    """jc_persist_tile_policy forces a width where the phase allows it and returns the old policy."""
+    lib = jc.lib()
+    assert jc.persist_tile_policy(32) == 0
+    try:
+        assert lib.jc_persist_tile(293, 768, 768, EPI["wo"], SMS) == 32
+        assert lib.jc_persist_tile(293, 2304, 768, EPI["qkv"], SMS) == 64  # RoPE pairs span 64
+        assert jc.persist_tile_policy(64) == 32
+        assert lib.jc_persist_tile(293, 768, 768, EPI["wo"], SMS) == 64
+        assert jc.persist_tile_policy(48) == -1  # refused: unchanged
+        assert lib.jc_persist_tile(293, 768, 768, EPI["wo"], SMS) == 64
+    finally:
+        jc.persist_tile_policy(0)
+    assert lib.jc_persist_tile(293, 768, 768, EPI["wo"], SMS) == 64
