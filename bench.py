@@ -656,6 +656,9 @@ def profile_arm(args, local):
     mk_d = torch.from_numpy(markers.view(np.int32)).cuda()
     logits = torch.zeros(MARKERS, dtype=torch.float32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    mode = 1 if args.layer_fused else args.mode
+    if mode:
+        return profile_persistent(args, eng, cfg, ids_d, mk_d, logits, flush, mode)
     for _ in range(max(args.warmup, 3)):
         eng.forward_device(ids_d, mk_d, 0, logits)
     rows = {}
@@ -670,7 +673,7 @@ def profile_arm(args, local):
         for li in launches:
             if li["kind"] not in (0, 1):
                 continue
-            r = recs[li["record"]][: min(li["ctas"], 512)].astype(np.int64)
+            r = recs[li["record"]:li["record"] + li["records"]].astype(np.int64)
             r = r[r[:, 0] > 0]
             if not len(r):
                 continue
@@ -713,6 +716,85 @@ def profile_arm(args, local):
                       "stamped_span_us": med(totals),
                       "note": "first GEMM/attention CTA entry to the last one's exit (the embedding "
                               "before and the gather / score after are not stamped)"}), flush=True)
+
+
+def phase_name(cfg, li):
+    """A persistent phase's name: the GEMM / attention launch names, or its row-wise kind."""
+    if li["kind"] in (0, 1):
+        return launch_name(cfg, li)
+    return {2: "embed", 3: "head input", 4: "marker gather", 5: "score", 6: "copy"}[li["kind"]]
+
+
+def profile_persistent(args, eng, cfg, ids_d, mk_d, logits, flush, mode):
+    """profile_arm for the persistent kernel (mode 1: a launch per encoder layer, 2: the whole
+    model): every work item stamps when it was taken, when its inputs were ready (its dependency
+    counters reached), its first stage, accumulator, outputs written and when it was reported.
+    Per phase name (medians over its items, then over its phases and forwards, us): the dependency
+    wait (taken -> inputs ready), first stage, main loop, epilogue, report (outputs written ->
+    reported), the phase's span (first item taken -> last reported) and what it adds to the
+    forward (its last report after the previous phase's). Then the forward's span, the CTAs' busy
+    fraction (item time over grid x span) and the median gap between a CTA's report and its next
+    item being taken (the claim)."""
+    import torch
+    for _ in range(max(args.warmup, 3)):
+        eng.forward_device(ids_d, mk_d, 0, logits, layer_fused=mode)
+    rows, totals, busy, gaps = {}, [], [], []
+    reps = max(1, min(args.steps, 100))
+    for _ in range(reps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        recs, launches = eng.forward_profile(ids_d, mk_d, 0, logits, records_per_launch=512,
+                                             layer_fused=mode)
+        assert eng.device_error() == 0
+        phases = [li for li in launches if li["items"]]
+        prev_end, start, end, item_ns = None, None, None, 0
+        per_cta = {}
+        grid = phases[0]["ctas"]
+        for li in phases:
+            r = recs[li["record"]:li["record"] + li["records"]].astype(np.int64)
+            if not len(r) or (r[:, 0] == 0).any():
+                continue
+            t0, t1 = int(r[:, 0].min()), int(r[:, 5].max())
+            start = t0 if start is None else min(start, t0)
+            end = t1 if end is None else max(end, t1)
+            item_ns += int((r[:, 5] - r[:, 0]).sum())
+            for row in r:
+                per_cta.setdefault((li["launch"], int(row[7])), []).append((int(row[0]), int(row[5])))
+            d = rows.setdefault(phase_name(cfg, li), {k: [] for k in ("dep", "first", "main", "epi",
+                                                                       "report", "span", "added")}
+                                | {"items": li["items"], "tile": li["tile"], "count": 0})
+            d["count"] += 1
+            d["dep"].append(float(np.median(r[:, 1] - r[:, 0])) / 1e3)
+            ok = (r[:, 2] > 0) & (r[:, 3] > 0) & (r[:, 4] > 0)
+            if ok.any():
+                d["first"].append(float(np.median(r[ok, 2] - r[ok, 1])) / 1e3)
+                d["main"].append(float(np.median(r[ok, 3] - r[ok, 2])) / 1e3)
+                d["epi"].append(float(np.median(r[ok, 4] - r[ok, 3])) / 1e3)
+                d["report"].append(float(np.median(r[ok, 5] - r[ok, 4])) / 1e3)
+            d["span"].append((t1 - t0) / 1e3)
+            if prev_end is not None:
+                d["added"].append((t1 - prev_end) / 1e3)
+            prev_end = t1
+        for v in per_cta.values():
+            v.sort()
+            gaps.extend((b[0] - a[1]) / 1e3 for a, b in zip(v, v[1:]))
+        totals.append((end - start) / 1e3)
+        busy.append(item_ns / (grid * (end - start)))
+    eng.close()
+    med = lambda v: float(statistics.median(v)) if v else None  # noqa: E731
+    for name, d in rows.items():
+        print(json.dumps({"profile": name, "mode": mode, "phases_per_forward": d["count"] // reps,
+                          "items": d["items"], "tile_cols": d["tile"] & 0xFFFF,
+                          "dependency_wait_us": med(d["dep"]), "first_stage_us": med(d["first"]),
+                          "main_loop_us": med(d["main"]), "epilogue_us": med(d["epi"]),
+                          "report_us": med(d["report"]), "phase_span_us": med(d["span"]),
+                          "added_to_forward_us": med(d["added"])}), flush=True)
+    print(json.dumps({"profile": "forward", "mode": mode, "tokens": args.seq, "forwards": reps,
+                      "stamped_span_us": med(totals), "cta_busy_fraction": med(busy),
+                      "claim_gap_us": med(gaps),
+                      "note": "first item taken to the last reported, over the persistent launches "
+                              "(mode 1: the per-step edges and head between them not stamped)"}),
+          flush=True)
 
 
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
@@ -828,7 +910,8 @@ def main():
                     help="the persistent forward at 64-, 32-column and planned tiles, configs 1's "
                          "row counts")
     ap.add_argument("--profile", action="store_true",
-                    help="per-CTA phase stamps of the per-step kernels: where a forward's time goes")
+                    help="phase stamps (per CTA of the per-step kernels, per item of the "
+                         "persistent kernel with --mode 1/2): where a forward's time goes")
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
                                       "attn_global", "attn_window"],
                     help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")

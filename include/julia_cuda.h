@@ -172,25 +172,48 @@ typedef struct jc_launch_info {
     int32_t layer;   /* encoder layer, -1 before the encoder, -2 the head and scorer */
     uint32_t ctas;   /* CTAs launched */
     uint32_t tile;   /* GEMM: tile rows << 16 | tile columns */
-    uint32_t record; /* its first phase-stamp record (GEMM and attention launches) */
+    uint32_t record; /* its first phase-stamp record (GEMM and attention launches, persistent
+                        phases) */
+    uint32_t launch;  /* the kernel launch it belongs to (a persistent launch logs one entry per
+                         phase, all with its index) */
+    uint32_t records; /* phase-stamp records it owns, from `record` on: a per-step launch's CTAs
+                         (at most records_per_launch), a persistent phase's items */
+    uint32_t items;   /* a persistent phase's work items (0 for per-step launches) */
 } jc_launch_info;
 
-/* A profiled forward of the per-step kernels (the reference's --time, src/timing.rs and
- * src/profile.rs, with device-side stamps as kernels/src/prof.rs): the forward is captured into a
- * CUDA graph with programmatic dependent launch exactly as julia_cuda_run runs it, every GEMM and
- * attention CTA recording eight 64-bit words into d_prof: [0] entry, [1] inputs ready (the previous
- * kernel done), [2] first operand stage in shared memory (GEMMs) / first tiles loaded (attention),
- * [3] accumulator complete / key loop done, [4] outputs written, [5] exit (%globaltimer ns, 0 where a
- * stage does not apply), [6] the SM, [7] the CTA's index. Launch i writes records [i *
- * records_per_launch, (i + 1) * records_per_launch) (d_prof: that many records for every launch,
- * 8 words each; CTAs past records_per_launch are not recorded). info (info_cap entries) receives
- * each launch's description and *n_launches their count. Waits for the forward. Returns 0 or -1.
- * The stamps cost a few global stores per CTA; a forward without a record array runs none. */
+/* A profiled forward (the reference's --time, src/timing.rs and src/profile.rs, with device-side
+ * stamps as kernels/src/prof.rs). The forward's steps (julia_cuda_launches_per_forward of them in
+ * per-step mode) own records_per_launch records of eight 64-bit words each in d_prof, step s the
+ * records from s * records_per_launch on (d_prof: that many records for every step).
+ *
+ * julia_cuda_forward_profile runs the per-step kernels, captured into a CUDA graph with
+ * programmatic dependent launch exactly as julia_cuda_run runs them; every GEMM and attention CTA
+ * records [0] entry, [1] inputs ready (the previous kernel done), [2] first operand stage in shared
+ * memory (GEMMs) / first tiles loaded (attention), [3] accumulator complete / key loop done, [4]
+ * outputs written, [5] exit (%globaltimer ns, 0 where a stage does not apply), [6] the SM, [7] the
+ * CTA's index (CTAs past records_per_launch are not recorded).
+ *
+ * julia_cuda_forward_profile_mode runs the forward in any mode (layer_fused 0, 1 or 2, as
+ * julia_cuda_run_ex); the persistent kernel (not graphed here) records one record per work item,
+ * in item order from its first step's records on (items past the launch's steps x
+ * records_per_launch are not recorded): [0] item taken, [1] its inputs ready (dependency counters
+ * reached), [2] first operand stage (GEMM tiles) / first tiles loaded (attention), [3] accumulator
+ * complete / key loop done, [4] outputs written, [5] item reported, [6] the SM, [7] the CTA.
+ *
+ * info (info_cap entries) receives each launch's description, a persistent launch's one per
+ * phase, and *n_launches their count. Waits for the forward. Returns 0 or -1. The stamps cost a
+ * few global stores per CTA or item; a forward without a record array runs none. */
 int julia_cuda_forward_profile(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
                                const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
                                float *d_logits, uint64_t *d_prof, uint32_t records_per_launch,
                                jc_launch_info *info, size_t info_cap, size_t *n_launches,
                                void *stream, char *err, size_t err_len);
+int julia_cuda_forward_profile_mode(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                                    const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                                    int layer_fused, float *d_logits, uint64_t *d_prof,
+                                    uint32_t records_per_launch, jc_launch_info *info,
+                                    size_t info_cap, size_t *n_launches, void *stream, char *err,
+                                    size_t err_len);
 
 /* Failure detection: runs the persistent kernel with a grid barrier that waits for one CTA more
  * than the grid has, so every wait must give up after timeout_ns; writes the device error code it

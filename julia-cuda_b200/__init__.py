@@ -44,7 +44,8 @@ class LaunchInfo(ctypes.Structure):
 
     _fields_ = [("kind", ctypes.c_uint32), ("epi", ctypes.c_uint32), ("m", ctypes.c_uint32),
                 ("n", ctypes.c_uint32), ("k", ctypes.c_uint32), ("layer", ctypes.c_int32),
-                ("ctas", ctypes.c_uint32), ("tile", ctypes.c_uint32), ("record", ctypes.c_uint32)]
+                ("ctas", ctypes.c_uint32), ("tile", ctypes.c_uint32), ("record", ctypes.c_uint32),
+                ("launch", ctypes.c_uint32), ("records", ctypes.c_uint32), ("items", ctypes.c_uint32)]
 
 
 LAUNCH_KINDS = {0: "gemm", 1: "attention", 2: "embed", 3: "head input", 4: "gather", 5: "score",
@@ -109,6 +110,8 @@ def lib():
         "julia_cuda_forward_device": ([P, P, u32, P, u32, u32, i32, P, P, P, P, sz], i32),
         "julia_cuda_forward_trace": ([P, P, u32, P, u32, u32, i32, P, P, P, P, P, P, sz], i32),
         "julia_cuda_forward_profile": ([P, P, u32, P, u32, u32, P, P, u32, P, sz, P, P, P, sz], i32),
+        "julia_cuda_forward_profile_mode": ([P, P, u32, P, u32, u32, i32, P, P, u32, P, sz, P, P, P, sz],
+                                            i32),
         "julia_cuda_launches_per_forward": ([P, u32, u32, i32], i32),
         "julia_cuda_set_head_length": ([P, sz], i32),
         "julia_cuda_set_packing": ([P, sz], i32),
@@ -524,25 +527,29 @@ class Engine:
             raise JuliaCudaError(err.value.decode(errors="replace"))
 
     def forward_profile(self, ids, markers, qtype: int, logits, records_per_launch: int = 1024,
-                        stream=None):
-        """A per-step forward with per-CTA phase stamps (julia_cuda_forward_profile). Returns
-        (records uint64 [launches, records_per_launch, 8], list of launch dicts). A record holds
-        %globaltimer ns at entry, inputs ready, first stage, results complete, outputs written,
-        exit (0 where a stage does not apply), then the SM and the CTA index."""
+                        stream=None, layer_fused: int = 0):
+        """A forward with phase stamps (julia_cuda_forward_profile_mode): per CTA for the
+        per-step kernels, per work item for the persistent kernel (layer_fused 1 or 2). Returns
+        (records uint64 [n, 8], list of launch dicts; entry e owns records[e["record"]:
+        e["record"] + e["records"]]). A per-step record holds %globaltimer ns at entry, inputs
+        ready, first stage, results complete, outputs written, exit; an item's at item taken,
+        inputs ready, first stage, results complete, outputs written, reported (0 where a stage
+        does not apply); then the SM and the CTA index."""
         import torch
         cap = 4 * (self.cfg.n_layers + self.cfg.n_head_layers) * 6 + 64
         prof = torch.zeros(cap * records_per_launch * 8, dtype=torch.int64, device=ids.device)
         info = (LaunchInfo * cap)()
         n = ctypes.c_size_t(0)
         err = ctypes.create_string_buffer(1024)
-        rc = lib().julia_cuda_forward_profile(self._h, _t_ptr(ids), ids.numel(), _t_ptr(markers),
-                                              markers.numel(), qtype, _t_ptr(logits),
-                                              _t_ptr(prof), records_per_launch, info, cap,
-                                              ctypes.byref(n), _stream(stream), err, 1024)
+        rc = lib().julia_cuda_forward_profile_mode(self._h, _t_ptr(ids), ids.numel(),
+                                                   _t_ptr(markers), markers.numel(), qtype,
+                                                   int(layer_fused), _t_ptr(logits), _t_ptr(prof),
+                                                   records_per_launch, info, cap, ctypes.byref(n),
+                                                   _stream(stream), err, 1024)
         if rc != 0:
             raise JuliaCudaError(err.value.decode(errors="replace"))
         launches = [{f: getattr(info[i], f) for f, _ in LaunchInfo._fields_} for i in range(n.value)]
-        recs = prof.view(-1, records_per_launch, 8).cpu().numpy().view(np.uint64)
+        recs = prof.view(-1, 8).cpu().numpy().view(np.uint64)
         return recs, launches
 
     def set_packing(self, rows: int) -> None:

@@ -422,9 +422,24 @@ int julia_cuda_forward_profile(JcEngine *engine, const uint32_t *d_ids, uint32_t
                                float *d_logits, uint64_t *d_prof, uint32_t records_per_launch,
                                jc_launch_info *info, size_t info_cap, size_t *n_launches,
                                void *stream, char *err, size_t err_len) {
+    return julia_cuda_forward_profile_mode(engine, d_ids, n, d_markers, n_markers, qtype, 0,
+                                           d_logits, d_prof, records_per_launch, info, info_cap,
+                                           n_launches, stream, err, err_len);
+}
+
+int julia_cuda_forward_profile_mode(JcEngine *engine, const uint32_t *d_ids, uint32_t n,
+                                    const uint32_t *d_markers, uint32_t n_markers, uint32_t qtype,
+                                    int layer_fused, float *d_logits, uint64_t *d_prof,
+                                    uint32_t records_per_launch, jc_launch_info *info,
+                                    size_t info_cap, size_t *n_launches, void *stream, char *err,
+                                    size_t err_len) {
     return guarded(err, err_len, [&]() -> int {
         if (!engine || !d_prof || records_per_launch == 0) {
             report(err, err_len, "profile: null engine or record array");
+            return -1;
+        }
+        if (layer_fused < jc::MODE_STEPS || layer_fused > jc::MODE_MODEL) {
+            report(err, err_len, "profile: no execution mode " + std::to_string(layer_fused));
             return -1;
         }
         jc::Engine *e = engine->e;
@@ -443,12 +458,28 @@ int julia_cuda_forward_profile(JcEngine *engine, const uint32_t *d_ids, uint32_t
             report(err, err_len, jc::last_error());
             return -1;
         }
-        // The forward captured into a CUDA graph (with its programmatic dependent launches) on
-        // the engine's stream, as julia_cuda_run's forwards are, then run on `stream`.
         std::vector<jc_launch_info> log;
         jc::Trace tr;
         tr.prof = d_prof;
         tr.prof_cap = records_per_launch;
+        if (layer_fused != jc::MODE_STEPS) {
+            // Persistent modes run on `stream` directly (their phase list is uploaded per call).
+            e->launch_log = &log;
+            const bool ok = e->enqueue_forward(n, n_markers, qtype, layer_fused, tr, s);
+            e->launch_log = nullptr;
+            if (!ok || (n_markers && !jc::cuda_ok(cudaMemcpyAsync(d_logits, e->logits, n_markers * 4,
+                                                                  cudaMemcpyDeviceToDevice, s),
+                                                  "logits")) ||
+                !jc::cuda_ok(cudaStreamSynchronize(s), "profile")) {
+                report(err, err_len, std::string("profile: ") + jc::last_error());
+                return -1;
+            }
+            if (n_launches) *n_launches = log.size();
+            for (size_t i = 0; info && i < log.size() && i < info_cap; i++) info[i] = log[i];
+            return 0;
+        }
+        // The forward captured into a CUDA graph (with its programmatic dependent launches) on
+        // the engine's stream, as julia_cuda_run's forwards are, then run on `stream`.
         cudaStream_t cap = e->stream;
         if (!jc::cuda_ok(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "begin capture")) {
             report(err, err_len, std::string("profile: ") + jc::last_error());

@@ -44,6 +44,7 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // (%globaltimer ns; 0 where a stage does not apply), [6] the SM, [7] the CTA's linear index.
 __device__ __forceinline__ uint64_t *prof_record(uint64_t *prof, uint32_t cap) {
     if (!prof) return nullptr;
+    if (cap == 0) return prof;  // the persistent kernel's item: prof is the item's own record
     const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
     return cta < cap ? prof + 8 * (size_t)cta : nullptr;
 }

@@ -270,7 +270,8 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, co
     for (size_t i = 0; i < steps.size(); i++) {
         Step &st = steps[i];
         st.slot = (int)i;
-        if (tr.prof && mode == MODE_STEPS) {
+        // Per-step launches stamp per CTA (the persistent kernel stamps per item itself).
+        if (tr.prof && (mode == MODE_STEPS || (mode == MODE_LAYER && st.layer < 0))) {
             uint64_t *rec = tr.prof + (size_t)i * tr.prof_cap * 8;
             if (st.d.kind == PH_GEMM) st.d.g.prof = rec, st.d.g.prof_cap = tr.prof_cap;
             if (st.d.kind == PH_ATTN) st.d.a.prof = rec, st.d.a.prof_cap = tr.prof_cap;
@@ -435,9 +436,14 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
     jc_launch_info info{};
     info.kind = d.kind;
     info.layer = st.layer;
-    info.record = (uint32_t)std::max(st.slot, 0);
+    const uint32_t cap = d.kind == PH_GEMM ? d.g.prof_cap : d.kind == PH_ATTN ? d.a.prof_cap : 0;
+    info.record = (uint32_t)std::max(st.slot, 0) * cap;
     auto logged = [&](bool ok) {
-        if (ok && launch_log) launch_log->push_back(info);
+        if (ok && launch_log) {
+            info.launch = launch_log->empty() ? 0 : launch_log->back().launch + 1;
+            info.records = std::min(info.ctas, cap);
+            launch_log->push_back(info);
+        }
         return ok;
     };
     switch (d.kind) {
@@ -534,26 +540,58 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
     }
 }
 
+void Engine::log_persist(const std::vector<Step> &steps, size_t i, size_t j, uint32_t prof_cap) {
+    if (!launch_log) return;
+    const uint32_t launch = launch_log->empty() ? 0 : launch_log->back().launch + 1;
+    const uint32_t cap = (uint32_t)(j - i) * prof_cap;
+    for (size_t t = i; t < j; t++) {
+        const PhaseDesc &d = steps[t].d;
+        jc_launch_info info{};
+        info.kind = d.kind;
+        info.epi = d.kind == PH_GEMM ? d.epi : 0;
+        if (d.kind == PH_GEMM)
+            info.m = d.g.m, info.n = d.g.n, info.k = d.g.k, info.tile = (uint32_t)FLOW_BLOCK << 16 | d.bn;
+        else if (d.kind == PH_ATTN)
+            info.m = d.a.n, info.n = d.a.heads, info.k = d.a.window;
+        else
+            info.m = d.r.n, info.n = d.r.d;
+        info.layer = steps[t].layer;
+        info.ctas = persist_grid;
+        info.record = (uint32_t)i * prof_cap + d.first_item;
+        info.launch = launch;
+        info.records = d.first_item < cap ? std::min(d.items, cap - d.first_item) : 0;
+        info.items = d.items;
+        launch_log->push_back(info);
+    }
+}
+
 bool Engine::enqueue_steps(const std::vector<Step> &steps, int mode, const PhaseDesc *descs,
-                           uint16_t *d_trace, uint32_t n, cudaStream_t s) {
+                           uint16_t *d_trace, uint32_t n, cudaStream_t s, uint64_t *prof,
+                           uint32_t prof_cap) {
     const uint32_t D = cfg.d_model;
     auto trace_copy = [&](int l) {
         return cuda_ok(cudaMemcpyAsync(d_trace + (size_t)l * n * D, x, (size_t)n * D * 2,
                                        cudaMemcpyDeviceToDevice, s),
                        "trace copy");
     };
-    if (mode == MODE_MODEL)
-        return launch_persist(descs, (uint32_t)steps.size(), steps[0].flow_total, flow_ctr,
-                              flow_blocks, persist_grid, barrier_timeout_ns, s, dev_err);
+    // A persistent launch of steps [i, j): its items' records (profiling runs) start at step i's.
+    auto persist = [&](size_t i, size_t j) {
+        uint64_t *pr = prof ? prof + (size_t)i * prof_cap * 8 : nullptr;
+        if (!launch_persist(descs + i, (uint32_t)(j - i), steps[i].flow_total, flow_ctr, flow_blocks,
+                            persist_grid, barrier_timeout_ns, s, dev_err, pr,
+                            (uint32_t)(j - i) * prof_cap))
+            return false;
+        if (prof) log_persist(steps, i, j, prof_cap);
+        return true;
+    };
+    if (mode == MODE_MODEL) return persist(0, steps.size());
     size_t i = 0;
     while (i < steps.size()) {
         const int layer = steps[i].layer;
         if (mode == MODE_LAYER && layer >= 0) {
             size_t j = i;
             while (j < steps.size() && steps[j].layer == layer) j++;
-            if (!launch_persist(descs + i, (uint32_t)(j - i), steps[i].flow_total, flow_ctr,
-                                flow_blocks, persist_grid, barrier_timeout_ns, s, dev_err))
-                return false;
+            if (!persist(i, j)) return false;
             i = j;
         } else {
             if (!run_step(steps[i], s)) return false;
@@ -595,7 +633,7 @@ bool Engine::enqueue_forward(uint32_t n, uint32_t k, uint32_t qtype, int mode,
             return false;
         // The copy above is from pageable memory, so it is staged before this call returns.
     }
-    return enqueue_steps(steps, mode, scratch_descs, tr.enc, n, s);
+    return enqueue_steps(steps, mode, scratch_descs, tr.enc, n, s, tr.prof, tr.prof_cap);
 }
 
 int Engine::launches_per_forward(uint32_t n, uint32_t k, int mode) const {

@@ -120,7 +120,8 @@ class Engine {
     // The error word copied into h_err (the stream has synchronised since): 0, or the reason.
     bool check_device_error_copy(std::string *why);
     cudaEvent_t ev_start[QUEUE] = {}, ev_end[QUEUE] = {};
-    // While set, every per-step launch appends what it ran (a profiling run's launch list).
+    // While set, every launch appends what it ran, a persistent launch one entry per phase (a
+    // profiling run's launch list).
     std::vector<jc_launch_info> *launch_log = nullptr;
 
    private:
@@ -147,8 +148,13 @@ class Engine {
                    const float *colsum, float *stats_out, float *zero, uint32_t zero_len,
                    const float *rope, const float *bias, float eps, int layer) const;
     bool run_step(const Step &st, cudaStream_t s);
+    // prof / prof_cap: a profiling run's records (prof_cap per step; a persistent launch of steps
+    // [i, j) records its items in the (j - i) x prof_cap records from step i's).
     bool enqueue_steps(const std::vector<Step> &steps, int mode, const PhaseDesc *descs,
-                       uint16_t *d_trace, uint32_t n, cudaStream_t s);
+                       uint16_t *d_trace, uint32_t n, cudaStream_t s, uint64_t *prof = nullptr,
+                       uint32_t prof_cap = 0);
+    // A profiling run: appends one entry per phase of a persistent launch of steps [i, j).
+    void log_persist(const std::vector<Step> &steps, size_t i, size_t j, uint32_t prof_cap);
     // After a device error: clears the error word and every counter a wait that gave up may have
     // left non-zero (synchronous).
     bool reset_after_error();

@@ -184,6 +184,6 @@ inline size_t flow_counter_words(uint32_t n_phases, uint32_t blocks) {
 // err: the error word a timeout is recorded in (nullptr: the module's).
 bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
                     uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s,
-                    unsigned int *err);
+                    unsigned int *err, uint64_t *prof = nullptr, uint32_t prof_cap = 0);
 
 }  // namespace jc

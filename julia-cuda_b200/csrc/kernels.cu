@@ -882,10 +882,10 @@ uint32_t plan_flow(PhaseDesc *d, uint32_t n, uint32_t grid) {
 
 bool launch_persist(const PhaseDesc *phases, uint32_t n_phases, uint32_t total_items, uint32_t *ctr,
                     uint32_t blocks, uint32_t grid, uint64_t timeout_ns, cudaStream_t s,
-                    unsigned int *err) {
+                    unsigned int *err, uint64_t *prof, uint32_t prof_cap) {
     static std::atomic<uint64_t> smem_set{0};
     if (!ensure_smem(persist_kernel, PERSIST_SMEM, smem_set)) return false;
-    FlowParams P{phases, n_phases, total_items, blocks, ctr, timeout_ns, err};
+    FlowParams P{phases, n_phases, total_items, blocks, ctr, timeout_ns, err, prof, prof ? prof_cap : 0u};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(PERSIST_THREADS);

@@ -120,6 +120,10 @@ struct FlowParams {
     uint32_t *ctr;
     uint64_t timeout_ns;
     unsigned int *err;  // error word (nullptr: the module's)
+    // A profiling run's phase stamps: record i (8 words) for the launch's item i < prof_cap
+    // (nullptr: none).
+    uint64_t *prof;
+    uint32_t prof_cap;
 };
 
 }  // namespace jc

@@ -121,6 +121,11 @@ __device__ __forceinline__ bool wait_item(const FlowParams &F, const PhaseDesc &
     return ok;
 }
 
+// A profiling run's record of the launch's item `item` (nullptr: none).
+__device__ __forceinline__ uint64_t *item_record(const FlowParams *F, uint32_t item) {
+    return F->prof && item < F->prof_cap ? F->prof + 8 * (size_t)item : nullptr;
+}
+
 // gemm_tile's gate in the persistent kernel: the TMA thread waits for the tile's row block; the
 // other threads wait for it at a CTA barrier.
 struct FlowGate {
@@ -140,7 +145,9 @@ __device__ __noinline__ uint2 flow_gemm_tile(const FlowParams *F, const PhaseDes
                                              uint32_t tmem, uint2 pos, uint32_t tm, uint32_t tn,
                                              uint32_t *ok_s) {
     constexpr int STAGES = BN == PERSIST_BN ? PERSIST_STAGES : PERSIST_STAGES_NARROW;
-    const GemmParams g = d->g;
+    GemmParams g = d->g;
+    g.prof = item_record(F, d->first_item + tm * (g.n / BN) + tn);
+    g.prof_cap = 0;
     const GemmSmemView<BN, STAGES> sv(base, PERSIST_TAIL, BN == PERSIST_BN ? 0 : PERSIST_NARROW_BAR_OFF);
     GemmRun run;
     run.it = pos.x;
@@ -198,8 +205,11 @@ __device__ __forceinline__ uint2 flow_gemm(const FlowParams *F, const PhaseDesc 
 }
 
 // One attention task of the current phase, its parameters as local values.
-__device__ __noinline__ void flow_attention(const PhaseDesc *d, uint8_t *base, uint32_t chunk, uint32_t head) {
-    const AttnParams a = d->a;
+__device__ __noinline__ void flow_attention(const PhaseDesc *d, uint8_t *base, uint32_t chunk,
+                                            uint32_t head, uint64_t *rec) {
+    AttnParams a = d->a;
+    a.prof = rec;
+    a.prof_cap = 0;
     attention_task<2, 4>(a, base, chunk, head, 0, 1, false);
 }
 
@@ -319,7 +329,18 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
     if (threadIdx.x == 0) next = atomicAdd(work, 1u);
     uint32_t ph = 0, desc_ph = 0;
     for (uint32_t iter = 0;; iter++) {
-        if (threadIdx.x == 0) item_s[iter & 1] = next;
+        if (threadIdx.x == 0) {
+            item_s[iter & 1] = next;
+            // Profiling runs: the item's record is opened before any thread of the CTA stamps it.
+            if (uint64_t *rec = next < F.total_items ? item_record(&F, next) : nullptr) {
+                uint32_t sm;
+                asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+                rec[0] = globaltimer();
+                rec[1] = rec[2] = rec[3] = rec[4] = rec[5] = 0;
+                rec[6] = sm;
+                rec[7] = blockIdx.x;
+            }
+        }
         __syncthreads();
         const uint32_t item = item_s[iter & 1];
         if (item >= F.total_items) break;
@@ -357,11 +378,15 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
             const uint32_t chunk = d.kind == PH_ATTN ? local / d.a.heads : local;
             block = chunk * rows / FLOW_BLOCK;
             const uint32_t r0 = chunk * rows, r1 = min(r0 + rows, d.rows);
-            if (threadIdx.x == 0) ok_s = wait_item(F, d, r0, r1) ? 1u : 0u;
+            uint64_t *rec = threadIdx.x == 0 ? item_record(&F, item) : nullptr;
+            if (threadIdx.x == 0) {
+                ok_s = wait_item(F, d, r0, r1) ? 1u : 0u;
+                prof_stamp(rec, 1);
+            }
             __syncthreads();
             if (ok_s) {
                 if (d.kind == PH_ATTN) {
-                    flow_attention(&desc_s, base, chunk, local % d.a.heads);
+                    flow_attention(&desc_s, base, chunk, local % d.a.heads, rec);
                 } else {
                     const uint32_t lane = threadIdx.x & 31;
                     for (uint32_t i = r0 + (threadIdx.x >> 5); i < r1; i += PERSIST_THREADS / 32)
@@ -377,6 +402,7 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
         // could not start on an idle one).
         if (threadIdx.x == 0) {
             red_release_add(F.ctr + ph * F.blocks + block, 1u);
+            prof_stamp(item_record(&F, item), 5);
             next = atomicAdd(work, 1u);
         }
     }

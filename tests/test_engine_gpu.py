@@ -464,8 +464,45 @@ def test_profiled_forward_stamps_every_phase(jc, O, small_engine):
     for li in launches:
         if li["kind"] not in (0, 1):
             continue
-        r = recs[li["record"]][:min(li["ctas"], 256)].astype(np.int64)
+        assert li["records"] == min(li["ctas"], 256) and li["launch"] == launches.index(li)
+        r = recs[li["record"]:li["record"] + li["records"]].astype(np.int64)
         assert (r[:, 0] > 0).all() and (r[:, 6] < sms).all()
         assert np.array_equal(r[:, 7], np.arange(len(r)))
         if li["kind"] == 0:
             assert (np.diff(r[:, :6], axis=1) >= 0).all(), li
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_profiled_persistent_forward_stamps_every_item(jc, O, small_engine, mode):
+    """julia_cuda_forward_profile_mode with the persistent kernel: the same logits as the plain
+    forward; one entry per phase of every persistent launch (mode 2: one launch, mode 1: one per
+    encoder layer beside the per-step edges and head), each owning all of its items' records; in
+    every item's record the stages in order (taken <= inputs ready <= reported; a GEMM tile's
+    first stage, accumulator and outputs in between) on a valid SM and CTA."""
+    c, raw, eng = small_engine
+    rng = np.random.default_rng(78)
+    n = 293
+    ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+    markers = np.sort(rng.choice(n, 4, replace=False)).astype(np.uint32)
+    plain = device_forward(jc, eng, ids, markers, 0, c.n_layers, c.d_model, trace=False, mode=mode)
+    ids_t = torch.from_numpy(ids.view(np.int32)).cuda()
+    mk_t = torch.from_numpy(markers.view(np.int32)).cuda()
+    logits = torch.zeros(4, dtype=torch.float32, device="cuda")
+    recs, launches = eng.forward_profile(ids_t, mk_t, 0, logits, records_per_launch=256,
+                                         layer_fused=mode)
+    assert eng.device_error() == 0
+    assert np.max(np.abs(logits.cpu().numpy() - plain)) < 1e-3
+    assert len({li["launch"] for li in launches}) == eng.launches_per_forward(n, 4, mode)
+    phases = [li for li in launches if li["items"]]
+    assert len({li["launch"] for li in phases}) == (1 if mode == 2 else c.n_layers)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    gemm_items = 0
+    for li in phases:
+        assert li["records"] == li["items"], li
+        r = recs[li["record"]:li["record"] + li["records"]].astype(np.int64)
+        assert (r[:, 0] > 0).all() and (r[:, 1] >= r[:, 0]).all() and (r[:, 5] >= r[:, 1]).all(), li
+        assert (r[:, 6] < sms).all() and (r[:, 7] < li["ctas"]).all()
+        if li["kind"] == 0:
+            gemm_items += len(r)
+            assert (np.diff(r[:, :6], axis=1) >= 0).all(), li
+    assert gemm_items > 0
