@@ -131,6 +131,7 @@ def lib():
         "jc_attention_counters": ([u32, u32], sz),
         "jc_attention_tc_min": ([P, P], None),
         "jc_gemm_tile_rows": ([P], None),
+        "jc_gemm_pair_policy": ([P], None),
         "jc_persist_tile": ([u32, u32, u32, u32, u32], i32),
         "jc_gemm_phase_us": ([u32, u32, u32, i32, u32], ctypes.c_double),
         "jc_persist_phase_us": ([u32, u32, u32, i32, u32], ctypes.c_double),
@@ -357,6 +358,14 @@ def gemm_tile_rows(rows: int) -> int:
     jc_gemm_tile_rows); returns the previous one."""
     r = ctypes.c_int(rows)
     lib().jc_gemm_tile_rows(ctypes.byref(r))
+    return r.value
+
+
+def gemm_pair_policy(policy: int) -> int:
+    """Sets the CTA-pair GEMM policy (1 every unsplit 128/256-column launch, 0 automatic, -1
+    never; jc_gemm_pair_policy); returns the previous one (-2: not a policy, nothing changed)."""
+    r = ctypes.c_int(policy)
+    lib().jc_gemm_pair_policy(ctypes.byref(r))
     return r.value
 
 

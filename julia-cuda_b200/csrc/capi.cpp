@@ -734,7 +734,7 @@ int jc_gemm(uint32_t epi, int bn, int splits, const uint16_t *a, const uint16_t 
         g.rope = rope;
         g.bias = bias;
         if (!jc::check_gemm(g, cfg) || !jc::make_tmap_f16(&g.map_a, a, m, k, (uint32_t)cfg.bm) ||
-            !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
+            !jc::make_tmap_f16(&g.map_w, w, n, k, jc::gemm_w_rows(cfg)))
             return -1;
         return jc::launch_gemm(g, cfg, (cudaStream_t)stream, true) ? 0 : -1;
     });
@@ -770,6 +770,14 @@ void jc_persist_tile_policy(int *bn) {
 
 void jc_gemm_tile_rows(int *rows) {
     if (rows && (*rows == 0 || *rows == 64 || *rows == 128)) jc::swap_gemm_tile_rows(rows);
+}
+
+void jc_gemm_pair_policy(int *policy) {
+    if (!policy) return;
+    if (*policy >= -1 && *policy <= 1)
+        jc::swap_gemm_pair_policy(policy);
+    else
+        *policy = -2;  // not a policy: nothing changed
 }
 
 void jc_attention_tc_min(uint32_t *global_min, uint32_t *window_min) {

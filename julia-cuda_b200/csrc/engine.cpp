@@ -458,7 +458,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
                 set_error("engine: split-K scratch too small");
                 return false;
             }
-            const CUtensorMap *wm = wmap(st.w, p.n, p.k, c.bn);
+            const CUtensorMap *wm = wmap(st.w, p.n, p.k, (int)gemm_w_rows(c));
             // The A operand in boxes of the tile height (the engine's maps hold 128-row boxes).
             const MapSrc &as = map_src[st.map_a];
             const CUtensorMap *am = c.bm == 128 ? &hmaps[st.map_a] : wmap(as.p, as.rows, as.cols, c.bm);

@@ -8,8 +8,10 @@
 //     accumulator buffers (NI accumulators each, taking the MMAs of a stage round-robin and
 //     summed in issuer order, as in gemm_tile.cuh), a buffer reused once the epilogue has read it;
 //   - warps 4-7 run the epilogue, one tile row per thread, 64 columns at a time (RoPE pairs
-//     (i, i + 32) and GeGLU input / gate pairs stay inside a thread), with direct stores: they are
-//     off the critical path here;
+//     (i, i + 32) and GeGLU input / gate pairs stay inside a thread); residuals come in and
+//     outputs go out through a 4 KB buffer a warp, so 8 lanes move one 128-byte row segment (one
+//     row a lane, as TMEM hands them out, touched 32 cache lines an instruction: the stores alone
+//     cost the 6144-row qkv GEMM a third of its time);
 //   - warp 3 clears the statistics buffer a later GEMM adds into.
 // 128-column tiles use two issuers (two 128-wide accumulators a buffer), 256-column tiles one
 // (a single N = 256 chain already runs at the tensor pipe's rate): 512 TMEM columns either way.
@@ -20,6 +22,16 @@
 
 namespace jc {
 
+// ---- the persistent epilogues' output path ----
+//
+// Each epilogue warp owns 32 tile rows (one a thread, as TMEM hands them out) and a 4 KB
+// shared-memory buffer of 32 rows x 128 bytes, XOR-swizzled in 16-byte chunks (chunk c of row r at
+// c ^ (r & 7): a warp's row-per-lane writes and its line-per-8-lanes reads are both free of bank
+// conflicts). Residuals come in and outputs go out through it with 16-byte accesses whose 8
+// consecutive lanes cover one 128-byte row segment, instead of one row (one cache line) a lane.
+constexpr int PERSIST_EPI_WARP_BYTES = 32 * 128;
+constexpr int PERSIST_EPI_BYTES = 4 * PERSIST_EPI_WARP_BYTES;
+
 template <int BN, int STAGES_>
 struct GemmPersistShape {
     static constexpr int STAGES = STAGES_;
@@ -29,17 +41,78 @@ struct GemmPersistShape {
     static constexpr int W_KB = BN * GEMM_BK * 2;
     static constexpr int A_BYTES = GEMM_KPS * A_KB;
     static constexpr int STAGE_BYTES = A_BYTES + GEMM_KPS * W_KB;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+    // stages | barriers (1 KB) | the epilogue warps' buffers
+    static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 1024;
+    static constexpr int SMEM_BYTES = EPI_OFF + PERSIST_EPI_BYTES;
     static_assert(2 * ACC <= 512, "two accumulator buffers in TMEM");
     static_assert(STAGE_BYTES % 1024 == 0, "stages keep 1024-byte alignment");
 };
 
-// The epilogue of columns [c0, c0 + 64) (tile-local, c0 a multiple of 64) of tile row r, held by
-// one thread: v[64] the accumulator; ropev: (cos, sin) of the row's 32 pairs, two per float4.
+__device__ __forceinline__ uint4 *warp_buf_chunk(uint8_t *buf, uint32_t row, uint32_t c) {
+    return reinterpret_cast<uint4 *>(buf + row * 128 + ((c ^ (row & 7)) << 4));
+}
+
+// Rows [row0, row0 + 32) x columns [col, col + 64) of a row-major f16 matrix (ld columns a row)
+// into registers, 8 x 16 bytes a lane (rows from `m` on read as zero).
+__device__ __forceinline__ void warp_load_rows64(const __half *src, uint32_t ld, uint32_t row0,
+                                                 uint32_t m, uint32_t col, uint32_t lane,
+                                                 uint4 (&regs)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t r = row0 + k * 4 + (lane >> 3);
+        regs[k] = r < m ? *reinterpret_cast<const uint4 *>(src + (size_t)r * ld + col + (lane & 7) * 8)
+                        : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// warp_load_rows64's registers into the buffer, then this lane's own row (lane) out of it as 32
+// packed half2 words.
+__device__ __forceinline__ void warp_rows_to_lane(uint8_t *buf, const uint4 (&regs)[8], uint32_t lane,
+                                                  uint32_t *row_words) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) *warp_buf_chunk(buf, k * 4 + (lane >> 3), lane & 7) = regs[k];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const uint4 t = *warp_buf_chunk(buf, lane, j);
+        row_words[4 * j] = t.x; row_words[4 * j + 1] = t.y; row_words[4 * j + 2] = t.z; row_words[4 * j + 3] = t.w;
+    }
+    __syncwarp();
+}
+
+// This lane's row of W f16 outputs (W / 2 packed words, W = 64 or 32) into the buffer, then the
+// warp's 32 rows to rows [row0, row0 + 32) x columns [col, col + W) of a row-major f16 matrix (ld
+// columns a row; rows from `m` on are not written).
+template <int W>
+__device__ __forceinline__ void warp_store_rows(uint8_t *buf, const uint32_t *row_words, uint32_t lane,
+                                                __half *dst, uint32_t ld, uint32_t row0, uint32_t m,
+                                                uint32_t col) {
+    static_assert(W == 64 || W == 32, "64- or 32-column rows");
+    constexpr int CH = W / 8;  // 16-byte chunks a row
+#pragma unroll
+    for (int j = 0; j < CH; j++)
+        *warp_buf_chunk(buf, lane, j) = make_uint4(row_words[4 * j], row_words[4 * j + 1],
+                                                   row_words[4 * j + 2], row_words[4 * j + 3]);
+    __syncwarp();
+    constexpr int RPI = 32 / CH;  // rows one instruction covers
+#pragma unroll
+    for (int k = 0; k < 32 / RPI; k++) {
+        const uint32_t rr = k * RPI + lane / CH, c = lane % CH, r = row0 + rr;
+        if (r < m) *reinterpret_cast<uint4 *>(dst + (size_t)r * ld + col + c * 8) = *warp_buf_chunk(buf, rr, c);
+    }
+    __syncwarp();
+}
+
+// The epilogue arithmetic of columns [c0, c0 + 64) (tile-local, c0 a multiple of 64) of one tile
+// row, held by one thread: v[64] the accumulator; ropev: (cos, sin) of the row's 32 pairs, two per
+// float4; resw: the residual of those columns (32 packed words, RES epilogues). Writes the output
+// words to `out` (32, or 16 for GeGLU's 32 output columns) and adds the statistics of the stored
+// values to s / q (STATS epilogues).
 template <uint32_t EPI>
-__device__ __forceinline__ void row_chunk_epilogue(const GemmParams &p, float *v, uint32_t r,
-                                                   uint32_t n0, uint32_t c0, float mean, float rstd,
-                                                   const float4 *ropev, float &s, float &q) {
+__device__ __forceinline__ void row_chunk_values(const GemmParams &p, float *v, uint32_t n0,
+                                                 uint32_t c0, float mean, float rstd,
+                                                 const float4 *ropev, const uint32_t *resw,
+                                                 uint32_t *out, float &s, float &q) {
     const uint32_t gc = n0 + c0;
     if constexpr ((EPI & JC_EPI_LN) != 0) {
 #pragma unroll
@@ -73,18 +146,37 @@ __device__ __forceinline__ void row_chunk_epilogue(const GemmParams &p, float *v
     if constexpr ((EPI & JC_EPI_GEGLU) != 0) {
         // Packed columns [gc, gc + 32) are GELU inputs of output columns [gc/2, gc/2 + 32), the
         // next 32 their gates.
-        uint32_t out[16];
 #pragma unroll
         for (int j = 0; j < 16; j++)
             out[j] = pack_half2(gelu_as(v[2 * j]) * v[32 + 2 * j], gelu_as(v[2 * j + 1]) * v[32 + 2 * j + 1]);
-        store_halves<32>(p.c + (size_t)r * (p.n / 2) + gc / 2, out);
     } else {
-        uint32_t resw[32];
-        if constexpr ((EPI & JC_EPI_RES) != 0) load_halves<64>(p.res + (size_t)r * p.n + gc, resw);
-        uint32_t out[32];
         pack_group<64, EPI>(v, resw, out, s, q);
-        store_halves<64>(p.c + (size_t)r * p.n + gc, out);
     }
+}
+
+// The epilogue of one 64-column accumulator chunk of a persistent kernel's tile, by one warp (its
+// 32 rows from row0, this lane's row r valid or not): the residual (RES: staged in `res` by the
+// caller, the warp's registers from warp_load_rows64) through the buffer, the arithmetic, and the
+// outputs through the buffer to c.
+template <uint32_t EPI>
+__device__ __forceinline__ void persist_chunk_epilogue(const GemmParams &p, float *v, uint8_t *buf,
+                                                       const uint4 (&res)[8], uint32_t lane,
+                                                       uint32_t row0, bool valid, uint32_t n0,
+                                                       uint32_t c0, float mean, float rstd,
+                                                       const float4 *ropev, float &s, float &q) {
+    uint32_t resw[32];
+    if constexpr ((EPI & JC_EPI_RES) != 0) warp_rows_to_lane(buf, res, lane, resw);
+    uint32_t out[32];
+    float s1 = 0.f, q1 = 0.f;
+    row_chunk_values<EPI>(p, v, n0, c0, mean, rstd, ropev, resw, out, s1, q1);
+    if (valid) {
+        s += s1;
+        q += q1;
+    }
+    if constexpr ((EPI & JC_EPI_GEGLU) != 0)
+        warp_store_rows<32>(buf, out, lane, p.c, p.n / 2, row0, p.m, (n0 + c0) / 2);
+    else
+        warp_store_rows<64>(buf, out, lane, p.c, p.n, row0, p.m, n0 + c0);
 }
 
 template <int BN, int STAGES, uint32_t EPI>
@@ -201,6 +293,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         pdl_launch_dependents();
         const uint32_t quarter = warp - 4, row = quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((quarter * 32) << 16);
+        uint8_t *wbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_WARP_BYTES;
         for (uint32_t t = blockIdx.x, i = 0; t < total; t += gridDim.x, i++) {
             const uint32_t buf = i & 1;
             const uint32_t m0 = (t / tiles_n) * GEMM_BM, n0 = (t % tiles_n) * BN;
@@ -217,6 +310,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? 16 : 1;
             float4 ropev[ROPE_V];
+#pragma unroll
+            for (int g4 = 0; g4 < ROPE_V; g4++) ropev[g4] = make_float4(0.f, 0.f, 0.f, 0.f);
             if constexpr ((EPI & JC_EPI_ROPE) != 0) {
                 if (valid) {
                     const uint32_t pos = p.seg ? r - p.seg[r].x : r;
@@ -225,6 +320,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     for (int g4 = 0; g4 < 16; g4++) ropev[g4] = __ldg(t4 + (size_t)g4 * p.rope_stride);
                 }
             }
+            // The first chunk's residual rows (coalesced, through this warp's buffer later).
+            const uint32_t row0 = m0 + quarter * 32;
+            uint4 res[8];
+            if constexpr ((EPI & JC_EPI_RES) != 0) warp_load_rows64(p.res, p.n, row0, p.m, n0, lane, res);
             if (!mbar_wait_sleep(&acc_full[buf], (i >> 1) & 1, JC_DEV_TIMEOUT_MMA)) break;
             tc_fence_after();
             float s = 0.f, q = 0.f;
@@ -251,7 +350,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
-                if (valid) row_chunk_epilogue<EPI>(p, v, r, n0, ci * 64, mean, rstd, ropev, s, q);
+                persist_chunk_epilogue<EPI>(p, v, wbuf, res, lane, row0, valid, n0, ci * 64, mean, rstd,
+                                            ropev, s, q);
+                // The next chunk's residual rows.
+                if constexpr ((EPI & JC_EPI_RES) != 0)
+                    if (ci + 1 < (uint32_t)BN / 64) warp_load_rows64(p.res, p.n, row0, p.m, n0 + (ci + 1) * 64, lane, res);
             }
             if constexpr ((EPI & JC_EPI_STATS) != 0) {
                 if (valid) red_add_f32x2(p.stats_out + 2 * (size_t)r, s, q);

@@ -80,7 +80,15 @@ struct GemmConfig {
     // with the epilogue of one under the main loop of the next (gemm_persist.cuh) on `grid` CTAs.
     bool persistent = false;
     uint32_t grid = 0;
+    // CTA pairs (gemm_pair.cuh): 256 x bn tiles, a cluster of two CTAs each holding 128 rows
+    // and half of the weight rows (its W tensor map's box is bn / 2 rows: gemm_w_rows).
+    bool pair = false;
 };
+
+// Rows of the W tensor map's box for a configuration: the tile width, or half of it for pairs.
+inline uint32_t gemm_w_rows(const GemmConfig &c) { return (uint32_t)(c.pair ? c.bn / 2 : c.bn); }
+// CTA-pair policy (1 always where legal, 0 automatic, -1 never): sets it, returns the old one.
+void swap_gemm_pair_policy(int *policy);
 
 // Floats of split-K workspace and counters a launch of this shape needs.
 size_t gemm_ws_floats(uint32_t m, uint32_t n, GemmConfig cfg);

@@ -12,6 +12,7 @@
 #include "attention_tc.cuh"
 #include "edges.cuh"
 #include "gemm.cuh"
+#include "gemm_pair.cuh"
 #include "gemm_persist.cuh"
 #include "jc_internal.h"
 #include "persist.cuh"
@@ -309,6 +310,70 @@ static bool launch_gemm_persist(uint32_t epi, const GemmKernelParams &p, dim3 gr
     return false;
 }
 
+// The CTA-pair kernel (gemm_pair.cuh): clusters of two CTAs along x, as many pairs as the tiles
+// need and the GPU holds at once (cudaOccupancyMaxActiveClusters, cached per device).
+template <int BN, int STAGES>
+static bool launch_gemm_pair(uint32_t epi, const GemmKernelParams &p, uint32_t tiles, cudaStream_t s,
+                             bool pdl) {
+    constexpr uint32_t RS = JC_EPI_RES | JC_EPI_STATS, LB = JC_EPI_LN | JC_EPI_BIAS;
+    constexpr int smem = GemmPairShape<BN, STAGES>::SMEM_BYTES + 1024;
+    auto go = [&](auto kern, std::atomic<uint64_t> &set, std::atomic<int> &max_pairs) {
+        if (!ensure_smem(kern, smem, set)) return false;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (max_pairs.load() <= 0) {
+            int dev = 0, sms = 0, n = 0;
+            if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice") ||
+                !cuda_ok(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "sm count"))
+                return false;
+            cfg.gridDim = dim3(2 * (sms / 2));
+            if (!cuda_ok(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "cluster occupancy")) return false;
+            if (n <= 0) {
+                set_error("gemm: no CTA pair of the pair kernel fits an SM pair");
+                return false;
+            }
+            max_pairs.store(n);
+        }
+        cfg.gridDim = dim3(2 * std::min<uint32_t>(tiles, (uint32_t)max_pairs.load()));
+        if (pdl && pdl_allowed()) {
+            attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[1].val.programmaticStreamSerializationAllowed = 1;
+            cfg.numAttrs = 2;
+        }
+        return cuda_ok(cudaLaunchKernelEx(&cfg, kern, p), "gemm pair launch");
+    };
+#define JC_PAIR(E)                                                      \
+    case E: {                                                           \
+        static std::atomic<uint64_t> set{0};                            \
+        static std::atomic<int> max_pairs{0};                           \
+        return go(gemm_pair_kernel<BN, STAGES, E>, set, max_pairs);     \
+    }
+    switch (epi) {
+        JC_PAIR(0)
+        JC_PAIR(RS)
+        JC_PAIR(JC_EPI_BIAS | RS)
+        JC_PAIR(LB)
+        JC_PAIR(LB | JC_EPI_RELU)
+        JC_PAIR(LB | JC_EPI_GELU)
+        JC_PAIR(JC_EPI_ROPE)
+        JC_PAIR(JC_EPI_LN | JC_EPI_ROPE)
+        JC_PAIR(JC_EPI_LN | JC_EPI_GEGLU)
+        default: break;
+    }
+#undef JC_PAIR
+    set_error("gemm: no compiled pair kernel for epilogue " + std::to_string(epi));
+    return false;
+}
+
 bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     if (!check_gemm(g, cfg)) return false;
     GemmKernelParams kp;
@@ -358,10 +423,17 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.err = g.err;
     p.prof = g.prof;
     p.prof_cap = g.prof_cap;
+    if (cfg.pair) {
+        const uint32_t tiles = (g.n / cfg.bn) * ((g.m + 2 * GEMM_BM - 1) / (2 * GEMM_BM));
+        kp.p.store_tma = 0;  // stores through the epilogue warps' own buffers
+        kp.p.prof = nullptr;  // no phase stamps (a pair walks several tiles)
+        return cfg.bn == 128 ? launch_gemm_pair<128, 4>(g.epi, kp, tiles, s, pdl)
+                             : launch_gemm_pair<256, 3>(g.epi, kp, tiles, s, pdl);
+    }
     if (cfg.persistent && (cfg.bn == 128 || cfg.bn == 256) && cfg.splits == 1 && cfg.cluster == 1) {
         const uint32_t tiles = (g.n / cfg.bn) * ((g.m + GEMM_BM - 1) / GEMM_BM);
         const dim3 pgrid(std::min(tiles, std::max(cfg.grid, 1u)));
-        kp.p.store_tma = 0;  // direct stores: the epilogue runs under the next tile's main loop
+        kp.p.store_tma = 0;  // stores through the epilogue warps' own buffers
         kp.p.prof = nullptr;  // no phase stamps (a CTA walks several tiles)
         return cfg.bn == 128 ? launch_gemm_persist<128, 3>(g.epi, kp, pgrid, s, pdl)
                              : launch_gemm_persist<256, 2>(g.epi, kp, pgrid, s, pdl);
@@ -385,6 +457,8 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
     if (cfg.bm != 128 && cfg.bm != 64) return fail("tile height must be 128 or 64");
     if (cfg.bm == 64 && (cfg.bn > 64 || cfg.splits != 1 || cfg.cluster != 1 || cfg.persistent))
         return fail("64-row tiles are 32 or 64 columns wide, with no split-K");
+    if (cfg.pair && (cfg.bn < 128 || cfg.bm != 128 || cfg.splits != 1 || cfg.cluster != 1))
+        return fail("CTA-pair tiles are 128 or 256 columns wide (128 rows a CTA), with no split-K");
     if (g.m == 0) return fail("no rows");
     if (g.k == 0 || g.k % GEMM_BK) return fail("k must be a positive multiple of 64");
     if (g.n == 0 || g.n % cfg.bn) return fail("n must be a multiple of the tile width");
@@ -421,6 +495,17 @@ bool check_gemm(const GemmArgs &g, GemmConfig cfg) {
 static bool persistent_width(int bn) {
     static const char *persist = getenv("JC_GEMM_PERSIST");
     return (bn == 128 || bn == 256) && !(persist && persist[0] == '0');
+}
+
+// CTA-pair policy (gemm_pair.cuh): 1 (every 128- or 256-column unsplit launch), 0 (automatic:
+// the launches that would run the single-SM persistent kernel), -1 (never); a tuning and test
+// hook (jc_gemm_pair_policy), JC_GEMM_PAIR sets its start value.
+static std::atomic<int> g_pair{(int)env_u32_early("JC_GEMM_PAIR", 0xFFFFFFFFu)};
+void swap_gemm_pair_policy(int *policy) { *policy = g_pair.exchange(*policy); }
+static bool pair_for(const GemmConfig &c) {
+    const int policy = g_pair.load();
+    if (policy < 0 || c.bn < 128 || c.bm != 128 || c.splits != 1 || c.cluster != 1) return false;
+    return policy == 1 || c.persistent;
 }
 
 // Tile height policy: 0 (automatic), 128 (always 128 rows) or 64 (64 rows wherever legal, even
@@ -514,6 +599,7 @@ void set_gemm_depth(GemmConfig &c, uint32_t m, uint32_t n, int sms) {
     if (force && force[0] == 's') c.deep = false;
     c.persistent = ctas > (uint32_t)sms && persistent_width(c.bn) && c.splits == 1 && c.cluster == 1 &&
                    c.bm == 128;
+    c.pair = pair_for(c);
     c.grid = (uint32_t)sms;
 }
 

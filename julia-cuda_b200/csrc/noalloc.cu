@@ -118,7 +118,7 @@ extern "C" int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t 
         g.rope = rope;
         g.bias = bias;
         if (!jc::check_gemm(g, cfg) || !jc::make_tmap_f16(&g.map_a, a, m, k, (uint32_t)cfg.bm) ||
-            !jc::make_tmap_f16(&g.map_w, w, n, k, (uint32_t)cfg.bn))
+            !jc::make_tmap_f16(&g.map_w, w, n, k, jc::gemm_w_rows(cfg)))
             return -1;
         // The counters start every call at zero: a call that stopped early (a device-side
         // timeout) could have left some behind.

@@ -152,6 +152,39 @@ def test_gemm_persistent_multi_tile(jc, O, name, n, k, m, bn):
     run_gemm_case(jc, O, name, m, n, k, bn=bn)
 
 
+@pytest.fixture
+def pairs(jc):
+    """Every unsplit 128- or 256-column launch on CTA pairs (jc_gemm_pair_policy 1)."""
+    old = jc.gemm_pair_policy(1)
+    yield
+    assert jc.gemm_pair_policy(old) == 1
+
+
+PAIR_CASES = [(1, 256), (300, 256), (300, 128), (1000, 128), (3000, 256), (6400, 128)]
+
+
+@pytest.mark.parametrize("name,n,k", GEMM_CASES)
+@pytest.mark.parametrize("m,bn", PAIR_CASES)
+def test_gemm_cta_pairs(jc, O, pairs, name, n, k, m, bn):
+    """The CTA-pair kernel (tcgen05 cta_group::2: 256-row tiles, each SM of a pair holding 128
+    rows and half of the weight tile, the leader issuing every MMA) on every epilogue, at one
+    tile, ragged rows (a pair whose second CTA holds no row), one wave and several tiles a pair."""
+    if n % bn:
+        pytest.skip("the width does not divide n")
+    run_gemm_case(jc, O, name, m, n, k, bn=bn)
+
+
+def test_gemm_pair_policy_hook(jc):
+    """jc_gemm_pair_policy returns the previous policy and refuses other values."""
+    old = jc.gemm_pair_policy(1)
+    try:
+        assert jc.gemm_pair_policy(0) == 1
+        assert jc.gemm_pair_policy(5) == -2
+        assert jc.gemm_pair_policy(-1) == 0
+    finally:
+        jc.gemm_pair_policy(old)
+
+
 @pytest.fixture(params=[128, 64])
 def tile_rows(request, jc):
     """Both GEMM tile heights: 128 rows, and 64 rows (an M = 64 MMA, its rows in the first 16
