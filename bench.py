@@ -352,20 +352,23 @@ def sweep_arm(args, rank, local):
 
 def tile_sweep_arm(args, local):
     """Every tile width (32 / 64 / 128 / 256 columns, 128-row tiles, no split) of each encoder
-    GEMM (qkv, wo, wi, wo_mlp) at M in {72, 293, 448, 1024} tokens, each timed alone as
-    time_kernels does (a CUDA graph of L2-flushed launches, CUDA events): the measured sweep the
-    tile-width cost model is pinned to (tests/golden/gemm_tile_sweep.json). One JSON line per case.
-    Shapes past one wave of 128- and 256-column tiles run the persistent GEMM, as in production."""
+    GEMM (qkv, wo, wi, wo_mlp) at M in {72, 293, 448, 1024} tokens, and for packs of 2048, 3072 and
+    6144 rows the 128- and 256-column tiles on single SMs and on CTA pairs ("pair": true), each
+    timed alone as time_kernels does (a CUDA graph of L2-flushed launches, CUDA events): the
+    measured sweep the tile-width cost model is pinned to (tests/golden/gemm_tile_sweep.json). One
+    JSON line per case. Shapes past one wave of 128- and 256-column tiles run the persistent GEMM,
+    as in production."""
     import torch
     torch.cuda.set_device(local)
     jc = importlib.import_module("julia-cuda_b200")
     from oracle import oracle as O
-    cfg = jc.default_config(max_positions=1024)
+    cfg = jc.default_config(max_positions=6144)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     old_rows = jc.gemm_tile_rows(128)
+    old_pair = jc.gemm_pair_policy(-1)
     try:
-        for n in (72, 293, 448, 1024):
+        for n in (72, 293, 448, 1024, 2048, 3072, 6144):
             torch.manual_seed(n)
             for name, epi_name, N, K, _ in gemm_shapes(cfg, n)[:4]:
                 epi = jc.EPILOGUES[epi_name]
@@ -378,18 +381,26 @@ def tile_sweep_arm(args, local):
                 cs = torch.randn(N, device="cuda")
                 rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
                 so = torch.zeros(2 * n, device="cuda")
-                for bn in (32, 64, 128, 256):
+                cases = ([(bn, False) for bn in (32, 64, 128, 256)] if n <= 1024 else
+                         [(128, False), (256, False), (128, True), (256, True)])
+                for bn, pair in cases:
                     if N % bn or ((epi & (jc.EPI_ROPE | jc.EPI_GEGLU)) and bn < 64):
                         continue
+                    jc.gemm_pair_policy(1 if pair else -1)
 
                     def launch():
                         jc.gemm(epi, a, w, c, res=c if epi & jc.EPI_RES else None, stats_in=st,
                                 colsum=cs, stats_out=so, rope=rope, bn=bn, splits=1)
                     ms = timed(torch, stream, flush, launch, 30)
-                    print(json.dumps({"tile_sweep": name, "m": n, "n": N, "k": K, "bn": bn,
-                                      "us": round(ms * 1e3, 3)}), flush=True)
+                    line = {"tile_sweep": name, "m": n, "n": N, "k": K, "bn": bn,
+                            "us": round(ms * 1e3, 3)}
+                    if n > 1024:
+                        line["pair"] = pair
+                    print(json.dumps(line), flush=True)
+                jc.gemm_pair_policy(-1)
     finally:
         jc.gemm_tile_rows(old_rows)
+        jc.gemm_pair_policy(old_pair)
     assert jc.device_error() == 0
 
 

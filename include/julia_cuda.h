@@ -322,11 +322,11 @@ void jc_persist_tile_policy(int *bn);
 void jc_gemm_tile_rows(int *rows);
 /* The CTA-pair policy of later jc_gemm / jc_gemm_noalloc calls and later-captured engine graphs:
  * 1 runs every unsplit 128- or 256-column launch on CTA pairs (tcgen05 cta_group::2: 256-row
- * tiles, each SM of a pair holding 128 rows and half of the weight tile), 0 the launches that
- * would otherwise run the single-SM persistent kernel (more tiles than SMs), -1 none. Sets
- * *policy and returns the previous one in place; for any other value nothing changes and *policy
- * becomes -2. A tuning and test hook (JC_GEMM_PAIR sets the starting policy). No counterpart in
- * the reference. */
+ * tiles, each SM of a pair holding 128 rows and half of the weight tile), 0 (the default) the
+ * launches that would otherwise run the single-SM persistent kernel with 256-column tiles (more
+ * tiles than SMs: packs of thousands of rows), -1 none. Sets *policy and returns the previous one
+ * in place; for any other value nothing changes and *policy becomes -2. A tuning and test hook
+ * (JC_GEMM_PAIR sets the starting policy). No counterpart in the reference. */
 void jc_gemm_pair_policy(int *policy);
 /* The automatic choice (gemm::choose, src/gemm.rs:153-172, refit for the B200's SMs). */
 int jc_choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms, int *bn, int *splits);

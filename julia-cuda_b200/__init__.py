@@ -362,8 +362,9 @@ def gemm_tile_rows(rows: int) -> int:
 
 
 def gemm_pair_policy(policy: int) -> int:
-    """Sets the CTA-pair GEMM policy (1 every unsplit 128/256-column launch, 0 automatic, -1
-    never; jc_gemm_pair_policy); returns the previous one (-2: not a policy, nothing changed)."""
+    """Sets the CTA-pair GEMM policy (1 every unsplit 128/256-column launch, 0 automatic: the
+    persistent 256-column launches, -1 never; jc_gemm_pair_policy); returns the previous one (-2:
+    not a policy, nothing changed)."""
     r = ctypes.c_int(policy)
     lib().jc_gemm_pair_policy(ctypes.byref(r))
     return r.value

@@ -19,9 +19,9 @@
 //     receives rows 128 r .. 128 r + 127 of the tile, all BN columns, in one of two accumulator
 //     buffers; each stage is released in both CTAs by one tcgen05.commit multicast to both empty
 //     barriers, each finished tile by one commit multicast to both accumulator-full barriers;
-//   - warps 4-7 of each CTA run the epilogue of its 128 rows (persist_chunk_epilogue, as
+//   - warps 4-11 of each CTA run the epilogue of its 128 rows (persist_tile_epilogue, as
 //     gemm_persist.cuh) and report the buffer free on the leader's accumulator-empty barrier
-//     (8 arrivals: 4 warps of each CTA);
+//     (16 arrivals: 8 warps of each CTA);
 //   - warp 3 clears the statistics buffer a later GEMM adds into.
 // TMEM is allocated and freed with cta_group::2 by warp 0 of both CTAs; a cluster barrier after
 // the set-up (barriers initialised before any peer signals them) and one before the teardown
@@ -103,7 +103,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
 }
 
 template <int BN, int STAGES, uint32_t EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(PERSIST_GEMM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ GemmKernelParams kp) {
     dev_err_bind(kp.p.err);
     using S = GemmPairShape<BN, STAGES>;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);   // the leader's commit, multicast
-            mbar_init(&acc_empty[b], 8);  // lane 0 of the 4 epilogue warps of both CTAs
+            mbar_init(&acc_empty[b], 16);  // lane 0 of the 8 epilogue warps of both CTAs
         }
         fence_barrier_init();
     }
@@ -221,74 +221,26 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // This warp alone clears the buffer, striding over every CTA's warp 3.
         for (uint32_t i = blockIdx.x * 32 + lane; i < p.zero_len; i += gridDim.x * 32) p.zero[i] = 0.0f;
     } else if (warp >= 4) {
-        // Epilogue: warp w reads TMEM lanes 32 (w - 4) .. + 31, one tile row per thread.
+        // Epilogue (8 warps) of this CTA's 128 rows of each tile.
         pdl_wait();
         pdl_launch_dependents();
-        const uint32_t quarter = warp - 4, row = quarter * 32 + lane;
+        const uint32_t quarter = warp & 3, half = (warp - 4) >> 2;
         const uint32_t lane_base = tmem + ((quarter * 32) << 16);
         const uint32_t acc_empty0 = map_to_rank(smem_u32(acc_empty), 0);
-        uint8_t *wbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_WARP_BYTES;
+        uint8_t *qbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_QUARTER_BYTES;
         for (uint32_t t = pair, i = 0; t < total; t += pairs, i++) {
             const uint32_t buf = i & 1;
             const uint32_t m0 = (t / tiles_n) * PAIR_M + rank * GEMM_BM, n0 = (t % tiles_n) * BN;
-            const uint32_t r = m0 + row;
-            const bool valid = r < p.m;
-            // What the epilogue reads besides the accumulator, requested before waiting for it.
-            float mean = 0.f, rstd = 0.f;
-            if constexpr ((EPI & JC_EPI_LN) != 0) {
-                if (valid) {
-                    const float2 st = *reinterpret_cast<const float2 *>(p.stats_in + 2 * (size_t)r);
-                    mean = st.x / (float)p.k;
-                    rstd = rsqrtf(fmaxf(st.y / (float)p.k - mean * mean, 0.0f) + p.eps);
-                }
-            }
-            constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? 16 : 1;
-            float4 ropev[ROPE_V];
-#pragma unroll
-            for (int g4 = 0; g4 < ROPE_V; g4++) ropev[g4] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if constexpr ((EPI & JC_EPI_ROPE) != 0) {
-                if (valid) {
-                    const uint32_t pos = p.seg ? r - p.seg[r].x : r;
-                    const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + pos;
-#pragma unroll
-                    for (int g4 = 0; g4 < 16; g4++) ropev[g4] = __ldg(t4 + (size_t)g4 * p.rope_stride);
-                }
-            }
-            // The first chunk's residual rows (coalesced, through this warp's buffer later).
-            const uint32_t row0 = m0 + quarter * 32;
-            uint4 res[8];
-            if constexpr ((EPI & JC_EPI_RES) != 0) warp_load_rows64(p.res, p.n, row0, p.m, n0, lane, res);
-            if (!mbar_wait_sleep(&acc_full[buf], (i >> 1) & 1, JC_DEV_TIMEOUT_MMA)) break;
-            tc_fence_after();
-            float s = 0.f, q = 0.f;
-#pragma unroll 1
-            for (uint32_t ci = 0; ci < (uint32_t)BN / 64; ci++) {
-                float v[64];
-                const uint32_t col = lane_base + buf * BN + ci * 64;
-#pragma unroll
-                for (int c = 0; c < 4; c++) tmem_ld<16>(col + 16 * c, v + 16 * c);
-                tc_wait_ld();
-                if (ci == (uint32_t)BN / 64 - 1) {
-                    // Every column of this buffer is read: the leader's MMAs of the tile after
-                    // next may overwrite it.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (rank == 0)
-                            mbar_arrive(&acc_empty[buf]);
-                        else
-                            mbar_arrive_remote(acc_empty0 + buf * 8);
-                    }
-                }
-                persist_chunk_epilogue<EPI>(p, v, wbuf, res, lane, row0, valid, n0, ci * 64, mean, rstd,
-                                            ropev, s, q);
-                // The next chunk's residual rows.
-                if constexpr ((EPI & JC_EPI_RES) != 0)
-                    if (ci + 1 < (uint32_t)BN / 64) warp_load_rows64(p.res, p.n, row0, p.m, n0 + (ci + 1) * 64, lane, res);
-            }
-            if constexpr ((EPI & JC_EPI_STATS) != 0) {
-                if (valid) red_add_f32x2(p.stats_out + 2 * (size_t)r, s, q);
-            }
+            // The leader's MMAs of the tile after next may overwrite this buffer once all 16
+            // epilogue warps of the pair have read theirs.
+            if (!persist_tile_epilogue<BN, 1, EPI>(p, lane_base + buf * BN, &acc_full[buf], (i >> 1) & 1, qbuf,
+                                                   quarter, half, lane, m0, n0, [&] {
+                                                       if (rank == 0)
+                                                           mbar_arrive(&acc_empty[buf]);
+                                                       else
+                                                           mbar_arrive_remote(acc_empty0 + buf * 8);
+                                                   }))
+                break;
         }
     }
     // Every MMA into either CTA's TMEM has completed and both epilogues have read it (or given

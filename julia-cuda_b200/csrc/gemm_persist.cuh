@@ -7,11 +7,8 @@
 //   - lane 0 of warps 1..NI issue tcgen05.mma (M 128, N BN, K 16) into one of two TMEM
 //     accumulator buffers (NI accumulators each, taking the MMAs of a stage round-robin and
 //     summed in issuer order, as in gemm_tile.cuh), a buffer reused once the epilogue has read it;
-//   - warps 4-7 run the epilogue, one tile row per thread, 64 columns at a time (RoPE pairs
-//     (i, i + 32) and GeGLU input / gate pairs stay inside a thread); residuals come in and
-//     outputs go out through a 4 KB buffer a warp, so 8 lanes move one 128-byte row segment (one
-//     row a lane, as TMEM hands them out, touched 32 cache lines an instruction: the stores alone
-//     cost the 6144-row qkv GEMM a third of its time);
+//   - warps 4-11 run the epilogue (persist_tile_epilogue, below): a tile row and half of every
+//     64-column chunk a thread, residuals and outputs through a buffer a quarter of the rows;
 //   - warp 3 clears the statistics buffer a later GEMM adds into.
 // 128-column tiles use two issuers (two 128-wide accumulators a buffer), 256-column tiles one
 // (a single N = 256 chain already runs at the tensor pipe's rate): 512 TMEM columns either way.
@@ -22,15 +19,21 @@
 
 namespace jc {
 
-// ---- the persistent epilogues' output path ----
+// ---- the persistent epilogues ----
 //
-// Each epilogue warp owns 32 tile rows (one a thread, as TMEM hands them out) and a 4 KB
-// shared-memory buffer of 32 rows x 128 bytes, XOR-swizzled in 16-byte chunks (chunk c of row r at
-// c ^ (r & 7): a warp's row-per-lane writes and its line-per-8-lanes reads are both free of bank
-// conflicts). Residuals come in and outputs go out through it with 16-byte accesses whose 8
-// consecutive lanes cover one 128-byte row segment, instead of one row (one cache line) a lane.
-constexpr int PERSIST_EPI_WARP_BYTES = 32 * 128;
-constexpr int PERSIST_EPI_BYTES = 4 * PERSIST_EPI_WARP_BYTES;
+// Eight epilogue warps (4-11): warp w reads TMEM lanes 32 (w % 4) .. + 31 (its quarter's 32 tile
+// rows, one a thread, as TMEM hands them out) and one half h = (w - 4) / 4 of every 64-column
+// chunk: columns [16 h, 16 h + 16) and [32 + 16 h, 32 + 16 h + 16), so a thread holds both members
+// of its RoPE pairs (i, i + 32) and both the GELU inputs and the gates of its GeGLU outputs. The
+// two warps of a quarter share a 4 KB buffer of 32 rows x 128 bytes, XOR-swizzled in 16-byte
+// chunks (chunk c of row r at c ^ (r & 7): row-per-lane writes and line-per-8-lanes reads are both
+// free of bank conflicts), through which residuals come in and outputs go out with 16-byte
+// accesses whose 8 consecutive lanes cover one 128-byte row segment. (One row a lane, as TMEM
+// hands them out, touches 32 cache lines an instruction: those stores alone cost the 6144-row qkv
+// GEMM a third of its time.) The quarter's two warps meet at named barrier 1 + quarter.
+constexpr int PERSIST_GEMM_THREADS = 384;
+constexpr int PERSIST_EPI_QUARTER_BYTES = 32 * 128 + 32 * 8;  // rows, then the halves' statistics
+constexpr int PERSIST_EPI_BYTES = 4 * PERSIST_EPI_QUARTER_BYTES;
 
 template <int BN, int STAGES_>
 struct GemmPersistShape {
@@ -48,139 +51,233 @@ struct GemmPersistShape {
     static_assert(STAGE_BYTES % 1024 == 0, "stages keep 1024-byte alignment");
 };
 
-__device__ __forceinline__ uint4 *warp_buf_chunk(uint8_t *buf, uint32_t row, uint32_t c) {
+__device__ __forceinline__ uint4 *quarter_chunk(uint8_t *buf, uint32_t row, uint32_t c) {
     return reinterpret_cast<uint4 *>(buf + row * 128 + ((c ^ (row & 7)) << 4));
 }
 
-// Rows [row0, row0 + 32) x columns [col, col + 64) of a row-major f16 matrix (ld columns a row)
-// into registers, 8 x 16 bytes a lane (rows from `m` on read as zero).
-__device__ __forceinline__ void warp_load_rows64(const __half *src, uint32_t ld, uint32_t row0,
-                                                 uint32_t m, uint32_t col, uint32_t lane,
-                                                 uint4 (&regs)[8]) {
+__device__ __forceinline__ void quarter_sync(uint32_t quarter) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
+
+// quarter_sync that also ANDs a condition over the quarter's two warps (so both take the same
+// branch after it, and neither is left waiting at a later barrier for the other).
+__device__ __forceinline__ bool quarter_and(uint32_t quarter, bool c) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pc, pr;\n\t"
+        "setp.ne.u32 pc, %1, 0;\n\t"
+        "bar.red.and.pred pr, %2, 64, pc;\n\t"
+        "selp.u32 %0, 1, 0, pr;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)c), "r"(1 + quarter)
+        : "memory");
+    return r != 0;
+}
+
+// This warp's half of rows [row0, row0 + 32) (rows row0 + 16 half ..) x columns [col, col + 64) of
+// a row-major f16 matrix (ld columns a row) into registers, 4 x 16 bytes a lane, coalesced (rows
+// from `m` on read as zero).
+__device__ __forceinline__ void half_load_rows64(const __half *src, uint32_t ld, uint32_t row0,
+                                                 uint32_t m, uint32_t col, uint32_t half,
+                                                 uint32_t lane, uint4 (&regs)[4]) {
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const uint32_t r = row0 + k * 4 + (lane >> 3);
+    for (int k = 0; k < 4; k++) {
+        const uint32_t r = row0 + 16 * half + k * 4 + (lane >> 3);
         regs[k] = r < m ? *reinterpret_cast<const uint4 *>(src + (size_t)r * ld + col + (lane & 7) * 8)
                         : make_uint4(0, 0, 0, 0);
     }
 }
 
-// warp_load_rows64's registers into the buffer, then this lane's own row (lane) out of it as 32
-// packed half2 words.
-__device__ __forceinline__ void warp_rows_to_lane(uint8_t *buf, const uint4 (&regs)[8], uint32_t lane,
-                                                  uint32_t *row_words) {
+// The residual of a chunk: both warps of the quarter put their half_load_rows64 registers in the
+// buffer, then every thread takes its columns of its row (16 + 16 columns as 16 packed words).
+__device__ __forceinline__ void quarter_residual(uint8_t *buf, const uint4 (&regs)[4], uint32_t quarter,
+                                                 uint32_t half, uint32_t lane, uint32_t *w) {
 #pragma unroll
-    for (int k = 0; k < 8; k++) *warp_buf_chunk(buf, k * 4 + (lane >> 3), lane & 7) = regs[k];
-    __syncwarp();
+    for (int k = 0; k < 4; k++) *quarter_chunk(buf, 16 * half + k * 4 + (lane >> 3), lane & 7) = regs[k];
+    quarter_sync(quarter);
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const uint4 t = *warp_buf_chunk(buf, lane, j);
-        row_words[4 * j] = t.x; row_words[4 * j + 1] = t.y; row_words[4 * j + 2] = t.z; row_words[4 * j + 3] = t.w;
+    for (int j = 0; j < 4; j++) {
+        const uint4 t = *quarter_chunk(buf, lane, (j >> 1) * 4 + 2 * half + (j & 1));
+        w[4 * j] = t.x; w[4 * j + 1] = t.y; w[4 * j + 2] = t.z; w[4 * j + 3] = t.w;
     }
-    __syncwarp();
 }
 
-// This lane's row of W f16 outputs (W / 2 packed words, W = 64 or 32) into the buffer, then the
-// warp's 32 rows to rows [row0, row0 + 32) x columns [col, col + W) of a row-major f16 matrix (ld
-// columns a row; rows from `m` on are not written).
+// A chunk's outputs: every thread puts its words in its row of the buffer (W = 64 output columns
+// a row: out[0, 8) columns 16 half.., out[8, 16) columns 32 + 16 half..; W = 32 (GeGLU): out[0, 8)
+// columns 16 half..), then each warp stores its half of the rows to rows [row0, row0 + 32) x
+// columns [col, col + W) of a row-major f16 matrix (ld columns a row; rows from `m` on not
+// written), whole row segments at a time. The buffer is free again when this returns.
 template <int W>
-__device__ __forceinline__ void warp_store_rows(uint8_t *buf, const uint32_t *row_words, uint32_t lane,
-                                                __half *dst, uint32_t ld, uint32_t row0, uint32_t m,
-                                                uint32_t col) {
-    static_assert(W == 64 || W == 32, "64- or 32-column rows");
-    constexpr int CH = W / 8;  // 16-byte chunks a row
+__device__ __forceinline__ void quarter_store(uint8_t *buf, const uint32_t *out, uint32_t quarter,
+                                              uint32_t half, uint32_t lane, __half *dst, uint32_t ld,
+                                              uint32_t row0, uint32_t m, uint32_t col) {
+    static_assert(W == 64 || W == 32, "64 or 32 output columns a chunk");
+    constexpr int NW = W == 64 ? 4 : 2;  // 16-byte pieces a thread
 #pragma unroll
-    for (int j = 0; j < CH; j++)
-        *warp_buf_chunk(buf, lane, j) = make_uint4(row_words[4 * j], row_words[4 * j + 1],
-                                                   row_words[4 * j + 2], row_words[4 * j + 3]);
-    __syncwarp();
+    for (int j = 0; j < NW; j++)
+        *quarter_chunk(buf, lane, (j >> 1) * 4 + 2 * half + (j & 1)) =
+            make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+    quarter_sync(quarter);
+    constexpr int CH = W / 8;     // 16-byte chunks a row
     constexpr int RPI = 32 / CH;  // rows one instruction covers
 #pragma unroll
-    for (int k = 0; k < 32 / RPI; k++) {
-        const uint32_t rr = k * RPI + lane / CH, c = lane % CH, r = row0 + rr;
-        if (r < m) *reinterpret_cast<uint4 *>(dst + (size_t)r * ld + col + c * 8) = *warp_buf_chunk(buf, rr, c);
+    for (int k = 0; k < 16 / RPI; k++) {
+        const uint32_t rr = 16 * half + k * RPI + lane / CH, c = lane % CH, r = row0 + rr;
+        if (r < m) *reinterpret_cast<uint4 *>(dst + (size_t)r * ld + col + c * 8) = *quarter_chunk(buf, rr, c);
     }
-    __syncwarp();
+    quarter_sync(quarter);
 }
 
-// The epilogue arithmetic of columns [c0, c0 + 64) (tile-local, c0 a multiple of 64) of one tile
-// row, held by one thread: v[64] the accumulator; ropev: (cos, sin) of the row's 32 pairs, two per
-// float4; resw: the residual of those columns (32 packed words, RES epilogues). Writes the output
-// words to `out` (32, or 16 for GeGLU's 32 output columns) and adds the statistics of the stored
-// values to s / q (STATS epilogues).
+// The epilogue arithmetic of one thread's 32 columns of a 64-column chunk starting at tile-local
+// column c0 (v[0, 16): columns c0 + 16 half + j, v[16, 32): columns c0 + 32 + 16 half + j); ropev:
+// (cos, sin) of pairs 16 half .. 16 half + 15 of the row, two per float4; resw: the residual of
+// those columns (16 packed words, RES). Writes 16 output words (8 for GeGLU's 16 outputs) to out
+// and adds the statistics of the stored values to s / q (STATS).
 template <uint32_t EPI>
-__device__ __forceinline__ void row_chunk_values(const GemmParams &p, float *v, uint32_t n0,
-                                                 uint32_t c0, float mean, float rstd,
-                                                 const float4 *ropev, const uint32_t *resw,
-                                                 uint32_t *out, float &s, float &q) {
-    const uint32_t gc = n0 + c0;
+__device__ __forceinline__ void half_chunk_values(const GemmParams &p, float *v, uint32_t n0,
+                                                  uint32_t c0, uint32_t half, float mean, float rstd,
+                                                  const float4 *ropev, const uint32_t *resw,
+                                                  uint32_t *out, float &s, float &q) {
+    const uint32_t ga = n0 + c0 + 16 * half, gb = ga + 32;
     if constexpr ((EPI & JC_EPI_LN) != 0) {
 #pragma unroll
-        for (int j = 0; j < 64; j++) v[j] = rstd * (v[j] - mean * __ldg(p.colsum + gc + j));
+        for (int j = 0; j < 16; j++) {
+            v[j] = rstd * (v[j] - mean * __ldg(p.colsum + ga + j));
+            v[16 + j] = rstd * (v[16 + j] - mean * __ldg(p.colsum + gb + j));
+        }
     }
     if constexpr ((EPI & JC_EPI_BIAS) != 0) {
 #pragma unroll
-        for (int j = 0; j < 64; j++) v[j] += __ldg(p.bias + gc + j);
+        for (int j = 0; j < 16; j++) {
+            v[j] += __ldg(p.bias + ga + j);
+            v[16 + j] += __ldg(p.bias + gb + j);
+        }
     }
     if constexpr ((EPI & JC_EPI_RELU) != 0) {
 #pragma unroll
-        for (int j = 0; j < 64; j++) v[j] = fmaxf(v[j], 0.0f);
+        for (int j = 0; j < 32; j++) v[j] = fmaxf(v[j], 0.0f);
     }
     if constexpr ((EPI & JC_EPI_GELU) != 0) {
 #pragma unroll
-        for (int j = 0; j < 64; j++) v[j] = gelu_as(v[j]);
+        for (int j = 0; j < 32; j++) v[j] = gelu_as(v[j]);
     }
     if constexpr ((EPI & JC_EPI_ROPE) != 0) {
         // q and k are the first two thirds of a qkv row; the chunk is one head.
-        if (gc < 2 * (p.n / 3)) {
+        if (n0 + c0 < 2 * (p.n / 3)) {
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-                const float4 t = ropev[i / 2];
-                const float c = (i & 1) ? t.z : t.x, sn = (i & 1) ? t.w : t.y;
-                const float x1 = v[i], x2 = v[i + 32];
-                v[i] = x1 * c - x2 * sn;
-                v[i + 32] = x2 * c + x1 * sn;
+            for (int j = 0; j < 16; j++) {
+                const float4 t = ropev[j / 2];
+                const float c = (j & 1) ? t.z : t.x, sn = (j & 1) ? t.w : t.y;
+                const float x1 = v[j], x2 = v[16 + j];
+                v[j] = x1 * c - x2 * sn;
+                v[16 + j] = x2 * c + x1 * sn;
             }
         }
     }
     if constexpr ((EPI & JC_EPI_GEGLU) != 0) {
-        // Packed columns [gc, gc + 32) are GELU inputs of output columns [gc/2, gc/2 + 32), the
-        // next 32 their gates.
+        // Columns c0 .. c0 + 31 of the chunk are GELU inputs of outputs (c0 / 2) .. + 31, the next
+        // 32 their gates: this thread's 16 inputs and 16 gates give outputs 16 half ...
 #pragma unroll
-        for (int j = 0; j < 16; j++)
-            out[j] = pack_half2(gelu_as(v[2 * j]) * v[32 + 2 * j], gelu_as(v[2 * j + 1]) * v[32 + 2 * j + 1]);
+        for (int j = 0; j < 8; j++)
+            out[j] = pack_half2(gelu_as(v[2 * j]) * v[16 + 2 * j], gelu_as(v[2 * j + 1]) * v[16 + 2 * j + 1]);
     } else {
-        pack_group<64, EPI>(v, resw, out, s, q);
+        pack_group<16, EPI>(v, resw, out, s, q);
+        pack_group<16, EPI>(v + 16, resw + 8, out + 8, s, q);
     }
 }
 
-// The epilogue of one 64-column accumulator chunk of a persistent kernel's tile, by one warp (its
-// 32 rows from row0, this lane's row r valid or not): the residual (RES: staged in `res` by the
-// caller, the warp's registers from warp_load_rows64) through the buffer, the arithmetic, and the
-// outputs through the buffer to c.
-template <uint32_t EPI>
-__device__ __forceinline__ void persist_chunk_epilogue(const GemmParams &p, float *v, uint8_t *buf,
-                                                       const uint4 (&res)[8], uint32_t lane,
-                                                       uint32_t row0, bool valid, uint32_t n0,
-                                                       uint32_t c0, float mean, float rstd,
-                                                       const float4 *ropev, float &s, float &q) {
-    uint32_t resw[32];
-    if constexpr ((EPI & JC_EPI_RES) != 0) warp_rows_to_lane(buf, res, lane, resw);
-    uint32_t out[32];
-    float s1 = 0.f, q1 = 0.f;
-    row_chunk_values<EPI>(p, v, n0, c0, mean, rstd, ropev, resw, out, s1, q1);
-    if (valid) {
+// One tile's epilogue by one thread of the 8 epilogue warps (quarter, half, lane): its row
+// m0 + 32 quarter + lane of the tile, columns n0 .. n0 + BN, the accumulator at TMEM address acc
+// (this warp's lanes; NI accumulators BN columns apart, summed in issuer order) once `acc_full`
+// completes its phase of this parity. `release` runs on lane 0 of each warp after the warp's last
+// TMEM read of the tile. qbuf: the quarter's buffer, its statistics after the 32 rows. false if
+// the accumulator wait gave up.
+template <int BN, int NI, uint32_t EPI, class Release>
+__device__ __forceinline__ bool persist_tile_epilogue(const GemmParams &p, uint32_t acc, uint64_t *acc_full,
+                                                      uint32_t parity, uint8_t *qbuf, uint32_t quarter,
+                                                      uint32_t half, uint32_t lane, uint32_t m0,
+                                                      uint32_t n0, Release release) {
+    const uint32_t row0 = m0 + quarter * 32, r = row0 + lane;
+    const bool valid = r < p.m;
+    // What the epilogue reads besides the accumulator, requested before waiting for it.
+    float mean = 0.f, rstd = 0.f;
+    if constexpr ((EPI & JC_EPI_LN) != 0) {
+        if (valid) {
+            const float2 st = *reinterpret_cast<const float2 *>(p.stats_in + 2 * (size_t)r);
+            mean = st.x / (float)p.k;
+            rstd = rsqrtf(fmaxf(st.y / (float)p.k - mean * mean, 0.0f) + p.eps);
+        }
+    }
+    constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? 8 : 1;
+    float4 ropev[ROPE_V];
+#pragma unroll
+    for (int i = 0; i < ROPE_V; i++) ropev[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr ((EPI & JC_EPI_ROPE) != 0) {
+        if (valid) {
+            // Pair-group-major table: float4 g holds pairs 2g, 2g + 1 of every row.
+            const uint32_t pos = p.seg ? r - p.seg[r].x : r;
+            const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + (size_t)(8 * half) * p.rope_stride + pos;
+#pragma unroll
+            for (int i = 0; i < 8; i++) ropev[i] = __ldg(t4 + (size_t)i * p.rope_stride);
+        }
+    }
+    uint4 res[4];
+    if constexpr ((EPI & JC_EPI_RES) != 0) half_load_rows64(p.res, p.n, row0, p.m, n0, half, lane, res);
+    if (!quarter_and(quarter, mbar_wait_sleep(acc_full, parity, JC_DEV_TIMEOUT_MMA))) return false;
+    tc_fence_after();
+    float s = 0.f, q = 0.f;
+#pragma unroll 1
+    for (uint32_t ci = 0; ci < (uint32_t)BN / 64; ci++) {
+        float v[32];
+        const uint32_t col = acc + ci * 64 + 16 * half;
+        tmem_ld<16>(col, v);
+        tmem_ld<16>(col + 32, v + 16);
+        if constexpr (NI > 1) {
+            float t2[32];
+            tmem_ld<16>(col + BN, t2);
+            tmem_ld<16>(col + BN + 32, t2 + 16);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; e++) v[e] += t2[e];
+        } else {
+            tc_wait_ld();
+        }
+        if (ci == (uint32_t)BN / 64 - 1) {
+            // This warp has read every column of the buffer it reads.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release();
+        }
+        uint32_t resw[16];
+        if constexpr ((EPI & JC_EPI_RES) != 0) {
+            quarter_residual(qbuf, res, quarter, half, lane, resw);
+            if (ci + 1 < (uint32_t)BN / 64) half_load_rows64(p.res, p.n, row0, p.m, n0 + (ci + 1) * 64, half, lane, res);
+        }
+        uint32_t out[16];
+        float s1 = 0.f, q1 = 0.f;
+        half_chunk_values<EPI>(p, v, n0, ci * 64, half, mean, rstd, ropev, resw, out, s1, q1);
         s += s1;
         q += q1;
+        if constexpr ((EPI & JC_EPI_GEGLU) != 0)
+            quarter_store<32>(qbuf, out, quarter, half, lane, p.c, p.n / 2, row0, p.m, (n0 + ci * 64) / 2);
+        else
+            quarter_store<64>(qbuf, out, quarter, half, lane, p.c, p.n, row0, p.m, n0 + ci * 64);
     }
-    if constexpr ((EPI & JC_EPI_GEGLU) != 0)
-        warp_store_rows<32>(buf, out, lane, p.c, p.n / 2, row0, p.m, (n0 + c0) / 2);
-    else
-        warp_store_rows<64>(buf, out, lane, p.c, p.n, row0, p.m, n0 + c0);
+    if constexpr ((EPI & JC_EPI_STATS) != 0) {
+        // The row's two halves meet in the quarter's statistics slots: one atomic pair a row.
+        float2 *st = reinterpret_cast<float2 *>(qbuf + 32 * 128);
+        if (half) st[lane] = make_float2(s, q);
+        quarter_sync(quarter);
+        if (!half && valid) {
+            const float2 o = st[lane];
+            red_add_f32x2(p.stats_out + 2 * (size_t)r, s + o.x, q + o.y);
+        }
+    }
+    return true;
 }
 
 template <int BN, int STAGES, uint32_t EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(PERSIST_GEMM_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ GemmKernelParams kp) {
     dev_err_bind(kp.p.err);
     using S = GemmPersistShape<BN, STAGES>;
@@ -203,7 +300,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], NI);
-            mbar_init(&acc_empty[b], 4);  // lane 0 of each epilogue warp
+            mbar_init(&acc_empty[b], 8);  // lane 0 of each epilogue warp
         }
         fence_barrier_init();
     }
@@ -287,78 +384,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // This warp alone clears the buffer, striding over every CTA's warp 3.
         for (uint32_t i = blockIdx.x * 32 + lane; i < p.zero_len; i += gridDim.x * 32) p.zero[i] = 0.0f;
     } else if (warp >= 4) {
-        // Epilogue: warp w reads TMEM lanes 32 (w - 4) .. + 31, one tile row per thread. (With
-        // one issuer, warp 2 has no role and idles.)
+        // Epilogue (8 warps; with one issuer, warp 2 has no role and idles).
         pdl_wait();
         pdl_launch_dependents();
-        const uint32_t quarter = warp - 4, row = quarter * 32 + lane;
+        const uint32_t quarter = warp & 3, half = (warp - 4) >> 2;
         const uint32_t lane_base = tmem + ((quarter * 32) << 16);
-        uint8_t *wbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_WARP_BYTES;
+        uint8_t *qbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_QUARTER_BYTES;
         for (uint32_t t = blockIdx.x, i = 0; t < total; t += gridDim.x, i++) {
             const uint32_t buf = i & 1;
             const uint32_t m0 = (t / tiles_n) * GEMM_BM, n0 = (t % tiles_n) * BN;
-            const uint32_t r = m0 + row;
-            const bool valid = r < p.m;
-            // What the epilogue reads besides the accumulator, requested before waiting for it.
-            float mean = 0.f, rstd = 0.f;
-            if constexpr ((EPI & JC_EPI_LN) != 0) {
-                if (valid) {
-                    const float2 st = *reinterpret_cast<const float2 *>(p.stats_in + 2 * (size_t)r);
-                    mean = st.x / (float)p.k;
-                    rstd = rsqrtf(fmaxf(st.y / (float)p.k - mean * mean, 0.0f) + p.eps);
-                }
-            }
-            constexpr int ROPE_V = (EPI & JC_EPI_ROPE) ? 16 : 1;
-            float4 ropev[ROPE_V];
-#pragma unroll
-            for (int g4 = 0; g4 < ROPE_V; g4++) ropev[g4] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if constexpr ((EPI & JC_EPI_ROPE) != 0) {
-                if (valid) {
-                    const uint32_t pos = p.seg ? r - p.seg[r].x : r;
-                    const float4 *t4 = reinterpret_cast<const float4 *>(p.rope) + pos;
-#pragma unroll
-                    for (int g4 = 0; g4 < 16; g4++) ropev[g4] = __ldg(t4 + (size_t)g4 * p.rope_stride);
-                }
-            }
-            // The first chunk's residual rows (coalesced, through this warp's buffer later).
-            const uint32_t row0 = m0 + quarter * 32;
-            uint4 res[8];
-            if constexpr ((EPI & JC_EPI_RES) != 0) warp_load_rows64(p.res, p.n, row0, p.m, n0, lane, res);
-            if (!mbar_wait_sleep(&acc_full[buf], (i >> 1) & 1, JC_DEV_TIMEOUT_MMA)) break;
-            tc_fence_after();
-            float s = 0.f, q = 0.f;
-#pragma unroll 1
-            for (uint32_t ci = 0; ci < (uint32_t)BN / 64; ci++) {
-                float v[64];
-                const uint32_t col = lane_base + buf * S::ACC + ci * 64;
-#pragma unroll
-                for (int c = 0; c < 4; c++) tmem_ld<16>(col + 16 * c, v + 16 * c);
-                if constexpr (NI > 1) {
-                    float t2[64];
-#pragma unroll
-                    for (int c = 0; c < 4; c++) tmem_ld<16>(col + BN + 16 * c, t2 + 16 * c);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 64; e++) v[e] += t2[e];
-                } else {
-                    tc_wait_ld();
-                }
-                if (ci == (uint32_t)BN / 64 - 1) {
-                    // Every column of this buffer is read: the MMAs of the tile after next may
-                    // overwrite it.
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                }
-                persist_chunk_epilogue<EPI>(p, v, wbuf, res, lane, row0, valid, n0, ci * 64, mean, rstd,
-                                            ropev, s, q);
-                // The next chunk's residual rows.
-                if constexpr ((EPI & JC_EPI_RES) != 0)
-                    if (ci + 1 < (uint32_t)BN / 64) warp_load_rows64(p.res, p.n, row0, p.m, n0 + (ci + 1) * 64, lane, res);
-            }
-            if constexpr ((EPI & JC_EPI_STATS) != 0) {
-                if (valid) red_add_f32x2(p.stats_out + 2 * (size_t)r, s, q);
-            }
+            // The MMAs of the tile after next may overwrite this buffer once all 8 warps have read it.
+            if (!persist_tile_epilogue<BN, NI, EPI>(p, lane_base + buf * S::ACC, &acc_full[buf], (i >> 1) & 1,
+                                                    qbuf, quarter, half, lane, m0, n0,
+                                                    [&] { mbar_arrive(&acc_empty[buf]); }))
+                break;
         }
     }
     tc_fence_before();

@@ -286,7 +286,7 @@ static bool launch_gemm_persist(uint32_t epi, const GemmKernelParams &p, dim3 gr
     constexpr int smem = GemmPersistShape<BN, STAGES>::SMEM_BYTES + 1024;
     auto go = [&](auto kern, std::atomic<uint64_t> &set) {
         if (!ensure_smem(kern, smem, set)) return false;
-        return launch_ex(kern, grid, dim3(GEMM_THREADS), smem, s, pdl, "gemm launch", p);
+        return launch_ex(kern, grid, dim3(PERSIST_GEMM_THREADS), smem, s, pdl, "gemm launch", p);
     };
 #define JC_PERSIST(E)                                                   \
     case E: {                                                           \
@@ -325,7 +325,7 @@ static bool launch_gemm_pair(uint32_t epi, const GemmKernelParams &p, uint32_t t
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.blockDim = dim3(PERSIST_GEMM_THREADS);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = s;
         cfg.attrs = attr;
@@ -498,14 +498,18 @@ static bool persistent_width(int bn) {
 }
 
 // CTA-pair policy (gemm_pair.cuh): 1 (every 128- or 256-column unsplit launch), 0 (automatic:
-// the launches that would run the single-SM persistent kernel), -1 (never); a tuning and test
-// hook (jc_gemm_pair_policy), JC_GEMM_PAIR sets its start value.
-static std::atomic<int> g_pair{(int)env_u32_early("JC_GEMM_PAIR", 0xFFFFFFFFu)};
+// the launches that would run the single-SM persistent kernel with 256-column tiles), -1
+// (never); a tuning and test hook (jc_gemm_pair_policy), JC_GEMM_PAIR sets its start value.
+// Measured alone at 6144 rows (us, single-SM persistent against pairs): 2304-wide qkv 29.2 /
+// 27.7, wi 30.5 / 29.0 with 256 columns; 128-column pairs lose everywhere (qkv 30.5 / 37.0), and
+// below a few thousand rows the single-SM kernels win (qkv at 3072 rows: 18.9 with 128 columns,
+// pairs 21.3).
+static std::atomic<int> g_pair{(int)env_u32_early("JC_GEMM_PAIR", 0u)};
 void swap_gemm_pair_policy(int *policy) { *policy = g_pair.exchange(*policy); }
 static bool pair_for(const GemmConfig &c) {
     const int policy = g_pair.load();
     if (policy < 0 || c.bn < 128 || c.bm != 128 || c.splits != 1 || c.cluster != 1) return false;
-    return policy == 1 || c.persistent;
+    return policy == 1 || (c.persistent && c.bn == 256);
 }
 
 // Tile height policy: 0 (automatic), 128 (always 128 rows) or 64 (64 rows wherever legal, even
@@ -542,6 +546,10 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
     // 256-column tiles run persistent (gemm_persist.cuh): the fixed part is paid once and each
     // further wave costs about twice its width (measured per extra wave at k = 768: 5.0 us for
     // 128 columns, 9.5 us for 256, against 10.6 / 15.4 us for the first).
+    // A single wave of 256-column tiles pays another 256 for its epilogue (128 columns a thread
+    // over two accumulators): measured alone, the 768-wide GEMMs at 2048-6144 rows take 17-18.6
+    // us as one wave of 256 columns against 11.7-15.0 as 128 (one wave, or persistent), and the
+    // 2304-wide ones at 2048 rows 15.3 against 14.7.
     // The tile height for each width (pick_bm) enters the same way: a 64-row tile streams
     // 64 + width operand rows.
     c.bn = 32;
@@ -555,7 +563,7 @@ GemmConfig choose_gemm(uint32_t m, uint32_t n, uint32_t k, int sms) {
         const uint64_t waves = (ctas + sms - 1) / sms;
         const uint64_t cost = waves > 1 && bm == 128 && persistent_width(bn)
                                   ? (256 + (uint64_t)bm + bn) + (waves - 1) * 2 * (uint64_t)bn
-                                  : waves * (uint64_t)(256 + bm + bn);
+                                  : waves * (uint64_t)(256 + bm + bn + (bn == 256 ? 256 : 0));
         if (cost < best) {
             best = cost;
             c.bn = bn;
