@@ -413,12 +413,13 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
         __threadfence();
     }
 
-    // Output through TMA stores (single-GEMM kernel): the tile is staged in the stage memory,
-    // free now that every MMA has completed, in boxes of BW columns.
+    // The output tile is staged in the stage memory, free now that every MMA has completed, in
+    // boxes of BW columns, then written by TMA stores (p.map_c) or by every thread with 16-byte
+    // stores of whole 128-byte (64-byte) row segments.
     constexpr int W_OUT = (EPI & JC_EPI_GEGLU) ? BN / 2 : BN;
     constexpr int BW = W_OUT < 64 ? W_OUT : 64;
     constexpr bool CAN_STAGE = CS == 1 && (BW == 32 || BW == 64) && GT % 8 == 0;
-    uint8_t *stage = (CAN_STAGE && p.map_c) ? sv.stages : nullptr;
+    uint8_t *stage = CAN_STAGE ? sv.stages : nullptr;
     if (run_epilogue) {
         float s = 0.f, q = 0.f;
 #pragma unroll
@@ -483,7 +484,7 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
                 red_add_f32x2(p.stats_out + 2 * (size_t)r, s + o.x, q + o.y);
             }
         }
-        if (stage) {
+        if (stage && p.map_c) {
             // Every thread's staging writes are visible to the TMA (async proxy) before one
             // thread stores the boxes (rows past m are not written) and waits until they have
             // been read out of shared memory.
@@ -496,6 +497,22 @@ __device__ __forceinline__ void gemm_tile(const GemmParams &p,
                     tma_store_2d(p.map_c, stage + b * BM * BW * 2, out0 + b * BW, (int32_t)m0);
                 bulk_commit();
                 bulk_wait_read();
+            }
+        } else if (stage) {
+            // Every thread copies 16-byte chunks out of the staged tile, consecutive threads
+            // taking consecutive chunks of a row (rows past m are not written); the stores need
+            // no wait.
+            __syncthreads();
+            constexpr uint32_t CPR = W_OUT / 8, CPB = BW / 8;  // 16-byte chunks a row, a box row
+            const uint32_t ld = (EPI & JC_EPI_GEGLU) ? p.n / 2 : p.n;
+            __half *out = p.c + ((EPI & JC_EPI_GEGLU) ? n0 / 2 : n0);
+#pragma unroll 4
+            for (uint32_t idx = threadIdx.x; idx < (uint32_t)BM * CPR; idx += GEMM_THREADS) {
+                const uint32_t rr = idx / CPR, ch = idx % CPR, b = ch / CPB, c = ch % CPB;
+                const uint32_t sw = BW == 64 ? (rr & 7) : ((rr >> 1) & 3);
+                if (m0 + rr < p.m)
+                    *reinterpret_cast<uint4 *>(out + (size_t)(m0 + rr) * ld + ch * 8) =
+                        *reinterpret_cast<const uint4 *>(stage + b * BM * BW * 2 + rr * BW * 2 + ((c ^ sw) << 4));
             }
         }
     }

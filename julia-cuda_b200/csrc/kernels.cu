@@ -384,7 +384,10 @@ bool launch_gemm(const GemmArgs &g, GemmConfig cfg, cudaStream_t s, bool pdl) {
     p.map_w = nullptr;
     p.map_c = nullptr;
     p.store_tma = 0;
-    if (cfg.cluster == 1) {
+    // A/B knob JC_GEMM_STORE_TMA=0|1: the staged output tile written by TMA stores (1) or by
+    // every thread's coalesced 16-byte stores (0).
+    static const uint32_t store_tma = env_u32_early("JC_GEMM_STORE_TMA", 1u);
+    if (cfg.cluster == 1 && store_tma) {
         // The output through TMA stores: c as (columns, m rows), boxes of up to 64 columns x 128
         // rows with the swizzle the epilogue stages in; rows past m are not written.
         const bool geglu = g.epi & JC_EPI_GEGLU;
