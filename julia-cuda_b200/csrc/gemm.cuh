@@ -187,18 +187,29 @@ __device__ __forceinline__ void gemm_epilogue_part(const GemmParams &p, float *v
     // TMA stores for; the other instantiations store directly).
     constexpr bool STAGE_OK = (BW == 32 || BW == 64) && G % 8 == 0;
     const uint32_t la = c0 - n0 + pair0, lb = la + HALF;
+    // Column sums and biases from shared memory four at a time (la, lb multiples of 4).
     if constexpr ((EPI & JC_EPI_LN) != 0) {
 #pragma unroll
-        for (int j = 0; j < G; j++) {
-            v[j] = rstd * (v[j] - mean * cs[la + j]);
-            v[G + j] = rstd * (v[G + j] - mean * cs[lb + j]);
+        for (int j = 0; j < G; j += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(cs + la + j);
+            const float4 y = *reinterpret_cast<const float4 *>(cs + lb + j);
+            v[j] = rstd * (v[j] - mean * x.x);
+            v[j + 1] = rstd * (v[j + 1] - mean * x.y);
+            v[j + 2] = rstd * (v[j + 2] - mean * x.z);
+            v[j + 3] = rstd * (v[j + 3] - mean * x.w);
+            v[G + j] = rstd * (v[G + j] - mean * y.x);
+            v[G + j + 1] = rstd * (v[G + j + 1] - mean * y.y);
+            v[G + j + 2] = rstd * (v[G + j + 2] - mean * y.z);
+            v[G + j + 3] = rstd * (v[G + j + 3] - mean * y.w);
         }
     }
     if constexpr ((EPI & JC_EPI_BIAS) != 0) {
 #pragma unroll
-        for (int j = 0; j < G; j++) {
-            v[j] += bs[la + j];
-            v[G + j] += bs[lb + j];
+        for (int j = 0; j < G; j += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(bs + la + j);
+            const float4 y = *reinterpret_cast<const float4 *>(bs + lb + j);
+            v[j] += x.x; v[j + 1] += x.y; v[j + 2] += x.z; v[j + 3] += x.w;
+            v[G + j] += y.x; v[G + j + 1] += y.y; v[G + j + 2] += y.z; v[G + j + 3] += y.w;
         }
     }
     if constexpr ((EPI & JC_EPI_RELU) != 0) {

@@ -139,18 +139,31 @@ __device__ __forceinline__ void half_chunk_values(const GemmParams &p, float *v,
                                                   const float4 *ropev, const uint32_t *resw,
                                                   uint32_t *out, float &s, float &q) {
     const uint32_t ga = n0 + c0 + 16 * half, gb = ga + 32;
+    // Column sums and biases four at a time (ga, gb multiples of 16 columns: 64-byte aligned).
     if constexpr ((EPI & JC_EPI_LN) != 0) {
+        const float4 *ca = reinterpret_cast<const float4 *>(p.colsum + ga);
+        const float4 *cb = reinterpret_cast<const float4 *>(p.colsum + gb);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            v[j] = rstd * (v[j] - mean * __ldg(p.colsum + ga + j));
-            v[16 + j] = rstd * (v[16 + j] - mean * __ldg(p.colsum + gb + j));
+        for (int j = 0; j < 4; j++) {
+            const float4 x = __ldg(ca + j), y = __ldg(cb + j);
+            v[4 * j] = rstd * (v[4 * j] - mean * x.x);
+            v[4 * j + 1] = rstd * (v[4 * j + 1] - mean * x.y);
+            v[4 * j + 2] = rstd * (v[4 * j + 2] - mean * x.z);
+            v[4 * j + 3] = rstd * (v[4 * j + 3] - mean * x.w);
+            v[16 + 4 * j] = rstd * (v[16 + 4 * j] - mean * y.x);
+            v[16 + 4 * j + 1] = rstd * (v[16 + 4 * j + 1] - mean * y.y);
+            v[16 + 4 * j + 2] = rstd * (v[16 + 4 * j + 2] - mean * y.z);
+            v[16 + 4 * j + 3] = rstd * (v[16 + 4 * j + 3] - mean * y.w);
         }
     }
     if constexpr ((EPI & JC_EPI_BIAS) != 0) {
+        const float4 *ba = reinterpret_cast<const float4 *>(p.bias + ga);
+        const float4 *bb = reinterpret_cast<const float4 *>(p.bias + gb);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            v[j] += __ldg(p.bias + ga + j);
-            v[16 + j] += __ldg(p.bias + gb + j);
+        for (int j = 0; j < 4; j++) {
+            const float4 x = __ldg(ba + j), y = __ldg(bb + j);
+            v[4 * j] += x.x; v[4 * j + 1] += x.y; v[4 * j + 2] += x.z; v[4 * j + 3] += x.w;
+            v[16 + 4 * j] += y.x; v[16 + 4 * j + 1] += y.y; v[16 + 4 * j + 2] += y.z; v[16 + 4 * j + 3] += y.w;
         }
     }
     if constexpr ((EPI & JC_EPI_RELU) != 0) {
