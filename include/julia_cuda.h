@@ -297,6 +297,29 @@ int jc_gemm_noalloc(uint32_t epi, int bn, int splits, const uint16_t *a, const u
                     uint16_t *c, const uint16_t *res, const float *stats_in, const float *colsum,
                     float *stats_out, float *zero, uint32_t zero_len, uint32_t m, uint32_t n,
                     uint32_t k, float eps, const float *rope, const float *bias, void *stream);
+/* One encoder layer on the persistent kernel, over device buffers the caller owns: the kernel-level
+ * boundary of the reference's persistent `layer` kernel (kernels/src/main.rs:579-606, launched by
+ * src/forward.rs:226-359; its plan, split-K and key-range arguments are this library's own
+ * plan here). x [m][d_model] f16 is updated in place: qkv = RoPE(LN(x) Wqkv^T) (no LayerNorm when
+ * qkv_colsum is NULL, as in layer 0), o = attention(qkv) (window 0: global, else keys within
+ * +-window), x += o Wo^T, mbuf = GeGLU(LN(x) Wi^T), x += mbuf Wo_mlp^T. Scratch the caller owns:
+ * qkv [m][3 d_model], o [m][d_model], mbuf [m][inter] f16. Statistics ([m][2] f32: sum and sum
+ * of squares of the stored f16 rows): stats_mlp holds x's on entry (read when qkv_colsum is
+ * given) and the updated x's on return; stats_attn is scratch (the statistics after the
+ * attention block). Weights as prepared for the engine: wqkv [3 d_model][d_model] with the
+ * LayerNorm's gamma folded (qkv_colsum [3 d_model]: f64 sums of its rounded rows), wo
+ * [d_model][d_model], wi [2 inter][d_model] folded and interleaved for GeGLU
+ * (jc_prep_interleave_geglu_f16; wi_colsum interleaved the same way), wo_mlp [d_model][inter].
+ * rope: the GEMM layout of jc_gemm (16 x rope_stride float4, jc_prep_rope_gemm; rope_stride >= m,
+ * 0 means m). d_model = 64 x heads; inter a multiple of 64. The phase descriptors, tensor maps
+ * and completion counters live in a per-device scratch the library allocates on first use (and
+ * grows with m): calls on one device must not overlap in time. Device-side timeouts (2 s) are
+ * recorded in the module's error word (jc_device_error). Returns 0, or -1 (jc_last_error). */
+int jc_layer(uint16_t *x, uint16_t *qkv, uint16_t *o, uint16_t *mbuf, float *stats_attn,
+             float *stats_mlp, const uint16_t *wqkv, const float *qkv_colsum, const float *rope,
+             uint32_t rope_stride, const uint16_t *wo, const uint16_t *wi, const float *wi_colsum,
+             const uint16_t *wo_mlp, uint32_t m, uint32_t d_model, uint32_t heads, uint32_t inter,
+             float eps, uint32_t window, void *stream);
 size_t jc_gemm_ws_floats(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 size_t jc_gemm_counters(uint32_t m, uint32_t n, uint32_t k, int bn, int splits);
 /* The persistent kernel's plan (the reference's LayerPlan / gemm_plan / phase_cost,

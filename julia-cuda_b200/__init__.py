@@ -123,6 +123,8 @@ def lib():
         "julia_cuda_prepare_host": ([cfgp, P, sz, sz, P, sz, P, sz, P, P, P, sz], i32),
         "jc_gemm": ([u32, i32, i32, P, P, P, P, P, P, P, P, P, P, u32, u32, u32, u32, f32, P, P, P],
                     i32),
+        "jc_layer": ([P, P, P, P, P, P, P, P, P, u32, P, P, P, P, u32, u32, u32, u32, f32, u32, P],
+                     i32),
         "jc_gemm_ws_floats": ([u32, u32, u32, i32, i32], sz),
         "jc_gemm_counters": ([u32, u32, u32, i32, i32], sz),
         "jc_choose_gemm": ([u32, u32, u32, i32, P, P], i32),
@@ -332,6 +334,21 @@ def gemm(epi: int, a, w, c, *, res=None, stats_in=None, colsum=None, stats_out=N
                        _t_ptr(zero), 0 if zero is None else zero.numel(), m, n, k, eps,
                        _t_ptr(rope), _t_ptr(bias), _stream(stream))
     _check(rc, "jc_gemm")
+
+
+def layer(x, qkv, o, mbuf, stats_attn, stats_mlp, wqkv, qkv_colsum, rope, wo, wi, wi_colsum,
+          wo_mlp, heads: int, eps: float = 1e-5, window: int = 0, rope_stride: int = 0,
+          stream=None) -> None:
+    """One encoder layer on the persistent kernel (jc_layer): x [m, d] f16 updated in place;
+    qkv, o, mbuf scratch; stats_mlp x's row statistics in and out, stats_attn scratch;
+    qkv_colsum None for a layer without LayerNorm before qkv. rope in jc_gemm's layout."""
+    m, d = x.shape
+    inter = mbuf.shape[1]
+    rc = lib().jc_layer(_t_ptr(x), _t_ptr(qkv), _t_ptr(o), _t_ptr(mbuf), _t_ptr(stats_attn),
+                        _t_ptr(stats_mlp), _t_ptr(wqkv), _t_ptr(qkv_colsum), _t_ptr(rope),
+                        rope_stride, _t_ptr(wo), _t_ptr(wi), _t_ptr(wi_colsum), _t_ptr(wo_mlp),
+                        m, d, heads, inter, eps, window, _stream(stream))
+    _check(rc, "jc_layer")
 
 
 def attention(qkv, o, heads: int, window: int = 0, kv_chunks: int = 0, stream=None, ws=None,

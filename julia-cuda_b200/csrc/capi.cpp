@@ -9,6 +9,7 @@
 #include <exception>
 #include <fstream>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/julia_cuda.h"
@@ -40,7 +41,11 @@ auto guarded(char *err, size_t len, F &&f) -> decltype(f()) {
     } catch (...) {
         report(err, len, "julia-cuda: unknown exception");
     }
-    return decltype(f())();
+    // Failure: -1 for the int-returning entry points, NULL for the pointer-returning ones.
+    if constexpr (std::is_same_v<decltype(f()), int>)
+        return -1;
+    else
+        return decltype(f())();
 }
 
 bool set_device(int dev, char *err, size_t len) {

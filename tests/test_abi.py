@@ -144,3 +144,23 @@ def test_bad_config_rejected(jc):
     assert jc.raw_size(c) == 0
     with pytest.raises(jc.JuliaCudaError):
         jc.raw_offsets(c)
+
+
+def test_layer_rejects_bad_arguments_before_touching_a_gpu(jc):
+    """jc_layer (the reference's `layer` kernel boundary): null buffers, a width that is not 64 x
+    heads, an inter size that is not a multiple of 64 and a RoPE table shorter than the layer are
+    errors with a message, found on the host."""
+    lib = jc.lib()
+    buf = (ctypes.c_uint16 * 64)()
+    f = (ctypes.c_float * 64)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    q = ctypes.cast(f, ctypes.c_void_p)
+
+    def call(x=p, d=768, heads=12, inter=1152, m=293, rope_stride=0, colsum=q):
+        return lib.jc_layer(x, p, p, p, q, q, p, colsum, q, rope_stride, p, p, q, p, m, d, heads,
+                            inter, 1e-5, 64, None)
+    assert call(x=None) == -1 and "null buffer" in jc.last_error()
+    assert call(d=760) == -1 and "64 x heads" in jc.last_error()
+    assert call(inter=1000) == -1 and "multiple of 64" in jc.last_error()
+    assert call(m=0) == -1
+    assert call(rope_stride=100) == -1 and "RoPE table" in jc.last_error()

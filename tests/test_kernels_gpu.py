@@ -396,3 +396,51 @@ def test_score(jc, O):
              logits)
     torch.cuda.synchronize()
     assert np.max(np.abs(logits.cpu().numpy() - want)) < 1e-4
+
+
+@pytest.mark.parametrize("m,window,ln", [(1, 0, False), (100, 64, True), (293, 0, True),
+                                         (293, 64, True), (700, 64, False), (1024, 0, True)])
+def test_layer_kernel(jc, O, m, window, ln):
+    """jc_layer (the reference's persistent `layer` kernel boundary) against the oracle's emulation
+    of the same five steps chained: qkv (LN folded + RoPE, or RoPE alone), attention, wo with
+    residual and statistics, wi (LN + GeGLU), wo_mlp with residual and statistics. Every
+    intermediate buffer and both statistics buffers are checked."""
+    D, H, I, eps = 768, 12, 1152, 1e-5
+    x = O.f16(O.normal((m, D), m + 1))
+    stats = O.row_stats(x)
+    wqkv = O.f16(O.normal((3 * D, D), m + 2, std=0.05))
+    qkv_cs = O.f32(wqkv).astype(np.float64).sum(1).astype(np.float32)
+    wo = O.f16(O.normal((D, D), m + 3, std=0.05))
+    wi = O.f16(O.normal((2 * I, D), m + 4, std=0.05))
+    wi_cs = O.f32(wi).astype(np.float64).sum(1).astype(np.float32)
+    wo_mlp = O.f16(O.normal((D, I), m + 5, std=0.05))
+    rope = O.rope_table(160000.0 if window == 0 else 10000.0, m)
+    e_qkv = (jc.EPI_LN | jc.EPI_ROPE) if ln else jc.EPI_ROPE
+    qkv_w, _ = O.emu_gemm(e_qkv, x, wqkv, m, 3 * D, D, stats_in=stats, colsum=qkv_cs, eps=eps,
+                          rope=rope)
+    o_w = O.emu_attention(qkv_w, m, H, window)
+    x1, st_a = O.emu_gemm(jc.EPI_RES | jc.EPI_STATS, o_w, wo, m, D, D, c16=x)
+    m_w, _ = O.emu_gemm(jc.EPI_LN | jc.EPI_GEGLU, x1, wi, m, 2 * I, D, stats_in=st_a, colsum=wi_cs,
+                        eps=eps)
+    x2, st_b = O.emu_gemm(jc.EPI_RES | jc.EPI_STATS, m_w, wo_mlp, m, D, I, c16=x1)
+
+    xd = cuda_u16(x)
+    qkv_d = torch.zeros(m, 3 * D, dtype=torch.float16, device="cuda")
+    o_d = torch.zeros(m, D, dtype=torch.float16, device="cuda")
+    m_d = torch.zeros(m, I, dtype=torch.float16, device="cuda")
+    st_attn = torch.full((2 * m,), 7.0, dtype=torch.float32, device="cuda")
+    st_mlp = cuda_f32(stats.reshape(-1))
+    jc.layer(xd, qkv_d, o_d, m_d, st_attn, st_mlp, cuda_u16(wqkv), cuda_f32(qkv_cs) if ln else None,
+             cuda_f32(jc.prep_rope_gemm(rope, m)), cuda_u16(wo), cuda_u16(jc.prep_interleave_geglu(wi)),
+             cuda_f32(jc.prep_interleave_geglu(wi_cs)), cuda_u16(wo_mlp), H, eps=eps, window=window)
+    torch.cuda.synchronize()
+    assert jc.device_error() == 0
+    for name, got, want, bar in (("qkv", qkv_d, qkv_w, 1e-3), ("o", o_d, o_w, 2e-3),
+                                 ("mbuf", m_d, m_w, 3e-3), ("x", xd, x2, 3e-3)):
+        g, w = O.f32(host_u16(got)), O.f32(want)
+        e, el = rel_err(g, w), elem_err(g, w)
+        assert e < bar and el < 5 * ELEM_GEMM, f"{name} m={m} window={window}: {e:.2e} {el:.2e}"
+    assert stats_err(host_u16(xd), st_mlp.cpu().numpy()) < 1e-4
+    a_rows = st_attn.cpu().numpy().reshape(-1, 2)
+    x1_dev_rows = np.asarray(st_a, np.float64).reshape(-1, 2)
+    assert np.max(np.abs(a_rows - x1_dev_rows) / np.maximum(np.abs(x1_dev_rows), 1.0)) < 2e-2
