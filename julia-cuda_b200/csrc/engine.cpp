@@ -501,7 +501,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             a.heads = d.a.heads;
             a.window = d.a.window;
             a.seg = d.a.seg;
-            a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms);
+            a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms, a.seg != nullptr);
             a.ws = attn_ws;
             a.counters = attn_cnt;
             a.err = d.a.err;

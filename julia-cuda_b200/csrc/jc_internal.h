@@ -132,7 +132,7 @@ uint32_t attention_ctas(const AttnArgs &a);
 uint32_t gemm_ctas(uint32_t m, uint32_t n, const GemmConfig &cfg);
 size_t attn_counters(uint32_t n, uint32_t heads);
 bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl);
-uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms);
+uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms, bool packed = false);
 // The shortest global / sliding-window sequences for the tensor-core attention: sets both,
 // returns the old values in place.
 void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min);

@@ -648,13 +648,21 @@ void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
     *global_min = g_attn_tc_min.exchange(*global_min);
     *window_min = g_attn_tc_min_window.exchange(*window_min);
 }
-static AttnVariant attn_variant(uint32_t n, uint32_t window) {
-    if (n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load()))
+// Packed requests (`packed`: every row carries its request's row range) are a different regime:
+// a query sees only its own request's keys, and a pack has thousands of rows. The tcgen05
+// kernel's 128-query tiles straddle requests and its key loop pays for both, so packs stay on
+// the mma.sync kernel, and packs of more than 768 rows take 64-query CTAs with two key groups
+// (fewer, fuller CTAs for a grid of many waves). Measured on config 3 (4096 requests in packs of
+// up to 6144 rows): 7011 requests/s, against 6428 with the tcgen05 kernel for global layers and
+// 32-query CTAs, 6413 with 32-query CTAs throughout, 6928 with 32-query CTAs of one key group.
+static AttnVariant attn_variant(uint32_t n, uint32_t window, bool packed) {
+    if (!packed && n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load()))
         return AttnVariant{0, 0, true};
     // A/B knob: JC_ATTN_SHAPE=<query warps><key groups>, e.g. "41".
     static const char *force = getenv("JC_ATTN_SHAPE");
     if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '5')
         return AttnVariant{force[0] - '0', force[1] - '0', false};
+    if (packed && n > 768) return AttnVariant{4, 2, false};
     // Global attention over exactly five key tiles: one tile for each of five key groups.
     if (window == 0 && n > 256 && n <= 320) return AttnVariant{2, 5, false};
     // A 32-query CTA of a +-64 window reaches at most three key tiles: three groups of one tile,
@@ -703,7 +711,7 @@ static bool launch_attn_tc(const AttnParams &p, uint32_t chunks, cudaStream_t s,
 size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32) * heads; }
 
 uint32_t attention_ctas(const AttnArgs &a) {
-    const AttnVariant v = attn_variant(a.n, a.window);
+    const AttnVariant v = attn_variant(a.n, a.window, a.seg != nullptr);
     const uint32_t qt = v.tc ? (uint32_t)ATC_QT : 16u * (uint32_t)v.qw;
     return (a.n + qt - 1) / qt * a.heads * a.kv_chunks;
 }
@@ -772,7 +780,7 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
     }
     AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg, a.err, a.prof,
                  a.prof_cap};
-    const AttnVariant v = attn_variant(a.n, a.window);
+    const AttnVariant v = attn_variant(a.n, a.window, a.seg != nullptr);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     switch (v.qw * 10 + v.ks) {
         case 24: return launch_attn_inst<2, 4>(p, a.kv_chunks, s, pdl);
@@ -788,8 +796,8 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
     }
 }
 
-uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms) {
-    const AttnVariant v = attn_variant(n, window);
+uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms, bool packed) {
+    const AttnVariant v = attn_variant(n, window, packed);
     const uint32_t key_tiles = (n + 63) / 64;
     if (v.tc) {
         // Up to two CTAs per SM (the kernel's residency: each brings two more independent MMA

@@ -74,8 +74,8 @@ def test_packing_rejects_rows_above_max_length(jc, packed_case):
 
 def test_large_packs_run_the_persistent_gemm(jc, O):
     """Packs of a few thousand rows: the GEMMs have more tiles than SMs (the persistent kernel,
-    RoPE positions from each row's request), the global layers the tcgen05 attention. Each
-    request's logits match running it alone."""
+    RoPE positions from each row's request), attention 64-query mma.sync CTAs bounded by each
+    row's request. Each request's logits match running it alone."""
     rep = importlib.import_module("julia-cuda_b200.replicas")
     c = jc.default_config(max_positions=3072)
     eng = jc.Engine.load_raw(c, O.init_random(oracle_cfg(O, c), 7), max_length=3072)
