@@ -913,7 +913,7 @@ def main():
     ap.add_argument("--serving-requests", type=int, default=4096,
                     help="headline: config 3 served after the timed region on every rank with "
                          "this many requests (0: skip)")
-    ap.add_argument("--serving-pack", type=int, default=6144,
+    ap.add_argument("--serving-pack", type=int, default=12288,
                     help="headline: the config-3 pass's pack size in tokens (0: unpacked)")
     ap.add_argument("--tile-sweep", action="store_true",
                     help="every tile width of each encoder GEMM at configs 1's row counts, alone")

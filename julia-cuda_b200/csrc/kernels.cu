@@ -649,15 +649,21 @@ void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
     *window_min = g_attn_tc_min_window.exchange(*window_min);
 }
 // Packed requests (`packed`: every row carries its request's row range) are a different regime:
-// a query sees only its own request's keys, and a pack has thousands of rows. The tcgen05
-// kernel's 128-query tiles straddle requests and its key loop pays for both, so packs stay on
-// the mma.sync kernel, and packs of more than 768 rows take 64-query CTAs with two key groups
-// (fewer, fuller CTAs for a grid of many waves). Measured on config 3 (4096 requests in packs of
-// up to 6144 rows): 7011 requests/s, against 6428 with the tcgen05 kernel for global layers and
-// 32-query CTAs, 6413 with 32-query CTAs throughout, 6928 with 32-query CTAs of one key group.
+// a query sees only its own request's keys, and a pack has thousands of rows. For global layers
+// the tcgen05 kernel's 128-query tiles straddle requests and its key loop pays for both, so they
+// stay on the mma.sync kernel, packs of more than 768 rows with 64-query CTAs of two key groups
+// (fewer, fuller CTAs for a grid of many waves); a window bounds a tile's keys whatever requests
+// it straddles, so window layers of packs past 768 rows take the tcgen05 kernel. Measured on
+// config 3 (4096 requests), packs of up to 6144 rows: 7011 requests/s with 64 x 2 mma.sync CTAs
+// for both kinds of layer, against 6428 with the tcgen05 kernel for global layers and 32-query
+// CTAs, 6413 with 32-query CTAs throughout, 6928 with 32-query CTAs of one key group; packs of
+// up to 12288 rows: 7973 with the tcgen05 kernel for the window layers, against 7551.
 static AttnVariant attn_variant(uint32_t n, uint32_t window, bool packed) {
-    if (!packed && n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load()))
+    if (packed) {
+        if (window && n > 768) return AttnVariant{0, 0, true};
+    } else if (n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load())) {
         return AttnVariant{0, 0, true};
+    }
     // A/B knob: JC_ATTN_SHAPE=<query warps><key groups>, e.g. "41".
     static const char *force = getenv("JC_ATTN_SHAPE");
     if (force && force[0] >= '1' && force[0] <= '4' && force[1] >= '1' && force[1] <= '5')
