@@ -84,13 +84,25 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t q_tile = blockIdx.x, head = blockIdx.y, chunk = blockIdx.z, chunks = gridDim.z;
-    const uint32_t q0 = q_tile * ATC_QT, n = p.n, window = p.window;
+    const uint32_t n = p.n, window = p.window;
+    // This CTA's query rows [q0, q_end): a 128-row tile, or a request-aligned entry of a packed
+    // forward's tile list (written before the graph ran; an empty entry leaves at once).
+    uint32_t q0 = q_tile * ATC_QT, q_end = min(q0 + ATC_QT, n);
+    if (p.tiles) {
+        const uint2 t = p.tiles[q_tile];
+        q0 = t.x;
+        q_end = min(t.y, n);
+        if (q0 >= q_end || q_end - q0 > (uint32_t)ATC_QT) {
+            if (threadIdx.x == 0 && q0 < q_end) dev_fail(JC_DEV_BAD_INDEX);
+            return;
+        }
+    }
 
     // The key tiles some query of this CTA can reach (the spans of its first and last query
     // bound the others'), and this CTA's range of them.
     int lo_first, hi_first, lo_last, hi_last;
     key_span(p.seg, n, window, q0, lo_first, hi_first);
-    key_span(p.seg, n, window, min(q0 + ATC_QT - 1, n - 1), lo_last, hi_last);
+    key_span(p.seg, n, window, q_end - 1, lo_last, hi_last);
     const uint32_t kb_lo = (uint32_t)max(lo_first, 0) / ATC_KT;
     const uint32_t kb_hi = (uint32_t)max(hi_last, lo_first) / ATC_KT + 1;
     const uint32_t span = kb_hi - kb_lo;
@@ -324,7 +336,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) attention_tc_kernel(const __gr
                 ok = false;  // another range stores the rows
             }
         }
-        if (ok && q < n) {
+        if (ok && q < q_end) {
             const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
             uint4 *dst = reinterpret_cast<uint4 *>(p.o + (size_t)q * D + head * 64);
 #pragma unroll

@@ -605,7 +605,7 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                 // CUDA graphs serve every pack.
                 const size_t rows = packed ? std::min(L, (f.rows + 63) / 64 * 64) : f.rows;
                 const size_t marks = packed ? std::min(L, (f.marks + 7) / 8 * 8) : f.marks;
-                uint32_t *stage = e->h_ids + slot * 4 * L;
+                uint32_t *stage = e->h_ids + slot * e->input_words();
                 std::memcpy(stage, ids + f.id0, f.rows * 4);
                 uint32_t row = 0, mk = 0;
                 size_t m_src = f.mk0;  // request i's markers: markers[m_src, m_src + n_markers[i])
@@ -626,7 +626,42 @@ int julia_cuda_run(const JcEngine *engine, size_t b, const uint32_t *ids, const 
                     stage[2 * L + 2 * r + 1] = (uint32_t)rows;
                 }
                 for (size_t j = f.marks; j < marks; j++) stage[L + j] = 0;
-                const size_t words = packed ? 2 * L + 2 * rows : (f.marks ? L + f.marks : f.rows);
+                if (packed) {
+                    // The tcgen05 attention's tiles: up to 128 rows of one request each (the
+                    // padding rows are a request of their own), or, if they do not fit the
+                    // list, the plain 128-row tiles; empty entries after them.
+                    uint32_t *tl = stage + 4 * L;
+                    const uint32_t cap = jc::attn_tile_cap((uint32_t)rows);
+                    uint32_t t = 0;
+                    bool fits = true;
+                    auto add = [&](uint32_t s0, uint32_t s1) {
+                        for (uint32_t q = s0; fits && q < s1; q += 128) {
+                            if (t == cap) {
+                                fits = false;
+                                break;
+                            }
+                            tl[2 * t] = q;
+                            tl[2 * t + 1] = std::min(q + 128, s1);
+                            t++;
+                        }
+                    };
+                    uint32_t r0 = 0;
+                    for (size_t i = f.first; i < f.last; i++) {
+                        add(r0, r0 + (uint32_t)lens[i]);
+                        r0 += (uint32_t)lens[i];
+                    }
+                    add((uint32_t)f.rows, (uint32_t)rows);
+                    if (!fits) {
+                        t = 0;
+                        for (uint32_t q = 0; q < rows; q += 128, t++) {
+                            tl[2 * t] = q;
+                            tl[2 * t + 1] = std::min(q + 128, (uint32_t)rows);
+                        }
+                    }
+                    for (; t < cap; t++) tl[2 * t] = tl[2 * t + 1] = 0;
+                }
+                const size_t words = packed ? 4 * L + 2 * (size_t)jc::attn_tile_cap((uint32_t)rows)
+                                            : (f.marks ? L + f.marks : f.rows);
                 bool ok = jc::cuda_ok(cudaMemcpyAsync(e->ids, stage, words * 4, cudaMemcpyHostToDevice,
                                                       s), "ids and markers") &&
                           jc::cuda_ok(cudaEventRecord(e->ev_start[slot], s), "event") &&

@@ -120,12 +120,13 @@ bool Engine::init(const float *raw, std::string *why) {
               dalloc((void **)&hx, rows * D * 2) && dalloc((void **)&xs, rows * D * 2) &&
               dalloc((void **)&ys, rows * S * 2) && dalloc((void **)&stats_a, rows * 8) &&
               dalloc((void **)&stats_b, rows * 8) && dalloc((void **)&stats_s, rows * 8) &&
-              dalloc((void **)&ids, 4 * L * 4) &&
+              dalloc((void **)&ids, input_words() * 4) &&
               dalloc((void **)&iota, L * 4) && dalloc((void **)&logits, L * 4) &&
               dalloc((void **)&dev_err, 16);
     if (!ok || !cu(cudaMemset(dev_err, 0, 16), "memset")) return false;
     markers = ids + L;
     seg = reinterpret_cast<uint2 *>(ids + 2 * L);
+    tiles = reinterpret_cast<uint2 *>(ids + 4 * L);
     // Split-K scratch for up to 8 splits of the widest GEMM, split-KV scratch for up to 8 ranges.
     const size_t widest = std::max({3 * D, 2 * I, F, S});
     gemm_ws_cap = rows * widest * 8;
@@ -208,7 +209,7 @@ bool Engine::init(const float *raw, std::string *why) {
         return false;
     persist_grid = (uint32_t)(sms * std::max(0, persist_blocks_per_sm()));
 
-    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * 4 * L * 4), "cudaMallocHost") ||
+    if (!cu(cudaMallocHost((void **)&h_ids, QUEUE * input_words() * 4), "cudaMallocHost") ||
         !cu(cudaMallocHost((void **)&h_logits, QUEUE * L * 4), "cudaMallocHost") ||
         !cu(cudaMallocHost((void **)&h_err, sizeof(unsigned int)), "cudaMallocHost"))
         return false;
@@ -279,7 +280,9 @@ std::vector<Step> Engine::build_steps(uint32_t n, uint32_t k, uint32_t qtype, co
     }
     if (packed)
         for (Step &st : steps) {
-            if (st.d.kind == PH_ATTN) st.d.a.seg = seg;
+            // Request-aligned tiles for global attention only: a window already bounds a tile's
+            // keys, and splitting its tiles at requests only adds partial ones.
+            if (st.d.kind == PH_ATTN) st.d.a.seg = seg, st.d.a.tiles = st.d.a.window ? nullptr : tiles;
             if (st.d.kind == PH_GEMM && (st.d.epi & JC_EPI_ROPE)) st.d.g.seg = seg;
         }
     return steps;
@@ -501,6 +504,7 @@ bool Engine::run_step(const Step &st, cudaStream_t s) {
             a.heads = d.a.heads;
             a.window = d.a.window;
             a.seg = d.a.seg;
+            a.tiles = d.a.tiles;
             a.kv_chunks = choose_kv_chunks(a.n, a.heads, a.window, sms, a.seg != nullptr);
             a.ws = attn_ws;
             a.counters = attn_cnt;

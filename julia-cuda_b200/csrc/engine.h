@@ -105,6 +105,12 @@ class Engine {
     // packed requests, each row's request rows (uint2) at [2L, 4L) of one allocation
     uint32_t *ids = nullptr, *markers = nullptr, *iota = nullptr;
     uint2 *seg = nullptr;
+    // packed forwards: the tcgen05 attention's request-aligned tiles, at [4L, 4L + 2 cap) of the
+    // same allocation (cap = attn_tile_cap(L) entries)
+    uint2 *tiles = nullptr;
+    // Words of a forward's inputs (ids, markers, segments, tiles), on the device and in each
+    // staging slot.
+    size_t input_words() const { return 4 * (size_t)max_length + 2 * (size_t)attn_tile_cap((uint32_t)max_length); }
     float *logits = nullptr;
     // pinned staging for julia_cuda_run
     static constexpr int QUEUE = 16;

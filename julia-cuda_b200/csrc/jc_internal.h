@@ -124,6 +124,8 @@ struct AttnArgs {
     unsigned int *err = nullptr;  // error word (nullptr: the module's)
     uint64_t *prof = nullptr;     // profiling run: per-CTA phase stamps (8 words a CTA)
     uint32_t prof_cap = 0;
+    // packed requests: the tcgen05 kernel's request-aligned tiles (attn_tile_cap(n) entries)
+    const uint2 *tiles = nullptr;
 };
 size_t attn_ws_floats(uint32_t n, uint32_t heads, uint32_t kv_chunks);
 // CTAs a launch_attention of these arguments runs.

@@ -649,18 +649,21 @@ void swap_attn_tc_min(uint32_t *global_min, uint32_t *window_min) {
     *window_min = g_attn_tc_min_window.exchange(*window_min);
 }
 // Packed requests (`packed`: every row carries its request's row range) are a different regime:
-// a query sees only its own request's keys, and a pack has thousands of rows. For global layers
-// the tcgen05 kernel's 128-query tiles straddle requests and its key loop pays for both, so they
-// stay on the mma.sync kernel, packs of more than 768 rows with 64-query CTAs of two key groups
-// (fewer, fuller CTAs for a grid of many waves); a window bounds a tile's keys whatever requests
-// it straddles, so window layers of packs past 768 rows take the tcgen05 kernel. Measured on
-// config 3 (4096 requests), packs of up to 6144 rows: 7011 requests/s with 64 x 2 mma.sync CTAs
-// for both kinds of layer, against 6428 with the tcgen05 kernel for global layers and 32-query
-// CTAs, 6413 with 32-query CTAs throughout, 6928 with 32-query CTAs of one key group; packs of
-// up to 12288 rows: 7973 with the tcgen05 kernel for the window layers, against 7551.
+// a query sees only its own request's keys, and a pack has thousands of rows. Packs of more than
+// 768 rows take the tcgen05 kernel: for global layers on request-aligned tiles (the engine's
+// tile list: a 128-row tile straddling two requests made the key loop pay for both), for window
+// layers on plain 128-row tiles (a window bounds a tile's keys whatever it straddles). Smaller
+// packs stay on the mma.sync kernel. Measured on config 3 (4096 requests): packs of up to 6144
+// rows, 6428 requests/s with the tcgen05 kernel on straddling tiles for global layers, 7011 with
+// 64 x 2 mma.sync CTAs for both kinds of layer (6413 with 32-query CTAs, 6928 with 32-query CTAs
+// of one key group); packs of up to 12288 rows, 7551 with 64 x 2 mma.sync CTAs, 7805-7973 with
+// tcgen05 window layers, 8258-8320 with request-aligned tcgen05 global layers as well
+// (JC_ATTN_PACKED_GLOBAL_TC=0 keeps global layers of packs on 64 x 2 mma.sync CTAs).
 static AttnVariant attn_variant(uint32_t n, uint32_t window, bool packed) {
     if (packed) {
-        if (window && n > 768) return AttnVariant{0, 0, true};
+        static const uint32_t global_tc = env_u32("JC_ATTN_PACKED_GLOBAL_TC", 1u);
+        if ((window || global_tc) && n > 768) return AttnVariant{0, 0, true};
+        // (the A/B knob's mma.sync shape below for global layers of big packs: 64 x 2)
     } else if (n >= (window ? g_attn_tc_min_window.load() : g_attn_tc_min.load())) {
         return AttnVariant{0, 0, true};
     }
@@ -709,7 +712,7 @@ static bool launch_attn_tc(const AttnParams &p, uint32_t chunks, cudaStream_t s,
         set_error("attention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
         return false;
     }
-    dim3 grid((p.n + ATC_QT - 1) / ATC_QT, p.heads, chunks);
+    dim3 grid(p.tiles ? attn_tile_cap(p.n) : (p.n + ATC_QT - 1) / ATC_QT, p.heads, chunks);
     return launch_ex(attention_tc_kernel, grid, dim3(ATC_THREADS), AtcSmem::ALLOC, s, pdl,
                      "attention launch", kp);
 }
@@ -718,6 +721,7 @@ size_t attn_counters(uint32_t n, uint32_t heads) { return (size_t)((n + 31) / 32
 
 uint32_t attention_ctas(const AttnArgs &a) {
     const AttnVariant v = attn_variant(a.n, a.window, a.seg != nullptr);
+    if (v.tc && a.tiles) return attn_tile_cap(a.n) * a.heads * a.kv_chunks;
     const uint32_t qt = v.tc ? (uint32_t)ATC_QT : 16u * (uint32_t)v.qw;
     return (a.n + qt - 1) / qt * a.heads * a.kv_chunks;
 }
@@ -785,7 +789,11 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
         return false;
     }
     AttnParams p{a.qkv, a.o, a.ws, a.counters, a.n, a.heads, a.window, a.seg, a.err, a.prof,
-                 a.prof_cap};
+                 a.prof_cap, a.tiles};
+    if (a.tiles && a.kv_chunks != 1) {
+        set_error("attention: a tile list takes one key range a tile");
+        return false;
+    }
     const AttnVariant v = attn_variant(a.n, a.window, a.seg != nullptr);
     if (v.tc) return launch_attn_tc(p, a.kv_chunks, s, pdl);
     switch (v.qw * 10 + v.ks) {
@@ -805,6 +813,8 @@ bool launch_attention(const AttnArgs &a, cudaStream_t s, bool pdl) {
 uint32_t choose_kv_chunks(uint32_t n, uint32_t heads, uint32_t window, int sms, bool packed) {
     const AttnVariant v = attn_variant(n, window, packed);
     const uint32_t key_tiles = (n + 63) / 64;
+    // Packs run the tcgen05 kernel on request-aligned tiles (one key range each).
+    if (v.tc && packed) return 1;
     if (v.tc) {
         // Up to two CTAs per SM (the kernel's residency: each brings two more independent MMA
         // chains), at least two key tiles a range: the range count that minimises waves x key

@@ -51,7 +51,16 @@ struct AttnParams {
     unsigned int *err;  // error word (nullptr: the module's)
     uint64_t *prof;     // phase stamps of a profiling run (nullptr: none; standalone launches)
     uint32_t prof_cap;
+    // Packed requests, tcgen05 kernel: CTA x takes query rows [tiles[x].x, tiles[x].y), at most
+    // 128 rows of one request (empty entries: no work), attn_tile_cap(n) entries; nullptr: CTA x
+    // takes rows [128 x, 128 x + 128).
+    const uint2 *tiles;
 };
+
+// Entries of a packed forward's attention tile list: room for request-aligned tiles of up to 128
+// rows when the requests average 128 rows or more (otherwise the list holds the plain 128-row
+// tiles and the requests' keys still bound every query).
+__host__ __device__ constexpr uint32_t attn_tile_cap(uint32_t n) { return 2 * ((n + 127) / 128); }
 
 // Phase kinds of the persistent kernel.
 enum : uint32_t {
