@@ -361,9 +361,6 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
     return __half22float2(h);
 }
 
-// GELU(x) = x * Phi(x) with Phi from the Abramowitz & Stegun 7.1.26 erf approximation (the
-// formula julia-rs and the reference kernels use; kernels/src/gemm.rs:139-150). The reciprocal is
-// the hardware approximation (a couple of ulp; the result's error stays near 1e-7 relative).
 // 2^x on the special-function unit (PTX ex2.approx.ftz; 2^-inf = 0).
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -371,6 +368,9 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// GELU(x) = x * Phi(x) with Phi from the Abramowitz & Stegun 7.1.26 erf approximation (the
+// formula julia-rs and the reference kernels use; kernels/src/gemm.rs:139-150). The reciprocal is
+// the hardware approximation (a couple of ulp; the result's error stays near 1e-7 relative).
 __device__ __forceinline__ float gelu_as(float x) {
     float t = __fdividef(1.0f, 1.0f + 0.2316419f * fabsf(x));
     float p = 0.5f * 1.061405429f;
