@@ -677,6 +677,10 @@ static AttnVariant attn_variant(uint32_t n, uint32_t window, bool packed) {
     // A 32-query CTA of a +-64 window reaches at most three key tiles: three groups of one tile,
     // while the grid (12 heads) stays within two 100 KB CTAs an SM.
     if (window > 0 && window <= 64 && n > 192 && n <= 768) return AttnVariant{2, 3, false};
+    // Past 768 tokens a +-64 window's grid of 32-query CTAs takes several waves: one key group
+    // a CTA (64 threads, three CTAs' worth of key tiles in flight an SM) measured best (config 4,
+    // 1024 tokens: forward 925.7 us against 965.6 with two groups and 932.6 with 64-query CTAs).
+    if (window > 0 && window <= 64 && n > 768) return AttnVariant{2, 1, false};
     return n > 192 && n <= 384 ? AttnVariant{2, 4, false} : AttnVariant{2, 2, false};
 }
 
