@@ -19,9 +19,9 @@
 //     receives rows 128 r .. 128 r + 127 of the tile, all BN columns, in one of two accumulator
 //     buffers; each stage is released in both CTAs by one tcgen05.commit multicast to both empty
 //     barriers, each finished tile by one commit multicast to both accumulator-full barriers;
-//   - warps 4-11 of each CTA run the epilogue of its 128 rows (persist_tile_epilogue, as
+//   - warps 4 and up of each CTA run the epilogue of its 128 rows (persist_tile_epilogue, as
 //     gemm_persist.cuh) and report the buffer free on the leader's accumulator-empty barrier
-//     (16 arrivals: 8 warps of each CTA);
+//     (one arrival for each epilogue warp of both CTAs);
 //   - warp 3 clears the statistics buffer a later GEMM adds into.
 // TMEM is allocated and freed with cta_group::2 by warp 0 of both CTAs; a cluster barrier after
 // the set-up (barriers initialised before any peer signals them) and one before the teardown
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(PERSIST_GEMM_THREADS, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);   // the leader's commit, multicast
-            mbar_init(&acc_empty[b], 16);  // lane 0 of the 8 epilogue warps of both CTAs
+            mbar_init(&acc_empty[b], 8 * PERSIST_EPI_CG);  // lane 0 of every epilogue warp of both CTAs
         }
         fence_barrier_init();
     }
@@ -221,20 +221,20 @@ __global__ void __launch_bounds__(PERSIST_GEMM_THREADS, 1)
         // This warp alone clears the buffer, striding over every CTA's warp 3.
         for (uint32_t i = blockIdx.x * 32 + lane; i < p.zero_len; i += gridDim.x * 32) p.zero[i] = 0.0f;
     } else if (warp >= 4) {
-        // Epilogue (8 warps) of this CTA's 128 rows of each tile.
+        // Epilogue of this CTA's 128 rows of each tile.
         pdl_wait();
         pdl_launch_dependents();
-        const uint32_t quarter = warp & 3, half = (warp - 4) >> 2;
+        const uint32_t quarter = warp & 3, grp = (warp - 4) >> 2;
         const uint32_t lane_base = tmem + ((quarter * 32) << 16);
         const uint32_t acc_empty0 = map_to_rank(smem_u32(acc_empty), 0);
         uint8_t *qbuf = base + S::EPI_OFF + quarter * PERSIST_EPI_QUARTER_BYTES;
         for (uint32_t t = pair, i = 0; t < total; t += pairs, i++) {
             const uint32_t buf = i & 1;
             const uint32_t m0 = (t / tiles_n) * PAIR_M + rank * GEMM_BM, n0 = (t % tiles_n) * BN;
-            // The leader's MMAs of the tile after next may overwrite this buffer once all 16
-            // epilogue warps of the pair have read theirs.
+            // The leader's MMAs of the tile after next may overwrite this buffer once every
+            // epilogue warp of the pair has read its part.
             if (!persist_tile_epilogue<BN, 1, EPI>(p, lane_base + buf * BN, &acc_full[buf], (i >> 1) & 1, qbuf,
-                                                   quarter, half, lane, m0, n0, [&] {
+                                                   quarter, grp, lane, m0, n0, [&] {
                                                        if (rank == 0)
                                                            mbar_arrive(&acc_empty[buf]);
                                                        else
