@@ -399,7 +399,8 @@ __global__ void __launch_bounds__(PERSIST_THREADS, 1) persist_kernel(const __gri
         __syncthreads();
         if (!ok_s) break;
         // Report the item, then take the next one (taken only now: an item held by a busy CTA
-        // could not start on an idle one).
+        // could not start on an idle one; taking it one ahead, as the current one starts,
+        // measured 1353 against 1056 us for the whole model at 293 tokens).
         if (threadIdx.x == 0) {
             red_release_add(F.ctr + ph * F.blocks + block, 1u);
             prof_stamp(item_record(&F, item), 5);
