@@ -19,9 +19,12 @@
  *
  * Parity pinning: the prep transforms and the plan model are pinned by the reference's own
  * known-answer tests (src/prep.rs:252-327, src/forward.rs:815-823), restated in tests/. The forward
- * numerics cannot be pinned to julia-rs (crate and checkpoint absent); they are pinned to an
- * independent torch-CPU f32 restatement in tests/ and to the emulation within the reference's
- * tolerance design (src/check.rs:382-402).
+ * numerics cannot be pinned to julia-rs (crate and checkpoint absent); the f32 forward is pinned to
+ * implementations written outside this project on the same checkpoint (transformers'
+ * ModernBertModel for the encoder, torch.nn.TransformerEncoderLayer and nn.LayerNorm / Linear /
+ * GELU for the head and scorer, tests/test_hf_modernbert.py), to an independent torch-CPU f32
+ * restatement in tests/, and the emulation to the f32 forward within the reference's tolerance
+ * design (src/check.rs:382-402).
  */
 #ifndef JC_ORACLE_H
 #define JC_ORACLE_H
