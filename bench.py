@@ -202,12 +202,15 @@ def restated_module():
     return restated
 
 
-def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=True, restated=None):
+def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=True, restated=None,
+                 cublas=False):
     """Each GEMM shape and attention of the forward pass alone at n tokens (timed(): its launches
     in a CUDA graph on the launching stream, L2 flushed before every launch); `gemms` limits the
     GEMM shapes by name. Returns {name: (avg ms, launches per forward, algorithmic bytes,
     flops)}; with `restated` (baseline/restated's binding), also {name + "@restated": ...}: the
-    reference's kernel for the same shape on the same inputs, timed the same way."""
+    reference's kernel for the same shape on the same inputs, timed the same way; with `cublas`,
+    {name + "@cublas": ...}: torch.mm (cuBLAS) of the same f16 operands, a plain GEMM without
+    the fused epilogue, timed the same way."""
     from oracle import oracle as O
     out = {}
     stream = torch.cuda.current_stream()
@@ -247,6 +250,11 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
                               rope=rtab, bias=bias)
             out[name + "@restated"] = (timed(torch, stream, flush, launch_ref, reps), count,
                                        bytes_, 2.0 * n * N * K)
+        if cublas:
+            cb = torch.empty(n, N, device="cuda", dtype=torch.half)
+            out[name + "@cublas"] = (timed(torch, stream, flush,
+                                           lambda: torch.mm(a, w.t(), out=cb), reps), count,
+                                     2 * (n * K + N * K + n * N), 2.0 * n * N * K)
     if not attention:
         return out
     heads = cfg.n_heads
@@ -328,12 +336,15 @@ def sweep_arm(args, rank, local):
         for n in (72, 293, 448, 1024):
             rows += [("config1", n, k, v) for k, v in time_kernels(
                 jc, torch, cfg, flush, n=n, gemms=("qkv", "wo", "wi", "wo_mlp"),
-                attention=False, restated=rs).items()]
+                attention=False, restated=rs, cublas=True).items()]
         for n in (128, 512, 1024):
             rows += [("config2", n, k, v) for k, v in time_kernels(
                 jc, torch, cfg, flush, n=n, gemms=(), restated=rs).items()]
     assert jc.device_error() == 0
-    ref_us = {(n, name.split("@")[0]): v[0] * 1e3 for _, n, name, v in rows if "@" in name}
+    ref_us = {(n, name.split("@")[0]): v[0] * 1e3 for _, n, name, v in rows
+              if name.endswith("@restated")}
+    cublas_us = {(n, name.split("@")[0]): v[0] * 1e3 for _, n, name, v in rows
+                 if name.endswith("@cublas")}
     for conf, n, name, (ms, _, bytes_, flops) in rows:
         if "@" in name:
             continue
@@ -346,6 +357,11 @@ def sweep_arm(args, rank, local):
             # The reference's kernel (restated, baseline/restated) on the same inputs.
             line["restated_us"] = ref_us[(n, name)]
             line["speedup_vs_restated"] = ref_us[(n, name)] / (ms * 1e3)
+        if (n, name) in cublas_us:
+            # cuBLAS (torch.mm) on the same operands: a plain GEMM, no fused epilogue.
+            line["cublas_plain_us"] = cublas_us[(n, name)]
+            line["cublas_plain_tensor_frac"] = flops / (cublas_us[(n, name)] * 1e-6) / 1e12 / \
+                pk["bf16_tflops"]
         print(json.dumps(line), flush=True)
     print(json.dumps({"sweep": "clocks", "clocks": clk.summary()}), flush=True)
 
