@@ -441,6 +441,11 @@ def test_layer_kernel(jc, O, m, window, ln):
         e, el = rel_err(g, w), elem_err(g, w)
         assert e < bar and el < 5 * ELEM_GEMM, f"{name} m={m} window={window}: {e:.2e} {el:.2e}"
     assert stats_err(host_u16(xd), st_mlp.cpu().numpy()) < 1e-4
-    a_rows = st_attn.cpu().numpy().reshape(-1, 2)
-    x1_dev_rows = np.asarray(st_a, np.float64).reshape(-1, 2)
-    assert np.max(np.abs(a_rows - x1_dev_rows) / np.maximum(np.abs(x1_dev_rows), 1.0)) < 2e-2
+    # x1's statistics as the layer computed them, against those of the emulation's x1 (the same
+    # values rounded along another path): a row sum's rounding noise scales with the row's norm,
+    # so its error is taken relative to sqrt(sum of squares), the sum of squares relative to itself.
+    a_rows = st_attn.cpu().numpy().reshape(-1, 2).astype(np.float64)
+    x1_rows = np.asarray(st_a, np.float64).reshape(-1, 2)
+    sq = np.maximum(x1_rows[:, 1], 1e-30)
+    assert np.max(np.abs(a_rows[:, 0] - x1_rows[:, 0]) / np.sqrt(sq)) < 1e-2
+    assert np.max(np.abs(a_rows[:, 1] - x1_rows[:, 1]) / sq) < 1e-2
