@@ -518,8 +518,8 @@ static bool pair_for(const GemmConfig &c) {
 // Tile height policy: 0 (automatic), 128 (always 128 rows) or 64 (64 rows wherever legal, even
 // past one wave); a tuning and test hook (jc_gemm_tile_rows), JC_GEMM_BM sets its start value.
 // The default is 128: in the 293-token forward 64-row tiles measured 652.6 against 646.2 us (the
-// 768-wide GEMMs alone 6.59 / 7.77 against 6.72 / 7.55 us), since a narrow tile's main loop is
-// bound by its chain of K = 16 MMAs, not by its operand bytes.
+// 768-wide GEMMs alone 6.59 / 7.77 against 6.72 / 7.55 us): a narrow tile's main loop takes
+// 160 ns a k-block whatever its operand bytes (or its number of MMA issuer warps).
 static std::atomic<int> g_tile_rows{(int)env_u32_early("JC_GEMM_BM", 128u)};
 void swap_gemm_tile_rows(int *rows) { *rows = g_tile_rows.exchange(*rows); }
 
@@ -921,7 +921,7 @@ int persist_blocks_per_sm() {
 // The in-forward time (us) of one 128-row GEMM tile of width bn over depth k, as the phase stamps
 // of the per-step kernels measure it on a B200 (profiles/forward_293_phase_stamps.md): first
 // stage and drain 0.8 us, the main loop 0.163 us per 64-deep k-block whatever the tile's width
-// (the chain of K = 16 MMAs its four issuer warps run), the epilogue 0.70 us per 32 columns a
+// (or height, or number of MMA issuer warps), the epilogue 0.70 us per 32 columns a
 // row holds. The B200 restatement of the reference's per-task cost (src/forward.rs:783-806:
 // 5 us a task plus 0.35 us a K step on 68 SMs).
 double gemm_tile_us(uint32_t k, int bn) {
