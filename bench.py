@@ -28,6 +28,9 @@ Other BASELINE configs (extra lines, not the headline):
   --seq 1024 --head-length 512 --mode 2 config 4: the whole model in one cooperative launch
   --restated                            the reference's per-step GPU kernels restated in CUDA C++
                                         (baseline/restated) against this library, same request
+  --torch-runtime [--torch-dtype bf16]  the reference's torch-runtime comparison: the same model
+                                        in transformers + torch modules beside this library on
+                                        config-3 requests, agreement and latency
   --profile                             where a forward's time goes: per-CTA phase stamps of the
                                         per-step kernels (julia_cuda_forward_profile), per launch
 """
@@ -824,6 +827,62 @@ def profile_persistent(args, eng, cfg, ids_d, mk_d, logits, flush, mode):
           flush=True)
 
 
+def torch_runtime_arm(args, local):
+    """The reference's torch-runtime comparison (tools/torch_baseline.py with tools/score.py) on
+    one GPU: seeded config-0 weights written as a checkpoint, loaded both by this library
+    (julia_cuda_load) and by the torch runtime assembled from transformers' ModernBertModel and
+    torch modules (baseline/torch_runtime.py, autocast --torch-dtype: the reference runtime's
+    default is BF16); --torch-requests seeded config-3 requests (log-normal lengths) through both,
+    one at a time, wall time per request as the reference measures its runtime (host arrays in,
+    logits back on the host), timed on a second pass after an untimed one over the same requests;
+    the answers compared as tools/score.py compares two runs. One JSON line."""
+    import tempfile
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    replicas = importlib.import_module("julia-cuda_b200.replicas")
+    scoring = importlib.import_module("julia-cuda_b200.scoring")
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from torch_runtime import TorchRuntime
+    cfg = jc.default_config(max_positions=1024)
+    with tempfile.TemporaryDirectory() as d:
+        jc.save_checkpoint(d, cfg, jc.init_random(cfg, SEED))
+        eng = jc.Engine.load(d, max_length=1024)
+        rt = TorchRuntime(d, device=f"cuda:{local}", dtype=args.torch_dtype)
+    reqs = replicas.serving_requests(args.torch_requests, SEED, cfg.vocab)
+    for r in reqs:  # warm-up pass: every length once (this library's CUDA graph per length,
+        rt.forward(*r)  # the runtime's kernel choices per shape), then the timed pass
+        eng.run([r])
+    ours, theirs, t_ours, t_theirs = [], [], [], []
+    with ClockSampler(local) as clk:
+        for r in reqs:
+            t0 = time.perf_counter()
+            out, _ = eng.run([r])
+            t1 = time.perf_counter()
+            lg = rt.forward(*r)
+            t2 = time.perf_counter()
+            ours.append(out[0])
+            theirs.append(lg)
+            t_ours.append(t1 - t0)
+            t_theirs.append(t2 - t1)
+    eng.close()
+    a = scoring.agreement(ours, theirs)
+    rms = float(np.sqrt(np.mean(np.concatenate(theirs).astype(np.float64) ** 2)))
+    lens = [len(r[0]) for r in reqs]
+    print(json.dumps({
+        "torch_runtime": "transformers ModernBertModel + torch.nn.TransformerEncoderLayer head + "
+                         "scorer (baseline/torch_runtime.py), autocast " + args.torch_dtype,
+        "requests": len(reqs), "tokens_mean": float(np.mean(lens)),
+        "ours_ms_per_request": 1e3 * statistics.mean(t_ours),
+        "torch_ms_per_request": 1e3 * statistics.mean(t_theirs),
+        "speedup_vs_torch_runtime": statistics.mean(t_theirs) / statistics.mean(t_ours),
+        "agreement_vs_torch_runtime": a, "max_abs_dlogit_over_rms": a["max_abs_dlogit"] / rms,
+        "timing": "wall clock per request, one request at a time, host arrays in and logits out "
+                  "(julia_cuda_run for this library); requests alternate between the two; the "
+                  "timed pass follows an untimed pass over the same requests",
+        "clocks": clk.summary(), "data": "synthetic (seeded weights and requests)"}), flush=True)
+
+
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
 SERVING_METRIC = "requests/s (config 3 serving: log-normal lengths around 293 tokens, 4 markers)"
 
@@ -939,6 +998,11 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="phase stamps (per CTA of the per-step kernels, per item of the "
                          "persistent kernel with --mode 1/2): where a forward's time goes")
+    ap.add_argument("--torch-runtime", action="store_true",
+                    help="the reference's torch-runtime comparison (baseline/torch_runtime.py) "
+                         "beside this library on config-3 requests: agreement and latency")
+    ap.add_argument("--torch-dtype", default="bf16", choices=["bf16", "fp16", "fp32"])
+    ap.add_argument("--torch-requests", type=int, default=256)
     ap.add_argument("--one", choices=["qkv", "wo", "wi", "wo_mlp", "head_in", "head_l1", "head_l2",
                                       "attn_global", "attn_window"],
                     help="launch only this kernel (--seq tokens, --warmup + --steps times), for ncu")
@@ -961,6 +1025,10 @@ def main():
     if args.restated:
         if rank == 0:
             restated_arm(args, local)
+        return
+    if args.torch_runtime:
+        if rank == 0:
+            torch_runtime_arm(args, local)
         return
     if args.profile:
         if rank == 0:

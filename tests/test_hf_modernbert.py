@@ -172,3 +172,27 @@ def test_oracle_forward_matches_transformers_and_torch_modules(jc, O, tmp_path):
     d = np.max(np.abs(logits - want)) / max(float(np.sqrt(np.mean(want.astype(np.float64) ** 2))), 1e-30)
     assert d < 1e-4, (logits, want)
     print(f"logits {logits} vs {want}: max |d| / rms {d:.2e}")
+
+
+def test_torch_runtime_matches_the_oracle(jc, O, tmp_path):
+    """baseline/torch_runtime.py (the reference's torch-runtime comparison assembled from
+    transformers' ModernBertModel and torch modules; what `bench.py --torch-runtime` runs on the
+    GPU), in f32 on the CPU, against the oracle's f32 forward on a small model at one key tile and
+    at several: the same logits."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "baseline"))
+    from torch_runtime import TorchRuntime
+    c = jc.default_config(d_model=256, inter=384, n_layers=4, vocab=1000, max_positions=512)
+    raw = O.init_random(oracle_cfg(O, c), 5)
+    jc.save_checkpoint(str(tmp_path), c, raw)
+    rt = TorchRuntime(str(tmp_path), device="cpu", dtype="fp32", attn="eager")
+    rng = np.random.default_rng(7)
+    for n, qtype in ((37, 0), (300, 2)):
+        ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+        markers = np.sort(rng.choice(n, 4, replace=False)).astype(np.uint32)
+        got = rt.forward(ids, markers, qtype)
+        want = np.asarray(O.forward_f32(oracle_cfg(O, c), raw, ids, markers, qtype), np.float64)
+        rms = max(float(np.sqrt(np.mean(want ** 2))), 1e-30)
+        d = float(np.max(np.abs(got - want))) / rms
+        assert d < 1e-4, (n, got, want)
