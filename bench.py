@@ -16,6 +16,9 @@ embed -> logits. With --gpus N (torchrun), every rank runs its own engine on its
   roofline   the kernel with the largest share of a forward pass, timed alone (its launches in a CUDA
              graph, each after an L2 flush, less the flushes' own time) with CUDA events.
   cpu_baseline  the oracle's f32 forward (C, OpenMP over the host's cores) on a bounded sample.
+  torch_runtime  the same model in transformers + torch modules on the same GPU (the reference's
+             torch-runtime comparison, BF16 autocast): 128 config-3 requests one at a time through
+             both, agreement and wall time per request (N = 1 only).
 
 --impl reference: the reference's own CPU path cannot be built here (Rust / julia-rs absent), so
 the reference arm times the oracle's f32 restatement of it on all host cores.
@@ -827,19 +830,16 @@ def profile_persistent(args, eng, cfg, ids_d, mk_d, logits, flush, mode):
           flush=True)
 
 
-def torch_runtime_arm(args, local):
+def torch_runtime_compare(jc, local, dtype, n_requests):
     """The reference's torch-runtime comparison (tools/torch_baseline.py with tools/score.py) on
     one GPU: seeded config-0 weights written as a checkpoint, loaded both by this library
     (julia_cuda_load) and by the torch runtime assembled from transformers' ModernBertModel and
-    torch modules (baseline/torch_runtime.py, autocast --torch-dtype: the reference runtime's
-    default is BF16); --torch-requests seeded config-3 requests (log-normal lengths) through both,
-    one at a time, wall time per request as the reference measures its runtime (host arrays in,
-    logits back on the host), timed on a second pass after an untimed one over the same requests;
-    the answers compared as tools/score.py compares two runs. One JSON line."""
+    torch modules (baseline/torch_runtime.py, autocast `dtype`: the reference runtime's default is
+    BF16); `n_requests` seeded config-3 requests (log-normal lengths) through both, one at a time,
+    wall time per request as the reference measures its runtime (host arrays in, logits back on
+    the host), timed on a second pass after an untimed one over the same requests; the answers
+    compared as tools/score.py compares two runs. Returns the summary dict."""
     import tempfile
-    import torch
-    torch.cuda.set_device(local)
-    jc = importlib.import_module("julia-cuda_b200")
     replicas = importlib.import_module("julia-cuda_b200.replicas")
     scoring = importlib.import_module("julia-cuda_b200.scoring")
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
@@ -848,8 +848,8 @@ def torch_runtime_arm(args, local):
     with tempfile.TemporaryDirectory() as d:
         jc.save_checkpoint(d, cfg, jc.init_random(cfg, SEED))
         eng = jc.Engine.load(d, max_length=1024)
-        rt = TorchRuntime(d, device=f"cuda:{local}", dtype=args.torch_dtype)
-    reqs = replicas.serving_requests(args.torch_requests, SEED, cfg.vocab)
+        rt = TorchRuntime(d, device=f"cuda:{local}", dtype=dtype)
+    reqs = replicas.serving_requests(n_requests, SEED, cfg.vocab)
     for r in reqs:  # warm-up pass: every length once (this library's CUDA graph per length,
         rt.forward(*r)  # the runtime's kernel choices per shape), then the timed pass
         eng.run([r])
@@ -866,12 +866,13 @@ def torch_runtime_arm(args, local):
             t_ours.append(t1 - t0)
             t_theirs.append(t2 - t1)
     eng.close()
+    del rt
     a = scoring.agreement(ours, theirs)
     rms = float(np.sqrt(np.mean(np.concatenate(theirs).astype(np.float64) ** 2)))
     lens = [len(r[0]) for r in reqs]
-    print(json.dumps({
+    return {
         "torch_runtime": "transformers ModernBertModel + torch.nn.TransformerEncoderLayer head + "
-                         "scorer (baseline/torch_runtime.py), autocast " + args.torch_dtype,
+                         "scorer (baseline/torch_runtime.py), autocast " + dtype,
         "requests": len(reqs), "tokens_mean": float(np.mean(lens)),
         "ours_ms_per_request": 1e3 * statistics.mean(t_ours),
         "torch_ms_per_request": 1e3 * statistics.mean(t_theirs),
@@ -880,7 +881,16 @@ def torch_runtime_arm(args, local):
         "timing": "wall clock per request, one request at a time, host arrays in and logits out "
                   "(julia_cuda_run for this library); requests alternate between the two; the "
                   "timed pass follows an untimed pass over the same requests",
-        "clocks": clk.summary(), "data": "synthetic (seeded weights and requests)"}), flush=True)
+        "clocks": clk.summary(), "data": "synthetic (seeded weights and requests)"}
+
+
+def torch_runtime_arm(args, local):
+    """torch_runtime_compare alone (--torch-dtype, --torch-requests): one JSON line."""
+    import torch
+    torch.cuda.set_device(local)
+    jc = importlib.import_module("julia-cuda_b200")
+    print(json.dumps(torch_runtime_compare(jc, local, args.torch_dtype, args.torch_requests)),
+          flush=True)
 
 
 METRIC = "requests/s (embed->logits, 293-token requests, batch 1 per engine)"
@@ -1127,11 +1137,18 @@ def main():
                               if args.serving_pack else
                               "julia_cuda_run, per-step kernels, one forward per request"}}
 
-    roofline = kernels = restated_line = None
+    roofline = kernels = restated_line = torch_rt = None
     cpu = None
     if rank == 0 and n_tok == SEQ and not args.head_length and fused == 0:
         restated_line = restated_headline(jc, torch, cfg, eng, ids, markers, flush, args.steps,
                                           local)
+        if world == 1:
+            # The reference's torch-runtime comparison, after the timed region (128 config-3
+            # requests, BF16 autocast as the reference runtime runs by default).
+            try:
+                torch_rt = torch_runtime_compare(jc, local, "bf16", 128)
+            except Exception as exc:  # the headline stands without it
+                torch_rt = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0:
         pk, src = peaks()
         kt = time_kernels(jc, torch, cfg, flush, n=n_tok)
@@ -1203,6 +1220,8 @@ def main():
             line.update(restated_line)
         if serving:
             line["serving"] = serving
+        if torch_rt:
+            line["torch_runtime"] = torch_rt
         print(json.dumps(line), flush=True)
     eng.close()
     replicas.finalize(world)
