@@ -217,7 +217,6 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
     reference's kernel for the same shape on the same inputs, timed the same way; with `cublas`,
     {name + "@cublas": ...}: torch.mm (cuBLAS) of the same f16 operands, a plain GEMM without
     the fused epilogue, timed the same way."""
-    from oracle import oracle as O
     out = {}
     stream = torch.cuda.current_stream()
     torch.manual_seed(n)
@@ -232,7 +231,7 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
         st = torch.rand(2 * n, device="cuda") + 1.0
         st[1::2] += 800.0
         cs = torch.randn(N, device="cuda")
-        rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
+        rope = torch.from_numpy(jc.prep_rope_gemm(jc.prep_rope_table(160000.0, n), n)).cuda()
         bias = torch.randn(N, device="cuda")
         so = torch.zeros(2 * n, device="cuda")
         ws, cnt = jc.gemm_scratch(n, N, K)
@@ -248,7 +247,7 @@ def time_kernels(jc, torch, cfg, flush, reps=30, n=SEQ, gemms=None, attention=Tr
         if restated is not None:
             sms = torch.cuda.get_device_properties(0).multi_processor_count
             rws, rcnt = restated.gemm_scratch(torch, n, N, K, sms)
-            rtab = torch.from_numpy(O.rope_table(160000.0, n)).cuda()
+            rtab = torch.from_numpy(jc.prep_rope_table(160000.0, n)).cuda()
 
             def launch_ref():
                 restated.gemm(torch, epi, a, w, c, sms, res=c if epi & jc.EPI_RES else None,
@@ -383,7 +382,6 @@ def tile_sweep_arm(args, local):
     import torch
     torch.cuda.set_device(local)
     jc = importlib.import_module("julia-cuda_b200")
-    from oracle import oracle as O
     cfg = jc.default_config(max_positions=6144)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
@@ -401,7 +399,7 @@ def tile_sweep_arm(args, local):
                 st = torch.rand(2 * n, device="cuda") + 1.0
                 st[1::2] += 800.0
                 cs = torch.randn(N, device="cuda")
-                rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
+                rope = torch.from_numpy(jc.prep_rope_gemm(jc.prep_rope_table(160000.0, n), n)).cuda()
                 so = torch.zeros(2 * n, device="cuda")
                 cases = ([(bn, False) for bn in (32, 64, 128, 256)] if n <= 1024 else
                          [(128, False), (256, False), (128, True), (256, True)])
@@ -483,7 +481,6 @@ def one_kernel_arm(args, local):
     import torch
     torch.cuda.set_device(local)
     jc = importlib.import_module("julia-cuda_b200")
-    from oracle import oracle as O
     cfg = jc.default_config(max_positions=1024)
     n = args.seq
     torch.manual_seed(n)
@@ -497,7 +494,7 @@ def one_kernel_arm(args, local):
         st = torch.rand(2 * n, device="cuda") + 1.0
         st[1::2] += 800.0
         cs, bias, so = torch.randn(N, device="cuda"), torch.randn(N, device="cuda"), torch.zeros(2 * n, device="cuda")
-        rope = torch.from_numpy(jc.prep_rope_gemm(O.rope_table(160000.0, n), n)).cuda()
+        rope = torch.from_numpy(jc.prep_rope_gemm(jc.prep_rope_table(160000.0, n), n)).cuda()
         ws, cnt = jc.gemm_scratch(n, N, K)
 
         def launch():
