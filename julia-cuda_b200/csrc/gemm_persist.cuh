@@ -260,27 +260,37 @@ __device__ __forceinline__ bool persist_tile_epilogue(const GemmParams &p, uint3
     if (!quarter_and(quarter, mbar_wait_sleep(acc_full, parity, JC_DEV_TIMEOUT_MMA))) return false;
     tc_fence_after();
     float s = 0.f, q = 0.f;
-#pragma unroll 1
-    for (uint32_t ci = 0; ci < (uint32_t)BN / 64; ci++) {
-        float v[2 * GW];
+    // A chunk's accumulator columns are requested while the chunk before it is processed: two
+    // register sets, alternating (the loop is unrolled, so both stay in registers).
+    constexpr int CHUNKS = BN / 64;
+    float vv[2][2 * GW];
+    float tt[2][NI > 1 ? 2 * GW : 1];
+    auto request = [&](uint32_t ci, int b) {
         const uint32_t col = acc + ci * 64 + GW * g;
-        tmem_ld<GW>(col, v);
-        tmem_ld<GW>(col + 32, v + GW);
+        tmem_ld<GW>(col, vv[b]);
+        tmem_ld<GW>(col + 32, vv[b] + GW);
         if constexpr (NI > 1) {
-            float t2[2 * GW];
-            tmem_ld<GW>(col + BN, t2);
-            tmem_ld<GW>(col + BN + 32, t2 + GW);
-            tc_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 2 * GW; e++) v[e] += t2[e];
-        } else {
-            tc_wait_ld();
+            tmem_ld<GW>(col + BN, tt[b]);
+            tmem_ld<GW>(col + BN + 32, tt[b] + GW);
         }
-        if (ci == (uint32_t)BN / 64 - 1) {
+    };
+    request(0, 0);
+#pragma unroll
+    for (uint32_t ci = 0; ci < (uint32_t)CHUNKS; ci++) {
+        const int b = ci & 1;
+        tc_wait_ld();
+        if (ci + 1 < (uint32_t)CHUNKS) {
+            request(ci + 1, b ^ 1);
+        } else {
             // This warp has read every column of the buffer it reads.
             tc_fence_before();
             __syncwarp();
             if (lane == 0) release();
+        }
+        float *v = vv[b];
+        if constexpr (NI > 1) {
+#pragma unroll
+            for (int e = 0; e < 2 * GW; e++) v[e] += tt[b][e];
         }
         uint32_t resw[GW];
         if constexpr ((EPI & JC_EPI_RES) != 0) {
