@@ -18,6 +18,7 @@ julia_cuda_save_checkpoint writes it, default tensor names):
 
 tests/test_hf_modernbert.py pins this assembly to the oracle's f32 forward on the CPU, and
 `python bench.py --torch-runtime` runs it on a B200 beside this library (agreement and latency).
+Run as a script it serves request JSONL like the julia-cuda executable (see main()).
 """
 import json
 import os
@@ -132,3 +133,48 @@ class TorchRuntime:
             z = x[0, mk]
             logits = self.lin2(torch.nn.functional.gelu(self.lin1(self.norm(z))))[:, 0]
         return logits.float().cpu().numpy()
+
+
+QTYPES = {"choice": 0, "score": 1, "noul": 2}
+
+
+def result_line(logits: np.ndarray, ms: float) -> dict:
+    """A result in the format the julia-cuda executable writes (and tools/score.py reads): the
+    marker logits, their softmax, the argmax marker, "truncated" false, and the wall time."""
+    lg = np.asarray(logits, np.float64)
+    p = np.exp(lg - lg.max()) if lg.size else lg
+    return {"logits": [float(v) for v in lg],
+            "probabilities": [float(v) for v in p / p.sum()] if lg.size else [],
+            "choice": int(np.argmax(lg)) if lg.size else None, "truncated": False,
+            "wall_ms": ms}
+
+
+def main(argv=None) -> int:
+    """python baseline/torch_runtime.py MODEL_DIR [--device cuda] [--dtype bf16] < requests.jsonl
+    > results.jsonl: token-id requests ({"ids": [...], "markers": [...], "qtype": 0-2 or
+    "choice" / "score" / "noul"}, as the julia-cuda executable reads them) one at a time through
+    the torch runtime, one result line each; julia-cuda_b200/scoring.py compares two such runs."""
+    import argparse
+    import sys
+    import time
+    ap = argparse.ArgumentParser()
+    ap.add_argument("model_dir")
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp16", "fp32"])
+    ap.add_argument("--attn", default="sdpa", choices=["sdpa", "eager"])
+    args = ap.parse_args(argv)
+    rt = TorchRuntime(args.model_dir, device=args.device, dtype=args.dtype, attn=args.attn)
+    for line in sys.stdin:
+        if not line.strip():
+            continue
+        req = json.loads(line)
+        q = req.get("qtype", 0)
+        q = QTYPES[q] if isinstance(q, str) else int(q)
+        t0 = time.perf_counter()
+        logits = rt.forward(req["ids"], req["markers"], q)
+        print(json.dumps(result_line(logits, 1e3 * (time.perf_counter() - t0))), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -196,3 +196,38 @@ def test_torch_runtime_matches_the_oracle(jc, O, tmp_path):
         rms = max(float(np.sqrt(np.mean(want ** 2))), 1e-30)
         d = float(np.max(np.abs(got - want))) / rms
         assert d < 1e-4, (n, got, want)
+
+
+def test_torch_runtime_serves_request_jsonl(jc, O, tmp_path, monkeypatch, capsys):
+    """baseline/torch_runtime.py as a script: request JSONL in (the julia-cuda executable's
+    format, question types by number or name), result lines out with the oracle's logits, their
+    softmax and the argmax marker, as tools/score.py reads them."""
+    import io
+    import json as js
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "baseline"))
+    import torch_runtime
+    c = jc.default_config(d_model=256, inter=384, n_layers=4, vocab=1000, max_positions=512)
+    raw = O.init_random(oracle_cfg(O, c), 9)
+    jc.save_checkpoint(str(tmp_path), c, raw)
+    rng = np.random.default_rng(3)
+    reqs = []
+    for n, q in ((50, "score"), (130, 2)):
+        ids = rng.integers(0, c.vocab, n).astype(np.uint32)
+        markers = np.sort(rng.choice(n, 3, replace=False)).astype(np.uint32)
+        reqs.append((ids, markers, q))
+    text = "".join(js.dumps({"ids": ids.tolist(), "markers": m.tolist(), "qtype": q}) + "\n"
+                   for ids, m, q in reqs)
+    monkeypatch.setattr(sys, "stdin", io.StringIO(text))
+    assert torch_runtime.main([str(tmp_path), "--device", "cpu", "--dtype", "fp32",
+                               "--attn", "eager"]) == 0
+    lines = [js.loads(l) for l in capsys.readouterr().out.splitlines() if l.strip()]
+    assert len(lines) == 2
+    for (ids, m, q), res in zip(reqs, lines):
+        want = np.asarray(O.forward_f32(oracle_cfg(O, c), raw, ids, m,
+                                        torch_runtime.QTYPES.get(q, q)), np.float64)
+        got = np.asarray(res["logits"])
+        assert np.max(np.abs(got - want)) / max(float(np.sqrt(np.mean(want ** 2))), 1e-30) < 1e-4
+        assert res["choice"] == int(np.argmax(got))
+        assert abs(sum(res["probabilities"]) - 1.0) < 1e-9 and res["truncated"] is False
